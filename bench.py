@@ -1,0 +1,419 @@
+"""Benchmark: Jacobi-2D Gcell-updates/s (+ reduction GB/s) and % of HBM roofline on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl spmd|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU)
+
+Workload (one "step"): the multi-GPU Jacobi-2D configuration -- a 32768 x 32768
+f32 row slab per GPU (weak scaling: the global grid is (32768*N) x 32768),
+interior uniform [0,1) from seed 4, zero boundary rows/columns, 1000 ping-pong
+sweeps, a global L2 residual every 10 sweeps.  Inputs are device-resident when
+the timed region starts (4 GiB per grid, far above the 126 MB L2, so no L2
+flush is needed between steps).  At N > 1 the slabs exchange one halo row per
+neighbour per sweep over NVLink inside the persistent kernel.
+
+`value` is device time (CUDA events, max over ranks); `e2e` runs the same job
+through the host-buffer C entry (pinned host grid in, result grid out, both
+copies inside the timed region).  `roofline` uses the algorithmic 8 bytes per
+cell update (read u once, write v once) against the measured HBM copy
+bandwidth.  `cpu_baseline` times the oracle (the C/OpenMP restatement of the
+reference's SPMDToOpenMP lowering) on a bounded sample of the same grid.
+`--impl reference` times that CPU path alone (the reference itself needs
+MLIR/LLVM 20 to build and cannot run here).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Jacobi-2D Gcell-updates/s & reduction GB/s, % of HBM roofline, at 1/2/4/8 B200"
+GRID = 32768
+SWEEPS = 1000
+RES_EVERY = 10
+BYTES_PER_UPDATE = 8  # algorithmic: read u[i,j] once, write v[i,j] once
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic_per_update(kernel: str) -> float | None:
+    """DRAM bytes per cell update from the committed ncu summary, if one exists."""
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        for line in f.read_text().splitlines():
+            if line.startswith(f"traffic_bytes_per_update[{kernel}]:"):
+                try:
+                    return float(line.split(":", 1)[1].split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+# ------------------------------------------------------------------ clocks sampler
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread:
+                self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        under_load = [s for s in sm if s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(under_load), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ distributed plumbing
+def dist_env() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def cpu_count() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------ CPU (oracle) leg
+def cpu_jacobi_sample(target_s: float = 12.0, rows: int = 2048, cols: int = GRID) -> dict:
+    """Oracle Jacobi-2D sweeps over a rows x cols slab of the workload grid (same
+    row width), repeated until ~target_s of CPU work; Gcell-updates/s."""
+    from oracle import oracle
+    threads = oracle.num_threads()
+    rng = np.random.RandomState(4)
+    u = rng.random_sample((rows, cols)).astype(np.float32)
+    u[0] = 0; u[-1] = 0; u[:, 0] = 0; u[:, -1] = 0
+    v = np.empty_like(u)
+    rr = np.zeros(rows, np.float64)
+    oracle.jacobi2d_rows(u, v, 0, rows, 0, rows)  # warm-up (page faults, thread pool)
+    sweeps, t0 = 0, time.perf_counter()
+    while True:
+        want = (sweeps + 1) % RES_EVERY == 0
+        oracle.lib().oracle_jacobi2d_rows(oracle._p(u), oracle._p(v), cols, cols, 0, rows, 0, rows,
+                                          oracle._p(rr) if want else None)
+        u, v = v, u
+        sweeps += 1
+        el = time.perf_counter() - t0
+        if el >= target_s and sweeps >= 3:
+            break
+    gcell = rows * cols * sweeps / el / 1e9
+    return {"value": round(gcell, 4), "unit": "Gcell-updates/s", "cores": threads, "kind": "port",
+            "sample": f"{rows}x{cols} rows of the workload grid, {sweeps} sweeps (residual every {RES_EVERY}), "
+                      f"{el:.1f} s, OpenMP threads={threads}, host cpus={cpu_count()}"}
+
+
+def run_reference_arm(args) -> None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    # Each step: a bounded sample of the workload on all host cores.
+    for _ in range(args.warmup):
+        cpu_jacobi_sample(target_s=2.0)
+    vals, times = [], []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        r = cpu_jacobi_sample(target_s=6.0)
+        times.append((time.perf_counter() - t0) * 1e3)
+        vals.append(r["value"])
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "Gcell-updates/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(statistics.mean(times), 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic: RandomState(4) uniform [0,1), zero boundary",
+        "config": {"workload": "jacobi2d 5-point, 32768 columns x 2048-row sample, 1000-sweep config, CPU",
+                   "grid": [GRID, GRID], "sweeps": SWEEPS, "res_every": RES_EVERY},
+        "cpu_baseline": {**r, "value": value},
+        "e2e": {"value": value, "unit": "Gcell-updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's SPMDToOpenMP path needs MLIR/LLVM 20.1.7 to build (absent, no network); "
+                "this arm times the C/OpenMP restatement of that lowering (the oracle) on all host cores",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU legs
+def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
+    """The other configurations at N=1 (rank 0): f32/i32 sum 2^24, axpy 2^28,
+    Jacobi-2D 4096^2 x 100, Jacobi-3D 512^3 x 50.  L2 flushed between reps."""
+    out = {}
+    dev = torch.device("cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MiB > 126 MB L2
+    st = torch.cuda.current_stream()
+
+    def timed(fn, reps=10, warm=3, flush_l2=True):
+        for _ in range(warm):
+            fn()
+        ts = []
+        for _ in range(reps):
+            if flush_l2:
+                flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            fn()
+            b.record(st)
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    n = 1 << 24
+    a = torch.rand(n, device=dev, generator=g)
+    o = torch.zeros(1, device=dev)
+    ws = kernels.sum_workspace(n)
+    ms = timed(lambda: kernels.sum_f32(a, o, ws))
+    gbs = n * 4 / ms / 1e6
+    out["sum_f32_2^24"] = {"ms": round(ms, 5), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3)}
+    ai = torch.randint(0, 100, (n,), device=dev, dtype=torch.int32, generator=g)
+    oi = torch.zeros(1, device=dev, dtype=torch.int32)
+    ms = timed(lambda: kernels.sum_i32(ai, oi))
+    gbs = n * 4 / ms / 1e6
+    out["sum_i32_2^24"] = {"ms": round(ms, 5), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3)}
+    del a, ai
+    n = 1 << 28
+    x = torch.rand(n, device=dev, generator=g) * 2 - 1
+    y = torch.rand(n, device=dev, generator=g) * 2 - 1
+    ms = timed(lambda: kernels.axpy(2.5, x, y), flush_l2=False)
+    gbs = n * 12 / ms / 1e6
+    out["axpy_2^28"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3)}
+    del x, y
+    u = torch.rand((4096, 4096), device=dev, generator=g)
+    u[0] = 0; u[-1] = 0; u[:, 0] = 0; u[:, -1] = 0
+    v = torch.empty_like(u)
+    jws = kernels.jacobi_workspace()
+    res = torch.zeros(10, dtype=torch.float64, device=dev)
+    ms = timed(lambda: kernels.jacobi2d(u, v, 100, 10, ws=jws, res=res, check=False), reps=5)
+    kernels.workspace_status(jws)
+    gc = 4096 * 4096 * 100 / ms / 1e6
+    out["jacobi2d_4096^2_x100"] = {"ms": round(ms, 4), "Gcell/s": round(gc, 1),
+                                   "frac_of_hbm": round(gc * BYTES_PER_UPDATE / hbm_peak, 3),
+                                   "note": "128 MiB working set is L2-sized: fractions above 1 mean L2 reuse"}
+    del u, v
+    u = torch.rand((512, 512, 512), device=dev, generator=g)
+    v = torch.empty_like(u)
+    res = torch.zeros(5, dtype=torch.float64, device=dev)
+    ms = timed(lambda: kernels.jacobi3d(u, v, 50, 10, ws=jws, res=res, check=False), reps=3, warm=1)
+    kernels.workspace_status(jws)
+    gc = 512 ** 3 * 50 / ms / 1e6
+    out["jacobi3d_512^3_x50"] = {"ms": round(ms, 3), "Gcell/s": round(gc, 1),
+                                 "frac_of_hbm": round(gc * BYTES_PER_UPDATE / hbm_peak, 3)}
+    del u, v, flush
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_spmd_arm(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    kernels = importlib.import_module("spmd-dialect_b200.kernels")
+    slab = importlib.import_module("spmd-dialect_b200.slab") if world > 1 else None
+    hbm_peak, peak_kind = measured_peaks()
+
+    # ---- device-resident workload ------------------------------------------------
+    rows = GRID
+    if world == 1:
+        g = torch.Generator(device=dev).manual_seed(4)
+        u = torch.rand((rows, GRID), device=dev, generator=g)
+        u[0] = 0; u[-1] = 0; u[:, 0] = 0; u[:, -1] = 0
+        v = torch.empty_like(u)
+        ws = kernels.jacobi_workspace(dev)
+        res = torch.zeros(SWEEPS // RES_EVERY, dtype=torch.float64, device=dev)
+
+        def step():
+            kernels.jacobi2d(u, v, SWEEPS, RES_EVERY, ws=ws, res=res, check=False)
+
+        def finish():
+            kernels.workspace_status(ws)
+    else:
+        job = slab.SlabJacobi2D(rows_per_rank=rows, cols=GRID, seed=4, res_every=RES_EVERY)
+
+        def step():
+            job.run(SWEEPS, check=False)
+
+        def finish():
+            job.check()
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step()
+    finish()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        evs[0].record(stream)
+        for k in range(args.steps):
+            step()
+            evs[k + 1].record(stream)
+        torch.cuda.synchronize()
+    finish()
+    per_step = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
+    ms_local = evs[0].elapsed_time(evs[-1]) / args.steps
+    t = torch.tensor([ms_local, statistics.mean(per_step)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step, ms_kernel = float(t[0]), float(t[1])
+    updates = rows * GRID * SWEEPS * world
+    value = updates / (ms_step * 1e-3) / 1e9
+
+    # ---- e2e through the host-buffer C entry -------------------------------------
+    e2e = None
+    if world == 1:
+        host = importlib.import_module("spmd-dialect_b200.host")
+        hbuf = torch.empty((rows, GRID), dtype=torch.float32, pin_memory=True)
+        hbuf.copy_(u, non_blocking=False)
+        hnp = hbuf.numpy()
+        host.jacobi2d_host(hnp, 2, 0)  # warm-up: staging buffers allocated once
+        e2e_ts = []
+        for _ in range(max(1, min(args.steps, 3))):
+            hbuf.copy_(u, non_blocking=False)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            host.jacobi2d_host(hnp, SWEEPS, RES_EVERY)
+            e2e_ts.append(time.perf_counter() - t0)
+        e2e_s = statistics.mean(e2e_ts)
+        e2e = {"value": round(rows * GRID * SWEEPS / e2e_s / 1e9, 3), "unit": "Gcell-updates/s",
+               "h2d_bytes_per_step": rows * GRID * 4,
+               "d2h_bytes_per_step": rows * GRID * 4 + (SWEEPS // RES_EVERY) * 8,
+               "entry": "spmdb200_jacobi2d_host (pinned host grid)"}
+        del hbuf
+        getattr(importlib.import_module("spmd-dialect_b200._lib"), "lib")().spmdb200_release_cache()
+    else:
+        e2e = slab.e2e_measure(job, SWEEPS) if hasattr(slab, "e2e_measure") else None
+
+    # ---- roofline of the dominant kernel (the persistent sweep kernel) --------------
+    achieved = rows * GRID * SWEEPS * BYTES_PER_UPDATE / (ms_kernel * 1e-3) / 1e9
+    tpu = profile_traffic_per_update("jacobi2d_persistent_kernel")
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4),
+                "traffic": (round(tpu * rows * GRID * SWEEPS) if tpu else None),
+                "kernel": "jacobi2d_persistent_kernel", "peak_kind": f"{peak_kind} hbm_gbs (copy bandwidth)",
+                "algorithmic_bytes_per_launch": rows * GRID * SWEEPS * BYTES_PER_UPDATE}
+
+    cpu = None
+    secondary = None
+    if rank == 0 and world == 1:
+        secondary = secondary_benchmarks(kernels, torch, hbm_peak)
+        cpu = cpu_jacobi_sample()
+    clocks = clk.summary()
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "Gcell-updates/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: torch Philox uniform [0,1) seeded 4 on device, zero boundary",
+            "config": {"workload": "jacobi2d 5-point, 32768x32768 f32 row slab per GPU, 1000 sweeps, "
+                                   "residual every 10 (multi-GPU Jacobi-2D config, weak-scaled)",
+                       "grid_per_gpu": [rows, GRID], "global_grid": [rows * world, GRID], "sweeps": SWEEPS,
+                       "res_every": RES_EVERY, "parallelism": f"row-slab x{world}",
+                       "l2": "inputs (4 GiB per grid) larger than L2; no flush needed"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+            "clocks": clocks, "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        if slab is not None:
+            job.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["spmd", "reference"], default="spmd")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_spmd_arm(args)
+
+
+if __name__ == "__main__":
+    main()

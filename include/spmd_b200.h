@@ -1,0 +1,242 @@
+/*
+ * spmd_b200.h -- C ABI of libspmdb200.so, the B200 (sm_100a) implementation of
+ * the kernels that spmd-dialect's SPMDToGPU lowering emits:
+ *
+ *   (1) elementwise spmd.forall maps            (ewise, axpy)
+ *   (2) PromoteGroupMemory-tiled stencil sweeps (3-point promoted stencil,
+ *       Jacobi-2D 5-point, Jacobi-3D 7-point)
+ *   (3) ReduceToHierarchicalGPU spmd.reduce     (f32 sum, i32 sum)
+ *
+ * Memref descriptors follow MLIR's unpacked memref-to-LLVM convention
+ * (harness/run_host.py:8-11,41-65 in the reference):
+ *   rank-0 memref : (T* base, T* aligned, int64 offset)
+ *   rank-1 memref : (T* base, T* aligned, int64 offset, int64 size, int64 stride)
+ *   rank-2 memref : (base, aligned, offset, size0, size1, stride0, stride1)
+ *   rank-3 memref : (base, aligned, offset, size0, size1, size2,
+ *                    stride0, stride1, stride2)
+ * Element (i,j) of a rank-2 memref lives at aligned[offset + i*stride0 + j*stride1].
+ * `base` is carried for ABI compatibility and never dereferenced.
+ *
+ * Three families of entry points:
+ *
+ *  A. Reference-named HOST entries (`ewise`, `stencil_cpu`, `atomic_sum`,
+ *     `hierarchical_sum`).  Same names and unpacked signatures as the
+ *     SPMDToSCF / SPMDToOpenMP shared libraries that harness/run_host.py loads
+ *     with ctypes (restype=None).  Buffers are HOST memory; the entry copies
+ *     them to the current CUDA device, runs the B200 kernel, copies the result
+ *     back and synchronises.  Errors cannot be returned through `void`; they are
+ *     printed to stderr and kept for spmdb200_last_error().
+ *
+ *  B. `spmdb200_*` DEVICE entries.  Same descriptor convention, device
+ *     pointers, an explicit cudaStream_t (passed as void*; NULL = legacy default
+ *     stream), asynchronous, returning an int status (SPMDB200_OK = 0).
+ *
+ *  C. `spmdb200_*_host` END-TO-END entries for the configurations the
+ *     reference has no kernel for (axpy, Jacobi-2D/3D): host buffers in, host
+ *     buffers out, synchronous, int status.
+ *
+ * The device kernels with the reference's PTX entry names and .param layouts
+ * (ewise_kernel, promoted_stencil_kernel, atomic_sum_kernel,
+ * hierarchical_sum_kernel) ship in spmdb200_kernels.cubin for
+ * cuModuleLoadData-based callers (harness/cuda_driver.py:124-140); they are
+ * not C functions and are documented in INTEGRATION.md.
+ */
+#ifndef SPMD_B200_H
+#define SPMD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------- */
+#define SPMDB200_OK               0
+#define SPMDB200_ERR_INVALID_ARG (-1) /* bad descriptor: null data, negative size/stride, bound > size */
+#define SPMDB200_ERR_CUDA        (-2) /* a CUDA runtime call or a launch failed */
+#define SPMDB200_ERR_TIMEOUT     (-3) /* a bounded device-side wait expired (grid barrier / peer flag) */
+#define SPMDB200_ERR_UNSUPPORTED (-4) /* layout outside what the entry accepts */
+#define SPMDB200_ERR_WORKSPACE   (-5) /* workspace null, too small or misaligned */
+#define SPMDB200_ERR_NO_DEVICE   (-6) /* no CUDA device visible */
+
+const char *spmdb200_status_string(int status);
+/* Last status recorded by any entry on this host thread (0 after success). */
+int spmdb200_last_error(void);
+const char *spmdb200_last_error_message(void);
+/* Library version string and the device architecture it was built for. */
+const char *spmdb200_version(void);
+/* Frees the device staging buffers cached by the family-A/C host entries. */
+int spmdb200_release_cache(void);
+
+/* =========================================================================
+ * A. Reference-named host entries (drop-in for the SCF/OpenMP .so files).
+ * ========================================================================= */
+
+/* C[i] = A[i] + B[i], i < N.
+ * Replaces `ewise` from test/SPMD/lower-to-gpu-nvptx.mlir:54-71 as loaded by
+ * harness/run_host.py:84-101 (_EWISE_ARGTYPES). */
+void ewise(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+           float *B_base, float *B_aligned, int64_t B_offset, int64_t B_size, int64_t B_stride,
+           float *C_base, float *C_aligned, int64_t C_offset, int64_t C_size, int64_t C_stride,
+           int64_t N);
+
+/* B[i,j] = (A[i,j] + A[i,j+1]) + A[i+1,j] for i < N, j < M.  A is normally
+ * (N+1)x(M+1); reads outside A's sizes contribute 0.
+ * Replaces `stencil_cpu` from test/SPMD/differential-stencil.mlir:19-37 as
+ * loaded by harness/run_host.py:119-137 (_STENCIL_ARGTYPES). */
+void stencil_cpu(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size0, int64_t A_size1,
+                 int64_t A_stride0, int64_t A_stride1,
+                 float *B_base, float *B_aligned, int64_t B_offset, int64_t B_size0, int64_t B_size1,
+                 int64_t B_stride0, int64_t B_stride1,
+                 int64_t N, int64_t M);
+
+/* out[] += sum(A[0..N)).  Caller zero-initialises out for a plain sum.
+ * Replaces `atomic_sum` from test/SPMD/lower-to-gpu-nvptx-reduction.mlir:30-44
+ * as loaded by harness/run_host.py:160-175 (_REDUCTION_ARGTYPES). */
+void atomic_sum(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+                float *out_base, float *out_aligned, int64_t out_offset,
+                int64_t N);
+
+/* Same contract as atomic_sum.
+ * Replaces `hierarchical_sum` from
+ * test/SPMD/lower-to-gpu-nvptx-hierarchical-reduction.mlir:58-88 as loaded by
+ * harness/run_host.py:195-203. */
+void hierarchical_sum(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+                      float *out_base, float *out_aligned, int64_t out_offset,
+                      int64_t N);
+
+/* =========================================================================
+ * B. Device entries (device pointers, stream-ordered, int status).
+ * ========================================================================= */
+
+/* C = A + B (f32), the device-pointer form of the launch in
+ * harness/run_ewise.py:53-70 (ewise_kernel). */
+int spmdb200_ewise(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+                   float *B_base, float *B_aligned, int64_t B_offset, int64_t B_size, int64_t B_stride,
+                   float *C_base, float *C_aligned, int64_t C_offset, int64_t C_size, int64_t C_stride,
+                   int64_t N, void *stream);
+
+/* Y[i] = fadd(fmul(a, X[i]), Y[i]) with no FMA contraction: the elementwise
+ * spmd.forall y = a*x + y lowered the way lane foralls are lowered in
+ * lib/Conversion/SPMDToGPU/SPMDToGPU.cpp:491-580.  No reference entry. */
+int spmdb200_axpy(float a,
+                  float *X_base, float *X_aligned, int64_t X_offset, int64_t X_size, int64_t X_stride,
+                  float *Y_base, float *Y_aligned, int64_t Y_offset, int64_t Y_size, int64_t Y_stride,
+                  int64_t N, void *stream);
+
+/* 3-point promoted stencil B[i,j] = (A[i,j] + A[i,j+1]) + A[i+1,j] over
+ * i < N, j < M with a shared-memory tile plus 1-cell halo; reads outside A's
+ * sizes contribute 0.  Device-pointer form of promoted_stencil_kernel
+ * (test/SPMD/lower-to-gpu-nvptx-promoted.mlir:32-67,
+ * harness/run_promoted_stencil.py:68-108). */
+int spmdb200_stencil3pt(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size0, int64_t A_size1,
+                        int64_t A_stride0, int64_t A_stride1,
+                        float *B_base, float *B_aligned, int64_t B_offset, int64_t B_size0, int64_t B_size1,
+                        int64_t B_stride0, int64_t B_stride1,
+                        int64_t N, int64_t M, void *stream);
+
+/* Bytes of device workspace spmdb200_sum_f32 needs for N elements. */
+size_t spmdb200_sum_workspace_bytes(int64_t N);
+
+/* out[] = (float)((double)out[] + sum(A[0..N))), the hierarchical reduction of
+ * lib/Conversion/SPMDToGPU/SPMDToGPU.cpp:249-415 (strided per-thread sum,
+ * block tree, grid combine) redone as f64 per-thread accumulation, warp
+ * shuffles, a block tree and a deterministic last-block grid combine in f64:
+ * one rounding to f32, identical bits on every call.
+ * `ws` is device memory of at least spmdb200_sum_workspace_bytes(N) bytes,
+ * 256-byte aligned, ZERO-FILLED before its first use; every call leaves it
+ * zero-filled again.  Calls that share `ws` must not overlap on the GPU. */
+int spmdb200_sum_f32(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+                     float *out_base, float *out_aligned, int64_t out_offset,
+                     int64_t N, void *ws, size_t ws_bytes, void *stream);
+
+/* out[] += sum(A[0..N)) in int32 two's-complement arithmetic (wraps like
+ * arith.addi), exact in any order.  The int32 spmd.reduce add that the
+ * reference lowers through ReduceToSCFForGPU (SPMDToGPU.cpp:422-477). */
+int spmdb200_sum_i32(int32_t *A_base, int32_t *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+                     int32_t *out_base, int32_t *out_aligned, int64_t out_offset,
+                     int64_t N, void *stream);
+
+/* out[] += sum(A) with one f32 atomic per block: the exact semantics of the
+ * reference's hierarchical_sum_kernel (SPMDToGPU.cpp:397-408), order of the
+ * block atomics unspecified. */
+int spmdb200_hierarchical_sum(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+                              float *out_base, float *out_aligned, int64_t out_offset,
+                              int64_t N, void *stream);
+
+/* ---- Jacobi-2D 5-point --------------------------------------------------- */
+/* One sweep: for every cell (i,j) of the H x W grid
+ *   boundary (i==0 || i==H-1 || j==0 || j==W-1):  V[i,j] = U[i,j]
+ *   interior: V[i,j] = fmul(0.2f, ((((U[i,j] + U[i-1,j]) + U[i+1,j]) + U[i,j+1]) + U[i,j-1]))
+ * `sweeps` sweeps ping-pong U -> V -> U ...; the final grid is in U when
+ * `sweeps` is even and in V when it is odd.  When res_every > 0, after every
+ * sweep k with k % res_every == 0 (k = 1-based), res_out[k/res_every - 1] =
+ * sum over cells of ((double)new - (double)old)^2 (device memory, f64).
+ * U and V must have the same shape and strides.  Pitch-aligned grids
+ * (stride1 == 1, 16-byte aligned rows) run one persistent kernel that stages
+ * tiles with TMA and separates sweeps with a bounded grid barrier; other
+ * layouts run one launch per sweep.  `ws`: >= spmdb200_jacobi_workspace_bytes()
+ * bytes of device memory, 256-byte aligned, contents irrelevant.
+ * The promoted-stencil semantics follow lib/Transforms/PromoteGroupMemory.cpp:
+ * 113-314; the per-cell order of operations is MLIR source order. */
+size_t spmdb200_jacobi_workspace_bytes(void);
+int spmdb200_jacobi2d(float *U_base, float *U_aligned, int64_t U_offset, int64_t U_size0, int64_t U_size1,
+                      int64_t U_stride0, int64_t U_stride1,
+                      float *V_base, float *V_aligned, int64_t V_offset, int64_t V_size0, int64_t V_size1,
+                      int64_t V_stride0, int64_t V_stride1,
+                      int64_t sweeps, int64_t res_every, double *res_out,
+                      void *ws, size_t ws_bytes, void *stream);
+
+/* Reads the device status word a Jacobi run left in `ws` (synchronises
+ * `stream`): SPMDB200_OK or SPMDB200_ERR_TIMEOUT. */
+int spmdb200_workspace_status(void *ws, void *stream);
+
+/* End-to-end Jacobi-2D on HOST buffers: copies U (H x W, row pitch stride0
+ * elements, stride1 must be 1) to the device, runs `sweeps` sweeps, copies the
+ * final grid back into U and the residuals into res_out (host, f64, may be
+ * NULL when res_every == 0).  Synchronous. */
+int spmdb200_jacobi2d_host(float *U_base, float *U_aligned, int64_t U_offset, int64_t U_size0, int64_t U_size1,
+                           int64_t U_stride0, int64_t U_stride1,
+                           int64_t sweeps, int64_t res_every, double *res_out);
+
+/* ---- Jacobi-3D 7-point --------------------------------------------------- */
+/* One sweep over the D x H x W grid (index order [z][y][x]):
+ *   boundary (any index at 0 or size-1): V = U
+ *   interior: V = fmul((((((c + U[z][y][x-1]) + U[z][y][x+1]) + U[z][y-1][x])
+ *                      + U[z][y+1][x]) + U[z-1][y][x]) + U[z+1][y][x]), 1.0f/7.0f)
+ * with 1.0f/7.0f rounded to f32 once.  Ping-pong and residual contract as
+ * spmdb200_jacobi2d. */
+int spmdb200_jacobi3d(float *U_base, float *U_aligned, int64_t U_offset,
+                      int64_t U_size0, int64_t U_size1, int64_t U_size2,
+                      int64_t U_stride0, int64_t U_stride1, int64_t U_stride2,
+                      float *V_base, float *V_aligned, int64_t V_offset,
+                      int64_t V_size0, int64_t V_size1, int64_t V_size2,
+                      int64_t V_stride0, int64_t V_stride1, int64_t V_stride2,
+                      int64_t sweeps, int64_t res_every, double *res_out,
+                      void *ws, size_t ws_bytes, void *stream);
+
+/* =========================================================================
+ * C. End-to-end host entries for configurations without a reference entry.
+ * ========================================================================= */
+
+/* Y = a*X + Y on host buffers (copy in, kernel, copy out). */
+int spmdb200_axpy_host(float a,
+                       float *X_base, float *X_aligned, int64_t X_offset, int64_t X_size, int64_t X_stride,
+                       float *Y_base, float *Y_aligned, int64_t Y_offset, int64_t Y_size, int64_t Y_stride,
+                       int64_t N);
+
+/* out[] = (float)((double)out[] + sum(A)) on host buffers (deterministic). */
+int spmdb200_sum_f32_host(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+                          float *out_base, float *out_aligned, int64_t out_offset,
+                          int64_t N);
+
+/* out[] += sum(A) (int32, wrapping) on host buffers. */
+int spmdb200_sum_i32_host(int32_t *A_base, int32_t *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+                          int32_t *out_base, int32_t *out_aligned, int64_t out_offset,
+                          int64_t N);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPMD_B200_H */

@@ -1,0 +1,581 @@
+// api.cu -- the extern "C" entry points declared in include/spmd_b200.h.
+//
+// Argument validation happens here, before anything touches the GPU: a bad
+// descriptor returns SPMDB200_ERR_INVALID_ARG and launches nothing.  The
+// reference-named host entries keep the reference's void signatures and
+// report failures on stderr plus spmdb200_last_error().
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/spmd_b200.h"
+#include "internal.h"
+
+using namespace spmdb200;
+
+namespace {
+
+thread_local int g_last_status = SPMDB200_OK;
+thread_local char g_last_msg[512] = "";
+
+int fail(int status, const char *fmt, ...) {
+  g_last_status = status;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_msg, sizeof(g_last_msg), fmt, ap);
+  va_end(ap);
+  return status;
+}
+int ok() {
+  g_last_status = SPMDB200_OK;
+  g_last_msg[0] = '\0';
+  return SPMDB200_OK;
+}
+int cuda_fail(cudaError_t e, const char *what) {
+  cudaGetLastError();  // clear a sticky launch error so the next call starts clean
+  return fail(SPMDB200_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+#define CUDA_TRY(expr)                                     \
+  do {                                                     \
+    cudaError_t e_ = (expr);                               \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #expr);    \
+  } while (0)
+
+void report_void(const char *fn, int st) {
+  if (st != SPMDB200_OK) fprintf(stderr, "spmdb200: %s failed: %s\n", fn, g_last_msg);
+}
+
+// ---- descriptor validation ----------------------------------------------------
+int check1(const char *nm, const void *p, int64_t off, int64_t size, int64_t stride, int64_t n) {
+  if (n < 0) return fail(SPMDB200_ERR_INVALID_ARG, "%s: negative loop bound %lld", nm, (long long)n);
+  if (n == 0) return SPMDB200_OK;
+  if (!p) return fail(SPMDB200_ERR_INVALID_ARG, "%s: null aligned pointer", nm);
+  if (off < 0) return fail(SPMDB200_ERR_INVALID_ARG, "%s: negative offset", nm);
+  if (size < n) return fail(SPMDB200_ERR_INVALID_ARG, "%s: size %lld < loop bound %lld", nm, (long long)size, (long long)n);
+  if (stride < 1) return fail(SPMDB200_ERR_INVALID_ARG, "%s: stride %lld < 1", nm, (long long)stride);
+  return SPMDB200_OK;
+}
+int check2(const char *nm, const void *p, int64_t off, int64_t n0, int64_t n1, int64_t s0, int64_t s1) {
+  if (n0 < 0 || n1 < 0) return fail(SPMDB200_ERR_INVALID_ARG, "%s: negative size", nm);
+  if (n0 == 0 || n1 == 0) return SPMDB200_OK;
+  if (!p) return fail(SPMDB200_ERR_INVALID_ARG, "%s: null aligned pointer", nm);
+  if (off < 0) return fail(SPMDB200_ERR_INVALID_ARG, "%s: negative offset", nm);
+  if (s0 < 1 || s1 < 1) return fail(SPMDB200_ERR_INVALID_ARG, "%s: strides must be >= 1", nm);
+  return SPMDB200_OK;
+}
+int check3(const char *nm, const void *p, int64_t off, int64_t n0, int64_t n1, int64_t n2, int64_t s0,
+           int64_t s1, int64_t s2) {
+  if (n0 < 0 || n1 < 0 || n2 < 0) return fail(SPMDB200_ERR_INVALID_ARG, "%s: negative size", nm);
+  if (n0 == 0 || n1 == 0 || n2 == 0) return SPMDB200_OK;
+  if (!p) return fail(SPMDB200_ERR_INVALID_ARG, "%s: null aligned pointer", nm);
+  if (off < 0) return fail(SPMDB200_ERR_INVALID_ARG, "%s: negative offset", nm);
+  if (s0 < 1 || s1 < 1 || s2 < 1) return fail(SPMDB200_ERR_INVALID_ARG, "%s: strides must be >= 1", nm);
+  return SPMDB200_OK;
+}
+#define CHECK(expr)                        \
+  do {                                     \
+    int st_ = (expr);                      \
+    if (st_ != SPMDB200_OK) return st_;    \
+  } while (0)
+
+int have_device() {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    return fail(SPMDB200_ERR_NO_DEVICE, "no CUDA device visible (%s)", cudaGetErrorString(e));
+  }
+  return SPMDB200_OK;
+}
+
+// ---- staging buffers for the host entries --------------------------------------
+struct Staging {
+  std::vector<std::pair<void *, size_t>> slots;  // per slot: ptr, capacity
+};
+std::mutex g_stage_mu;
+std::vector<Staging> g_stage;  // indexed by device
+
+int staging(int slot, size_t bytes, void **out) {
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_stage_mu);
+  if ((int)g_stage.size() <= dev) g_stage.resize(dev + 1);
+  auto &sl = g_stage[dev].slots;
+  if ((int)sl.size() <= slot) sl.resize(slot + 1, {nullptr, 0});
+  if (sl[slot].second < bytes) {
+    if (sl[slot].first) cudaFree(sl[slot].first);
+    sl[slot] = {nullptr, 0};
+    void *p = nullptr;
+    CUDA_TRY(cudaMalloc(&p, bytes < 256 ? 256 : bytes));
+    sl[slot] = {p, bytes < 256 ? 256 : bytes};
+  }
+  *out = sl[slot].first;
+  return SPMDB200_OK;
+}
+
+// Strided host <-> dense device copies of rank-1 f32/i32 memrefs.
+int h2d_1d(void *dst, const void *src_elem0, int64_t n, int64_t stride, size_t esz) {
+  if (n <= 0) return SPMDB200_OK;
+  if (stride == 1) {
+    CUDA_TRY(cudaMemcpy(dst, src_elem0, (size_t)n * esz, cudaMemcpyHostToDevice));
+  } else {
+    CUDA_TRY(cudaMemcpy2D(dst, esz, src_elem0, (size_t)stride * esz, esz, (size_t)n, cudaMemcpyHostToDevice));
+  }
+  return SPMDB200_OK;
+}
+int d2h_1d(void *dst_elem0, const void *src, int64_t n, int64_t stride, size_t esz) {
+  if (n <= 0) return SPMDB200_OK;
+  if (stride == 1) {
+    CUDA_TRY(cudaMemcpy(dst_elem0, src, (size_t)n * esz, cudaMemcpyDeviceToHost));
+  } else {
+    CUDA_TRY(cudaMemcpy2D(dst_elem0, (size_t)stride * esz, src, esz, esz, (size_t)n, cudaMemcpyDeviceToHost));
+  }
+  return SPMDB200_OK;
+}
+// Rank-2: host (n0 x n1, strides s0, s1) <-> device dense with row pitch dp elements.
+int h2d_2d(float *dst, int64_t dp, const float *src, int64_t n0, int64_t n1, int64_t s0, int64_t s1) {
+  if (n0 <= 0 || n1 <= 0) return SPMDB200_OK;
+  if (s1 == 1) {
+    CUDA_TRY(cudaMemcpy2D(dst, (size_t)dp * 4, src, (size_t)s0 * 4, (size_t)n1 * 4, (size_t)n0,
+                          cudaMemcpyHostToDevice));
+  } else {
+    for (int64_t i = 0; i < n0; ++i)
+      CUDA_TRY(cudaMemcpy2D(dst + i * dp, 4, src + i * s0, (size_t)s1 * 4, 4, (size_t)n1, cudaMemcpyHostToDevice));
+  }
+  return SPMDB200_OK;
+}
+int d2h_2d(float *dst, int64_t n0, int64_t n1, int64_t s0, int64_t s1, const float *src, int64_t sp) {
+  if (n0 <= 0 || n1 <= 0) return SPMDB200_OK;
+  if (s1 == 1) {
+    CUDA_TRY(cudaMemcpy2D(dst, (size_t)s0 * 4, src, (size_t)sp * 4, (size_t)n1 * 4, (size_t)n0,
+                          cudaMemcpyDeviceToHost));
+  } else {
+    for (int64_t i = 0; i < n0; ++i)
+      CUDA_TRY(cudaMemcpy2D(dst + i * s0, (size_t)s1 * 4, src + i * sp, 4, 4, (size_t)n1, cudaMemcpyDeviceToHost));
+  }
+  return SPMDB200_OK;
+}
+
+int64_t round_up4(int64_t x) { return (x + 3) & ~int64_t(3); }
+
+int jacobi_status_from_ws(JacobiWs *ws, cudaStream_t s) {
+  CUDA_TRY(cudaStreamSynchronize(s));
+  int st = 0;
+  CUDA_TRY(cudaMemcpy(&st, &ws->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (st != kDevOk)
+    return fail(SPMDB200_ERR_TIMEOUT, "device-side bounded wait expired (code %d: %s)", st,
+                st == kDevTimeoutGridBarrier ? "grid barrier"
+                : st == kDevTimeoutFull      ? "TMA stage full"
+                : st == kDevTimeoutEmpty     ? "TMA stage empty"
+                : st == kDevTimeoutPeer      ? "peer halo delivery"
+                                             : "unknown");
+  return SPMDB200_OK;
+}
+
+}  // namespace
+
+// ---- helpers used by the kernel translation units ------------------------------
+namespace spmdb200 {
+
+int num_sms(int device) {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)cache.size() <= device) cache.resize(device + 1, 0);
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n < 1) n = 148;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+int encode_tensor_map_f32(void *tmap, void *gaddr, int rank, const uint64_t *dims,
+                          const uint64_t *strides_bytes, const uint32_t *box) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) return -1;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+  }
+  for (int i = 0; i < rank - 1; ++i) st[i] = strides_bytes[i];
+  CUresult r = fn(reinterpret_cast<CUtensorMap *>(tmap), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, gaddr, d,
+                  st, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
+}  // namespace spmdb200
+
+// =================================================================================
+extern "C" {
+
+const char *spmdb200_status_string(int status) {
+  switch (status) {
+    case SPMDB200_OK: return "ok";
+    case SPMDB200_ERR_INVALID_ARG: return "invalid argument";
+    case SPMDB200_ERR_CUDA: return "CUDA error";
+    case SPMDB200_ERR_TIMEOUT: return "device wait timed out";
+    case SPMDB200_ERR_UNSUPPORTED: return "unsupported layout";
+    case SPMDB200_ERR_WORKSPACE: return "bad workspace";
+    case SPMDB200_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+int spmdb200_last_error(void) { return g_last_status; }
+const char *spmdb200_last_error_message(void) { return g_last_msg; }
+const char *spmdb200_version(void) { return "spmdb200 0.1.0 (sm_100a)"; }
+
+int spmdb200_release_cache(void) {
+  std::lock_guard<std::mutex> lk(g_stage_mu);
+  int cur = 0;
+  cudaGetDevice(&cur);
+  for (size_t d = 0; d < g_stage.size(); ++d) {
+    if (g_stage[d].slots.empty()) continue;
+    cudaSetDevice((int)d);
+    for (auto &s : g_stage[d].slots)
+      if (s.first) cudaFree(s.first);
+    g_stage[d].slots.clear();
+  }
+  cudaSetDevice(cur);
+  return ok();
+}
+
+// ---------------------------------------------------------------- device entries
+int spmdb200_ewise(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                   float *B_base, float *B, int64_t B_off, int64_t B_size, int64_t B_st,
+                   float *C_base, float *C, int64_t C_off, int64_t C_size, int64_t C_st,
+                   int64_t N, void *stream) {
+  (void)A_base; (void)B_base; (void)C_base;
+  CHECK(check1("A", A, A_off, A_size, A_st, N));
+  CHECK(check1("B", B, B_off, B_size, B_st, N));
+  CHECK(check1("C", C, C_off, C_size, C_st, N));
+  if (N == 0) return ok();
+  CUDA_TRY(launch_ewise_add(View1{A + A_off, N, A_st}, View1{B + B_off, N, B_st}, View1{C + C_off, N, C_st}, N,
+                            (cudaStream_t)stream));
+  return ok();
+}
+
+int spmdb200_axpy(float a, float *X_base, float *X, int64_t X_off, int64_t X_size, int64_t X_st,
+                  float *Y_base, float *Y, int64_t Y_off, int64_t Y_size, int64_t Y_st, int64_t N, void *stream) {
+  (void)X_base; (void)Y_base;
+  CHECK(check1("X", X, X_off, X_size, X_st, N));
+  CHECK(check1("Y", Y, Y_off, Y_size, Y_st, N));
+  if (N == 0) return ok();
+  CUDA_TRY(launch_axpy(a, View1{X + X_off, N, X_st}, View1{Y + Y_off, N, Y_st}, N, (cudaStream_t)stream));
+  return ok();
+}
+
+int spmdb200_stencil3pt(float *A_base, float *A, int64_t A_off, int64_t A_n0, int64_t A_n1, int64_t A_s0,
+                        int64_t A_s1, float *B_base, float *B, int64_t B_off, int64_t B_n0, int64_t B_n1,
+                        int64_t B_s0, int64_t B_s1, int64_t N, int64_t M, void *stream) {
+  (void)A_base; (void)B_base;
+  CHECK(check2("A", A, A_off, A_n0, A_n1, A_s0, A_s1));
+  CHECK(check2("B", B, B_off, B_n0, B_n1, B_s0, B_s1));
+  if (N < 0 || M < 0 || N > B_n0 || M > B_n1)
+    return fail(SPMDB200_ERR_INVALID_ARG, "loop bounds (%lld, %lld) exceed B (%lld, %lld)", (long long)N,
+                (long long)M, (long long)B_n0, (long long)B_n1);
+  if (N == 0 || M == 0) return ok();
+  const View2 a{A ? A + A_off : nullptr, A_n0, A_n1, A_s0, A_s1};
+  const View2 b{B + B_off, B_n0, B_n1, B_s0, B_s1};
+  CUDA_TRY(launch_stencil3(a, b, N, M, (cudaStream_t)stream));
+  return ok();
+}
+
+size_t spmdb200_sum_workspace_bytes(int64_t N) { return sum_f32_workspace_bytes(N); }
+
+int spmdb200_sum_f32(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                     float *o_base, float *o, int64_t o_off, int64_t N, void *ws, size_t ws_bytes, void *stream) {
+  (void)A_base; (void)o_base;
+  CHECK(check1("A", A, A_off, A_size, A_st, N));
+  if (!o || o_off < 0) return fail(SPMDB200_ERR_INVALID_ARG, "out: null pointer or negative offset");
+  if (!ws || ((uintptr_t)ws & 255u) != 0 || ws_bytes < sum_f32_workspace_bytes(N))
+    return fail(SPMDB200_ERR_WORKSPACE, "workspace must be >= %zu bytes and 256-byte aligned",
+                sum_f32_workspace_bytes(N));
+  CUDA_TRY(launch_sum_f32(View1{A ? A + A_off : nullptr, N, A_st}, o + o_off, N, ws, (cudaStream_t)stream));
+  return ok();
+}
+
+int spmdb200_sum_i32(int32_t *A_base, int32_t *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                     int32_t *o_base, int32_t *o, int64_t o_off, int64_t N, void *stream) {
+  (void)A_base; (void)o_base;
+  CHECK(check1("A", A, A_off, A_size, A_st, N));
+  if (!o || o_off < 0) return fail(SPMDB200_ERR_INVALID_ARG, "out: null pointer or negative offset");
+  if (N == 0) return ok();
+  CUDA_TRY(launch_sum_i32(A + A_off, A_st, o + o_off, N, (cudaStream_t)stream));
+  return ok();
+}
+
+int spmdb200_hierarchical_sum(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                              float *o_base, float *o, int64_t o_off, int64_t N, void *stream) {
+  (void)A_base; (void)o_base;
+  CHECK(check1("A", A, A_off, A_size, A_st, N));
+  if (!o || o_off < 0) return fail(SPMDB200_ERR_INVALID_ARG, "out: null pointer or negative offset");
+  if (N == 0) return ok();
+  CUDA_TRY(launch_hier_sum_f32(View1{A + A_off, N, A_st}, o + o_off, N, (cudaStream_t)stream));
+  return ok();
+}
+
+size_t spmdb200_jacobi_workspace_bytes(void) { return sizeof(JacobiWs); }
+
+int spmdb200_workspace_status(void *ws, void *stream) {
+  if (!ws) return fail(SPMDB200_ERR_WORKSPACE, "null workspace");
+  CHECK(jacobi_status_from_ws(static_cast<JacobiWs *>(ws), (cudaStream_t)stream));
+  return ok();
+}
+
+static int check_jacobi_ws(void *ws, size_t ws_bytes) {
+  if (!ws || ((uintptr_t)ws & 255u) != 0 || ws_bytes < sizeof(JacobiWs))
+    return fail(SPMDB200_ERR_WORKSPACE, "workspace must be >= %zu bytes and 256-byte aligned", sizeof(JacobiWs));
+  return SPMDB200_OK;
+}
+static int check_res(int64_t sweeps, int64_t res_every, const double *res_out) {
+  if (sweeps < 0 || res_every < 0) return fail(SPMDB200_ERR_INVALID_ARG, "negative sweeps / res_every");
+  if (res_every > 0 && sweeps >= res_every && !res_out)
+    return fail(SPMDB200_ERR_INVALID_ARG, "res_out is null but %lld residuals are due",
+                (long long)(sweeps / res_every));
+  return SPMDB200_OK;
+}
+
+int spmdb200_jacobi2d(float *U_base, float *U, int64_t U_off, int64_t U_n0, int64_t U_n1, int64_t U_s0, int64_t U_s1,
+                      float *V_base, float *V, int64_t V_off, int64_t V_n0, int64_t V_n1, int64_t V_s0, int64_t V_s1,
+                      int64_t sweeps, int64_t res_every, double *res_out, void *ws, size_t ws_bytes, void *stream) {
+  (void)U_base; (void)V_base;
+  CHECK(check2("U", U, U_off, U_n0, U_n1, U_s0, U_s1));
+  CHECK(check2("V", V, V_off, V_n0, V_n1, V_s0, V_s1));
+  if (U_n0 != V_n0 || U_n1 != V_n1 || U_s0 != V_s0 || U_s1 != V_s1)
+    return fail(SPMDB200_ERR_INVALID_ARG, "U and V must have identical sizes and strides");
+  CHECK(check_res(sweeps, res_every, res_out));
+  CHECK(check_jacobi_ws(ws, ws_bytes));
+  if (sweeps == 0 || U_n0 == 0 || U_n1 == 0) return ok();
+  cudaStream_t s = (cudaStream_t)stream;
+  JacobiWs *w = static_cast<JacobiWs *>(ws);
+  CUDA_TRY(cudaMemsetAsync(w, 0, 256, s));
+  Jacobi2dProblem p{};
+  p.u = U + U_off;
+  p.v = V + V_off;
+  p.pitch = U_s0;
+  p.h_local = U_n0;
+  p.w = U_n1;
+  p.row_lo = 0;
+  p.row_hi = U_n0;
+  p.g_row0 = 0;
+  p.g_rows = U_n0;
+  p.sweeps = sweeps;
+  p.res_every = res_every;
+  p.res_out = res_out;
+  p.ws = w;
+  if (U_s1 == 1 && jacobi2d_tma_ok(p)) {
+    int grid = 0;
+    CUDA_TRY(launch_jacobi2d_persistent(p, SlabPeers{}, s, &grid));
+  } else {
+    CUDA_TRY(launch_jacobi2d_generic(p, U_s1, s));
+  }
+  return ok();
+}
+
+int spmdb200_jacobi3d(float *U_base, float *U, int64_t U_off, int64_t U_n0, int64_t U_n1, int64_t U_n2,
+                      int64_t U_s0, int64_t U_s1, int64_t U_s2,
+                      float *V_base, float *V, int64_t V_off, int64_t V_n0, int64_t V_n1, int64_t V_n2,
+                      int64_t V_s0, int64_t V_s1, int64_t V_s2,
+                      int64_t sweeps, int64_t res_every, double *res_out, void *ws, size_t ws_bytes, void *stream) {
+  (void)U_base; (void)V_base;
+  CHECK(check3("U", U, U_off, U_n0, U_n1, U_n2, U_s0, U_s1, U_s2));
+  CHECK(check3("V", V, V_off, V_n0, V_n1, V_n2, V_s0, V_s1, V_s2));
+  if (U_n0 != V_n0 || U_n1 != V_n1 || U_n2 != V_n2 || U_s0 != V_s0 || U_s1 != V_s1 || U_s2 != V_s2)
+    return fail(SPMDB200_ERR_INVALID_ARG, "U and V must have identical sizes and strides");
+  CHECK(check_res(sweeps, res_every, res_out));
+  CHECK(check_jacobi_ws(ws, ws_bytes));
+  if (sweeps == 0 || U_n0 == 0 || U_n1 == 0 || U_n2 == 0) return ok();
+  cudaStream_t s = (cudaStream_t)stream;
+  JacobiWs *w = static_cast<JacobiWs *>(ws);
+  CUDA_TRY(cudaMemsetAsync(w, 0, 256, s));
+  Jacobi3dProblem p{};
+  p.u = U + U_off;
+  p.v = V + V_off;
+  p.d = U_n0;
+  p.h = U_n1;
+  p.w = U_n2;
+  p.sz = U_s0;
+  p.sy = U_s1;
+  p.sx = U_s2;
+  p.sweeps = sweeps;
+  p.res_every = res_every;
+  p.res_out = res_out;
+  p.ws = w;
+  if (jacobi3d_tma_ok(p)) {
+    int grid = 0;
+    CUDA_TRY(launch_jacobi3d_persistent(p, s, &grid));
+  } else {
+    CUDA_TRY(launch_jacobi3d_generic(p, s));
+  }
+  return ok();
+}
+
+// ---------------------------------------------------------------- host entries (A)
+static int ewise_host_impl(float *A, int64_t A_off, int64_t A_size, int64_t A_st, float *B, int64_t B_off,
+                           int64_t B_size, int64_t B_st, float *C, int64_t C_off, int64_t C_size, int64_t C_st,
+                           int64_t N) {
+  CHECK(check1("A", A, A_off, A_size, A_st, N));
+  CHECK(check1("B", B, B_off, B_size, B_st, N));
+  CHECK(check1("C", C, C_off, C_size, C_st, N));
+  if (N == 0) return ok();
+  CHECK(have_device());
+  void *da, *db, *dc;
+  CHECK(staging(0, (size_t)N * 4, &da));
+  CHECK(staging(1, (size_t)N * 4, &db));
+  CHECK(staging(2, (size_t)N * 4, &dc));
+  CHECK(h2d_1d(da, A + A_off, N, A_st, 4));
+  CHECK(h2d_1d(db, B + B_off, N, B_st, 4));
+  CUDA_TRY(launch_ewise_add(View1{(float *)da, N, 1}, View1{(float *)db, N, 1}, View1{(float *)dc, N, 1}, N, 0));
+  CHECK(d2h_1d(C + C_off, dc, N, C_st, 4));
+  return ok();
+}
+
+void ewise(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,
+           float *B_base, float *B, int64_t B_off, int64_t B_size, int64_t B_st,
+           float *C_base, float *C, int64_t C_off, int64_t C_size, int64_t C_st, int64_t N) {
+  (void)A_base; (void)B_base; (void)C_base;
+  report_void("ewise", ewise_host_impl(A, A_off, A_size, A_st, B, B_off, B_size, B_st, C, C_off, C_size, C_st, N));
+}
+
+static int stencil_host_impl(float *A, int64_t A_off, int64_t A_n0, int64_t A_n1, int64_t A_s0, int64_t A_s1,
+                             float *B, int64_t B_off, int64_t B_n0, int64_t B_n1, int64_t B_s0, int64_t B_s1,
+                             int64_t N, int64_t M) {
+  CHECK(check2("A", A, A_off, A_n0, A_n1, A_s0, A_s1));
+  CHECK(check2("B", B, B_off, B_n0, B_n1, B_s0, B_s1));
+  if (N < 0 || M < 0 || N > B_n0 || M > B_n1)
+    return fail(SPMDB200_ERR_INVALID_ARG, "loop bounds exceed B's sizes");
+  if (N == 0 || M == 0) return ok();
+  CHECK(have_device());
+  const int64_t ap = round_up4(A_n1 > 0 ? A_n1 : 1), bp = round_up4(M);
+  void *da, *db;
+  CHECK(staging(0, (size_t)(A_n0 > 0 ? A_n0 : 1) * ap * 4, &da));
+  CHECK(staging(1, (size_t)N * bp * 4, &db));
+  CHECK(h2d_2d((float *)da, ap, A ? A + A_off : nullptr, A_n0, A_n1, A_s0, A_s1));
+  CUDA_TRY(launch_stencil3(View2{(float *)da, A_n0, A_n1, ap, 1}, View2{(float *)db, N, M, bp, 1}, N, M, 0));
+  CHECK(d2h_2d(B + B_off, N, M, B_s0, B_s1, (float *)db, bp));
+  return ok();
+}
+
+void stencil_cpu(float *A_base, float *A, int64_t A_off, int64_t A_n0, int64_t A_n1, int64_t A_s0, int64_t A_s1,
+                 float *B_base, float *B, int64_t B_off, int64_t B_n0, int64_t B_n1, int64_t B_s0, int64_t B_s1,
+                 int64_t N, int64_t M) {
+  (void)A_base; (void)B_base;
+  report_void("stencil_cpu",
+              stencil_host_impl(A, A_off, A_n0, A_n1, A_s0, A_s1, B, B_off, B_n0, B_n1, B_s0, B_s1, N, M));
+}
+
+static int sum_host_impl(float *A, int64_t A_off, int64_t A_size, int64_t A_st, float *o, int64_t o_off, int64_t N) {
+  CHECK(check1("A", A, A_off, A_size, A_st, N));
+  if (!o || o_off < 0) return fail(SPMDB200_ERR_INVALID_ARG, "out: null pointer or negative offset");
+  CHECK(have_device());
+  void *da, *dout, *dws;
+  CHECK(staging(0, (size_t)(N > 0 ? N : 1) * 4, &da));
+  CHECK(staging(1, 256, &dout));
+  const size_t wsb = sum_f32_workspace_bytes(N);
+  CHECK(staging(2, wsb, &dws));
+  CHECK(h2d_1d(da, A ? A + A_off : nullptr, N, A_st, 4));
+  CUDA_TRY(cudaMemcpy(dout, o + o_off, 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemset(dws, 0, 256));
+  CUDA_TRY(launch_sum_f32(View1{(float *)da, N, 1}, (float *)dout, N, dws, 0));
+  CUDA_TRY(cudaMemcpy(o + o_off, dout, 4, cudaMemcpyDeviceToHost));
+  return ok();
+}
+
+void atomic_sum(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                float *o_base, float *o, int64_t o_off, int64_t N) {
+  (void)A_base; (void)o_base;
+  report_void("atomic_sum", sum_host_impl(A, A_off, A_size, A_st, o, o_off, N));
+}
+
+void hierarchical_sum(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                      float *o_base, float *o, int64_t o_off, int64_t N) {
+  (void)A_base; (void)o_base;
+  report_void("hierarchical_sum", sum_host_impl(A, A_off, A_size, A_st, o, o_off, N));
+}
+
+// ---------------------------------------------------------------- host entries (C)
+int spmdb200_axpy_host(float a, float *X_base, float *X, int64_t X_off, int64_t X_size, int64_t X_st,
+                       float *Y_base, float *Y, int64_t Y_off, int64_t Y_size, int64_t Y_st, int64_t N) {
+  (void)X_base; (void)Y_base;
+  CHECK(check1("X", X, X_off, X_size, X_st, N));
+  CHECK(check1("Y", Y, Y_off, Y_size, Y_st, N));
+  if (N == 0) return ok();
+  CHECK(have_device());
+  void *dx, *dy;
+  CHECK(staging(0, (size_t)N * 4, &dx));
+  CHECK(staging(1, (size_t)N * 4, &dy));
+  CHECK(h2d_1d(dx, X + X_off, N, X_st, 4));
+  CHECK(h2d_1d(dy, Y + Y_off, N, Y_st, 4));
+  CUDA_TRY(launch_axpy(a, View1{(float *)dx, N, 1}, View1{(float *)dy, N, 1}, N, 0));
+  CHECK(d2h_1d(Y + Y_off, dy, N, Y_st, 4));
+  return ok();
+}
+
+int spmdb200_sum_f32_host(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                          float *o_base, float *o, int64_t o_off, int64_t N) {
+  (void)A_base; (void)o_base;
+  return sum_host_impl(A, A_off, A_size, A_st, o, o_off, N);
+}
+
+int spmdb200_sum_i32_host(int32_t *A_base, int32_t *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                          int32_t *o_base, int32_t *o, int64_t o_off, int64_t N) {
+  (void)A_base; (void)o_base;
+  CHECK(check1("A", A, A_off, A_size, A_st, N));
+  if (!o || o_off < 0) return fail(SPMDB200_ERR_INVALID_ARG, "out: null pointer or negative offset");
+  if (N == 0) return ok();
+  CHECK(have_device());
+  void *da, *dout;
+  CHECK(staging(0, (size_t)N * 4, &da));
+  CHECK(staging(1, 256, &dout));
+  CHECK(h2d_1d(da, A + A_off, N, A_st, 4));
+  CUDA_TRY(cudaMemcpy(dout, o + o_off, 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(launch_sum_i32((int32_t *)da, 1, (int32_t *)dout, N, 0));
+  CUDA_TRY(cudaMemcpy(o + o_off, dout, 4, cudaMemcpyDeviceToHost));
+  return ok();
+}
+
+int spmdb200_jacobi2d_host(float *U_base, float *U, int64_t U_off, int64_t U_n0, int64_t U_n1, int64_t U_s0,
+                           int64_t U_s1, int64_t sweeps, int64_t res_every, double *res_out) {
+  (void)U_base;
+  CHECK(check2("U", U, U_off, U_n0, U_n1, U_s0, U_s1));
+  CHECK(check_res(sweeps, res_every, res_out));
+  if (U_n0 == 0 || U_n1 == 0) return ok();
+  CHECK(have_device());
+  const int64_t dp = round_up4(U_n1);  // 16-byte row pitch on the device: always the TMA path
+  const size_t grid_bytes = (size_t)U_n0 * dp * 4;
+  const int64_t nres = res_every > 0 ? sweeps / res_every : 0;
+  void *du, *dv, *dws, *dres;
+  CHECK(staging(0, grid_bytes, &du));
+  CHECK(staging(1, grid_bytes, &dv));
+  CHECK(staging(2, sizeof(JacobiWs), &dws));
+  CHECK(staging(3, (size_t)(nres > 0 ? nres : 1) * 8, &dres));
+  CHECK(h2d_2d((float *)du, dp, U + U_off, U_n0, U_n1, U_s0, U_s1));
+  const int st = spmdb200_jacobi2d(nullptr, (float *)du, 0, U_n0, U_n1, dp, 1, nullptr, (float *)dv, 0, U_n0, U_n1,
+                                    dp, 1, sweeps, res_every, (double *)dres, dws, sizeof(JacobiWs), nullptr);
+  if (st != SPMDB200_OK) return st;
+  CHECK(jacobi_status_from_ws((JacobiWs *)dws, 0));
+  const float *fin = (sweeps % 2 == 0) ? (float *)du : (float *)dv;
+  CHECK(d2h_2d(U + U_off, U_n0, U_n1, U_s0, U_s1, fin, dp));
+  if (nres > 0) CUDA_TRY(cudaMemcpy(res_out, dres, (size_t)nres * 8, cudaMemcpyDeviceToHost));
+  return ok();
+}
+
+}  // extern "C"

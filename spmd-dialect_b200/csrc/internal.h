@@ -1,0 +1,97 @@
+// internal.h -- launchers shared between the translation units of libspmdb200.
+// Every launcher is asynchronous on `stream`, assumes validated arguments and
+// returns the cudaError_t of its launch.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace spmdb200 {
+
+// ---- elementwise (ewise.cu) -------------------------------------------------
+cudaError_t launch_ewise_add(View1 a, View1 b, View1 c, int64_t n, cudaStream_t s);
+cudaError_t launch_axpy(float alpha, View1 x, View1 y, int64_t n, cudaStream_t s);
+
+// ---- reductions (reduce.cu) ---------------------------------------------------
+// Workspace of the deterministic f32 sum: [ticket u32 | pad to 256 B | f64 partials].
+size_t sum_f32_workspace_bytes(int64_t n);
+int sum_f32_grid(int64_t n);
+cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_t s);
+cudaError_t launch_sum_i32(const int32_t *a, int64_t stride, int32_t *out, int64_t n, cudaStream_t s);
+cudaError_t launch_hier_sum_f32(View1 a, float *out, int64_t n, cudaStream_t s);
+
+// ---- 3-point promoted stencil (stencil3.cu) -----------------------------------------
+cudaError_t launch_stencil3(View2 a, View2 b, int64_t n, int64_t m, cudaStream_t s);
+
+// ---- Jacobi (jacobi2d.cu / jacobi3d.cu) ---------------------------------------------
+constexpr int kMaxCtas = 2048;
+constexpr int kMaxRanks = 8;
+constexpr int kMaxResSlots = 1024;
+
+// Device workspace of every Jacobi run.  The 256-byte header is cleared by the
+// host before each run.
+struct JacobiWs {
+  unsigned barrier;    // grid-barrier arrivals (one per CTA per sweep)
+  int status;          // DevStatus of the run
+  unsigned from_above; // halo-tile deliveries received from the rank above
+  unsigned from_below; // halo-tile deliveries received from the rank below
+  unsigned ticket;     // last-block ticket of the per-sweep (generic) path
+  unsigned pad[59];
+  double partial[2][kMaxCtas];                // per-CTA residual partials, by residual parity
+  double res_slots[kMaxResSlots][kMaxRanks];  // residual all-gather target (multi-GPU)
+};
+static_assert(offsetof(JacobiWs, partial) == 256, "JacobiWs header must be 256 bytes");
+
+// Multi-GPU slab parameters (all null / zero for one GPU).
+struct SlabPeers {
+  float *up_u = nullptr, *up_v = nullptr;  // neighbour above: our first owned row lands in its row up_row
+  float *dn_u = nullptr, *dn_v = nullptr;  // neighbour below: our last owned row lands in its row dn_row
+  long long up_row = 0, dn_row = 0;
+  unsigned *up_flag = nullptr;  // &ws_above->from_below
+  unsigned *dn_flag = nullptr;  // &ws_below->from_above
+  int rank = 0, nranks = 1;
+  JacobiWs *peer_ws[kMaxRanks] = {};  // every rank's workspace (residual all-gather)
+};
+
+struct Jacobi2dProblem {
+  float *u, *v;       // local arrays, offset applied
+  int64_t pitch;      // elements per row
+  int64_t h_local;    // rows of the local array (incl. halo rows)
+  int64_t w;          // columns
+  int64_t row_lo, row_hi;  // local rows updated by a sweep
+  int64_t g_row0, g_rows;  // global index of local row 0, global row count
+  int64_t sweeps, res_every;
+  double *res_out;    // device, [sweeps / res_every]
+  JacobiWs *ws;
+};
+
+bool jacobi2d_tma_ok(const Jacobi2dProblem &p);
+// Persistent TMA path (requires jacobi2d_tma_ok).  Returns the launch error.
+cudaError_t launch_jacobi2d_persistent(const Jacobi2dProblem &p, const SlabPeers &peers,
+                                       cudaStream_t s, int *grid_out);
+// One launch per sweep, any strides (single GPU only).
+cudaError_t launch_jacobi2d_generic(const Jacobi2dProblem &p, int64_t stride1, cudaStream_t s);
+
+struct Jacobi3dProblem {
+  float *u, *v;
+  int64_t d, h, w;     // sizes [z][y][x]
+  int64_t sz, sy, sx;  // strides
+  int64_t sweeps, res_every;
+  double *res_out;
+  JacobiWs *ws;
+};
+bool jacobi3d_tma_ok(const Jacobi3dProblem &p);
+cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, cudaStream_t s, int *grid_out);
+cudaError_t launch_jacobi3d_generic(const Jacobi3dProblem &p, cudaStream_t s);
+
+// ---- driver entry points resolved at run time (no link-time libcuda) ----------------
+// Encodes a row-major f32 tensor map (innermost dimension first).  Returns 0 on success.
+int encode_tensor_map_f32(void *tmap /*CUtensorMap*/, void *gaddr, int rank, const uint64_t *dims,
+                          const uint64_t *strides_bytes /*rank-1 entries*/, const uint32_t *box);
+
+int num_sms(int device);
+
+}  // namespace spmdb200

@@ -1,0 +1,119 @@
+"""Device-memory entry points over torch tensors (PyTorch = allocator + streams).
+
+Each function builds the unpacked memref descriptors the C ABI expects from a
+CUDA tensor (aligned pointer = tensor.data_ptr(), offset 0, sizes and strides
+in elements) and calls the matching spmdb200_* entry on the current stream.
+All compute happens in libspmdb200.so; nothing here computes anything.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._lib import c_i, c_p, call, lib
+
+_DTYPES = {torch.float32: "f32", torch.int32: "i32", torch.uint8: "u8", torch.float64: "f64"}
+
+
+def memref(t: torch.Tensor) -> tuple:
+    """Unpacked memref descriptor (base, aligned, offset, sizes..., strides...)."""
+    if not t.is_cuda:
+        raise ValueError("device entries take CUDA tensors")
+    if t.dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    p = c_p(t.data_ptr())
+    return (p, p, c_i(0), *[c_i(s) for s in t.shape], *[c_i(s) for s in t.stride()])
+
+
+def _stream(stream) -> c_p:
+    s = torch.cuda.current_stream() if stream is None else stream
+    return c_p(s.cuda_stream)
+
+
+def ewise(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """out = a + b (f32), the ewise_kernel forall."""
+    n = a.shape[0]
+    out = torch.empty_like(a) if out is None else out
+    call("spmdb200_ewise", *memref(a), *memref(b), *memref(out), c_i(n), _stream(stream))
+    return out
+
+
+def axpy(alpha: float, x: torch.Tensor, y: torch.Tensor, stream=None) -> torch.Tensor:
+    """y = fadd(fmul(alpha, x), y) in place."""
+    call("spmdb200_axpy", ctypes.c_float(alpha), *memref(x), *memref(y), c_i(x.shape[0]), _stream(stream))
+    return y
+
+
+def stencil3pt(a: torch.Tensor, out: torch.Tensor, n: int | None = None, m: int | None = None,
+               stream=None) -> torch.Tensor:
+    """out[i,j] = (a[i,j] + a[i,j+1]) + a[i+1,j] for i < n, j < m (reads off `a` are 0)."""
+    n = out.shape[0] if n is None else n
+    m = out.shape[1] if m is None else m
+    call("spmdb200_stencil3pt", *memref(a), *memref(out), c_i(n), c_i(m), _stream(stream))
+    return out
+
+
+def sum_workspace(n: int, device=None) -> torch.Tensor:
+    """Zero-filled workspace for sum_f32 (reusable: every call leaves it zeroed)."""
+    nbytes = int(lib().spmdb200_sum_workspace_bytes(c_i(n)))
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device or "cuda")
+
+
+def sum_f32(a: torch.Tensor, out: torch.Tensor, ws: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """out[0] = f32(f64(out[0]) + sum(a)), deterministic."""
+    n = a.shape[0]
+    ws = sum_workspace(n, a.device) if ws is None else ws
+    o = c_p(out.data_ptr())
+    call("spmdb200_sum_f32", *memref(a), o, o, c_i(0), c_i(n), c_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()),
+         _stream(stream))
+    return out
+
+
+def sum_i32(a: torch.Tensor, out: torch.Tensor, stream=None) -> torch.Tensor:
+    """out[0] += sum(a) in wrapping int32."""
+    o = c_p(out.data_ptr())
+    call("spmdb200_sum_i32", *memref(a), o, o, c_i(0), c_i(a.shape[0]), _stream(stream))
+    return out
+
+
+def hierarchical_sum(a: torch.Tensor, out: torch.Tensor, stream=None) -> torch.Tensor:
+    """out[0] += sum(a) with one f32 atomic per block (reference semantics)."""
+    o = c_p(out.data_ptr())
+    call("spmdb200_hierarchical_sum", *memref(a), o, o, c_i(0), c_i(a.shape[0]), _stream(stream))
+    return out
+
+
+def jacobi_workspace(device=None) -> torch.Tensor:
+    return torch.zeros(int(lib().spmdb200_jacobi_workspace_bytes()), dtype=torch.uint8, device=device or "cuda")
+
+
+def workspace_status(ws: torch.Tensor, stream=None) -> None:
+    """Synchronises and raises SpmdError if the run left a device-side timeout."""
+    call("spmdb200_workspace_status", c_p(ws.data_ptr()), _stream(stream))
+
+
+def _jacobi(entry: str, u: torch.Tensor, v: torch.Tensor, sweeps: int, res_every: int,
+            ws: torch.Tensor | None, res: torch.Tensor | None, check: bool, stream):
+    ws = jacobi_workspace(u.device) if ws is None else ws
+    nres = sweeps // res_every if res_every > 0 else 0
+    if res is None and nres > 0:
+        res = torch.zeros(nres, dtype=torch.float64, device=u.device)
+    rp = c_p(res.data_ptr()) if res is not None else c_p(0)
+    call(entry, *memref(u), *memref(v), c_i(sweeps), c_i(res_every), rp, c_p(ws.data_ptr()),
+         ctypes.c_size_t(ws.numel()), _stream(stream))
+    if check:
+        workspace_status(ws, stream)
+    return (u if sweeps % 2 == 0 else v), res
+
+
+def jacobi2d(u: torch.Tensor, v: torch.Tensor, sweeps: int, res_every: int = 0, ws=None, res=None,
+             check: bool = True, stream=None):
+    """`sweeps` 5-point sweeps ping-ponging u -> v -> u ...; returns (final grid, residuals)."""
+    return _jacobi("spmdb200_jacobi2d", u, v, sweeps, res_every, ws, res, check, stream)
+
+
+def jacobi3d(u: torch.Tensor, v: torch.Tensor, sweeps: int, res_every: int = 0, ws=None, res=None,
+             check: bool = True, stream=None):
+    """`sweeps` 7-point sweeps ping-ponging u -> v -> u ...; returns (final grid, residuals)."""
+    return _jacobi("spmdb200_jacobi3d", u, v, sweeps, res_every, ws, res, check, stream)

@@ -1,0 +1,124 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+include/spmd_b200.h declares, the cubin carries the reference kernel names,
+bad descriptors are rejected before any CUDA call, and -- on a machine with no
+GPU -- a valid call fails loudly instead of falling back to the CPU."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT, spmd_mod
+
+HEADER = ROOT / "include" / "spmd_b200.h"
+REF_KERNELS = ["ewise_kernel", "promoted_stencil_kernel", "promoted_stencil_kernel_square",
+               "atomic_sum_kernel", "hierarchical_sum_kernel"]
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^[A-Za-z_][\w \*]*?\b([a-z_][a-z0-9_]*)\s*\(", text, flags=re.M)
+    return sorted(set(n for n in names if n not in {"defined"}))
+
+
+def test_header_declares_reference_names():
+    names = declared_functions()
+    for n in ["ewise", "stencil_cpu", "atomic_sum", "hierarchical_sum", "spmdb200_jacobi2d", "spmdb200_sum_f32"]:
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = spmd_mod("_lib").lib()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_cubin_has_reference_entry_names():
+    cubin = spmd_mod("_lib").CUBIN_PATH
+    assert cubin.exists(), "spmdb200_kernels.cubin not built"
+    out = subprocess.run(["nm", str(cubin)], capture_output=True, text=True)
+    syms = out.stdout if out.returncode == 0 else cubin.read_bytes().decode("latin-1")
+    for k in REF_KERNELS:
+        assert re.search(rf"\b{k}\b", syms), f"{k} missing from the cubin"
+
+
+def test_version_string():
+    assert "sm_100a" in spmd_mod("_lib").lib().spmdb200_version().decode()
+
+
+def _d1(p, n, stride=1, off=0):
+    c_i = ctypes.c_int64
+    return (ctypes.c_void_p(p), ctypes.c_void_p(p), c_i(off), c_i(n), c_i(stride))
+
+
+@pytest.mark.parametrize("case", ["neg_n", "null", "short", "zero_stride", "neg_off"])
+def test_bad_descriptor_rejected_before_launch(case):
+    L = spmd_mod("_lib")
+    lib = L.lib()
+    fake = 0x1000  # never dereferenced: validation fails first
+    c_i = ctypes.c_int64
+    a = _d1(fake, 100)
+    n = 100
+    if case == "neg_n":
+        n = -1
+    elif case == "null":
+        a = _d1(0, 100)
+    elif case == "short":
+        a = _d1(fake, 50)
+    elif case == "zero_stride":
+        a = _d1(fake, 100, stride=0)
+    elif case == "neg_off":
+        a = _d1(fake, 100, off=-4)
+    st = lib.spmdb200_ewise(*a, *_d1(fake, 100), *_d1(fake, 100), c_i(n), None)
+    assert st == -1
+    assert lib.spmdb200_last_error() == -1
+    assert lib.spmdb200_last_error_message()
+
+
+def test_jacobi_rejects_mismatched_and_bad_workspace():
+    lib = spmd_mod("_lib").lib()
+    c_i = ctypes.c_int64
+    fake = ctypes.c_void_p(0x1000)
+
+    def d2(n0, n1, s0):
+        return (fake, fake, c_i(0), c_i(n0), c_i(n1), c_i(s0), c_i(1))
+
+    wsb = lib.spmdb200_jacobi_workspace_bytes()
+    assert wsb >= 256
+    st = lib.spmdb200_jacobi2d(*d2(8, 8, 8), *d2(8, 9, 9), c_i(1), c_i(0), None, fake, ctypes.c_size_t(wsb), None)
+    assert st == -1
+    st = lib.spmdb200_jacobi2d(*d2(8, 8, 8), *d2(8, 8, 8), c_i(1), c_i(0), None, None, ctypes.c_size_t(wsb), None)
+    assert st == -5
+    st = lib.spmdb200_jacobi2d(*d2(8, 8, 8), *d2(8, 8, 8), c_i(4), c_i(2), None, fake, ctypes.c_size_t(wsb), None)
+    assert st == -1  # residuals due but no res_out
+
+
+def test_sum_workspace_contract():
+    lib = spmd_mod("_lib").lib()
+    c_i = ctypes.c_int64
+    need = lib.spmdb200_sum_workspace_bytes(c_i(1 << 24))
+    assert need >= 256 + 8
+    fake = ctypes.c_void_p(0x1000)
+    o = (fake, fake, c_i(0))
+    st = lib.spmdb200_sum_f32(*_d1(0x1000, 10), *o, c_i(10), ctypes.c_void_p(0x1010), ctypes.c_size_t(need), None)
+    assert st == -5  # misaligned workspace
+    st = lib.spmdb200_sum_f32(*_d1(0x1000, 10), *o, c_i(10), fake, ctypes.c_size_t(8), None)
+    assert st == -5  # too small
+
+
+def test_no_silent_cpu_fallback_without_gpu():
+    """With no usable GPU a valid host-entry call must report an error, never compute on the CPU."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present; covered by the -m gpu tests")
+    import numpy as np
+    host = spmd_mod("host")
+    a = np.ones(16, np.float32)
+    b = np.ones(16, np.float32)
+    c = np.zeros(16, np.float32)
+    with pytest.raises(spmd_mod("_lib").SpmdError):
+        host.ewise(a, b, c)
+    assert not c.any(), "output written without a GPU"
