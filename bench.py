@@ -215,6 +215,7 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
         for _ in range(reps):
             if flush_l2:
                 flush.zero_()
+            torch.cuda._sleep(200_000)  # busy stream: the host's launch latency stays outside the interval
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(st)
             fn()
