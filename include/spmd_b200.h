@@ -151,6 +151,22 @@ int spmdb200_sum_f32(float *A_base, float *A_aligned, int64_t A_offset, int64_t 
                      float *out_base, float *out_aligned, int64_t out_offset,
                      int64_t N, void *ws, size_t ws_bytes, void *stream);
 
+/* The same deterministic sum as spmdb200_sum_f32 for callers that cannot
+ * allocate device memory: code inside a stream capture that must not
+ * allocate, a plugin whose host application owns every device allocation, or
+ * a path with no workspace to hand out.  No counterpart in the reference.
+ * The scratch (ticket + one f64 partial per block) lives in a file-scope
+ * __device__ array of 256 + 2048*8 = 16,640 bytes that every GPU loading the
+ * library holds until exit; a launch needing more than 2048 block partials is
+ * rejected with SPMDB200_ERR_WORKSPACE (the reduction never launches more, so
+ * every N >= 0 fits).  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress) and should come before any stream
+ * capture.  Allocates nothing.  All calls share the array and each clears its
+ * ticket first: calls that overlap on the GPU race and must be serialised. */
+int spmdb200_sum_f32_noalloc(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+                             float *out_base, float *out_aligned, int64_t out_offset,
+                             int64_t N, void *stream);
+
 /* out[] += sum(A[0..N)) in int32 two's-complement arithmetic (wraps like
  * arith.addi), exact in any order.  The int32 spmd.reduce add that the
  * reference lowers through ReduceToSCFForGPU (SPMDToGPU.cpp:422-477). */

@@ -51,6 +51,7 @@ _SIGS = {
     "spmdb200_stencil3pt": (ctypes.c_int, D2 + D2 + [c_i, c_i, c_p]),
     "spmdb200_sum_workspace_bytes": (c_sz, [c_i]),
     "spmdb200_sum_f32": (ctypes.c_int, D1 + D0 + [c_i, c_p, c_sz, c_p]),
+    "spmdb200_sum_f32_noalloc": (ctypes.c_int, D1 + D0 + [c_i, c_p]),
     "spmdb200_sum_i32": (ctypes.c_int, D1 + D0 + [c_i, c_p]),
     "spmdb200_hierarchical_sum": (ctypes.c_int, D1 + D0 + [c_i, c_p]),
     "spmdb200_jacobi_workspace_bytes": (c_sz, []),

@@ -195,6 +195,15 @@ int num_sms(int device) {
   return cache[device];
 }
 
+int record_api_status(int status, const char *fmt, ...) {
+  g_last_status = status;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_msg, sizeof(g_last_msg), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
 int encode_tensor_map_f32(void *tmap, void *gaddr, int rank, const uint64_t *dims,
                           const uint64_t *strides_bytes, const uint32_t *box) {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;

@@ -94,4 +94,7 @@ int encode_tensor_map_f32(void *tmap /*CUtensorMap*/, void *gaddr, int rank, con
 
 int num_sms(int device);
 
+// Records a status + message for spmdb200_last_error(); returns `status`.
+int record_api_status(int status, const char *fmt, ...);
+
 }  // namespace spmdb200
