@@ -204,6 +204,12 @@ int spmdb200_jacobi2d(float *U_base, float *U_aligned, int64_t U_offset, int64_t
                       int64_t sweeps, int64_t res_every, double *res_out,
                       void *ws, size_t ws_bytes, void *stream);
 
+/* Process-wide limits of the persistent kernels' bounded waits: `grid_ms` for
+ * waits inside one GPU (grid barrier, TMA stages), `peer_ms` for waits on a
+ * neighbouring GPU's halo delivery.  Defaults 4000 and 20000 ms.  A wait that
+ * runs out makes the run end with SPMDB200_ERR_TIMEOUT instead of hanging. */
+int spmdb200_set_wait_budget_ms(int64_t grid_ms, int64_t peer_ms);
+
 /* Reads the device status word a Jacobi run left in `ws` (synchronises
  * `stream`): SPMDB200_OK or SPMDB200_ERR_TIMEOUT. */
 int spmdb200_workspace_status(void *ws, void *stream);
@@ -215,6 +221,55 @@ int spmdb200_workspace_status(void *ws, void *stream);
 int spmdb200_jacobi2d_host(float *U_base, float *U_aligned, int64_t U_offset, int64_t U_size0, int64_t U_size1,
                            int64_t U_stride0, int64_t U_stride1,
                            int64_t sweeps, int64_t res_every, double *res_out);
+
+/* ---- Jacobi-2D over row slabs on several GPUs (one process per GPU) ------ */
+/* No reference counterpart: the reference runs on one GPU.  The global grid
+ * has G rows; this rank owns global rows [g_first, g_first + R).  U and V are
+ * (R + 2) x W local arrays (descriptor sizes (R+2, W), stride1 == 1, 16-byte
+ * aligned rows): local row 0 is the halo row above (global g_first - 1),
+ * local rows 1..R are owned, local row R + 1 is the halo row below.  Halo rows
+ * of U must hold the neighbours' initial rows; the kernel keeps every halo
+ * current by storing its first / last owned row straight into the neighbour's
+ * halo row over NVLink each sweep.  up_* / dn_* are the neighbours' U, V and
+ * workspace as mapped in this process (spmdb200_ipc_open), NULL at the global
+ * top / bottom.  all_ws[q] is rank q's workspace as mapped here (all_ws[rank]
+ * is `ws`); the residual of every residual sweep is all-gathered into each
+ * rank's workspace.  The caller must clear every rank's workspace
+ * (spmdb200_jacobi_ws_reset) and make all ranks wait for one another before
+ * any rank launches.  res_out (device, optional) receives this rank's local
+ * residual contributions.  Sweep semantics and ping-pong are those of
+ * spmdb200_jacobi2d; global rows 0 and G-1 and columns 0 and W-1 are fixed. */
+int spmdb200_jacobi2d_slab(float *U_base, float *U_aligned, int64_t U_offset, int64_t U_size0, int64_t U_size1,
+                           int64_t U_stride0, int64_t U_stride1,
+                           float *V_base, float *V_aligned, int64_t V_offset, int64_t V_size0, int64_t V_size1,
+                           int64_t V_stride0, int64_t V_stride1,
+                           int64_t g_first, int64_t G, int64_t sweeps, int64_t res_every, double *res_out,
+                           void *ws, float *up_u, float *up_v, void *up_ws, float *dn_u, float *dn_v, void *dn_ws,
+                           int rank, int nranks, void *const *all_ws, void *stream);
+/* Clears the 256-byte header of a Jacobi workspace on `stream`. */
+int spmdb200_jacobi_ws_reset(void *ws, void *stream);
+/* After every rank's slab run has finished: res_host[r] = sum over ranks q
+ * (in rank order) of rank q's residual contribution r, r < nres.  Synchronous. */
+int spmdb200_jacobi2d_slab_residuals(void *ws, int nranks, int64_t nres, double *res_host);
+
+/* Device memory and CUDA IPC for the slab path (cudaMalloc'd, so IPC-able). */
+int spmdb200_dev_alloc(size_t bytes, void **out);
+int spmdb200_dev_free(void *p);
+/* Copies `bytes` between any two addresses (host or device; direction from
+ * unified addressing) on `stream`, then synchronises it. */
+int spmdb200_memcpy(void *dst, const void *src, size_t bytes, void *stream);
+/* 64-byte IPC handle of a spmdb200_dev_alloc pointer. */
+int spmdb200_ipc_handle(void *dev_ptr, void *handle64_out);
+int spmdb200_ipc_open(const void *handle64, void **dev_ptr_out);
+int spmdb200_ipc_close(void *dev_ptr);
+/* Fills a rows x W block of a row-major f32 grid (row pitch `pitch`) with the
+ * seeded synthetic Jacobi input: cell (g, c) of the global G x W grid, g =
+ * g_row0 + local row, is uniform [0,1) from a counter-based hash of
+ * (seed, g, c); global boundary rows/columns and rows outside [0, G) are 0.
+ * Every rank computes the same value for a global cell, so halos need no
+ * exchange at start-up. */
+int spmdb200_fill_jacobi_input(float *p, int64_t pitch, int64_t rows, int64_t W, int64_t g_row0, int64_t G,
+                               uint64_t seed, void *stream);
 
 /* ---- Jacobi-3D 7-point --------------------------------------------------- */
 /* One sweep over the D x H x W grid (index order [z][y][x]):

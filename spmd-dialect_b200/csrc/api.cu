@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -195,6 +196,11 @@ int num_sms(int device) {
   return cache[device];
 }
 
+static std::atomic<unsigned long long> g_grid_budget_ns{kWaitBudgetNs};
+static std::atomic<unsigned long long> g_peer_budget_ns{kPeerWaitBudgetNs};
+
+unsigned long long wait_budget_ns(bool peer) { return peer ? g_peer_budget_ns.load() : g_grid_budget_ns.load(); }
+
 int record_api_status(int status, const char *fmt, ...) {
   g_last_status = status;
   va_list ap;
@@ -343,6 +349,14 @@ int spmdb200_hierarchical_sum(float *A_base, float *A, int64_t A_off, int64_t A_
 
 size_t spmdb200_jacobi_workspace_bytes(void) { return sizeof(JacobiWs); }
 
+int spmdb200_set_wait_budget_ms(int64_t grid_ms, int64_t peer_ms) {
+  if (grid_ms < 1 || peer_ms < 1 || grid_ms > 600000 || peer_ms > 600000)
+    return fail(SPMDB200_ERR_INVALID_ARG, "wait budgets must be in [1, 600000] ms");
+  g_grid_budget_ns.store((unsigned long long)grid_ms * 1000000ull);
+  g_peer_budget_ns.store((unsigned long long)peer_ms * 1000000ull);
+  return ok();
+}
+
 int spmdb200_workspace_status(void *ws, void *stream) {
   if (!ws) return fail(SPMDB200_ERR_WORKSPACE, "null workspace");
   CHECK(jacobi_status_from_ws(static_cast<JacobiWs *>(ws), (cudaStream_t)stream));
@@ -434,6 +448,138 @@ int spmdb200_jacobi3d(float *U_base, float *U, int64_t U_off, int64_t U_n0, int6
   } else {
     CUDA_TRY(launch_jacobi3d_generic(p, s));
   }
+  return ok();
+}
+
+// ---------------------------------------------------------------- multi-GPU slabs
+int spmdb200_jacobi_ws_reset(void *ws, void *stream) {
+  if (!ws) return fail(SPMDB200_ERR_WORKSPACE, "null workspace");
+  CUDA_TRY(cudaMemsetAsync(ws, 0, 256, (cudaStream_t)stream));
+  return ok();
+}
+
+int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0, int64_t U_n1, int64_t U_s0,
+                           int64_t U_s1, float *V_base, float *V, int64_t V_off, int64_t V_n0, int64_t V_n1,
+                           int64_t V_s0, int64_t V_s1, int64_t g_first, int64_t G, int64_t sweeps,
+                           int64_t res_every, double *res_out, void *ws, float *up_u, float *up_v, void *up_ws,
+                           float *dn_u, float *dn_v, void *dn_ws, int rank, int nranks, void *const *all_ws,
+                           void *stream) {
+  (void)U_base; (void)V_base;
+  CHECK(check2("U", U, U_off, U_n0, U_n1, U_s0, U_s1));
+  CHECK(check2("V", V, V_off, V_n0, V_n1, V_s0, V_s1));
+  if (U_n0 != V_n0 || U_n1 != V_n1 || U_s0 != V_s0 || U_s1 != V_s1)
+    return fail(SPMDB200_ERR_INVALID_ARG, "U and V must have identical sizes and strides");
+  if (U_n0 < 3 || U_n1 < 1) return fail(SPMDB200_ERR_INVALID_ARG, "a slab needs >= 1 owned row plus 2 halo rows");
+  const int64_t R = U_n0 - 2;
+  if (U_s1 != 1) return fail(SPMDB200_ERR_UNSUPPORTED, "slab rows must be contiguous (stride1 == 1)");
+  if (g_first < 0 || G < 1 || g_first + R > G)
+    return fail(SPMDB200_ERR_INVALID_ARG, "owned rows [%lld, %lld) outside the %lld global rows",
+                (long long)g_first, (long long)(g_first + R), (long long)G);
+  if (nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks)
+    return fail(SPMDB200_ERR_INVALID_ARG, "rank %d of %d (at most %d ranks)", rank, nranks, kMaxRanks);
+  if ((g_first > 0) != (up_u != nullptr) || (g_first + R < G) != (dn_u != nullptr))
+    return fail(SPMDB200_ERR_INVALID_ARG, "neighbour pointers must be given exactly where a neighbour exists");
+  if ((up_u && (!up_v || !up_ws)) || (dn_u && (!dn_v || !dn_ws)))
+    return fail(SPMDB200_ERR_INVALID_ARG, "incomplete neighbour (U, V, workspace)");
+  if (nranks > 1 && !all_ws) return fail(SPMDB200_ERR_INVALID_ARG, "all_ws is required for nranks > 1");
+  if (sweeps < 0 || res_every < 0) return fail(SPMDB200_ERR_INVALID_ARG, "negative sweeps / res_every");
+  if (res_every > 0 && sweeps / res_every > kMaxResSlots)
+    return fail(SPMDB200_ERR_UNSUPPORTED, "at most %d residuals per slab run", kMaxResSlots);
+  CHECK(check_jacobi_ws(ws, sizeof(JacobiWs)));
+  if (sweeps == 0) return ok();
+  Jacobi2dProblem p{};
+  p.u = U + U_off;
+  p.v = V + V_off;
+  p.pitch = U_s0;
+  p.h_local = U_n0;
+  p.w = U_n1;
+  p.row_lo = 1;
+  p.row_hi = R + 1;
+  p.g_row0 = g_first - 1;
+  p.g_rows = G;
+  p.sweeps = sweeps;
+  p.res_every = res_every;
+  p.res_out = res_out;
+  p.ws = static_cast<JacobiWs *>(ws);
+  if (!jacobi2d_tma_ok(p))
+    return fail(SPMDB200_ERR_UNSUPPORTED, "slab arrays need 16-byte aligned rows (pitch multiple of 4 floats)");
+  SlabPeers peers;
+  peers.up_u = up_u;
+  peers.up_v = up_v;
+  peers.dn_u = dn_u;
+  peers.dn_v = dn_v;
+  peers.up_row = R + 1;  // our first owned row is the bottom halo row of the rank above
+  peers.dn_row = 0;      // our last owned row is the top halo row of the rank below
+  peers.up_flag = up_ws ? &static_cast<JacobiWs *>(up_ws)->from_below : nullptr;
+  peers.dn_flag = dn_ws ? &static_cast<JacobiWs *>(dn_ws)->from_above : nullptr;
+  peers.rank = rank;
+  peers.nranks = nranks;
+  for (int q = 0; q < nranks; ++q)
+    peers.peer_ws[q] = static_cast<JacobiWs *>(all_ws ? all_ws[q] : (q == rank ? ws : nullptr));
+  if (!peers.peer_ws[rank]) peers.peer_ws[rank] = static_cast<JacobiWs *>(ws);
+  int grid = 0;
+  CUDA_TRY(launch_jacobi2d_persistent(p, peers, (cudaStream_t)stream, &grid));
+  return ok();
+}
+
+int spmdb200_jacobi2d_slab_residuals(void *ws, int nranks, int64_t nres, double *res_host) {
+  if (!ws) return fail(SPMDB200_ERR_WORKSPACE, "null workspace");
+  if (nranks < 1 || nranks > kMaxRanks || nres < 0 || nres > kMaxResSlots || (nres > 0 && !res_host))
+    return fail(SPMDB200_ERR_INVALID_ARG, "bad nranks / nres / output");
+  if (nres == 0) return ok();
+  std::vector<double> slots((size_t)nres * kMaxRanks);
+  CUDA_TRY(cudaMemcpy(slots.data(), static_cast<JacobiWs *>(ws)->res_slots, slots.size() * sizeof(double),
+                      cudaMemcpyDeviceToHost));
+  for (int64_t r = 0; r < nres; ++r) {
+    double t = 0.0;
+    for (int q = 0; q < nranks; ++q) t += slots[(size_t)r * kMaxRanks + q];
+    res_host[r] = t;
+  }
+  return ok();
+}
+
+int spmdb200_dev_alloc(size_t bytes, void **out) {
+  if (!out) return fail(SPMDB200_ERR_INVALID_ARG, "null output pointer");
+  *out = nullptr;
+  CHECK(have_device());
+  CUDA_TRY(cudaMalloc(out, bytes ? bytes : 256));
+  return ok();
+}
+int spmdb200_dev_free(void *p) {
+  if (p) CUDA_TRY(cudaFree(p));
+  return ok();
+}
+int spmdb200_memcpy(void *dst, const void *src, size_t bytes, void *stream) {
+  if (bytes == 0) return ok();
+  if (!dst || !src) return fail(SPMDB200_ERR_INVALID_ARG, "null pointer");
+  CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, (cudaStream_t)stream));
+  CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+  return ok();
+}
+int spmdb200_ipc_handle(void *dev_ptr, void *handle64_out) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  if (!dev_ptr || !handle64_out) return fail(SPMDB200_ERR_INVALID_ARG, "null pointer");
+  cudaIpcMemHandle_t h;
+  CUDA_TRY(cudaIpcGetMemHandle(&h, dev_ptr));
+  memcpy(handle64_out, &h, sizeof(h));
+  return ok();
+}
+int spmdb200_ipc_open(const void *handle64, void **dev_ptr_out) {
+  if (!handle64 || !dev_ptr_out) return fail(SPMDB200_ERR_INVALID_ARG, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  CUDA_TRY(cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess));
+  return ok();
+}
+int spmdb200_ipc_close(void *dev_ptr) {
+  if (dev_ptr) CUDA_TRY(cudaIpcCloseMemHandle(dev_ptr));
+  return ok();
+}
+int spmdb200_fill_jacobi_input(float *p, int64_t pitch, int64_t rows, int64_t W, int64_t g_row0, int64_t G,
+                               uint64_t seed, void *stream) {
+  if (rows < 0 || W < 0 || pitch < W || (rows > 0 && W > 0 && !p))
+    return fail(SPMDB200_ERR_INVALID_ARG, "bad fill arguments");
+  CUDA_TRY(launch_fill_jacobi_input(p, pitch, rows, W, g_row0, G, seed, (cudaStream_t)stream));
   return ok();
 }
 

@@ -72,6 +72,9 @@ bool jacobi2d_tma_ok(const Jacobi2dProblem &p);
 // Persistent TMA path (requires jacobi2d_tma_ok).  Returns the launch error.
 cudaError_t launch_jacobi2d_persistent(const Jacobi2dProblem &p, const SlabPeers &peers,
                                        cudaStream_t s, int *grid_out);
+// Seeded synthetic Jacobi input (counter-based hash of (seed, global row, column)).
+cudaError_t launch_fill_jacobi_input(float *p, int64_t pitch, int64_t rows, int64_t w, int64_t g_row0,
+                                     int64_t g_rows, uint64_t seed, cudaStream_t s);
 // One launch per sweep, any strides (single GPU only).
 cudaError_t launch_jacobi2d_generic(const Jacobi2dProblem &p, int64_t stride1, cudaStream_t s);
 
@@ -93,6 +96,9 @@ int encode_tensor_map_f32(void *tmap /*CUtensorMap*/, void *gaddr, int rank, con
                           const uint64_t *strides_bytes /*rank-1 entries*/, const uint32_t *box);
 
 int num_sms(int device);
+
+// Bounded-wait limits of the persistent kernels (process-wide, nanoseconds).
+unsigned long long wait_budget_ns(bool peer);
 
 // Records a status + message for spmdb200_last_error(); returns `status`.
 int record_api_status(int status, const char *fmt, ...);

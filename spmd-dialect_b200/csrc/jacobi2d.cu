@@ -5,13 +5,15 @@
 // Persistent path (pitch-aligned grids)
 // -------------------------------------
 // One cooperative launch runs every sweep.  Each CTA = 1 producer warp + 8
-// consumer warps.  Tiles are 32 rows x 128 columns of output; the producer
-// stages each tile's footprint -- a 34 x 136 box starting one row above and
-// four columns left of the tile, so the TMA x coordinate stays 16-byte aligned
-// -- into a 4-deep shared-memory ring with cp.async.bulk.tensor.2d, completion
-// tracked by mbarrier expect_tx.  Out-of-grid box cells are zero-filled by the
+// consumer warps, two CTAs per SM.  Tiles are 64 rows x 128 columns of
+// output; the producer stages each tile's footprint -- a 66 x 136 box starting
+// one row above and four columns left of the tile, so the TMA x coordinate
+// stays 16-byte aligned -- into a 3-deep shared-memory ring (3 x 36 KB) with
+// cp.async.bulk.tensor.2d, completion tracked by mbarrier expect_tx.  (Tile
+// height and ring depth were chosen by measurement on B200: 1 CTA per SM or a
+// 2-deep ring leaves HBM idle; 64 x 3 beat 16/32/40/48/96/128-row tiles.)  Out-of-grid box cells are zero-filled by the
 // TMA unit (the guard of PromoteGroupMemory.cpp:268-292, done in hardware).
-// Consumer warp w computes tile rows 4w..4w+3; lane l owns 4 contiguous
+// Consumer warp w computes tile rows 8w..8w+7; lane l owns 4 contiguous
 // columns, reads north/centre/south as float4 from the ring (sliding down the
 // rows), gets west/east from neighbouring lanes by shuffle and stores float4.
 //
@@ -35,14 +37,20 @@
 namespace spmdb200 {
 namespace {
 
+#ifndef SPMDB200_J2_BH
+#define SPMDB200_J2_BH 64
+#endif
+#ifndef SPMDB200_J2_STAGES
+#define SPMDB200_J2_STAGES 3
+#endif
 constexpr int BW = 128;                   // tile columns
-constexpr int BH = 32;                    // tile rows
+constexpr int BH = SPMDB200_J2_BH;        // tile rows (multiple of 8)
 constexpr int XPAD = 4;                   // left pad of the footprint box (16 bytes)
 constexpr int BOXW = BW + 2 * XPAD;       // 136 floats = 544 bytes per box row
-constexpr int BOXH = BH + 2;              // 34 rows
-constexpr int STAGES = 4;
-constexpr int STAGE_BYTES = BOXW * BOXH * 4;                    // 18496
-constexpr int STAGE_STRIDE = (STAGE_BYTES + 127) / 128 * 128;    // 18560
+constexpr int BOXH = BH + 2;              // footprint rows
+constexpr int STAGES = SPMDB200_J2_STAGES;
+constexpr int STAGE_BYTES = BOXW * BOXH * 4;
+constexpr int STAGE_STRIDE = (STAGE_BYTES + 127) / 128 * 128;
 constexpr int CWARPS = 8;
 constexpr int RPW = BH / CWARPS;          // rows per consumer warp
 constexpr int THREADS = 32 * (CWARPS + 1);
@@ -65,6 +73,7 @@ struct J2Kernel {
   double *res_out;
   JacobiWs *ws;
   SlabPeers peers;
+  unsigned long long grid_budget_ns, peer_budget_ns;  // bounded-wait limits
 };
 
 __device__ __forceinline__ void record_status(JacobiWs *ws, volatile int *abort, int code) {
@@ -72,14 +81,18 @@ __device__ __forceinline__ void record_status(JacobiWs *ws, volatile int *abort,
   *abort = 1;
 }
 
-// Waits until *p >= target (wrap-safe); acquire at gpu or sys scope.
+// Waits until *p >= target (wrap-safe); acquire at gpu or sys scope.  Gives
+// up when the budget runs out, when this CTA aborts, or when any CTA of the
+// grid has recorded an error in the workspace status word.
 __device__ __forceinline__ bool wait_counter(const unsigned *p, unsigned target, bool sys,
-                                             volatile int *abort, unsigned long long budget) {
+                                             volatile int *abort, unsigned long long budget,
+                                             const JacobiWs *ws) {
   const unsigned long long t0 = globaltimer_ns();
-  for (;;) {
+  for (uint32_t i = 0;; ++i) {
     const unsigned v = sys ? ld_acquire_sys(p) : ld_acquire_gpu(p);
     if ((int)(v - target) >= 0) return true;
     if (*abort) return false;
+    if ((i & 7u) == 7u && *reinterpret_cast<const volatile int *>(&ws->status) != 0) return false;
     if (globaltimer_ns() - t0 > budget) return false;
     __nanosleep(64);
   }
@@ -122,7 +135,7 @@ __device__ __forceinline__ void combine_residual(const J2Kernel &k, int r, int l
   p = warp_sum_f64(p);
   if (lane == 0) {
     if (k.res_out) k.res_out[r] = p;
-    if (k.peers.nranks > 1 && r < kMaxResSlots) {
+    if (k.peers.peer_ws[0] && r < kMaxResSlots) {  // slab mode: all-gather into every rank's slots
       for (int q = 0; q < k.peers.nranks; ++q)
         if (k.peers.peer_ws[q]) k.peers.peer_ws[q]->res_slots[r][k.peers.rank] = p;
       __threadfence_system();
@@ -164,7 +177,7 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
     for (int s = 0; s < k.sweeps && ok; ++s) {
       const void *src = (s & 1) ? (const void *)&map_v : (const void *)&map_u;
       if (s > 0) {
-        if (lane == 0 && !wait_counter(&k.ws->barrier, (unsigned)s * (unsigned)G, false, abort, kWaitBudgetNs)) {
+        if (lane == 0 && !wait_counter(&k.ws->barrier, (unsigned)s * (unsigned)G, false, abort, k.grid_budget_ns, k.ws)) {
           record_status(k.ws, abort, kDevTimeoutGridBarrier);
           ok = false;
         }
@@ -179,13 +192,13 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
           if (s > 0) {
             const unsigned need = (unsigned)s * (unsigned)k.tiles_x;
             if (ty == 0 && k.peers.up_flag &&
-                !wait_counter(&k.ws->from_above, need, true, abort, kPeerWaitBudgetNs)) {
+                !wait_counter(&k.ws->from_above, need, true, abort, k.peer_budget_ns, k.ws)) {
               record_status(k.ws, abort, kDevTimeoutPeer);
               ok = false;
               break;
             }
             if (ty == k.tiles_y - 1 && k.peers.dn_flag &&
-                !wait_counter(&k.ws->from_below, need, true, abort, kPeerWaitBudgetNs)) {
+                !wait_counter(&k.ws->from_below, need, true, abort, k.peer_budget_ns, k.ws)) {
               record_status(k.ws, abort, kDevTimeoutPeer);
               ok = false;
               break;
@@ -209,7 +222,7 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
     }
     if (ok && blockIdx.x == 0 && k.sweeps > 0 && k.res_every > 0 && k.sweeps % k.res_every == 0) {
       if (lane == 0 &&
-          !wait_counter(&k.ws->barrier, (unsigned)k.sweeps * (unsigned)G, false, abort, kWaitBudgetNs)) {
+          !wait_counter(&k.ws->barrier, (unsigned)k.sweeps * (unsigned)G, false, abort, k.grid_budget_ns, k.ws)) {
         record_status(k.ws, abort, kDevTimeoutGridBarrier);
         ok = false;
       }
@@ -383,7 +396,43 @@ __global__ void __launch_bounds__(256) jacobi2d_sweep_generic_kernel(
   }
 }
 
+// splitmix64 finaliser over (seed, row, column): a counter-based generator, so
+// any rank can produce any global cell without coordination.
+__device__ __forceinline__ float hash_uniform(uint64_t seed, uint64_t g, uint64_t c) {
+  uint64_t x = seed * 0x9E3779B97F4A7C15ull + g * 0xD1B54A32D192ED03ull + c * 0x8CB92BA72F3D8DD7ull;
+  x ^= x >> 30;
+  x *= 0xBF58476D1CE4E5B9ull;
+  x ^= x >> 27;
+  x *= 0x94D049BB133111EBull;
+  x ^= x >> 31;
+  return (float)(x >> 40) * (1.0f / 16777216.0f);  // 24 random bits -> [0, 1)
+}
+
+__global__ void __launch_bounds__(256) fill_jacobi_input_kernel(float *p, long long pitch, long long rows,
+                                                                long long w, long long g_row0, long long g_rows,
+                                                                uint64_t seed) {
+  const long long nth = (long long)gridDim.x * blockDim.x;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < rows * w; idx += nth) {
+    const long long r = idx / w, c = idx - r * w;
+    const long long g = g_row0 + r;
+    const bool interior = g > 0 && g < g_rows - 1 && c > 0 && c < w - 1;
+    p[r * pitch + c] = interior ? hash_uniform(seed, (uint64_t)g, (uint64_t)c) : 0.0f;
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_fill_jacobi_input(float *p, int64_t pitch, int64_t rows, int64_t w, int64_t g_row0,
+                                     int64_t g_rows, uint64_t seed, cudaStream_t s) {
+  if (rows <= 0 || w <= 0) return cudaSuccess;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  long long g = (rows * w + 255) / 256;
+  const long long cap = (long long)num_sms(dev) * 8;
+  if (g > cap) g = cap;
+  fill_jacobi_input_kernel<<<(unsigned)g, 256, 0, s>>>(p, pitch, rows, w, g_row0, g_rows, seed);
+  return cudaGetLastError();
+}
 
 bool jacobi2d_tma_ok(const Jacobi2dProblem &p) {
   const uintptr_t a = reinterpret_cast<uintptr_t>(p.u), b = reinterpret_cast<uintptr_t>(p.v);
@@ -417,6 +466,8 @@ cudaError_t launch_jacobi2d_persistent(const Jacobi2dProblem &p, const SlabPeers
   k.res_out = p.res_out;
   k.ws = p.ws;
   k.peers = peers;
+  k.grid_budget_ns = wait_budget_ns(false);
+  k.peer_budget_ns = wait_budget_ns(true);
 
   static thread_local int configured_dev = -1;
   int dev = 0;

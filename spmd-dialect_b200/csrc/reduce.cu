@@ -8,10 +8,25 @@ namespace spmdb200 {
 constexpr int kSumThreads = 256;
 constexpr size_t kSumWsHeader = 256;  // ticket + padding, partials follow
 
-int sum_f32_grid(int64_t n) {
+// Resident blocks of `kernel` on the device (blocks per SM x SM count), so a
+// reduction grid is exactly one wave: no half-empty second wave at the tail.
+template <class K>
+static int resident_blocks(K kernel, int dev, int *cache) {
+  if (dev < 0 || dev >= 64) return num_sms(dev) * 4;
+  if (cache[dev] == 0) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kSumThreads, 0) != cudaSuccess || per_sm < 1)
+      per_sm = 4;
+    cache[dev] = per_sm * num_sms(dev);
+  }
+  return cache[dev];
+}
+
+template <class K>
+static int reduce_grid(K kernel, int *cache, int64_t n) {
   int dev = 0;
   cudaGetDevice(&dev);
-  const int64_t cap = (int64_t)num_sms(dev) * 8;  // 8 x 256 threads = full SM
+  const int64_t cap = resident_blocks(kernel, dev, cache);
   int64_t want = (n + kSumThreads * 16 - 1) / (kSumThreads * 16);
   if (want < 1) want = 1;
   if (want > cap) want = cap;
@@ -28,7 +43,7 @@ size_t sum_f32_workspace_bytes(int64_t n) {
 // Deterministic f32 sum: per-block f64 partials, last block (ticket) combines
 // them in index order and performs the single f32 rounding of
 // out = out + total.  The ticket is reset to 0 so the workspace stays reusable.
-__global__ void __launch_bounds__(kSumThreads) sum_f32_kernel(const float *__restrict__ a, int64_t sa,
+__global__ void __launch_bounds__(kSumThreads, 8) sum_f32_kernel(const float *__restrict__ a, int64_t sa,
                                                               int64_t n, float *out,
                                                               unsigned *ticket, double *partials) {
   __shared__ double sh[32];
@@ -60,12 +75,16 @@ __global__ void __launch_bounds__(kSumThreads) sum_i32_kernel(const int32_t *__r
   if (threadIdx.x == 0 && b != 0u) atomicAdd(reinterpret_cast<unsigned *>(out), b);
 }
 
-__global__ void __launch_bounds__(kSumThreads) hier_sum_f32_kernel(const float *__restrict__ a, int64_t sa,
+__global__ void __launch_bounds__(kSumThreads, 8) hier_sum_f32_kernel(const float *__restrict__ a, int64_t sa,
                                                                    int64_t n, float *out) {
   __shared__ double sh[32];
   const double b = block_sum_f64(thread_sum_f64(a, sa, n), sh);
   if (threadIdx.x == 0) atomicAdd(out, __double2float_rn(b));
 }
+
+static int g_f32_cache[64], g_i32_cache[64], g_hier_cache[64];
+
+int sum_f32_grid(int64_t n) { return reduce_grid(sum_f32_kernel, g_f32_cache, n); }
 
 cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_t s) {
   const int g = sum_f32_grid(n);
@@ -77,13 +96,13 @@ cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_
 
 cudaError_t launch_sum_i32(const int32_t *a, int64_t stride, int32_t *out, int64_t n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
-  sum_i32_kernel<<<sum_f32_grid(n), kSumThreads, 0, s>>>(a, stride, n, out);
+  sum_i32_kernel<<<reduce_grid(sum_i32_kernel, g_i32_cache, n), kSumThreads, 0, s>>>(a, stride, n, out);
   return cudaGetLastError();
 }
 
 cudaError_t launch_hier_sum_f32(View1 a, float *out, int64_t n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
-  hier_sum_f32_kernel<<<sum_f32_grid(n), kSumThreads, 0, s>>>(a.p, a.s, n, out);
+  hier_sum_f32_kernel<<<reduce_grid(hier_sum_f32_kernel, g_hier_cache, n), kSumThreads, 0, s>>>(a.p, a.s, n, out);
   return cudaGetLastError();
 }
 

@@ -1,0 +1,281 @@
+"""Row-slab Jacobi-2D on several GPUs: one process per GPU.
+
+torch.distributed is plumbing only (exchanging CUDA IPC handles, the
+rendezvous before each launch, gathering results for tests).  The data path --
+one halo row up and one down per sweep, and the residual all-gather every
+`res_every` sweeps -- runs inside the persistent kernel over NVLink
+(spmdb200_jacobi2d_slab): no NCCL call sits between sweeps.
+
+Decomposition: the G x W global grid is cut into contiguous row blocks; rank p
+owns global rows [g_first, g_first + rows) and keeps a (rows + 2) x pitch local
+array whose rows 0 and rows + 1 mirror the neighbours' edge rows.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._lib import c_i, c_p, call, lib
+
+
+# ---------------------------------------------------------------- decomposition
+def partition(G: int, world: int, rank: int) -> tuple[int, int]:
+    """(g_first, rows) of `rank`'s contiguous block of the G global rows."""
+    if not (0 <= rank < world) or G < world:
+        raise ValueError(f"cannot split {G} rows over {world} ranks")
+    base, extra = divmod(G, world)
+    rows = base + (1 if rank < extra else 0)
+    return rank * base + min(rank, extra), rows
+
+
+def neighbours(G: int, world: int, rank: int) -> tuple[int | None, int | None]:
+    """Ranks owning the rows just above and just below this rank's block."""
+    return (rank - 1 if rank > 0 else None), (rank + 1 if rank < world - 1 else None)
+
+
+def local_row_range(G: int, world: int, rank: int) -> tuple[int, int]:
+    """Global rows [lo, hi) a rank's local array mirrors: its block plus one halo
+    row on each side (rows outside [0, G) exist locally but are never read)."""
+    g_first, rows = partition(G, world, rank)
+    return g_first - 1, g_first + rows + 1
+
+
+def pitch_for(cols: int) -> int:
+    """Row pitch in floats: a multiple of 4 so every row is 16-byte aligned (TMA)."""
+    return (cols + 3) & ~3
+
+
+# ---------------------------------------------------------------- device memory
+class DeviceBuffer:
+    """cudaMalloc'd device memory (IPC-shareable), freed by close()."""
+
+    def __init__(self, nbytes: int):
+        p = c_p()
+        call("spmdb200_dev_alloc", ctypes.c_size_t(nbytes), ctypes.byref(p))
+        self.ptr = p.value
+        self.nbytes = nbytes
+
+    def ipc_handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        call("spmdb200_ipc_handle", c_p(self.ptr), buf)
+        return buf.raw
+
+    def close(self) -> None:
+        if self.ptr:
+            call("spmdb200_dev_free", c_p(self.ptr))
+            self.ptr = 0
+
+
+def ipc_open(handle: bytes) -> int:
+    p = c_p()
+    call("spmdb200_ipc_open", ctypes.create_string_buffer(handle, 64), ctypes.byref(p))
+    return p.value
+
+
+@dataclass
+class _Peer:
+    u: int = 0
+    v: int = 0
+    ws: int = 0
+
+
+def _dist():
+    import torch.distributed as dist
+    return dist if dist.is_available() and dist.is_initialized() else None
+
+
+def rendezvous() -> None:
+    """Every rank reaches this point before any rank launches: a rank that never
+    arrives makes the others fail here (process-group timeout) instead of
+    launching a kernel that would wait on its halo rows."""
+    d = _dist()
+    if d is not None and d.get_world_size() > 1:
+        d.barrier()
+
+
+class SlabJacobi2D:
+    """This rank's share of a multi-GPU Jacobi-2D run.
+
+    G x cols global grid (G defaults to rows_per_rank * world: weak scaling).
+    `init` is None (seeded synthetic input generated on the device, identical
+    to what a single-GPU run of the same global grid would see) or the full
+    global grid as a numpy array (tests)."""
+
+    def __init__(self, cols: int, rows_per_rank: int | None = None, G: int | None = None, seed: int = 4,
+                 res_every: int = 10, init: np.ndarray | None = None):
+        import torch
+        d = _dist()
+        self.rank = d.get_rank() if d else 0
+        self.world = d.get_world_size() if d else 1
+        if G is None:
+            if rows_per_rank is None:
+                raise ValueError("give rows_per_rank or G")
+            G = rows_per_rank * self.world
+        self.G, self.cols, self.res_every = G, cols, res_every
+        self.g_first, self.rows = partition(G, self.world, self.rank)
+        self.pitch = pitch_for(cols)
+        self.local_rows = self.rows + 2
+        nbytes = self.local_rows * self.pitch * 4
+        self._u = DeviceBuffer(nbytes)
+        self._v = DeviceBuffer(nbytes)
+        self._ws = DeviceBuffer(int(lib().spmdb200_jacobi_workspace_bytes()))
+        self.sweeps_done = 0
+        self._nres_last = 0
+        stream = c_p(torch.cuda.current_stream().cuda_stream)
+        if init is None:
+            call("spmdb200_fill_jacobi_input", c_p(self._u.ptr), c_i(self.pitch), c_i(self.local_rows),
+                 c_i(cols), c_i(self.g_first - 1), c_i(G), ctypes.c_uint64(seed), stream)
+            call("spmdb200_fill_jacobi_input", c_p(self._v.ptr), c_i(self.pitch), c_i(self.local_rows),
+                 c_i(cols), c_i(self.g_first - 1), c_i(G), ctypes.c_uint64(seed), stream)
+        else:
+            self.load_global(init)
+        torch.cuda.current_stream().synchronize()
+        # Map the neighbours' grids and every rank's workspace into this process.
+        self._up, self._dn = _Peer(), _Peer()
+        self._all_ws = [0] * self.world
+        self._opened: list[int] = []
+        self._all_ws[self.rank] = self._ws.ptr
+        if self.world > 1:
+            mine = (self._u.ipc_handle(), self._v.ipc_handle(), self._ws.ipc_handle())
+            handles: list = [None] * self.world
+            d.all_gather_object(handles, mine)
+            up, dn = neighbours(G, self.world, self.rank)
+            for q in range(self.world):
+                if q != self.rank:
+                    self._all_ws[q] = self._open(handles[q][2])
+            if up is not None:
+                self._up = _Peer(self._open(handles[up][0]), self._open(handles[up][1]), self._all_ws[up])
+            if dn is not None:
+                self._dn = _Peer(self._open(handles[dn][0]), self._open(handles[dn][1]), self._all_ws[dn])
+        self._all_ws_arr = (c_p * max(self.world, 1))(*[c_p(x) for x in self._all_ws])
+
+    def _open(self, h: bytes) -> int:
+        p = ipc_open(h)
+        self._opened.append(p)
+        return p
+
+    # ---------------------------------------------------------------- data movement
+    def _desc(self, ptr: int) -> tuple:
+        p = c_p(ptr)
+        return (p, p, c_i(0), c_i(self.local_rows), c_i(self.cols), c_i(self.pitch), c_i(1))
+
+    def load_global(self, grid: np.ndarray) -> None:
+        """Copies this rank's rows (+ halos) of a global G x cols grid into U (and V)."""
+        lo, hi = local_row_range(self.G, self.world, self.rank)
+        local = np.zeros((self.local_rows, self.pitch), np.float32)
+        src_lo, src_hi = max(lo, 0), min(hi, self.G)
+        local[src_lo - lo:src_hi - lo, :self.cols] = grid[src_lo:src_hi]
+        for buf in (self._u, self._v):
+            call("spmdb200_memcpy", c_p(buf.ptr), local.ctypes.data_as(c_p), ctypes.c_size_t(local.nbytes), None)
+        self.sweeps_done = 0
+
+    def local_owned(self) -> np.ndarray:
+        """This rank's owned rows of the current grid (host copy)."""
+        local = np.empty((self.local_rows, self.pitch), np.float32)
+        call("spmdb200_memcpy", local.ctypes.data_as(c_p), c_p(self._u.ptr), ctypes.c_size_t(local.nbytes), None)
+        return local[1:self.rows + 1, :self.cols].copy()
+
+    def gather(self) -> np.ndarray | None:
+        """The full global grid on rank 0 (None elsewhere)."""
+        mine = self.local_owned()
+        d = _dist()
+        if d is None or self.world == 1:
+            return mine
+        parts: list = [None] * self.world if self.rank == 0 else None
+        d.gather_object(mine, parts, dst=0)
+        return np.concatenate(parts, axis=0) if self.rank == 0 else None
+
+    # ---------------------------------------------------------------- running
+    def run(self, sweeps: int, check: bool = True) -> None:
+        """`sweeps` sweeps on every rank (all ranks must call with the same count)."""
+        import torch
+        stream = c_p(torch.cuda.current_stream().cuda_stream)
+        call("spmdb200_jacobi_ws_reset", c_p(self._ws.ptr), stream)
+        torch.cuda.current_stream().synchronize()
+        rendezvous()  # every workspace is clear before any kernel can deliver a halo
+        up, dn = self._up, self._dn
+        call("spmdb200_jacobi2d_slab", *self._desc(self._u.ptr), *self._desc(self._v.ptr), c_i(self.g_first),
+             c_i(self.G), c_i(sweeps), c_i(self.res_every), c_p(0), c_p(self._ws.ptr),
+             c_p(up.u or None), c_p(up.v or None), c_p(up.ws or None),
+             c_p(dn.u or None), c_p(dn.v or None), c_p(dn.ws or None),
+             ctypes.c_int(self.rank), ctypes.c_int(self.world), self._all_ws_arr, stream)
+        self._nres_last = sweeps // self.res_every if self.res_every > 0 else 0
+        self.sweeps_done += sweeps
+        if sweeps % 2 == 1:
+            # The result sits in V on every rank: swap roles so U is current everywhere.
+            self._u, self._v = self._v, self._u
+            up.u, up.v = up.v, up.u
+            dn.u, dn.v = dn.v, dn.u
+        if check:
+            self.check()
+
+    def check(self) -> None:
+        """Synchronises and raises SpmdError if this rank's kernel hit a bounded-wait timeout."""
+        import torch
+        call("spmdb200_workspace_status", c_p(self._ws.ptr), c_p(torch.cuda.current_stream().cuda_stream))
+
+    def residuals(self) -> np.ndarray:
+        """Global residuals (sum of squared updates) of the last run, identical on every rank."""
+        import torch
+        torch.cuda.current_stream().synchronize()
+        rendezvous()  # every rank's kernel has finished writing its slots
+        out = np.zeros(max(self._nres_last, 1), np.float64)
+        call("spmdb200_jacobi2d_slab_residuals", c_p(self._ws.ptr), ctypes.c_int(self.world),
+             c_i(self._nres_last), out.ctypes.data_as(c_p))
+        return out[:self._nres_last]
+
+    def run_host(self, host_local: np.ndarray, sweeps: int) -> np.ndarray:
+        """End to end on host memory: host_local is this rank's (rows + 2) x pitch
+        slab (pinned for full speed); copied in, `sweeps` sweeps, owned rows
+        copied back into host_local[1:rows+1]."""
+        if host_local.shape != (self.local_rows, self.pitch) or host_local.dtype != np.float32:
+            raise ValueError("host slab must be (rows + 2) x pitch float32")
+        # Only U needs the input: V's owned rows are all written by sweep 0 and
+        # its halo rows by the neighbours before anyone reads them.
+        call("spmdb200_memcpy", c_p(self._u.ptr), host_local.ctypes.data_as(c_p),
+             ctypes.c_size_t(host_local.nbytes), None)
+        self.run(sweeps, check=True)
+        row = self.pitch * 4
+        call("spmdb200_memcpy", c_p(host_local.ctypes.data + row), c_p(self._u.ptr + row),
+             ctypes.c_size_t(self.rows * row), None)
+        return host_local
+
+    def close(self) -> None:
+        import torch
+        torch.cuda.synchronize()
+        rendezvous()  # no peer still writes into our memory or reads our workspace
+        for p in self._opened:
+            call("spmdb200_ipc_close", c_p(p))
+        self._opened = []
+        rendezvous()
+        for b in (self._u, self._v, self._ws):
+            b.close()
+
+
+def e2e_measure(job: SlabJacobi2D, sweeps: int, reps: int = 2) -> dict:
+    """Whole-job end-to-end rate through SlabJacobi2D.run_host with pinned host
+    slabs (H2D + sweeps + D2H timed on every rank, max over ranks)."""
+    import time
+
+    import torch
+    d = _dist()
+    host = torch.empty((job.local_rows, job.pitch), dtype=torch.float32, pin_memory=True)
+    arr = host.numpy()
+    arr[:] = 0.0
+    job.run_host(arr, 2)  # warm-up
+    ts = []
+    for _ in range(reps):
+        rendezvous()
+        t0 = time.perf_counter()
+        job.run_host(arr, sweeps)
+        ts.append(time.perf_counter() - t0)
+    t = torch.tensor([sum(ts) / len(ts)], dtype=torch.float64, device="cuda")
+    if d is not None and job.world > 1:
+        d.all_reduce(t, op=d.ReduceOp.MAX)
+    secs = float(t.item())
+    return {"value": round(job.G * job.cols * sweeps / secs / 1e9, 3), "unit": "Gcell-updates/s",
+            "h2d_bytes_per_step": job.local_rows * job.pitch * 4,
+            "d2h_bytes_per_step": job.rows * job.pitch * 4,
+            "entry": "SlabJacobi2D.run_host (pinned host slab per rank)"}

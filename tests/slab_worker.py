@@ -1,0 +1,57 @@
+"""One rank of the 2-GPU slab parity test (launched by test_gpu_slab.py via torchrun).
+
+Every rank builds the same seeded global grid, runs its row slab on its own
+GPU (halo rows stored into the neighbour over NVLink inside the kernel), and
+rank 0 compares the gathered grid and the all-gathered residuals with the
+single-domain oracle."""
+from __future__ import annotations
+
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+
+def main() -> None:
+    import torch
+    import torch.distributed as dist
+
+    from conftest import jacobi_init, spmd_mod
+
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=120))
+    slab = spmd_mod("slab")
+    rank = dist.get_rank()
+    ok = True
+    for (G, W, sweeps, res_every) in [(514, 1000, 13, 3), (67, 130, 8, 1), (4096, 4096, 20, 10)]:
+        u0 = jacobi_init((G, W), 4)
+        job = slab.SlabJacobi2D(cols=W, G=G, res_every=res_every, init=u0)
+        job.run(sweeps)
+        res = job.residuals()
+        grid = job.gather()
+        job.close()
+        if rank == 0:
+            from oracle import oracle
+            want, wres = oracle.jacobi2d(u0, sweeps, res_every)
+            same = np.array_equal(grid.view(np.uint32), want.view(np.uint32))
+            rel = np.max(np.abs(res - wres) / np.abs(wres)) if wres.size else 0.0
+            print(f"G={G} W={W} sweeps={sweeps}: grid bit-exact={same} residual max rel err={rel:.3g}", flush=True)
+            ok = ok and same and rel <= 1e-12
+    flag = torch.tensor([1 if ok else 0], device="cuda")
+    dist.broadcast(flag, 0)
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0 and bool(flag.item()):
+        print("SLAB PARITY OK", flush=True)
+    sys.exit(0 if bool(flag.item()) else 1)
+
+
+if __name__ == "__main__":
+    main()
