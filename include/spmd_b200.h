@@ -174,6 +174,29 @@ int spmdb200_sum_i32(int32_t *A_base, int32_t *A_aligned, int64_t A_offset, int6
                      int32_t *out_base, int32_t *out_aligned, int64_t out_offset,
                      int64_t N, void *stream);
 
+/* spmd.reduce of every reduction kind (include/spmd/IR/SPMDAttrs.td:74-80):
+ * kind 0 add, 1 mul, 2 max, 3 min, 4 and, 5 or, 6 xor (f32 takes 0-3).
+ * out[] = init (+) A[0] (+) ... (+) A[N-1].  The reference lowers these through
+ * the serial ReduceToSCFForGPU fallback (lib/Conversion/SPMDToGPU/SPMDToGPU.cpp:
+ * 422-477, combine :425-449); here they get the hierarchical shape with a
+ * deterministic grid combine.  i32 kinds and f32 max/min are exact in any
+ * order (max/min follow arith.maximumf/minimumf: NaN in, NaN out; -0 < +0;
+ * i32 max/min are signed; i32 add/mul wrap).  f32 add and mul accumulate in
+ * f64 and round once.  `ws` as for spmdb200_sum_f32
+ * (spmdb200_sum_workspace_bytes(N), 256-byte aligned, zero-filled before its
+ * first use, left zero-filled by every call). */
+int spmdb200_reduce_f32(int kind, float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size,
+                        int64_t A_stride, float *out_base, float *out_aligned, int64_t out_offset, int64_t N,
+                        float init, void *ws, size_t ws_bytes, void *stream);
+int spmdb200_reduce_i32(int kind, int32_t *A_base, int32_t *A_aligned, int64_t A_offset, int64_t A_size,
+                        int64_t A_stride, int32_t *out_base, int32_t *out_aligned, int64_t out_offset, int64_t N,
+                        int32_t init, void *ws, size_t ws_bytes, void *stream);
+
+/* Synchronises the current device and reports whether any reduction launched
+ * since the last call hit a bounded-wait timeout in its shared-memory staging
+ * (SPMDB200_ERR_TIMEOUT; the affected result is invalid) -- clears the flag. */
+int spmdb200_reduction_status(void);
+
 /* out[] += sum(A) with one f32 atomic per block: the exact semantics of the
  * reference's hierarchical_sum_kernel (SPMDToGPU.cpp:397-408), order of the
  * block atomics unspecified. */

@@ -347,6 +347,44 @@ int spmdb200_hierarchical_sum(float *A_base, float *A, int64_t A_off, int64_t A_
   return ok();
 }
 
+static int check_reduce_args(int kind, int max_kind, const void *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                             const void *o, int64_t o_off, int64_t N, void *ws, size_t ws_bytes) {
+  if (kind < 0 || kind > max_kind)
+    return fail(SPMDB200_ERR_INVALID_ARG, "reduction kind %d not in [0, %d]", kind, max_kind);
+  CHECK(check1("A", A, A_off, A_size, A_st, N));
+  if (!o || o_off < 0) return fail(SPMDB200_ERR_INVALID_ARG, "out: null pointer or negative offset");
+  if (!ws || ((uintptr_t)ws & 255u) != 0 || ws_bytes < sum_f32_workspace_bytes(N))
+    return fail(SPMDB200_ERR_WORKSPACE, "workspace must be >= %zu bytes and 256-byte aligned",
+                sum_f32_workspace_bytes(N));
+  return SPMDB200_OK;
+}
+
+int spmdb200_reduce_f32(int kind, float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                        float *o_base, float *o, int64_t o_off, int64_t N, float init, void *ws, size_t ws_bytes,
+                        void *stream) {
+  (void)A_base; (void)o_base;
+  CHECK(check_reduce_args(kind, 3, A, A_off, A_size, A_st, o, o_off, N, ws, ws_bytes));
+  CUDA_TRY(launch_reduce_f32(kind, A ? A + A_off : nullptr, A_st, N, o + o_off, init, ws, (cudaStream_t)stream));
+  return ok();
+}
+
+int spmdb200_reduce_i32(int kind, int32_t *A_base, int32_t *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                        int32_t *o_base, int32_t *o, int64_t o_off, int64_t N, int32_t init, void *ws,
+                        size_t ws_bytes, void *stream) {
+  (void)A_base; (void)o_base;
+  CHECK(check_reduce_args(kind, 6, A, A_off, A_size, A_st, o, o_off, N, ws, ws_bytes));
+  CUDA_TRY(launch_reduce_i32(kind, A ? A + A_off : nullptr, A_st, N, o + o_off, init, ws, (cudaStream_t)stream));
+  return ok();
+}
+
+int spmdb200_reduction_status(void) {
+  CUDA_TRY(cudaDeviceSynchronize());
+  const int f = reduction_timeout_flag(true);
+  if (f < 0) return fail(SPMDB200_ERR_CUDA, "reading the reduction status flag failed");
+  if (f) return fail(SPMDB200_ERR_TIMEOUT, "a staged reduction's bounded wait expired; its result is invalid");
+  return ok();
+}
+
 size_t spmdb200_jacobi_workspace_bytes(void) { return sizeof(JacobiWs); }
 
 int spmdb200_set_wait_budget_ms(int64_t grid_ms, int64_t peer_ms) {

@@ -22,6 +22,14 @@ int sum_f32_grid(int64_t n);
 cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_t s);
 cudaError_t launch_sum_i32(const int32_t *a, int64_t stride, int32_t *out, int64_t n, cudaStream_t s);
 cudaError_t launch_hier_sum_f32(View1 a, float *out, int64_t n, cudaStream_t s);
+// Every spmd.reduce kind (0 add, 1 mul, 2 max, 3 min, 4 and, 5 or, 6 xor):
+// out = init (+) reduce(a); ws = [ticket | pad to 256 B | 8-byte partials].
+cudaError_t launch_reduce_f32(int kind, const float *a, int64_t sa, int64_t n, float *out, float init, void *ws,
+                              cudaStream_t s);
+cudaError_t launch_reduce_i32(int kind, const int32_t *a, int64_t sa, int64_t n, int32_t *out, int32_t init,
+                              void *ws, cudaStream_t s);
+// Device flag set when a bounded wait of a staged reduction expired (-1 on error).
+int reduction_timeout_flag(bool clear);
 
 // ---- 3-point promoted stencil (stencil3.cu) -----------------------------------------
 cudaError_t launch_stencil3(View2 a, View2 b, int64_t n, int64_t m, cudaStream_t s);

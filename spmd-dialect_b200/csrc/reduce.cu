@@ -1,6 +1,7 @@
 // reduce.cu -- library launches of spmd.reduce add (f32 deterministic, i32
 // exact, and the reference's one-atomic-per-block form).
 #include "internal.h"
+#include "reduce_bulk.cuh"
 #include "reduction.cuh"
 
 namespace spmdb200 {
@@ -82,28 +83,159 @@ __global__ void __launch_bounds__(kSumThreads, 8) hier_sum_f32_kernel(const floa
   if (threadIdx.x == 0) atomicAdd(out, __double2float_rn(b));
 }
 
+// ---- shared-memory-staged kernels (unit stride, 16-byte aligned input) --------
+// Set when a bounded wait of a staged reduction expires (read by
+// spmdb200_reduction_status).
+__device__ int g_reduce_timeout;
+
+enum class BulkMode { kF32Det, kI32, kF32Atomic };
+
+template <BulkMode M>
+__global__ void __launch_bounds__(kBulkThreads) sum_bulk_kernel(const void *__restrict__ a, int64_t n, void *out,
+                                                               unsigned *ticket, double *partials) {
+  extern __shared__ __align__(128) unsigned char bulk_raw[];
+  unsigned char *smem =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(bulk_raw) + 127) & ~uintptr_t(127));
+  __shared__ uint64_t full[kBulkStages];
+  __shared__ double shd[32];
+  __shared__ uint32_t shu[32];
+  __shared__ int last, abort_flag;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBulkStages; ++s) mbar_init(&full[s], 1);
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  const int64_t units = n >> 2;  // 16-byte units; the last n % 4 elements are the tail
+  int64_t lo, hi;
+  cta_range(units, lo, hi);
+  const uint4 *base = reinterpret_cast<const uint4 *>(a);
+  if constexpr (M == BulkMode::kI32) {
+    uint32_t acc = 0;
+    const bool ok = bulk_stream(base, lo, hi, smem, full, &abort_flag,
+                                [&](uint4 v) { acc += v.x + v.y + v.z + v.w; });
+    if (!ok && threadIdx.x == 0) atomicExch(&g_reduce_timeout, 1);
+    if (blockIdx.x == gridDim.x - 1) {
+      const int64_t t = (units << 2) + threadIdx.x;
+      if (t < n) acc += (uint32_t) static_cast<const int32_t *>(a)[t];
+    }
+    const uint32_t b = block_sum_u32(acc, shu);
+    if (threadIdx.x == 0 && b != 0u) atomicAdd(static_cast<unsigned *>(out), b);
+  } else {
+    double acc0 = 0.0, acc1 = 0.0;
+    const bool ok = bulk_stream(base, lo, hi, smem, full, &abort_flag, [&](uint4 v) {
+      acc0 = __dadd_rn(acc0, (double)__uint_as_float(v.x));
+      acc1 = __dadd_rn(acc1, (double)__uint_as_float(v.y));
+      acc0 = __dadd_rn(acc0, (double)__uint_as_float(v.z));
+      acc1 = __dadd_rn(acc1, (double)__uint_as_float(v.w));
+    });
+    if (!ok && threadIdx.x == 0) atomicExch(&g_reduce_timeout, 1);
+    if (blockIdx.x == gridDim.x - 1) {
+      const int64_t t = (units << 2) + threadIdx.x;
+      if (t < n) acc0 = __dadd_rn(acc0, (double)static_cast<const float *>(a)[t]);
+    }
+    const double b = block_sum_f64(__dadd_rn(acc0, acc1), shd);
+    if constexpr (M == BulkMode::kF32Atomic) {
+      if (threadIdx.x == 0) atomicAdd(static_cast<float *>(out), __double2float_rn(b));
+    } else {
+      if (threadIdx.x == 0) {
+        partials[blockIdx.x] = b;
+        __threadfence();
+        last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+      }
+      __syncthreads();
+      if (!last) return;
+      __threadfence();
+      double p = 0.0;
+      for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) p = __dadd_rn(p, __ldcg(partials + i));
+      const double tot = block_sum_f64(p, shd);
+      if (threadIdx.x == 0) {
+        float *o = static_cast<float *>(out);
+        *o = __double2float_rn(__dadd_rn((double)*o, tot));
+        *ticket = 0u;
+      }
+    }
+  }
+}
+
+template <BulkMode M>
+static int bulk_grid(int64_t n) {
+  static int cache[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 1;
+  if (cache[dev] == 0) {
+    cudaFuncSetAttribute(sum_bulk_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmem);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sum_bulk_kernel<M>, kBulkThreads, kBulkSmem) !=
+            cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    cache[dev] = per_sm * num_sms(dev);
+  }
+  const int64_t chunks = ((n >> 2) * 16 + kBulkChunk - 1) / kBulkChunk;  // at least one chunk per CTA
+  int64_t g = chunks < 1 ? 1 : chunks;
+  if (g > cache[dev]) g = cache[dev];
+  if (g > kMaxCtas) g = kMaxCtas;
+  return (int)g;
+}
+
+static bool bulk_ok(const void *p, int64_t stride) {
+  return stride == 1 && (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
 static int g_f32_cache[64], g_i32_cache[64], g_hier_cache[64];
 
-int sum_f32_grid(int64_t n) { return reduce_grid(sum_f32_kernel, g_f32_cache, n); }
+int sum_f32_grid(int64_t n) {
+  // The larger of the two paths' grids (both write one partial per block).
+  const int a = reduce_grid(sum_f32_kernel, g_f32_cache, n), b = bulk_grid<BulkMode::kF32Det>(n);
+  return a > b ? a : b;
+}
 
 cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_t s) {
-  const int g = sum_f32_grid(n);
   unsigned *ticket = static_cast<unsigned *>(ws);
   double *partials = reinterpret_cast<double *>(static_cast<char *>(ws) + kSumWsHeader);
-  sum_f32_kernel<<<g, kSumThreads, 0, s>>>(a.p, a.s, n, out, ticket, partials);
+  if (bulk_ok(a.p, a.s)) {
+    sum_bulk_kernel<BulkMode::kF32Det><<<bulk_grid<BulkMode::kF32Det>(n), kBulkThreads, kBulkSmem, s>>>(
+        a.p, n, out, ticket, partials);
+  } else {
+    sum_f32_kernel<<<reduce_grid(sum_f32_kernel, g_f32_cache, n), kSumThreads, 0, s>>>(a.p, a.s, n, out, ticket,
+                                                                                       partials);
+  }
   return cudaGetLastError();
 }
 
 cudaError_t launch_sum_i32(const int32_t *a, int64_t stride, int32_t *out, int64_t n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
-  sum_i32_kernel<<<reduce_grid(sum_i32_kernel, g_i32_cache, n), kSumThreads, 0, s>>>(a, stride, n, out);
+  if (bulk_ok(a, stride))
+    sum_bulk_kernel<BulkMode::kI32><<<bulk_grid<BulkMode::kI32>(n), kBulkThreads, kBulkSmem, s>>>(a, n, out,
+                                                                                                 nullptr, nullptr);
+  else
+    sum_i32_kernel<<<reduce_grid(sum_i32_kernel, g_i32_cache, n), kSumThreads, 0, s>>>(a, stride, n, out);
   return cudaGetLastError();
 }
 
 cudaError_t launch_hier_sum_f32(View1 a, float *out, int64_t n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
-  hier_sum_f32_kernel<<<reduce_grid(hier_sum_f32_kernel, g_hier_cache, n), kSumThreads, 0, s>>>(a.p, a.s, n, out);
+  if (bulk_ok(a.p, a.s))
+    sum_bulk_kernel<BulkMode::kF32Atomic><<<bulk_grid<BulkMode::kF32Atomic>(n), kBulkThreads, kBulkSmem, s>>>(
+        a.p, n, out, nullptr, nullptr);
+  else
+    hier_sum_f32_kernel<<<reduce_grid(hier_sum_f32_kernel, g_hier_cache, n), kSumThreads, 0, s>>>(a.p, a.s, n,
+                                                                                                  out);
   return cudaGetLastError();
 }
 
+}  // namespace spmdb200
+
+namespace spmdb200 {
+int reduction_timeout_flag(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_reduce_timeout, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_reduce_timeout, &zero, sizeof(int));
+  }
+  return v;
+}
 }  // namespace spmdb200

@@ -84,6 +84,28 @@ def hierarchical_sum(a: torch.Tensor, out: torch.Tensor, stream=None) -> torch.T
     return out
 
 
+KINDS = {"add": 0, "mul": 1, "max": 2, "min": 3, "and": 4, "or": 5, "xor": 6}
+
+
+def reduce(kind: str, a: torch.Tensor, init, out: torch.Tensor | None = None, ws: torch.Tensor | None = None,
+           stream=None) -> torch.Tensor:
+    """out[0] = init (+) a[0] (+) ... for an spmd.reduce kind (f32: add/mul/max/min; i32: all seven)."""
+    n = a.shape[0]
+    out = torch.empty(1, dtype=a.dtype, device=a.device) if out is None else out
+    ws = sum_workspace(n, a.device) if ws is None else ws
+    o = c_p(out.data_ptr())
+    common = (*memref(a), o, o, c_i(0), c_i(n))
+    if a.dtype == torch.float32:
+        call("spmdb200_reduce_f32", ctypes.c_int(KINDS[kind]), *common, ctypes.c_float(init), c_p(ws.data_ptr()),
+             ctypes.c_size_t(ws.numel()), _stream(stream))
+    elif a.dtype == torch.int32:
+        call("spmdb200_reduce_i32", ctypes.c_int(KINDS[kind]), *common, ctypes.c_int32(init), c_p(ws.data_ptr()),
+             ctypes.c_size_t(ws.numel()), _stream(stream))
+    else:
+        raise TypeError("reduce takes float32 or int32 tensors")
+    return out
+
+
 def jacobi_workspace(device=None) -> torch.Tensor:
     return torch.zeros(int(lib().spmdb200_jacobi_workspace_bytes()), dtype=torch.uint8, device=device or "cuda")
 

@@ -9,7 +9,8 @@ JSON line with the CUDA-event time per rep and the bandwidth it implies.
     python spmd-dialect_b200/run.py jacobi3d --shape 512x512x512 --sweeps 4
 
 Kernels: ewise, axpy, sum_f32, sum_i32, hierarchical_sum, stencil3, jacobi2d,
-jacobi3d.  No checking happens here (the parity tests compare against the
+jacobi3d, reduce_f32 / reduce_i32 (--kind add|mul|max|min|and|or|xor).  No checking
+happens here (the parity tests compare against the
 oracle); this is for timing and for profiler captures.
 """
 from __future__ import annotations
@@ -27,7 +28,8 @@ sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["ewise", "axpy", "sum_f32", "sum_i32", "hierarchical_sum", "stencil3",
-                                       "jacobi2d", "jacobi3d"])
+                                       "jacobi2d", "jacobi3d", "reduce_f32", "reduce_i32"])
+    ap.add_argument("--kind", default="max", help="reduction kind for reduce_f32 / reduce_i32")
     ap.add_argument("--size", type=int, default=1 << 24)
     ap.add_argument("--shape", default="4096x4096")
     ap.add_argument("--sweeps", type=int, default=100)
@@ -62,6 +64,15 @@ def main() -> None:
         x = torch.randint(0, 100, (a.size,), device=dev, dtype=torch.int32, generator=g)
         o = torch.zeros(1, device=dev, dtype=torch.int32)
         fn = lambda: k.sum_i32(x, o)  # noqa: E731
+        work_bytes = 4 * a.size
+    elif a.kernel in ("reduce_f32", "reduce_i32"):
+        if a.kernel == "reduce_f32":
+            x = torch.rand(a.size, device=dev, generator=g)
+        else:
+            x = torch.randint(-1000, 1000, (a.size,), device=dev, dtype=torch.int32, generator=g)
+        ws = k.sum_workspace(a.size)
+        o = torch.zeros(1, device=dev, dtype=x.dtype)
+        fn = lambda: k.reduce(a.kind, x, 0, o, ws)  # noqa: E731
         work_bytes = 4 * a.size
     elif a.kernel == "stencil3":
         n, m = shape

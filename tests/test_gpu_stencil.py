@@ -145,7 +145,10 @@ def _run_j3(kernels, u0, sweeps, res_every):
 
 
 @pytest.mark.parametrize("shape,sw,re", [((10, 12, 20), 3, 1), ((6, 7, 9), 2, 2), ((3, 4, 5), 1, 1),
-                                         ((33, 17, 130), 5, 1), ((64, 64, 64), 4, 2), ((2, 2, 2), 2, 1)])
+                                         ((33, 17, 130), 5, 1), ((64, 64, 64), 4, 2), ((2, 2, 2), 2, 1),
+                                         # x-contiguous rows of a multiple of 16 bytes: persistent TMA path
+                                         ((33, 17, 132), 5, 1), ((5, 3, 4), 3, 1), ((17, 50, 136), 4, 2),
+                                         ((40, 33, 260), 7, 7), ((1, 1, 4), 2, 1)])
 def test_jacobi3d_matches_oracle(kernels, oracle_mod, shape, sw, re):
     u0 = jacobi_init(shape, 3)
     fin, res = _run_j3(kernels, u0, sw, re)
