@@ -255,7 +255,8 @@ int spmdb200_jacobi2d_host(float *U_base, float *U_aligned, int64_t U_offset, in
  * current by storing its first / last owned row straight into the neighbour's
  * halo row over NVLink each sweep.  up_* / dn_* are the neighbours' U, V and
  * workspace as mapped in this process (spmdb200_ipc_open), NULL at the global
- * top / bottom.  all_ws[q] is rank q's workspace as mapped here (all_ws[rank]
+ * top / bottom; up_rows is the number of rows the neighbour above owns (our
+ * first owned row lands in its local row up_rows + 1).  all_ws[q] is rank q's workspace as mapped here (all_ws[rank]
  * is `ws`); the residual of every residual sweep is all-gathered into each
  * rank's workspace.  The caller must clear every rank's workspace
  * (spmdb200_jacobi_ws_reset) and make all ranks wait for one another before
@@ -267,7 +268,8 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U_aligned, int64_t U_offset, in
                            float *V_base, float *V_aligned, int64_t V_offset, int64_t V_size0, int64_t V_size1,
                            int64_t V_stride0, int64_t V_stride1,
                            int64_t g_first, int64_t G, int64_t sweeps, int64_t res_every, double *res_out,
-                           void *ws, float *up_u, float *up_v, void *up_ws, float *dn_u, float *dn_v, void *dn_ws,
+                           void *ws, float *up_u, float *up_v, void *up_ws, int64_t up_rows,
+                           float *dn_u, float *dn_v, void *dn_ws,
                            int rank, int nranks, void *const *all_ws, void *stream);
 /* Clears the 256-byte header of a Jacobi workspace on `stream`. */
 int spmdb200_jacobi_ws_reset(void *ws, void *stream);

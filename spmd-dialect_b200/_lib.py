@@ -63,8 +63,8 @@ _SIGS = {
     "spmdb200_workspace_status": (ctypes.c_int, [c_p, c_p]),
     "spmdb200_set_wait_budget_ms": (ctypes.c_int, [c_i, c_i]),
     # multi-GPU row slabs
-    "spmdb200_jacobi2d_slab": (ctypes.c_int, D2 + D2 + [c_i, c_i, c_i, c_i, c_p, c_p, c_p, c_p, c_p, c_p, c_p, c_p,
-                                                       ctypes.c_int, ctypes.c_int, c_p, c_p]),
+    "spmdb200_jacobi2d_slab": (ctypes.c_int, D2 + D2 + [c_i, c_i, c_i, c_i, c_p, c_p, c_p, c_p, c_p, c_i, c_p, c_p,
+                                                       c_p, ctypes.c_int, ctypes.c_int, c_p, c_p]),
     "spmdb200_jacobi_ws_reset": (ctypes.c_int, [c_p, c_p]),
     "spmdb200_jacobi2d_slab_residuals": (ctypes.c_int, [c_p, ctypes.c_int, c_i, c_p]),
     "spmdb200_dev_alloc": (ctypes.c_int, [c_sz, ctypes.POINTER(c_p)]),

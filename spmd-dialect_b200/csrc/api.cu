@@ -500,8 +500,8 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
                            int64_t U_s1, float *V_base, float *V, int64_t V_off, int64_t V_n0, int64_t V_n1,
                            int64_t V_s0, int64_t V_s1, int64_t g_first, int64_t G, int64_t sweeps,
                            int64_t res_every, double *res_out, void *ws, float *up_u, float *up_v, void *up_ws,
-                           float *dn_u, float *dn_v, void *dn_ws, int rank, int nranks, void *const *all_ws,
-                           void *stream) {
+                           int64_t up_rows, float *dn_u, float *dn_v, void *dn_ws, int rank, int nranks,
+                           void *const *all_ws, void *stream) {
   (void)U_base; (void)V_base;
   CHECK(check2("U", U, U_off, U_n0, U_n1, U_s0, U_s1));
   CHECK(check2("V", V, V_off, V_n0, V_n1, V_s0, V_s1));
@@ -519,6 +519,9 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
     return fail(SPMDB200_ERR_INVALID_ARG, "neighbour pointers must be given exactly where a neighbour exists");
   if ((up_u && (!up_v || !up_ws)) || (dn_u && (!dn_v || !dn_ws)))
     return fail(SPMDB200_ERR_INVALID_ARG, "incomplete neighbour (U, V, workspace)");
+  if (up_u && (up_rows < 1 || up_rows > g_first))
+    return fail(SPMDB200_ERR_INVALID_ARG, "neighbour above owns %lld rows: must be in [1, %lld]",
+                (long long)up_rows, (long long)g_first);
   if (nranks > 1 && !all_ws) return fail(SPMDB200_ERR_INVALID_ARG, "all_ws is required for nranks > 1");
   if (sweeps < 0 || res_every < 0) return fail(SPMDB200_ERR_INVALID_ARG, "negative sweeps / res_every");
   if (res_every > 0 && sweeps / res_every > kMaxResSlots)
@@ -546,7 +549,7 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   peers.up_v = up_v;
   peers.dn_u = dn_u;
   peers.dn_v = dn_v;
-  peers.up_row = R + 1;  // our first owned row is the bottom halo row of the rank above
+  peers.up_row = up_rows + 1;  // our first owned row is the bottom halo row of the rank above
   peers.dn_row = 0;      // our last owned row is the top halo row of the rank below
   peers.up_flag = up_ws ? &static_cast<JacobiWs *>(up_ws)->from_below : nullptr;
   peers.dn_flag = dn_ws ? &static_cast<JacobiWs *>(dn_ws)->from_above : nullptr;

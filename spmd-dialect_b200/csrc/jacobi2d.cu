@@ -112,6 +112,17 @@ __device__ __forceinline__ bool consumers_any(bool pred) {
   return r != 0;
 }
 
+// Tile index -> (ty, tx).  In slab mode the first and last tile rows (the
+// ones a neighbouring GPU waits for) come first in every sweep, so halo rows
+// are delivered early and a neighbour's edge tiles never wait for the end of
+// this GPU's sweep; the interior rows follow in order.  One GPU: row order.
+__device__ __forceinline__ void tile_coords(int t, int tiles_x, int tiles_y, bool edges_first, int &ty, int &tx) {
+  int row = t / tiles_x;
+  tx = t - row * tiles_x;
+  if (edges_first && tiles_y > 2) row = row == 0 ? 0 : row == 1 ? tiles_y - 1 : row - 1;
+  ty = row;
+}
+
 __device__ __forceinline__ void store4_masked(float *p, int gx0, int w, float4 o) {
   if (gx0 + 3 < w) {
     st_f4(p, o);
@@ -155,6 +166,7 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
   const int T = k.tiles_x * k.tiles_y;
+  const bool edges_first = k.peers.up_flag != nullptr || k.peers.dn_flag != nullptr;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -188,7 +200,8 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
       }
       if (lane == 0) {
         for (int t = blockIdx.x; t < T; t += G) {
-          const int ty = t / k.tiles_x, tx = t - ty * k.tiles_x;
+          int ty, tx;
+          tile_coords(t, k.tiles_x, k.tiles_y, edges_first, ty, tx);
           if (s > 0) {
             const unsigned need = (unsigned)s * (unsigned)k.tiles_x;
             if (ty == 0 && k.peers.up_flag &&
@@ -253,7 +266,8 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
     const bool want = k.res_every > 0 && ((s + 1) % k.res_every == 0);
     bool ok = true;
     for (int t = blockIdx.x; t < T; t += G) {
-      const int ty = t / k.tiles_x, tx = t - ty * k.tiles_x;
+      int ty, tx;
+      tile_coords(t, k.tiles_x, k.tiles_y, edges_first, ty, tx);
       const uint32_t st = it % STAGES, ph = (it / STAGES) & 1u;
       const bool got = mbar_wait_bounded(&tail->full[st], ph, abort);
       if (!__all_sync(0xffffffffu, got)) {  // warp-uniform outcome

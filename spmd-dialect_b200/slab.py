@@ -134,6 +134,7 @@ class SlabJacobi2D:
         torch.cuda.current_stream().synchronize()
         # Map the neighbours' grids and every rank's workspace into this process.
         self._up, self._dn = _Peer(), _Peer()
+        self._up_rows = 0
         self._all_ws = [0] * self.world
         self._opened: list[int] = []
         self._all_ws[self.rank] = self._ws.ptr
@@ -142,6 +143,8 @@ class SlabJacobi2D:
             handles: list = [None] * self.world
             d.all_gather_object(handles, mine)
             up, dn = neighbours(G, self.world, self.rank)
+            if up is not None:
+                self._up_rows = partition(G, self.world, up)[1]
             for q in range(self.world):
                 if q != self.rank:
                     self._all_ws[q] = self._open(handles[q][2])
@@ -198,7 +201,7 @@ class SlabJacobi2D:
         up, dn = self._up, self._dn
         call("spmdb200_jacobi2d_slab", *self._desc(self._u.ptr), *self._desc(self._v.ptr), c_i(self.g_first),
              c_i(self.G), c_i(sweeps), c_i(self.res_every), c_p(0), c_p(self._ws.ptr),
-             c_p(up.u or None), c_p(up.v or None), c_p(up.ws or None),
+             c_p(up.u or None), c_p(up.v or None), c_p(up.ws or None), c_i(self._up_rows),
              c_p(dn.u or None), c_p(dn.v or None), c_p(dn.ws or None),
              ctypes.c_int(self.rank), ctypes.c_int(self.world), self._all_ws_arr, stream)
         self._nres_last = sweeps // self.res_every if self.res_every > 0 else 0

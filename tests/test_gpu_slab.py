@@ -71,7 +71,7 @@ def test_peer_wait_runs_out_and_reports_timeout(kernels):
         # this rank owns global rows [64, 128) of 128: a neighbour above, none below
         st = lib.spmdb200_jacobi2d_slab(*d(u), *d(v), c_i(rows), c_i(2 * rows), c_i(3), c_i(0), None,
                                         c_p(ws.data_ptr()), c_p(fake_u.data_ptr()), c_p(fake_v.data_ptr()),
-                                        c_p(fake_ws.data_ptr()), None, None, None, ctypes.c_int(1),
+                                        c_p(fake_ws.data_ptr()), c_i(rows), None, None, None, ctypes.c_int(1),
                                         ctypes.c_int(2), (c_p * 2)(c_p(fake_ws.data_ptr()), c_p(ws.data_ptr())), s)
         assert st == 0, lib.spmdb200_last_error_message()
         st = lib.spmdb200_workspace_status(c_p(ws.data_ptr()), s)
