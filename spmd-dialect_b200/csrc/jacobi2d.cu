@@ -269,8 +269,7 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
       int ty, tx;
       tile_coords(t, k.tiles_x, k.tiles_y, edges_first, ty, tx);
       const uint32_t st = it % STAGES, ph = (it / STAGES) & 1u;
-      const bool got = mbar_wait_bounded(&tail->full[st], ph, abort);
-      if (!__all_sync(0xffffffffu, got)) {  // warp-uniform outcome
+      if (!mbar_wait_warp(&tail->full[st], ph, abort)) {  // warp-uniform outcome
         if (lane == 0) record_status(k.ws, abort, kDevTimeoutFull);
         ok = false;
         break;

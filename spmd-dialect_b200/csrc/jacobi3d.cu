@@ -309,9 +309,9 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
       const int gx0 = tx * BW3 + 4 * lane;
       const int y0 = ty * BH3 + r0;
       // planes 0 (z0-1) and 1 (z0) of this item
-      bool got = mbar_wait_bounded(&tail->full[pc % ST3], (pc / ST3) & 1u, abort) &&
-                 mbar_wait_bounded(&tail->full[(pc + 1) % ST3], ((pc + 1) / ST3) & 1u, abort);
-      if (!__all_sync(0xffffffffu, got)) {
+      bool got = mbar_wait_warp(&tail->full[pc % ST3], (pc / ST3) & 1u, abort) &&
+                 mbar_wait_warp(&tail->full[(pc + 1) % ST3], ((pc + 1) / ST3) & 1u, abort);
+      if (!got) {
         if (lane == 0) record3(k.ws, abort, kDevTimeoutFull);
         ok = false;
         break;
@@ -328,8 +328,8 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
       }
       for (int j = 1; j <= BZ3; ++j) {
         const uint32_t pz = pc + j, pp = pc + j + 1;  // ring positions of planes z and z+1
-        got = mbar_wait_bounded(&tail->full[pp % ST3], (pp / ST3) & 1u, abort);
-        if (!__all_sync(0xffffffffu, got)) {
+        got = mbar_wait_warp(&tail->full[pp % ST3], (pp / ST3) & 1u, abort);
+        if (!got) {
           if (lane == 0) record3(k.ws, abort, kDevTimeoutFull);
           ok = false;
           break;
