@@ -26,6 +26,7 @@ _SIGS = {
     "stencil_cpu": (None, D2 + D2 + [c_i, c_i]),
     "atomic_sum": (None, D1 + D0 + [c_i]),
     "hierarchical_sum": (None, D1 + D0 + [c_i]),
+    "hierarchical_sum_omp": (None, D1 + D0 + [c_i]),
     "oracle_axpy": (None, [c_f] + D1 + D1 + [c_i]),
     "oracle_sum_f64": (ctypes.c_double, D1 + [c_i]),
     "oracle_sum_i32": (ctypes.c_int32, D1 + [c_i]),
@@ -109,6 +110,13 @@ def atomic_sum(A: np.ndarray, init: float = 0.0) -> np.float32:
 def hierarchical_sum(A: np.ndarray, init: float = 0.0) -> np.float32:
     out = np.array([init], dtype=np.float32)
     lib().hierarchical_sum(*_d1(A), _p(out), _p(out), c_i(0), c_i(A.shape[0]))
+    return out[0]
+
+
+def hierarchical_sum_omp(A: np.ndarray, init: float = 0.0) -> np.float32:
+    """The OpenMP-lowering form (parallel tiles, atomic combine): timing baseline."""
+    out = np.array([init], dtype=np.float32)
+    lib().hierarchical_sum_omp(*_d1(A), _p(out), _p(out), c_i(0), c_i(A.shape[0]))
     return out[0]
 
 

@@ -167,6 +167,30 @@ EXPORT void hierarchical_sum(float *A_base, float *A, int64_t A_off, int64_t A_s
   o[o_off] = acc;
 }
 
+/* The SPMDToOpenMP form of hierarchical_sum (SPMDToOpenMP.cpp:48-118): the
+ * group forall over 256-element tiles becomes an OpenMP static worksharing
+ * loop, each tile reduces serially from 0.0f, and the tile sums meet in one
+ * atomic add -- so the f32 result depends on thread timing.  Used as the
+ * timed CPU baseline; parity checks use the serial hierarchical_sum above. */
+EXPORT void hierarchical_sum_omp(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,
+                                 float *o_base, float *o, int64_t o_off, int64_t N) {
+  (void)A_base; (void)A_size; (void)o_base;
+  const int64_t T = 256;
+  const int64_t ntiles = (N + T - 1) / T;
+  float *out = o + o_off;
+#pragma omp parallel for schedule(static)
+  for (int64_t t = 0; t < ntiles; ++t) {
+    float s = 0.0f;
+    for (int64_t l = 0; l < T; ++l) {
+      int64_t g = t * T + l;
+      float v = (g < N) ? A[A_off + g * A_st] : 0.0f;
+      s = s + v;
+    }
+#pragma omp atomic
+    *out += s;
+  }
+}
+
 /* f64 reference sum (the yardstick the f32 reductions are held to). */
 EXPORT double oracle_sum_f64(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,
                              int64_t N) {
