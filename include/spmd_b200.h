@@ -247,16 +247,17 @@ int spmdb200_jacobi2d_host(float *U_base, float *U_aligned, int64_t U_offset, in
 
 /* ---- Jacobi-2D over row slabs on several GPUs (one process per GPU) ------ */
 /* No reference counterpart: the reference runs on one GPU.  The global grid
- * has G rows; this rank owns global rows [g_first, g_first + R).  U and V are
- * (R + 2) x W local arrays (descriptor sizes (R+2, W), stride1 == 1, 16-byte
- * aligned rows): local row 0 is the halo row above (global g_first - 1),
- * local rows 1..R are owned, local row R + 1 is the halo row below.  Halo rows
- * of U must hold the neighbours' initial rows; the kernel keeps every halo
- * current by storing its first / last owned row straight into the neighbour's
- * halo row over NVLink each sweep.  up_* / dn_* are the neighbours' U, V and
+ * has G rows; this rank owns global rows [g_first, g_first + R), R >= 2.  U
+ * and V are (R + 4) x W local arrays (descriptor sizes (R+4, W), stride1 == 1,
+ * 16-byte aligned rows): local rows 0-1 are the two halo rows above (global
+ * g_first - 2, g_first - 1), rows 2..R+1 are owned, rows R+2 and R+3 are the
+ * halo rows below.  Halo rows of U must hold the neighbours' initial rows; the
+ * kernel keeps every halo current by storing its first / last two owned rows
+ * straight into the neighbour's halo rows over NVLink (two sweeps are fused
+ * per pass, so two rows are exchanged per pass).  up_* / dn_* are the neighbours' U, V and
  * workspace as mapped in this process (spmdb200_ipc_open), NULL at the global
  * top / bottom; up_rows is the number of rows the neighbour above owns (our
- * first owned row lands in its local row up_rows + 1).  all_ws[q] is rank q's workspace as mapped here (all_ws[rank]
+ * first owned rows land in its local rows up_rows + 2 and up_rows + 3).  all_ws[q] is rank q's workspace as mapped here (all_ws[rank]
  * is `ws`); the residual of every residual sweep is all-gathered into each
  * rank's workspace.  The caller must clear every rank's workspace
  * (spmdb200_jacobi_ws_reset) and make all ranks wait for one another before

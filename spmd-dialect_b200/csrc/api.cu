@@ -443,8 +443,7 @@ int spmdb200_jacobi2d(float *U_base, float *U, int64_t U_off, int64_t U_n0, int6
   p.res_out = res_out;
   p.ws = w;
   if (U_s1 == 1 && jacobi2d_tma_ok(p)) {
-    int grid = 0;
-    CUDA_TRY(launch_jacobi2d_persistent(p, SlabPeers{}, s, &grid));
+    CUDA_TRY(run_jacobi2d_persistent(p, SlabPeers{}, s));
   } else {
     CUDA_TRY(launch_jacobi2d_generic(p, U_s1, s));
   }
@@ -507,8 +506,11 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   CHECK(check2("V", V, V_off, V_n0, V_n1, V_s0, V_s1));
   if (U_n0 != V_n0 || U_n1 != V_n1 || U_s0 != V_s0 || U_s1 != V_s1)
     return fail(SPMDB200_ERR_INVALID_ARG, "U and V must have identical sizes and strides");
-  if (U_n0 < 3 || U_n1 < 1) return fail(SPMDB200_ERR_INVALID_ARG, "a slab needs >= 1 owned row plus 2 halo rows");
-  const int64_t R = U_n0 - 2;
+  const int64_t H = kSlabHalo;
+  if (U_n0 < 3 * H || U_n1 < 1)
+    return fail(SPMDB200_ERR_INVALID_ARG, "a slab needs >= %lld owned rows plus %lld halo rows on each side",
+                (long long)H, (long long)H);
+  const int64_t R = U_n0 - 2 * H;
   if (U_s1 != 1) return fail(SPMDB200_ERR_UNSUPPORTED, "slab rows must be contiguous (stride1 == 1)");
   if (g_first < 0 || G < 1 || g_first + R > G)
     return fail(SPMDB200_ERR_INVALID_ARG, "owned rows [%lld, %lld) outside the %lld global rows",
@@ -519,9 +521,9 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
     return fail(SPMDB200_ERR_INVALID_ARG, "neighbour pointers must be given exactly where a neighbour exists");
   if ((up_u && (!up_v || !up_ws)) || (dn_u && (!dn_v || !dn_ws)))
     return fail(SPMDB200_ERR_INVALID_ARG, "incomplete neighbour (U, V, workspace)");
-  if (up_u && (up_rows < 1 || up_rows > g_first))
-    return fail(SPMDB200_ERR_INVALID_ARG, "neighbour above owns %lld rows: must be in [1, %lld]",
-                (long long)up_rows, (long long)g_first);
+  if (up_u && (up_rows < H || up_rows > g_first))
+    return fail(SPMDB200_ERR_INVALID_ARG, "neighbour above owns %lld rows: must be in [%lld, %lld]",
+                (long long)up_rows, (long long)H, (long long)g_first);
   if (nranks > 1 && !all_ws) return fail(SPMDB200_ERR_INVALID_ARG, "all_ws is required for nranks > 1");
   if (sweeps < 0 || res_every < 0) return fail(SPMDB200_ERR_INVALID_ARG, "negative sweeps / res_every");
   if (res_every > 0 && sweeps / res_every > kMaxResSlots)
@@ -534,10 +536,11 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   p.pitch = U_s0;
   p.h_local = U_n0;
   p.w = U_n1;
-  p.row_lo = 1;
-  p.row_hi = R + 1;
-  p.g_row0 = g_first - 1;
+  p.row_lo = H;
+  p.row_hi = R + H;
+  p.g_row0 = g_first - H;
   p.g_rows = G;
+  p.halo = (int)H;
   p.sweeps = sweeps;
   p.res_every = res_every;
   p.res_out = res_out;
@@ -549,8 +552,8 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   peers.up_v = up_v;
   peers.dn_u = dn_u;
   peers.dn_v = dn_v;
-  peers.up_row = up_rows + 1;  // our first owned row is the bottom halo row of the rank above
-  peers.dn_row = 0;      // our last owned row is the top halo row of the rank below
+  peers.up_row = up_rows + H;  // our first owned rows are the bottom halo rows of the rank above
+  peers.dn_row = 0;            // our last owned rows are the top halo rows of the rank below
   peers.up_flag = up_ws ? &static_cast<JacobiWs *>(up_ws)->from_below : nullptr;
   peers.dn_flag = dn_ws ? &static_cast<JacobiWs *>(dn_ws)->from_above : nullptr;
   peers.rank = rank;
@@ -558,8 +561,7 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   for (int q = 0; q < nranks; ++q)
     peers.peer_ws[q] = static_cast<JacobiWs *>(all_ws ? all_ws[q] : (q == rank ? ws : nullptr));
   if (!peers.peer_ws[rank]) peers.peer_ws[rank] = static_cast<JacobiWs *>(ws);
-  int grid = 0;
-  CUDA_TRY(launch_jacobi2d_persistent(p, peers, (cudaStream_t)stream, &grid));
+  CUDA_TRY(run_jacobi2d_persistent(p, peers, (cudaStream_t)stream));
   return ok();
 }
 

@@ -48,7 +48,7 @@ struct JacobiWs {
   unsigned from_below; // halo-tile deliveries received from the rank below
   unsigned ticket;     // last-block ticket of the per-sweep (generic) path
   unsigned pad[59];
-  double partial[2][kMaxCtas];                // per-CTA residual partials, by residual parity
+  double partial[4][kMaxCtas];                // per-CTA residual partials, slot = residual index % 4
   double res_slots[kMaxResSlots][kMaxRanks];  // residual all-gather target (multi-GPU)
 };
 static_assert(offsetof(JacobiWs, partial) == 256, "JacobiWs header must be 256 bytes");
@@ -74,12 +74,19 @@ struct Jacobi2dProblem {
   int64_t sweeps, res_every;
   double *res_out;    // device, [sweeps / res_every]
   JacobiWs *ws;
+  int halo = 0;       // slab mode: halo rows on each side (rows exchanged per neighbour per pass)
 };
 
+// Halo depth of the multi-GPU slab layout: two rows on each side, so a pass
+// may fuse two sweeps.
+constexpr int kSlabHalo = 2;
+
 bool jacobi2d_tma_ok(const Jacobi2dProblem &p);
-// Persistent TMA path (requires jacobi2d_tma_ok).  Returns the launch error.
-cudaError_t launch_jacobi2d_persistent(const Jacobi2dProblem &p, const SlabPeers &peers,
-                                       cudaStream_t s, int *grid_out);
+// Runs p.sweeps sweeps on the persistent TMA path (requires jacobi2d_tma_ok):
+// an even number of two-sweep passes (temporal blocking) followed by 0-3
+// single sweeps, so the result lands in u after an even and in v after an odd
+// number of sweeps.  The workspace header must be clear.  Asynchronous.
+cudaError_t run_jacobi2d_persistent(const Jacobi2dProblem &p, const SlabPeers &peers, cudaStream_t s);
 // Seeded synthetic Jacobi input (counter-based hash of (seed, global row, column)).
 cudaError_t launch_fill_jacobi_input(float *p, int64_t pitch, int64_t rows, int64_t w, int64_t g_row0,
                                      int64_t g_rows, uint64_t seed, cudaStream_t s);

@@ -7,8 +7,9 @@ one halo row up and one down per sweep, and the residual all-gather every
 (spmdb200_jacobi2d_slab): no NCCL call sits between sweeps.
 
 Decomposition: the G x W global grid is cut into contiguous row blocks; rank p
-owns global rows [g_first, g_first + rows) and keeps a (rows + 2) x pitch local
-array whose rows 0 and rows + 1 mirror the neighbours' edge rows.
+owns global rows [g_first, g_first + rows) and keeps a (rows + 4) x pitch local
+array whose first and last HALO = 2 rows mirror the neighbours' edge rows (two
+rows deep, because the kernel fuses two sweeps per pass).
 """
 from __future__ import annotations
 
@@ -18,6 +19,8 @@ from dataclasses import dataclass
 import numpy as np
 
 from ._lib import c_i, c_p, call, lib
+
+HALO = 2  # halo rows on each side of a slab (kSlabHalo in the C library)
 
 
 # ---------------------------------------------------------------- decomposition
@@ -35,11 +38,11 @@ def neighbours(G: int, world: int, rank: int) -> tuple[int | None, int | None]:
     return (rank - 1 if rank > 0 else None), (rank + 1 if rank < world - 1 else None)
 
 
-def local_row_range(G: int, world: int, rank: int) -> tuple[int, int]:
-    """Global rows [lo, hi) a rank's local array mirrors: its block plus one halo
-    row on each side (rows outside [0, G) exist locally but are never read)."""
+def local_row_range(G: int, world: int, rank: int, halo: int = HALO) -> tuple[int, int]:
+    """Global rows [lo, hi) a rank's local array mirrors: its block plus `halo`
+    rows on each side (rows outside [0, G) exist locally but are never read)."""
     g_first, rows = partition(G, world, rank)
-    return g_first - 1, g_first + rows + 1
+    return g_first - halo, g_first + rows + halo
 
 
 def pitch_for(cols: int) -> int:
@@ -115,8 +118,10 @@ class SlabJacobi2D:
             G = rows_per_rank * self.world
         self.G, self.cols, self.res_every = G, cols, res_every
         self.g_first, self.rows = partition(G, self.world, self.rank)
+        if self.rows < HALO:
+            raise ValueError(f"each rank needs >= {HALO} rows (rank {self.rank} has {self.rows})")
         self.pitch = pitch_for(cols)
-        self.local_rows = self.rows + 2
+        self.local_rows = self.rows + 2 * HALO
         nbytes = self.local_rows * self.pitch * 4
         self._u = DeviceBuffer(nbytes)
         self._v = DeviceBuffer(nbytes)
@@ -126,9 +131,9 @@ class SlabJacobi2D:
         stream = c_p(torch.cuda.current_stream().cuda_stream)
         if init is None:
             call("spmdb200_fill_jacobi_input", c_p(self._u.ptr), c_i(self.pitch), c_i(self.local_rows),
-                 c_i(cols), c_i(self.g_first - 1), c_i(G), ctypes.c_uint64(seed), stream)
+                 c_i(cols), c_i(self.g_first - HALO), c_i(G), ctypes.c_uint64(seed), stream)
             call("spmdb200_fill_jacobi_input", c_p(self._v.ptr), c_i(self.pitch), c_i(self.local_rows),
-                 c_i(cols), c_i(self.g_first - 1), c_i(G), ctypes.c_uint64(seed), stream)
+                 c_i(cols), c_i(self.g_first - HALO), c_i(G), ctypes.c_uint64(seed), stream)
         else:
             self.load_global(init)
         torch.cuda.current_stream().synchronize()
@@ -178,7 +183,7 @@ class SlabJacobi2D:
         """This rank's owned rows of the current grid (host copy)."""
         local = np.empty((self.local_rows, self.pitch), np.float32)
         call("spmdb200_memcpy", local.ctypes.data_as(c_p), c_p(self._u.ptr), ctypes.c_size_t(local.nbytes), None)
-        return local[1:self.rows + 1, :self.cols].copy()
+        return local[HALO:HALO + self.rows, :self.cols].copy()
 
     def gather(self) -> np.ndarray | None:
         """The full global grid on rank 0 (None elsewhere)."""
@@ -230,18 +235,18 @@ class SlabJacobi2D:
         return out[:self._nres_last]
 
     def run_host(self, host_local: np.ndarray, sweeps: int) -> np.ndarray:
-        """End to end on host memory: host_local is this rank's (rows + 2) x pitch
+        """End to end on host memory: host_local is this rank's (rows + 4) x pitch
         slab (pinned for full speed); copied in, `sweeps` sweeps, owned rows
-        copied back into host_local[1:rows+1]."""
+        copied back into host_local[HALO:HALO + rows]."""
         if host_local.shape != (self.local_rows, self.pitch) or host_local.dtype != np.float32:
-            raise ValueError("host slab must be (rows + 2) x pitch float32")
+            raise ValueError("host slab must be (rows + 4) x pitch float32")
         # Only U needs the input: V's owned rows are all written by sweep 0 and
         # its halo rows by the neighbours before anyone reads them.
         call("spmdb200_memcpy", c_p(self._u.ptr), host_local.ctypes.data_as(c_p),
              ctypes.c_size_t(host_local.nbytes), None)
         self.run(sweeps, check=True)
         row = self.pitch * 4
-        call("spmdb200_memcpy", c_p(host_local.ctypes.data + row), c_p(self._u.ptr + row),
+        call("spmdb200_memcpy", c_p(host_local.ctypes.data + HALO * row), c_p(self._u.ptr + HALO * row),
              ctypes.c_size_t(self.rows * row), None)
         return host_local
 

@@ -53,7 +53,8 @@ def test_peer_wait_runs_out_and_reports_timeout(kernels):
     lib = L.lib()
     c_i, c_p = ctypes.c_int64, ctypes.c_void_p
     rows, cols = 64, 256
-    u = torch.zeros((rows + 2, cols), device="cuda")
+    H = spmd_mod("slab").HALO
+    u = torch.zeros((rows + 2 * H, cols), device="cuda")
     v = torch.zeros_like(u)
     fake_u, fake_v = torch.zeros_like(u), torch.zeros_like(u)
     nbytes = int(lib.spmdb200_jacobi_workspace_bytes())
@@ -62,7 +63,7 @@ def test_peer_wait_runs_out_and_reports_timeout(kernels):
 
     def d(t):
         p = c_p(t.data_ptr())
-        return (p, p, c_i(0), c_i(rows + 2), c_i(cols), c_i(cols), c_i(1))
+        return (p, p, c_i(0), c_i(rows + 2 * H), c_i(cols), c_i(cols), c_i(1))
 
     s = c_p(torch.cuda.current_stream().cuda_stream)
     assert lib.spmdb200_set_wait_budget_ms(c_i(2000), c_i(300)) == 0

@@ -1,10 +1,12 @@
 """Host logic of the multi-GPU row-slab Jacobi-2D, on CPU ranks (gloo).
 
 * partition / neighbours / local_row_range cover every global row exactly once;
-* the slab protocol (sweep the owned rows of a (rows+2)-row local array, hand
-  the first/last owned row to the neighbours' halo rows, all-gather the
-  residual and sum it in rank order) reproduces the single-domain oracle
-  bit for bit -- the oracle does each rank's sweep, gloo carries the halos;
+* the slab protocol (passes of one or two sweeps over a (rows+4)-row local
+  array -- a two-sweep pass first re-sweeps one halo row on each side --,
+  the first/last two owned rows handed to the neighbours' halo rows after
+  each pass, the residual all-gathered and summed in rank order) reproduces
+  the single-domain oracle bit for bit -- the oracle does each rank's sweeps,
+  gloo carries the halos;
 * a rank that never reaches the rendezvous makes the other rank fail there
   (process-group timeout) instead of proceeding to a launch.
 """
@@ -39,12 +41,19 @@ def test_partition_covers_rows_once():
                 assert rows >= 1
                 seen.extend(range(g0, g0 + rows))
                 lo, hi = slab.local_row_range(G, world, r)
-                assert (lo, hi) == (g0 - 1, g0 + rows + 1)
+                assert (lo, hi) == (g0 - slab.HALO, g0 + rows + slab.HALO)
                 up, dn = slab.neighbours(G, world, r)
                 assert up == (r - 1 if r else None) and dn == (r + 1 if r < world - 1 else None)
             assert seen == list(range(G))
     with pytest.raises(ValueError):
         slab.partition(3, 4, 0)
+
+
+def _pass_plan(sweeps: int) -> list[int]:
+    """Sweeps per pass as the C library schedules them: an even number of
+    two-sweep passes, then the 0-3 sweeps left over one per pass."""
+    fused = (sweeps // 4) * 2
+    return [2] * fused + [1] * (sweeps - 2 * fused)
 
 
 def _slab_worker(rank: int, world: int, port: int, G: int, W: int, sweeps: int, res_every: int, q):
@@ -57,51 +66,63 @@ def _slab_worker(rank: int, world: int, port: int, G: int, W: int, sweeps: int, 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     slab = _m("slab")
+    H = slab.HALO
     u0 = jacobi_init((G, W), 4)
     g0, rows = slab.partition(G, world, rank)
     lo, hi = slab.local_row_range(G, world, rank)
-    u = np.zeros((rows + 2, W), np.float32)
+    u = np.zeros((rows + 2 * H, W), np.float32)
     u[max(lo, 0) - lo:min(hi, G) - lo] = u0[max(lo, 0):min(hi, G)]
     v = np.zeros_like(u)
     up, dn = slab.neighbours(G, world, rank)
     res = []
-    for k in range(1, sweeps + 1):
-        want = res_every > 0 and k % res_every == 0
-        rr = oracle.jacobi2d_rows(u, v, 1, rows + 1, g0 - 1, G, want_res=want)
-        # halo hand-off: first owned row up, last owned row down
+    k = 0
+    for pno, F in enumerate(_pass_plan(sweeps)):
+        # A two-sweep pass first sweeps one halo row beyond each edge (the
+        # second sweep of the owned edge rows reads it), then the owned rows.
+        for f in range(F):
+            k += 1
+            want = res_every > 0 and k % res_every == 0
+            ext = F - 1 - f
+            src, dst = (u, v) if f == 0 else (v, u)
+            oracle.jacobi2d_rows(src, dst, H - ext, H + rows + ext, g0 - H, G)
+            rr = oracle.jacobi2d_rows(src, dst, H, H + rows, g0 - H, G, want_res=True) if want else None
+            if want:
+                mine = 0.0
+                for x in rr:
+                    mine = mine + float(x)
+                slots = [None] * world
+                dist.all_gather_object(slots, mine)
+                tot = 0.0
+                for x in slots:  # rank order, as spmdb200_jacobi2d_slab_residuals sums
+                    tot = tot + x
+                res.append(tot)
+        out = v if F == 1 else u
+        # halo hand-off after each pass: the first H owned rows up, the last H down
         reqs = []
         if up is not None:
-            reqs.append(dist.isend(torch.from_numpy(v[1].copy()), up, tag=2 * k))
-            buf = torch.empty(W)
-            dist.recv(buf, up, tag=2 * k + 1)
-            v[0] = buf.numpy()
+            reqs.append(dist.isend(torch.from_numpy(out[H:2 * H].copy()), up, tag=2 * pno))
+            buf = torch.empty((H, W))
+            dist.recv(buf, up, tag=2 * pno + 1)
+            out[0:H] = buf.numpy()
         if dn is not None:
-            reqs.append(dist.isend(torch.from_numpy(v[rows].copy()), dn, tag=2 * k + 1))
-            buf = torch.empty(W)
-            dist.recv(buf, dn, tag=2 * k)
-            v[rows + 1] = buf.numpy()
+            reqs.append(dist.isend(torch.from_numpy(out[rows:rows + H].copy()), dn, tag=2 * pno + 1))
+            buf = torch.empty((H, W))
+            dist.recv(buf, dn, tag=2 * pno)
+            out[rows + H:rows + 2 * H] = buf.numpy()
         for r in reqs:
             r.wait()
-        if want:
-            mine = 0.0
-            for x in rr:
-                mine = mine + float(x)
-            slots = [None] * world
-            dist.all_gather_object(slots, mine)
-            tot = 0.0
-            for x in slots:  # rank order, as spmdb200_jacobi2d_slab_residuals sums
-                tot = tot + x
-            res.append(tot)
-        u, v = v, u
+        if F == 1:
+            u, v = v, u
     parts = [None] * world
-    dist.all_gather_object(parts, u[1:rows + 1])
+    dist.all_gather_object(parts, u[H:rows + H])
     if rank == 0:
         q.put((np.concatenate(parts, 0), np.array(res)))
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,G,W,sweeps", [(2, 37, 29, 7), (3, 64, 17, 5), (2, 3, 8, 3)])
+@pytest.mark.parametrize("world,G,W,sweeps", [(2, 37, 29, 7), (3, 64, 17, 5), (2, 4, 8, 3), (2, 37, 29, 12),
+                                               (4, 41, 13, 9)])
 def test_slab_protocol_matches_single_domain_oracle(oracle_mod, world, G, W, sweeps):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
