@@ -247,17 +247,18 @@ int spmdb200_jacobi2d_host(float *U_base, float *U_aligned, int64_t U_offset, in
 
 /* ---- Jacobi-2D over row slabs on several GPUs (one process per GPU) ------ */
 /* No reference counterpart: the reference runs on one GPU.  The global grid
- * has G rows; this rank owns global rows [g_first, g_first + R), R >= 2.  U
- * and V are (R + 4) x W local arrays (descriptor sizes (R+4, W), stride1 == 1,
- * 16-byte aligned rows): local rows 0-1 are the two halo rows above (global
- * g_first - 2, g_first - 1), rows 2..R+1 are owned, rows R+2 and R+3 are the
+ * has G rows; this rank owns global rows [g_first, g_first + R), R >= 4.  U
+ * and V are (R + 8) x W local arrays (descriptor sizes (R+8, W), stride1 == 1,
+ * 16-byte aligned rows): local rows 0-3 are the four halo rows above (global
+ * g_first - 4 .. g_first - 1), rows 4..R+3 are owned, rows R+4..R+7 are the
  * halo rows below.  Halo rows of U must hold the neighbours' initial rows; the
- * kernel keeps every halo current by storing its first / last two owned rows
- * straight into the neighbour's halo rows over NVLink (two sweeps are fused
- * per pass, so two rows are exchanged per pass).  up_* / dn_* are the neighbours' U, V and
- * workspace as mapped in this process (spmdb200_ipc_open), NULL at the global
- * top / bottom; up_rows is the number of rows the neighbour above owns (our
- * first owned rows land in its local rows up_rows + 2 and up_rows + 3).  all_ws[q] is rank q's workspace as mapped here (all_ws[rank]
+ * kernel keeps every halo current by storing its first / last four owned rows
+ * straight into the neighbour's halo rows over NVLink (up to four sweeps are
+ * fused per pass, so four rows are exchanged per pass).  up_* / dn_* are the
+ * neighbours' U, V and workspace as mapped in this process (spmdb200_ipc_open),
+ * NULL at the global top / bottom; up_rows is the number of rows the neighbour
+ * above owns (our first owned rows land in its local rows up_rows + 4 ..
+ * up_rows + 7).  all_ws[q] is rank q's workspace as mapped here (all_ws[rank]
  * is `ws`); the residual of every residual sweep is all-gathered into each
  * rank's workspace.  The caller must clear every rank's workspace
  * (spmdb200_jacobi_ws_reset) and make all ranks wait for one another before

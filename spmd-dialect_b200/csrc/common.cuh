@@ -126,6 +126,11 @@ __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy (TMA) accesses of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 // ---- flags --------------------------------------------------------------------
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {

@@ -48,7 +48,7 @@ struct JacobiWs {
   unsigned from_below; // halo-tile deliveries received from the rank below
   unsigned ticket;     // last-block ticket of the per-sweep (generic) path
   unsigned pad[59];
-  double partial[4][kMaxCtas];                // per-CTA residual partials, slot = residual index % 4
+  double partial[8][kMaxCtas];                // per-CTA residual partials, slot = residual index % 8
   double res_slots[kMaxResSlots][kMaxRanks];  // residual all-gather target (multi-GPU)
 };
 static_assert(offsetof(JacobiWs, partial) == 256, "JacobiWs header must be 256 bytes");
@@ -79,13 +79,16 @@ struct Jacobi2dProblem {
 
 // Halo depth of the multi-GPU slab layout: two rows on each side, so a pass
 // may fuse two sweeps.
-constexpr int kSlabHalo = 2;
+constexpr int kSlabHalo = 4;  // rows; the deepest pass advances 4 sweeps
 
 bool jacobi2d_tma_ok(const Jacobi2dProblem &p);
-// Runs p.sweeps sweeps on the persistent TMA path (requires jacobi2d_tma_ok):
-// an even number of two-sweep passes (temporal blocking) followed by 0-3
-// single sweeps, so the result lands in u after an even and in v after an odd
-// number of sweeps.  The workspace header must be clear.  Asynchronous.
+// Passes the persistent path runs for `sweeps` sweeps: plan[0] four-sweep,
+// plan[1] two-sweep and plan[2] single-sweep passes (the first two even).
+void jacobi2d_pass_plan(int64_t sweeps, int64_t plan[3]);
+// Runs p.sweeps sweeps on the persistent TMA path (requires jacobi2d_tma_ok)
+// as jacobi2d_pass_plan lays them out (temporal blocking), so the result
+// lands in u after an even and in v after an odd number of sweeps.  The
+// workspace header must be clear.  Asynchronous.
 cudaError_t run_jacobi2d_persistent(const Jacobi2dProblem &p, const SlabPeers &peers, cudaStream_t s);
 // Seeded synthetic Jacobi input (counter-based hash of (seed, global row, column)).
 cudaError_t launch_fill_jacobi_input(float *p, int64_t pitch, int64_t rows, int64_t w, int64_t g_row0,

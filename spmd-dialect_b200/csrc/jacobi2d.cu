@@ -4,39 +4,48 @@
 //
 // Persistent path (pitch-aligned grids)
 // -------------------------------------
-// One cooperative launch runs many sweeps.  Each CTA = 1 producer warp + 8
-// consumer warps, two CTAs per SM.  The producer stages each tile's
-// footprint -- a box starting F rows above and four columns left of the tile,
-// so the TMA x coordinate stays 16-byte aligned -- into a 3-deep shared-memory
-// ring with cp.async.bulk.tensor.2d, completion tracked by mbarrier expect_tx.
-// Out-of-grid box cells are zero-filled by the TMA unit (the guard of
-// PromoteGroupMemory.cpp:268-292, done in hardware).  Consumer lanes own 4
-// contiguous columns, read north/centre/south as float4 from shared memory,
-// get west/east from neighbouring lanes by shuffle, and store float4.
+// One cooperative launch runs many passes; a pass advances F sweeps
+// (temporal blocking, F = 1, 2 or 4).  Each CTA = 1 producer warp + 8
+// consumer warps, two CTAs per SM.  A tile is BH rows x 120 columns.  The
+// producer stages its footprint -- a (BH + 2F) x 128 box starting F rows above
+// and 4 columns left of the tile, so the TMA x coordinate stays 16-byte
+// aligned -- into a shared-memory ring with cp.async.bulk.tensor.2d,
+// completion tracked by mbarrier expect_tx.  Out-of-grid box cells are
+// zero-filled by the TMA unit (the guard of PromoteGroupMemory.cpp:268-292,
+// done in hardware).
 //
-// Temporal blocking: a pass advances F sweeps.  F = 1 stages a (BH+2) x 136
-// box per 64-row tile and computes one sweep.  F = 2 stages a (BH+4) x 136
-// box per 32-row tile, computes the intermediate sweep on the tile plus a
-// 1-cell ring into a shared-memory buffer, then the second sweep from that
-// buffer: each cell update costs 4 bytes of HBM traffic instead of 8, with
-// bit-identical results (the same operations in the same order, only the
-// intermediate grid never leaves the SM).  The host runs an even number of
-// F = 2 passes and then 0-3 F = 1 sweeps, so the result lands in U after an
-// even and in V after an odd number of sweeps.
+// Consumer lanes own 4 contiguous box columns each (the warp covers all 128),
+// read north/centre/south as float4 from shared memory, get west/east from the
+// neighbouring lanes by shuffle, and write float4.  Sweep k of a pass computes
+// box rows [k, BOXH - k): every sweep the valid region shrinks by one row and
+// one column on each side (lane 0's west and lane 31's east neighbours are
+// simply not valid), and after F sweeps box rows [F, F + BH) x columns
+// [4, 124) -- the tile -- are exact.  Intermediate sweeps ping-pong between an
+// intermediate buffer and the stage itself (S -> I -> S -> I -> global for
+// F = 4); only the last sweep writes HBM.  A pass costs one read and one write
+// of the grid however many sweeps it advances, and every cell value is the
+// same operations in the same order as a sweep-by-sweep run (bit-identical).
+//
+// The host runs an even number of 4-sweep passes, an even number of 2-sweep
+// passes and 0-3 single sweeps, so the result lands in U after an even and in
+// V after an odd number of sweeps.
+//
+// Interior tiles (no fixed boundary cell in the valid region, full height, no
+// row delivered to a neighbour) run straight-line code; other tiles apply the
+// boundary rule and column masks per cell.
 //
 // Passes are separated by a split grid barrier: consumers of a CTA arrive
 // (one red.release.gpu per CTA) after their last store of a pass; only the
-// producer waits for all arrivals before issuing the next pass's loads, so
-// compute never stalls on the barrier itself.  Every wait is bounded
-// (%globaltimer budget); on expiry the CTA records a status word, drains its
-// in-flight TMA loads and exits.
+// producer waits for all arrivals before issuing the next pass's loads.  Every
+// wait is bounded (%globaltimer budget); on expiry the CTA records a status
+// word, drains its in-flight TMA loads and exits.
 //
-// Row slabs across GPUs (SlabPeers, halo = 2 rows): the consumers that write
-// the first (last) two owned rows also store them into the halo rows of the
+// Row slabs across GPUs (SlabPeers, halo = 4 rows): the consumers that write
+// the first (last) four owned rows also store them into the halo rows of the
 // neighbour above (below) over NVLink, then bump that neighbour's delivery
 // counter (one per row and tile) with a release at system scope.  The
 // neighbour's producer acquires the counter before it stages any tile whose
-// footprint reaches into that halo.  The last tile row is kept at least two
+// footprint reaches into that halo.  The last tile row is kept at least four
 // rows tall, so only the first and last tile rows touch a halo -- the same
 // tiles that deliver -- which also orders every halo overwrite after the
 // neighbour's reads of the previous pass.  TMA only ever reads this GPU's own
@@ -48,47 +57,58 @@
 namespace spmdb200 {
 namespace {
 
-constexpr int BW = 128;              // tile columns
-constexpr int XPAD = 4;              // left pad of the footprint box (16 bytes)
-constexpr int BOXW = BW + 2 * XPAD;  // 136 floats = 544 bytes per box row
+constexpr int LW = 128;            // box columns: 32 lanes x 4
+constexpr int XOFF = 4;            // the box starts 4 columns (16 bytes) left of its tile
+constexpr int TW = LW - 2 * XOFF;  // 120 output columns per tile
 constexpr int CWARPS = 8;
 constexpr int THREADS = 32 * (CWARPS + 1);
 constexpr int CONSUMERS = 32 * CWARPS;
+constexpr int kMaxF = 4;
+constexpr int kPartialSlots = 8;  // >= 2 x the residuals one pass can produce
+static_assert(kSlabHalo == kMaxF, "slab halos must cover the deepest pass");
 
-// Tile height and ring depth per fusion depth, chosen by measurement on B200
-// (F = 1: 64 x 3 beat 16/32/40/48/96/128-row tiles and 2- or 4-deep rings).
+// Tile height, ring depth and intermediate buffers per pass depth, chosen by
+// measurement on B200.
 template <int F>
 struct Cfg;
 template <>
 struct Cfg<1> {
-  static constexpr int BH = 64, STAGES = 3;
+  static constexpr int BH = 64, STAGES = 3, IBUFS = 0;
 };
 template <>
 struct Cfg<2> {
-  static constexpr int BH = 32, STAGES = 3;
+  static constexpr int BH = 48, STAGES = 2, IBUFS = 2;
+};
+template <>
+struct Cfg<4> {
+  static constexpr int BH = 40, STAGES = 2, IBUFS = 2;
 };
 template <int F>
 struct Geo {
   static constexpr int BH = Cfg<F>::BH;
   static constexpr int STAGES = Cfg<F>::STAGES;
+  static constexpr int IBUFS = Cfg<F>::IBUFS;
   static constexpr int BOXH = BH + 2 * F;
-  static constexpr int RPW = BH / CWARPS;  // output rows per consumer warp
-  static constexpr int STAGE_BYTES = BOXW * BOXH * 4;
+  static constexpr int RPW = BH / CWARPS;  // final-sweep rows per consumer warp
+  static constexpr int STAGE_BYTES = LW * BOXH * 4;
   static constexpr int STAGE_STRIDE = (STAGE_BYTES + 127) / 128 * 128;
-  static constexpr int IROWS = F == 2 ? BH + 2 : 0;  // intermediate buffer rows
-  static constexpr int IBYTES = IROWS * BOXW * 4;
+  static constexpr int IBYTES = STAGE_STRIDE;
   static_assert(BH % CWARPS == 0, "tile rows must split evenly over the consumer warps");
+  static_assert(BH >= kSlabHalo, "a tile row must hold a whole halo");
+  static_assert(F == 1 || IBUFS >= 1, "multi-sweep passes need an intermediate buffer");
+  static_assert(STAGES <= 4, "SmemTail holds four stages");
 };
 
 struct SmemTail {
   uint64_t full[4];
   uint64_t empty[4];
-  double wsum[2][CWARPS];
+  double wsum[kMaxF][CWARPS];
   int abort;
 };
 template <int F>
 constexpr size_t smem_bytes() {
-  return (size_t)Geo<F>::STAGES * Geo<F>::STAGE_STRIDE + Geo<F>::IBYTES + sizeof(SmemTail) + 128;
+  return (size_t)Geo<F>::STAGES * Geo<F>::STAGE_STRIDE + (size_t)Geo<F>::IBUFS * Geo<F>::IBYTES +
+         sizeof(SmemTail) + 128;
 }
 
 struct J2Kernel {
@@ -170,6 +190,9 @@ __device__ __forceinline__ void tile_rows(const J2Kernel &k, int ty, int &r0, in
   }
 }
 
+__device__ __forceinline__ float4 lds4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ void sts4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+
 __device__ __forceinline__ void store4_masked(float *p, int gx0, int w, float4 o) {
   if (gx0 + 3 < w) {
     st_f4(p, o);
@@ -192,91 +215,6 @@ __device__ __forceinline__ double sq_diff4(float4 a, float4 b, int gx0, int w) {
   if (gx0 + 3 < w) acc = __dadd_rn(acc, sq_diff(a.w, b.w));
   return acc;
 }
-
-// One 5-point update of the 4 cells centred at c (columns gx0..gx0+3 of
-// global row g), MLIR source order ((((c + n) + s) + e) + w) * 0.2f; fixed
-// boundary cells keep their value.
-__device__ __forceinline__ float4 update4(float4 c, float4 n, float4 s, float west, float east, long long g,
-                                          long long g_rows, int gx0, int w) {
-  float4 o;
-  o.x = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.x, n.x), s.x), c.y), west), 0.2f);
-  o.y = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.y, n.y), s.y), c.z), c.x), 0.2f);
-  o.z = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.z, n.z), s.z), c.w), c.y), 0.2f);
-  o.w = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.w, n.w), s.w), east), c.z), 0.2f);
-  if (g <= 0 || g >= g_rows - 1) return c;
-  const int wl = w - 1;
-  if (gx0 == 0) o.x = c.x;
-  if (gx0 == wl) o.x = c.x;
-  if (gx0 + 1 == wl) o.y = c.y;
-  if (gx0 + 2 == wl) o.z = c.z;
-  if (gx0 + 3 == wl) o.w = c.w;
-  return o;
-}
-
-// Scalar 5-point update of one cell (global row g, column gx).
-__device__ __forceinline__ float update1(float c, float n, float s, float e, float wv, long long g,
-                                         long long g_rows, int gx, int w) {
-  if (g <= 0 || g >= g_rows - 1 || gx <= 0 || gx >= w - 1) return c;
-  return __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c, n), s), e), wv), 0.2f);
-}
-
-// Producer-warp residual combine for residual index r: the CTA partials of
-// that sweep in CTA order, lane-strided then a shuffle tree (deterministic).
-// CTA 0 combines the residuals of pass p-1 early in pass p, while other CTAs
-// may already be writing the partials of pass p; with up to two residuals per
-// pass, four slots (index % 4) keep those apart.
-__device__ __forceinline__ void combine_residual(const J2Kernel &k, int r, int lane) {
-  double p = 0.0;
-  for (int i = lane; i < (int)gridDim.x; i += 32) p = __dadd_rn(p, __ldcg(&k.ws->partial[r & 3][i]));
-  p = warp_sum_f64(p);
-  if (lane == 0) {
-    if (k.res_out) k.res_out[r] = p;
-    if (k.peers.peer_ws[0] && r < kMaxResSlots) {  // slab mode: all-gather into every rank's slots
-      for (int q = 0; q < k.peers.nranks; ++q)
-        if (k.peers.peer_ws[q]) k.peers.peer_ws[q]->res_slots[r][k.peers.rank] = p;
-      __threadfence_system();
-    }
-  }
-}
-
-// Residual indices produced by pass p (global sweep numbering): -1 if none.
-template <int F>
-__device__ __forceinline__ void pass_residuals(const J2Kernel &k, int p, int &r_a, int &r_b) {
-  r_a = r_b = -1;
-  if (k.res_every <= 0) return;
-  const int s0 = k.sweep_base + F * p;  // first sweep of the pass (0-based, global)
-  if ((s0 + 1) % k.res_every == 0) r_a = (s0 + 1) / k.res_every - 1;
-  if (F == 2 && (s0 + 2) % k.res_every == 0) r_b = (s0 + 2) / k.res_every - 1;
-}
-
-// Halo deliveries of the owned rows a warp just wrote: stores into the
-// neighbours' halo rows happen with the rows; this bumps the counters.
-__device__ __forceinline__ void signal_deliveries(const J2Kernel &k, int n_up, int n_dn) {
-  if (n_up | n_dn) __threadfence_system();
-  if (n_up) red_release_sys_add(k.peers.up_flag, (unsigned)n_up);
-  if (n_dn) red_release_sys_add(k.peers.dn_flag, (unsigned)n_dn);
-}
-
-// ---------------------------------------------------------------------------
-// Interior fast path.  A tile whose computed region (the output rows and
-// columns, widened by F-1 for the intermediate ring) holds no fixed boundary
-// cell and no row delivered to a neighbour runs straight-line code: no
-// boundary tests, no masks, no peer stores.  The arithmetic is the same
-// expression as update4, so results are bit-identical to the general path.
-// Lanes 0 and 31 take their west/east value from the box pad column (exo);
-// all other lanes load the same address as lane 31, a broadcast.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ float4 lds4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
-
-__device__ __forceinline__ float4 stencil4(float4 c, float4 n, float4 s, float west, float east) {
-  float4 o;
-  o.x = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.x, n.x), s.x), c.y), west), 0.2f);
-  o.y = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.y, n.y), s.y), c.z), c.x), 0.2f);
-  o.z = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.z, n.z), s.z), c.w), c.y), 0.2f);
-  o.w = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.w, n.w), s.w), east), c.z), 0.2f);
-  return o;
-}
-
 __device__ __forceinline__ double acc_sq4(double acc, float4 a, float4 b) {
   double d = __dsub_rn((double)a.x, (double)b.x);
   acc = __fma_rn(d, d, acc);
@@ -288,108 +226,204 @@ __device__ __forceinline__ double acc_sq4(double acc, float4 a, float4 b) {
   return __fma_rn(d, d, acc);
 }
 
-struct LaneCols {
-  int sc;      // first of this lane's 4 columns in a box/buffer row
-  int exo;     // pad column: x0-1 for lane 0, x0+BW for the others
-  int faro;    // one further out: x0-2 for lane 0, x0+BW+1 for the others
-  bool l0, l31;
+// The 5-point update of 4 cells centred at c, MLIR source order
+// ((((c + n) + s) + e) + w) * 0.2f.
+__device__ __forceinline__ float4 stencil4(float4 c, float4 n, float4 s, float west, float east) {
+  float4 o;
+  o.x = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.x, n.x), s.x), c.y), west), 0.2f);
+  o.y = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.y, n.y), s.y), c.z), c.x), 0.2f);
+  o.z = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.z, n.z), s.z), c.w), c.y), 0.2f);
+  o.w = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c.w, n.w), s.w), east), c.z), 0.2f);
+  return o;
+}
+
+// The same update for cells of global row g, columns gx0..gx0+3: fixed
+// boundary cells (and cells outside the grid) keep their value.
+__device__ __forceinline__ float4 update4(float4 c, float4 n, float4 s, float west, float east, long long g,
+                                          long long g_rows, int gx0, int w) {
+  float4 o = stencil4(c, n, s, west, east);
+  if (g <= 0 || g >= g_rows - 1) return c;
+  const int wl = w - 1;
+  if (gx0 <= 0 || gx0 >= wl) o.x = c.x;
+  if (gx0 + 1 <= 0 || gx0 + 1 >= wl) o.y = c.y;
+  if (gx0 + 2 <= 0 || gx0 + 2 >= wl) o.z = c.z;
+  if (gx0 + 3 <= 0 || gx0 + 3 >= wl) o.w = c.w;
+  return o;
+}
+
+// ---------------------------------------------------------------------------
+// Straight-line rows of one sweep (interior tiles).  Rows [b0, b0 + ROWS) of
+// the box from `in` into `out` (same box layout) or, for the last sweep, into
+// global memory at dp (lanes 1..30 hold the tile's 120 columns).  RES adds the
+// squared updates of owned cells (box rows [own_lo, own_hi), lanes 1..30).
+// ---------------------------------------------------------------------------
+template <int ROWS, bool TO_GLOBAL, bool RES>
+__device__ __forceinline__ void rows_fast(const float *in, float *out, int b0, int c4, float *dp, long long pitch,
+                                          bool out_lane, int own_lo, int own_hi, double &acc) {
+  const float *p = in + (b0 - 1) * LW + c4;
+  float4 n = lds4(p);
+  float4 c = lds4(p + LW);
+#pragma unroll
+  for (int q = 0; q < ROWS; ++q) {
+    const float4 s = lds4(p + (q + 2) * LW);
+    const float wv = __shfl_up_sync(0xffffffffu, c.w, 1);
+    const float ev = __shfl_down_sync(0xffffffffu, c.x, 1);
+    const float4 o = stencil4(c, n, s, wv, ev);
+    if (TO_GLOBAL) {
+      if (out_lane) *reinterpret_cast<float4 *>(dp) = o;
+      dp += pitch;
+      if (RES && out_lane) acc = acc_sq4(acc, o, c);
+    } else {
+      sts4(out + (b0 + q) * LW + c4, o);
+      if (RES && out_lane && b0 + q >= own_lo && b0 + q < own_hi) acc = acc_sq4(acc, o, c);
+    }
+    n = c;
+    c = s;
+  }
+}
+
+// Per-tile context of the general (boundary) rows.
+struct TileCtx {
+  long long g_box0;  // global row of box row 0
+  int l_box0;        // local row of box row 0
+  int r1;            // end of the tile's owned local rows
+  int gx0;           // global column of this lane's first cell
+  bool out_lane;     // lanes 1..30
 };
 
-// ROWS output rows from a row-major buffer `in` (row stride BOXW) whose row
-// `first` holds the north neighbours of the first output row.  Writes to dp
-// (advancing by pitch); RES adds the squared updates to acc.
-template <int ROWS, bool RES>
-__device__ __forceinline__ void sweep_rows_fast(const float *in, int first, float *dp, long long pitch,
-                                                const LaneCols &lc, double &acc) {
-  const float *row = in + first * BOXW;
-  float4 n = lds4(row + lc.sc);
-  float4 c = lds4(row + BOXW + lc.sc);
-  float exc = row[BOXW + lc.exo];
-#pragma unroll
-  for (int q = 0; q < ROWS; ++q) {
-    const float *srow = row + (q + 2) * BOXW;
-    const float4 s = lds4(srow + lc.sc);
-    const float exs = srow[lc.exo];
-    const float wu = __shfl_up_sync(0xffffffffu, c.w, 1);
-    const float ed = __shfl_down_sync(0xffffffffu, c.x, 1);
-    const float4 o = stencil4(c, n, s, lc.l0 ? exc : wu, lc.l31 ? exc : ed);
-    *reinterpret_cast<float4 *>(dp) = o;
-    dp += pitch;
-    if (RES) acc = acc_sq4(acc, o, c);
-    n = c;
-    c = s;
-    exc = exs;
+// General rows [b_lo, b_hi) of one sweep: the boundary rule per cell, column
+// masks, owned-row limits; the last sweep also stores the rows a neighbour
+// needs into its halo (peer memory) and counts them.
+template <bool TO_GLOBAL>
+__device__ __noinline__ void rows_general(const J2Kernel &k, const float *in, float *out, int b_lo, int b_hi,
+                                          int c4, const TileCtx &t, int own_lo, int own_hi, bool res,
+                                          double &acc, float *dst, float *up_dst, float *dn_dst, int &n_up,
+                                          int &n_dn) {
+  for (int b = b_lo; b < b_hi; ++b) {
+    const float4 n = lds4(in + (b - 1) * LW + c4);
+    const float4 c = lds4(in + b * LW + c4);
+    const float4 s = lds4(in + (b + 1) * LW + c4);
+    const float wv = __shfl_up_sync(0xffffffffu, c.w, 1);
+    const float ev = __shfl_down_sync(0xffffffffu, c.x, 1);
+    const float4 o = update4(c, n, s, wv, ev, t.g_box0 + b, k.g_rows, t.gx0, k.w);
+    const int L = t.l_box0 + b;
+    const bool owned = b >= own_lo && b < own_hi && L < t.r1;
+    if (!TO_GLOBAL) {
+      sts4(out + b * LW + c4, o);
+    } else if (owned) {
+      if (t.out_lane && t.gx0 < k.w) store4_masked(dst + (long long)L * k.pitch + t.gx0, t.gx0, k.w, o);
+      if (up_dst && L < k.row_lo + k.halo) {
+        if (t.out_lane && t.gx0 < k.w)
+          store4_masked(up_dst + (k.peers.up_row + (L - k.row_lo)) * k.pitch + t.gx0, t.gx0, k.w, o);
+        ++n_up;
+      }
+      if (dn_dst && L >= k.row_hi - k.halo) {
+        if (t.out_lane && t.gx0 < k.w)
+          store4_masked(dn_dst + (k.peers.dn_row + (L - (k.row_hi - k.halo))) * k.pitch + t.gx0, t.gx0, k.w, o);
+        ++n_dn;
+      }
+    }
+    if (res && owned && t.out_lane) acc = __dadd_rn(acc, sq_diff4(o, c, t.gx0, k.w));
   }
 }
 
-// Phase 1 of a two-sweep tile: intermediate rows [a, a + ROWS) (row i from
-// box rows i .. i+2) into ibuf, plus the ring cells x0-1 (lane 0) and x0+BW
-// (lane 31), each from the same operands in the same order as update1.
-template <int ROWS>
-__device__ __forceinline__ void intermediate_rows_fast(const float *S, float *ibuf, int a, const LaneCols &lc) {
-  const float *row = S + a * BOXW;
-  float4 n = lds4(row + lc.sc);
-  float4 c = lds4(row + BOXW + lc.sc);
-  float exn = row[lc.exo];
-  float exc = row[BOXW + lc.exo];
-#pragma unroll
-  for (int q = 0; q < ROWS; ++q) {
-    const float *crow = row + (q + 1) * BOXW;
-    const float4 s = lds4(crow + BOXW + lc.sc);
-    const float exs = crow[BOXW + lc.exo];
-    const float far = crow[lc.faro];
-    const float wu = __shfl_up_sync(0xffffffffu, c.w, 1);
-    const float ed = __shfl_down_sync(0xffffffffu, c.x, 1);
-    float *irow = ibuf + (a + q) * BOXW;
-    *reinterpret_cast<float4 *>(irow + lc.sc) = stencil4(c, n, s, lc.l0 ? exc : wu, lc.l31 ? exc : ed);
-    const float re = lc.l0 ? c.x : far, rw = lc.l0 ? far : c.w;
-    const float ring = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(exc, exn), exs), re), rw), 0.2f);
-    if (lc.l0 | lc.l31) irow[lc.exo] = ring;
-    n = c;
-    c = s;
-    exn = exc;
-    exc = exs;
+// Sweep K (1..F) of a pass for consumer warp cw: the warp's share of box rows
+// [K, BOXH - K) -- contiguous, split as evenly as possible (the final sweep:
+// RPW rows each) -- from `in` into `out` or, for K == F, global memory.
+template <int F, int K>
+__device__ __forceinline__ void sweep_rows(const J2Kernel &k, bool fast, const float *in, float *out, int cw,
+                                           int c4, const TileCtx &t, float *dst, long long out_row0, bool res,
+                                           double &acc, float *up_dst, float *dn_dst, int &n_up, int &n_dn) {
+  using Gm = Geo<F>;
+  constexpr int own_lo = F, own_hi = F + Gm::BH;
+  if constexpr (K == F) {
+    const int b0 = F + cw * Gm::RPW;
+    if (fast) {
+      float *dp = dst + (out_row0 + cw * Gm::RPW) * k.pitch + t.gx0;
+      if (res)
+        rows_fast<Gm::RPW, true, true>(in, nullptr, b0, c4, dp, k.pitch, t.out_lane, own_lo, own_hi, acc);
+      else
+        rows_fast<Gm::RPW, true, false>(in, nullptr, b0, c4, dp, k.pitch, t.out_lane, own_lo, own_hi, acc);
+    } else {
+      rows_general<true>(k, in, nullptr, b0, b0 + Gm::RPW, c4, t, own_lo, own_hi, res, acc, dst, up_dst, dn_dst,
+                         n_up, n_dn);
+    }
+  } else {
+    constexpr int N = Gm::BOXH - 2 * K;
+    constexpr int B = N / CWARPS, X = N % CWARPS;
+    const int b0 = K + cw * B + (cw < X ? cw : X);
+    if (fast) {
+      if (cw < X) {
+        if (res)
+          rows_fast<B + 1, false, true>(in, out, b0, c4, nullptr, 0, t.out_lane, own_lo, own_hi, acc);
+        else
+          rows_fast<B + 1, false, false>(in, out, b0, c4, nullptr, 0, t.out_lane, own_lo, own_hi, acc);
+      } else {
+        if (res)
+          rows_fast<B, false, true>(in, out, b0, c4, nullptr, 0, t.out_lane, own_lo, own_hi, acc);
+        else
+          rows_fast<B, false, false>(in, out, b0, c4, nullptr, 0, t.out_lane, own_lo, own_hi, acc);
+      }
+    } else {
+      int dummy_up = 0, dummy_dn = 0;
+      rows_general<false>(k, in, out, b0, b0 + B + (cw < X ? 1 : 0), c4, t, own_lo, own_hi, res, acc, nullptr,
+                          nullptr, nullptr, dummy_up, dummy_dn);
+    }
   }
 }
 
-// Phase 2 of a two-sweep tile: RPW output rows of this warp from ibuf.  RA:
-// residual of the first sweep (intermediate minus input, input from the
-// staged box), RB: of the second (output minus intermediate).
-template <int RPW, bool RA, bool RB>
-__device__ __forceinline__ void second_rows_fast(const float *S, const float *ibuf, int j0, float *dp,
-                                                 long long pitch, const LaneCols &lc, double &acc_a,
-                                                 double &acc_b) {
-  const float *row = ibuf + j0 * BOXW;
-  float4 n = lds4(row + lc.sc);
-  float4 c = lds4(row + BOXW + lc.sc);
-  float exc = row[BOXW + lc.exo];
-#pragma unroll
-  for (int q = 0; q < RPW; ++q) {
-    const float *srow = row + (q + 2) * BOXW;
-    const float4 s = lds4(srow + lc.sc);
-    const float exs = srow[lc.exo];
-    const float wu = __shfl_up_sync(0xffffffffu, c.w, 1);
-    const float ed = __shfl_down_sync(0xffffffffu, c.x, 1);
-    const float4 o = stencil4(c, n, s, lc.l0 ? exc : wu, lc.l31 ? exc : ed);
-    *reinterpret_cast<float4 *>(dp) = o;
-    dp += pitch;
-    if (RA) acc_a = acc_sq4(acc_a, c, lds4(S + (j0 + q + 2) * BOXW + lc.sc));
-    if (RB) acc_b = acc_sq4(acc_b, o, c);
-    n = c;
-    c = s;
-    exc = exs;
-  }
-}
-
-// True when the tile's computed region -- local rows [r0-(F-1), r1+(F-1)),
-// columns [x0-(F-1), x0+BW+(F-1)) -- is all interior cells, the tile is full
-// height, and none of its output rows is delivered to a neighbour.
+// True when the union of the pass's valid regions -- local rows
+// [r0-F+1, r1+F-1), columns [x0-3, x0+123) -- is all interior cells, the tile
+// is full height, and none of its rows is delivered to a neighbour.
 template <int F>
-__device__ __forceinline__ bool tile_is_interior(const J2Kernel &k, int r0, int r1, int tx) {
-  const long long g0 = k.g_row0 + r0 - (F - 1), g1 = k.g_row0 + r1 - 1 + (F - 1);
-  const int c0 = tx * BW - (F - 1), c1 = tx * BW + BW - 1 + (F - 1);
-  return r1 - r0 == Geo<F>::BH && g0 >= 1 && g1 <= k.g_rows - 2 && c0 >= 1 && c1 <= k.w - 2 &&
-         r0 >= k.row_lo + k.halo && r1 <= k.row_hi - k.halo;
+__device__ __forceinline__ bool tile_is_interior(const J2Kernel &k, int r0, int r1, int x0) {
+  return r1 - r0 == Geo<F>::BH && k.g_row0 + r0 - F + 1 >= 1 && k.g_row0 + r1 + F - 2 <= k.g_rows - 2 &&
+         x0 >= XOFF && x0 + TW + XOFF <= k.w && r0 >= k.row_lo + k.halo && r1 <= k.row_hi - k.halo;
+}
+
+// Producer-warp residual combine for residual index r: the CTA partials of
+// that sweep in CTA order, lane-strided then a shuffle tree (deterministic).
+// CTA 0 combines the residuals of pass p-1 early in pass p, while other CTAs
+// may already be writing the partials of pass p; with up to four residuals
+// per pass, eight slots (index % 8) keep those apart.
+__device__ __forceinline__ void combine_residual(const J2Kernel &k, int r, int lane) {
+  double p = 0.0;
+  for (int i = lane; i < (int)gridDim.x; i += 32)
+    p = __dadd_rn(p, __ldcg(&k.ws->partial[r % kPartialSlots][i]));
+  p = warp_sum_f64(p);
+  if (lane == 0) {
+    if (k.res_out) k.res_out[r] = p;
+    if (k.peers.peer_ws[0] && r < kMaxResSlots) {  // slab mode: all-gather into every rank's slots
+      for (int q = 0; q < k.peers.nranks; ++q)
+        if (k.peers.peer_ws[q]) k.peers.peer_ws[q]->res_slots[r][k.peers.rank] = p;
+      __threadfence_system();
+    }
+  }
+}
+
+// Residual index of sweep K (1-based within the pass) of pass p, or -1.
+template <int F>
+__device__ __forceinline__ int sweep_residual(const J2Kernel &k, int p, int K) {
+  if (k.res_every <= 0) return -1;
+  const int s = k.sweep_base + F * p + K;  // global 1-based sweep number
+  return s % k.res_every == 0 ? s / k.res_every - 1 : -1;
+}
+
+template <int F>
+__device__ __forceinline__ void combine_pass(const J2Kernel &k, int p, int lane) {
+#pragma unroll
+  for (int K = 1; K <= F; ++K) {
+    const int r = sweep_residual<F>(k, p, K);
+    if (r >= 0) combine_residual(k, r, lane);
+  }
+}
+
+// Halo deliveries of the owned rows a warp just wrote: stores into the
+// neighbours' halo rows happen with the rows; this bumps the counters.
+__device__ __forceinline__ void signal_deliveries(const J2Kernel &k, int n_up, int n_dn) {
+  if (n_up | n_dn) __threadfence_system();
+  if (n_up) red_release_sys_add(k.peers.up_flag, (unsigned)n_up);
+  if (n_dn) red_release_sys_add(k.peers.dn_flag, (unsigned)n_dn);
 }
 
 template <int F>
@@ -398,12 +432,13 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
     const __grid_constant__ J2Kernel k) {
   using Gm = Geo<F>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  unsigned char *smem = reinterpret_cast<unsigned char *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  float *ibuf = reinterpret_cast<float *>(smem + (size_t)Gm::STAGES * Gm::STAGE_STRIDE);  // F == 2 only
-  SmemTail *tail = reinterpret_cast<SmemTail *>(smem + (size_t)Gm::STAGES * Gm::STAGE_STRIDE + Gm::IBYTES);
+  // Aligned by pointer arithmetic on the shared array itself, so the compiler
+  // keeps shared-space addressing (LDS/STS) for everything derived from it.
+  unsigned char *smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  float *ibase = reinterpret_cast<float *>(smem + (size_t)Gm::STAGES * Gm::STAGE_STRIDE);
+  SmemTail *tail = reinterpret_cast<SmemTail *>(smem + (size_t)Gm::STAGES * Gm::STAGE_STRIDE +
+                                                (size_t)Gm::IBUFS * Gm::IBYTES);
   volatile int *abort = &tail->abort;
-  static_assert(Gm::STAGES <= 4, "SmemTail holds four stages");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
@@ -439,12 +474,7 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
-        if (blockIdx.x == 0) {
-          int ra, rb;
-          pass_residuals<F>(k, p - 1, ra, rb);
-          if (ra >= 0) combine_residual(k, ra, lane);
-          if (rb >= 0) combine_residual(k, rb, lane);
-        }
+        if (blockIdx.x == 0) combine_pass<F>(k, p - 1, lane);
       }
       if (lane == 0) {
         // Deliveries each neighbour has made once it finished pass p-1 (this
@@ -477,7 +507,7 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
             break;
           }
           mbar_arrive_expect_tx(&tail->full[st], Gm::STAGE_BYTES);
-          tma_load_2d(smem + (size_t)st * Gm::STAGE_STRIDE, src, &tail->full[st], tx * BW - XPAD, r0 - F);
+          tma_load_2d(smem + (size_t)st * Gm::STAGE_STRIDE, src, &tail->full[st], tx * TW - XOFF, r0 - F);
           ++it;
         }
       }
@@ -485,19 +515,16 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
       it = __shfl_sync(0xffffffffu, it, 0);
     }
     if (ok && blockIdx.x == 0 && k.passes > 0) {
-      int ra, rb;
-      pass_residuals<F>(k, k.passes - 1, ra, rb);
-      if (ra >= 0 || rb >= 0) {
+      bool any = false;
+      for (int K = 1; K <= F; ++K) any |= sweep_residual<F>(k, k.passes - 1, K) >= 0;
+      if (any) {
         if (lane == 0 && !wait_counter(&k.ws->barrier, (unsigned)k.passes * (unsigned)G, false, abort,
                                        k.grid_budget_ns, k.ws)) {
           record_status(k.ws, abort, kDevTimeoutGridBarrier);
           ok = false;
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (ok) {
-          if (ra >= 0) combine_residual(k, ra, lane);
-          if (rb >= 0) combine_residual(k, rb, lane);
-        }
+        if (ok) combine_pass<F>(k, k.passes - 1, lane);
       }
     }
     if (!ok && lane == 0) {
@@ -515,26 +542,18 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
 
   // ------------------------------ consumer warps ------------------------------
   const int cw = warp;
-  const int j0 = cw * Gm::RPW;  // this warp's first output row within a tile
-  const int sc = XPAD + 4 * lane;
-  LaneCols lc;
-  lc.sc = sc;
-  lc.l0 = lane == 0;
-  lc.l31 = lane == 31;
-  lc.exo = lc.l0 ? XPAD - 1 : XPAD + BW;
-  lc.faro = lc.l0 ? XPAD - 2 : XPAD + BW + 1;
-  // Intermediate rows of a two-sweep tile, contiguous per warp: IROWS split
-  // as evenly as possible (the first IX warps take one more).
-  constexpr int IB = F == 2 ? Gm::IROWS / CWARPS : 0, IX = F == 2 ? Gm::IROWS % CWARPS : 0;
-  const int ia = cw * IB + (cw < IX ? cw : IX);
+  const int c4 = 4 * lane;  // this lane's first box column
   uint32_t it = 0;
-  double acc_a = 0.0, acc_b = 0.0;
+  double acc[F];
+#pragma unroll
+  for (int K = 0; K < F; ++K) acc[K] = 0.0;
   for (int p = 0; p < k.passes; ++p) {
     float *dst = (p & 1) ? k.u : k.v;
     float *up_dst = (p & 1) ? k.peers.up_u : k.peers.up_v;
     float *dn_dst = (p & 1) ? k.peers.dn_u : k.peers.dn_v;
-    int ra, rb;
-    pass_residuals<F>(k, p, ra, rb);
+    int rk[F];
+#pragma unroll
+    for (int K = 0; K < F; ++K) rk[K] = sweep_residual<F>(k, p, K + 1);
     bool ok = true;
     for (int t = blockIdx.x; t < T; t += G) {
       int ty, tx, r0, r1;
@@ -549,131 +568,40 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
           break;
         }
       }
-      const float *S = reinterpret_cast<const float *>(smem + (size_t)st * Gm::STAGE_STRIDE);
-      const int gx0 = tx * BW + 4 * lane;
+      float *S = reinterpret_cast<float *>(smem + (size_t)st * Gm::STAGE_STRIDE);
+      float *I = ibase + (Gm::IBUFS == 2 ? (it & 1u) : 0u) * (Gm::IBYTES / 4);
+      const int x0 = tx * TW;
+      const bool fast = tile_is_interior<F>(k, r0, r1, x0);
+      TileCtx tc;
+      tc.g_box0 = k.g_row0 + r0 - F;
+      tc.l_box0 = r0 - F;
+      tc.r1 = r1;
+      tc.gx0 = x0 - XOFF + c4;
+      tc.out_lane = lane >= 1 && lane <= 30;
       int n_up = 0, n_dn = 0;
 
-      // Reads a row of 4 cells plus the west/east neighbours of the row `rowp`.
-      auto edges = [&](const float *rowp, float4 c, float &west, float &east) {
-        west = __shfl_up_sync(0xffffffffu, c.w, 1);
-        east = __shfl_down_sync(0xffffffffu, c.x, 1);
-        if (lane == 0) west = rowp[XPAD - 1];
-        if (lane == 31) east = rowp[XPAD + BW];
-      };
-      // Stores an output row (and its halo copies in slab mode).
-      auto emit = [&](int L, float4 o) {
-        store4_masked(dst + (long long)L * k.pitch + gx0, gx0, k.w, o);
-        if (up_dst && L < k.row_lo + k.halo) {
-          store4_masked(up_dst + (k.peers.up_row + (L - k.row_lo)) * k.pitch + gx0, gx0, k.w, o);
-          ++n_up;
-        }
-        if (dn_dst && L >= k.row_hi - k.halo) {
-          store4_masked(dn_dst + (k.peers.dn_row + (L - (k.row_hi - k.halo))) * k.pitch + gx0, gx0, k.w, o);
-          ++n_dn;
-        }
-      };
-
-      const bool fast = tile_is_interior<F>(k, r0, r1, tx);
-      float *dp = dst + (long long)(r0 + j0) * k.pitch + gx0;
-      if constexpr (F == 1) {
-        if (fast) {
-          if (ra >= 0)
-            sweep_rows_fast<Gm::RPW, true>(S, j0, dp, k.pitch, lc, acc_a);
-          else
-            sweep_rows_fast<Gm::RPW, false>(S, j0, dp, k.pitch, lc, acc_a);
-        } else {
-        // box row of local row L is L - r0 + 1
-        float4 n = *reinterpret_cast<const float4 *>(S + j0 * BOXW + sc);
-        float4 c = *reinterpret_cast<const float4 *>(S + (j0 + 1) * BOXW + sc);
-#pragma unroll
-        for (int q = 0; q < Gm::RPW; ++q) {
-          const float *crow = S + (j0 + q + 1) * BOXW;
-          const float4 so = *reinterpret_cast<const float4 *>(crow + BOXW + sc);
-          float west, east;
-          edges(crow, c, west, east);
-          const int L = r0 + j0 + q;
-          if (L < r1) {
-            const float4 o = update4(c, n, so, west, east, k.g_row0 + L, k.g_rows, gx0, k.w);
-            emit(L, o);
-            if (ra >= 0) acc_a = __dadd_rn(acc_a, sq_diff4(o, c, gx0, k.w));
-          }
-          n = c;
-          c = so;
-        }
-        }
-      } else {
-        // Phase 1: the intermediate sweep on the tile rows plus a one-cell ring,
-        // rows i = 0 .. BH+1 <-> local rows r0-1+i (box row i+1).
-        if (landed && fast) {
-          if (cw < IX)
-            intermediate_rows_fast<IB + 1>(S, ibuf, ia, lc);
-          else
-            intermediate_rows_fast<IB>(S, ibuf, ia, lc);
-        }
-        for (int i = cw; landed && !fast && i < Gm::IROWS; i += CWARPS) {
-          const float *brow = S + (i + 1) * BOXW;
-          const float4 n4 = *reinterpret_cast<const float4 *>(S + i * BOXW + sc);
-          const float4 c4 = *reinterpret_cast<const float4 *>(brow + sc);
-          const float4 s4 = *reinterpret_cast<const float4 *>(S + (i + 2) * BOXW + sc);
-          float west, east;
-          edges(brow, c4, west, east);
-          const long long g = k.g_row0 + (r0 - 1 + i);
-          *reinterpret_cast<float4 *>(ibuf + i * BOXW + sc) =
-              update4(c4, n4, s4, west, east, g, k.g_rows, gx0, k.w);
-          if (lane == 0) {  // ring column x0 - 1
-            const int cc = XPAD - 1;
-            ibuf[i * BOXW + cc] = update1(brow[cc], S[i * BOXW + cc], S[(i + 2) * BOXW + cc], brow[cc + 1],
-                                          brow[cc - 1], g, k.g_rows, tx * BW - 1, k.w);
-          }
-          if (lane == 31) {  // ring column x0 + BW
-            const int cc = XPAD + BW;
-            ibuf[i * BOXW + cc] = update1(brow[cc], S[i * BOXW + cc], S[(i + 2) * BOXW + cc], brow[cc + 1],
-                                          brow[cc - 1], g, k.g_rows, tx * BW + BW, k.w);
-          }
-        }
-        // One warp's bounded wait can give up while another's succeeds: the
-        // barrier after phase 1 also ORs the failures, so every consumer warp
-        // leaves the tile loop together (no warp is left at a named barrier).
+      // Sweep 1 (S -> I, or S -> global when F == 1).  A warp whose wait gave
+      // up skips it; the barrier after it ORs the failures so every consumer
+      // warp leaves the tile loop together.
+      if (landed)
+        sweep_rows<F, 1>(k, fast, S, I, cw, c4, tc, dst, r0, rk[0] >= 0, acc[0], up_dst, dn_dst, n_up, n_dn);
+      if constexpr (F >= 2) {
         if (consumers_any(!landed)) {
           ok = false;
           break;
         }
-        // Phase 2: the second sweep from the intermediate buffer (ibuf row of
-        // local row L is L - r0 + 1; box row is L - r0 + 2).
-        if (fast) {
-          if (ra >= 0 && rb >= 0)
-            second_rows_fast<Gm::RPW, true, true>(S, ibuf, j0, dp, k.pitch, lc, acc_a, acc_b);
-          else if (ra >= 0)
-            second_rows_fast<Gm::RPW, true, false>(S, ibuf, j0, dp, k.pitch, lc, acc_a, acc_b);
-          else if (rb >= 0)
-            second_rows_fast<Gm::RPW, false, true>(S, ibuf, j0, dp, k.pitch, lc, acc_a, acc_b);
-          else
-            second_rows_fast<Gm::RPW, false, false>(S, ibuf, j0, dp, k.pitch, lc, acc_a, acc_b);
-        } else {
-        float4 n = *reinterpret_cast<const float4 *>(ibuf + j0 * BOXW + sc);
-        float4 c = *reinterpret_cast<const float4 *>(ibuf + (j0 + 1) * BOXW + sc);
-#pragma unroll
-        for (int q = 0; q < Gm::RPW; ++q) {
-          const float *irow = ibuf + (j0 + q + 1) * BOXW;
-          const float4 so = *reinterpret_cast<const float4 *>(irow + BOXW + sc);
-          float west, east;
-          edges(irow, c, west, east);
-          const int L = r0 + j0 + q;
-          if (L < r1) {
-            const float4 o = update4(c, n, so, west, east, k.g_row0 + L, k.g_rows, gx0, k.w);
-            emit(L, o);
-            if (ra >= 0) {  // first sweep of the pair: intermediate minus input
-              const float4 in = *reinterpret_cast<const float4 *>(S + (j0 + q + 2) * BOXW + sc);
-              acc_a = __dadd_rn(acc_a, sq_diff4(c, in, gx0, k.w));
-            }
-            if (rb >= 0) acc_b = __dadd_rn(acc_b, sq_diff4(o, c, gx0, k.w));
-          }
-          n = c;
-          c = so;
-        }
-        }
-        consumers_sync();  // the buffer is rewritten by the next tile
+        // Sweep 2: I -> global (F == 2) or I -> S (F == 4).
+        sweep_rows<F, 2>(k, fast, I, S, cw, c4, tc, dst, r0, rk[1] >= 0, acc[1], up_dst, dn_dst, n_up, n_dn);
       }
+      if constexpr (F == 4) {
+        consumers_sync();
+        sweep_rows<F, 3>(k, fast, S, I, cw, c4, tc, dst, r0, rk[2] >= 0, acc[2], up_dst, dn_dst, n_up, n_dn);
+        consumers_sync();
+        sweep_rows<F, 4>(k, fast, I, nullptr, cw, c4, tc, dst, r0, rk[3] >= 0, acc[3], up_dst, dn_dst, n_up,
+                         n_dn);
+        fence_proxy_async_shared();  // the stage was written by sweep 2; TMA refills it next
+      }
+      if constexpr (Gm::IBUFS == 1) consumers_sync();  // one intermediate buffer: the next tile rewrites it
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&tail->empty[st]);
@@ -682,28 +610,24 @@ __global__ void __launch_bounds__(THREADS) jacobi2d_persistent_kernel(
       ++it;
     }
     // ---- end of pass p: CTA partials, then one grid-barrier arrival ----
-    if (ra >= 0) {
-      const double wv = warp_sum_f64(acc_a);
-      if (lane == 0) tail->wsum[ra & 1][cw] = wv;
-      acc_a = 0.0;
-    }
-    if (rb >= 0) {
-      const double wv = warp_sum_f64(acc_b);
-      if (lane == 0) tail->wsum[rb & 1][cw] = wv;
-      acc_b = 0.0;
+#pragma unroll
+    for (int K = 0; K < F; ++K) {
+      if (rk[K] >= 0) {
+        const double wv = warp_sum_f64(acc[K]);
+        if (lane == 0) tail->wsum[K][cw] = wv;
+        acc[K] = 0.0;
+      }
     }
     fence_proxy_async_global();
     __syncwarp();
     const bool fail = consumers_any(!ok || *abort);
     if (fail) break;
     if (threadIdx.x == 0) {
-      const int rs[2] = {ra, rb};
-      for (int j = 0; j < 2; ++j) {
-        const int r = rs[j];
-        if (r < 0) continue;
+      for (int K = 0; K < F; ++K) {
+        if (rk[K] < 0) continue;
         double tot = 0.0;
-        for (int i = 0; i < CWARPS; ++i) tot = __dadd_rn(tot, tail->wsum[r & 1][i]);
-        k.ws->partial[r & 3][blockIdx.x] = tot;
+        for (int i = 0; i < CWARPS; ++i) tot = __dadd_rn(tot, tail->wsum[K][i]);
+        k.ws->partial[rk[K] % kPartialSlots][blockIdx.x] = tot;
       }
       __threadfence();
       red_release_gpu_add(&k.ws->barrier, 1u);
@@ -799,7 +723,7 @@ cudaError_t launch_fill_jacobi_input(float *p, int64_t pitch, int64_t rows, int6
 bool jacobi2d_tma_ok(const Jacobi2dProblem &p) {
   const uintptr_t a = reinterpret_cast<uintptr_t>(p.u), b = reinterpret_cast<uintptr_t>(p.v);
   return ((a | b) & 15u) == 0 && (p.pitch * 4) % 16 == 0 && p.w >= 1 && p.h_local >= 1 &&
-         p.w <= (1ll << 31) - 1 - BW && p.h_local <= (1ll << 31) - 1 - 128 && p.pitch < (1ll << 37) &&
+         p.w <= (1ll << 31) - 1 - LW && p.h_local <= (1ll << 31) - 1 - 256 && p.pitch < (1ll << 37) &&
          p.row_lo >= 0 && p.row_hi <= p.h_local && p.row_hi > p.row_lo && p.sweeps <= (1ll << 30);
 }
 
@@ -812,7 +736,7 @@ cudaError_t launch_passes(const Jacobi2dProblem &p, const SlabPeers &peers, int6
   CUtensorMap mu, mv;
   const uint64_t dims[2] = {(uint64_t)p.w, (uint64_t)p.h_local};
   const uint64_t strides[1] = {(uint64_t)p.pitch * 4u};
-  const uint32_t box[2] = {(uint32_t)BOXW, (uint32_t)Gm::BOXH};
+  const uint32_t box[2] = {(uint32_t)LW, (uint32_t)Gm::BOXH};
   if (encode_tensor_map_f32(&mu, p.u, 2, dims, strides, box) != 0) return cudaErrorInvalidValue;
   if (encode_tensor_map_f32(&mv, p.v, 2, dims, strides, box) != 0) return cudaErrorInvalidValue;
 
@@ -824,7 +748,7 @@ cudaError_t launch_passes(const Jacobi2dProblem &p, const SlabPeers &peers, int6
   k.row_lo = (int)p.row_lo;
   k.row_hi = (int)p.row_hi;
   const int rows = (int)(p.row_hi - p.row_lo);
-  k.tiles_x = (int)((p.w + BW - 1) / BW);
+  k.tiles_x = (int)((p.w + TW - 1) / TW);
   k.tiles_y = (rows + Gm::BH - 1) / Gm::BH;
   const int rem = rows - (k.tiles_y - 1) * Gm::BH;
   k.last_start = (p.halo > 0 && k.tiles_y >= 2 && rem < p.halo) ? (int)p.row_hi - p.halo
@@ -877,23 +801,35 @@ cudaError_t launch_passes(const Jacobi2dProblem &p, const SlabPeers &peers, int6
 
 }  // namespace
 
+void jacobi2d_pass_plan(int64_t sweeps, int64_t plan[3]) {
+  // Even pass counts keep the ping-pong parity of single sweeps.
+  plan[0] = (sweeps / 8) * 2;                             // four-sweep passes
+  plan[1] = ((sweeps - 4 * plan[0]) / 4) * 2;             // two-sweep passes (0 or 2)
+  plan[2] = sweeps - 4 * plan[0] - 2 * plan[1];           // single sweeps (0-3)
+}
+
 cudaError_t run_jacobi2d_persistent(const Jacobi2dProblem &p, const SlabPeers &peers, cudaStream_t s) {
-  // An even number of two-sweep passes keeps the ping-pong parity of single
-  // sweeps; the 0-3 sweeps left over run as single-sweep passes.
-  const int64_t fused = (p.sweeps / 4) * 2;
-  const int64_t single = p.sweeps - 2 * fused;
-  const unsigned per_pass = (unsigned)((p.w + BW - 1) / BW) * (unsigned)p.halo;
+  int64_t plan[3];
+  jacobi2d_pass_plan(p.sweeps, plan);
+  const unsigned per_pass = (unsigned)((p.w + TW - 1) / TW) * (unsigned)p.halo;
+  int64_t sweeps_done = 0, passes_done = 0;
   cudaError_t e = cudaSuccess;
-  if (fused > 0) {
-    e = launch_passes<2>(p, peers, fused, 0, 0u, s);
-    if (e != cudaSuccess) return e;
-  }
-  if (single > 0) {
-    if (fused > 0) {
+  for (int d = 0; d < 3; ++d) {
+    if (plan[d] == 0) continue;
+    if (passes_done > 0) {
       e = cudaMemsetAsync(&p.ws->barrier, 0, sizeof(unsigned), s);  // fresh grid barrier, same status word
       if (e != cudaSuccess) return e;
     }
-    e = launch_passes<1>(p, peers, single, 2 * fused, (unsigned)fused * per_pass, s);
+    const unsigned fb = (unsigned)passes_done * per_pass;
+    if (d == 0)
+      e = launch_passes<4>(p, peers, plan[0], sweeps_done, fb, s);
+    else if (d == 1)
+      e = launch_passes<2>(p, peers, plan[1], sweeps_done, fb, s);
+    else
+      e = launch_passes<1>(p, peers, plan[2], sweeps_done, fb, s);
+    if (e != cudaSuccess) return e;
+    sweeps_done += plan[d] * (d == 0 ? 4 : d == 1 ? 2 : 1);
+    passes_done += plan[d];
   }
   return e;
 }

@@ -7,9 +7,9 @@ one halo row up and one down per sweep, and the residual all-gather every
 (spmdb200_jacobi2d_slab): no NCCL call sits between sweeps.
 
 Decomposition: the G x W global grid is cut into contiguous row blocks; rank p
-owns global rows [g_first, g_first + rows) and keeps a (rows + 4) x pitch local
-array whose first and last HALO = 2 rows mirror the neighbours' edge rows (two
-rows deep, because the kernel fuses two sweeps per pass).
+owns global rows [g_first, g_first + rows) and keeps a (rows + 8) x pitch local
+array whose first and last HALO = 4 rows mirror the neighbours' edge rows (four
+rows deep, because the kernel fuses up to four sweeps per pass).
 """
 from __future__ import annotations
 
@@ -20,7 +20,7 @@ import numpy as np
 
 from ._lib import c_i, c_p, call, lib
 
-HALO = 2  # halo rows on each side of a slab (kSlabHalo in the C library)
+HALO = 4  # halo rows on each side of a slab (kSlabHalo in the C library)
 
 
 # ---------------------------------------------------------------- decomposition
@@ -235,11 +235,11 @@ class SlabJacobi2D:
         return out[:self._nres_last]
 
     def run_host(self, host_local: np.ndarray, sweeps: int) -> np.ndarray:
-        """End to end on host memory: host_local is this rank's (rows + 4) x pitch
+        """End to end on host memory: host_local is this rank's (rows + 8) x pitch
         slab (pinned for full speed); copied in, `sweeps` sweeps, owned rows
         copied back into host_local[HALO:HALO + rows]."""
         if host_local.shape != (self.local_rows, self.pitch) or host_local.dtype != np.float32:
-            raise ValueError("host slab must be (rows + 4) x pitch float32")
+            raise ValueError("host slab must be (rows + 2 * HALO) x pitch float32")
         # Only U needs the input: V's owned rows are all written by sweep 0 and
         # its halo rows by the neighbours before anyone reads them.
         call("spmdb200_memcpy", c_p(self._u.ptr), host_local.ctypes.data_as(c_p),

@@ -77,12 +77,14 @@ J2_CASES = [
     (33, 33, 4, 2, None),    # 132-byte rows: per-sweep path
     (1, 1, 1, 1, 4),
     (64, 1024, 11, 1, None),
-    # grids with interior tiles (the straight-line path) for both pass kinds:
-    # two-sweep passes then 0-3 single sweeps, residuals landing in each
+    # grids with interior tiles (the straight-line path) for every pass kind:
+    # four-sweep, two-sweep and single-sweep passes, residuals landing in each
     (300, 1000, 7, 3, None),
     (200, 700, 9, 1, 704),
     (260, 1100, 6, 2, None),
     (333, 777, 12, 4, 780),
+    (520, 1300, 17, 3, None),
+    (130, 245, 16, 5, 248),
 ]
 
 

@@ -1,10 +1,10 @@
 """Host logic of the multi-GPU row-slab Jacobi-2D, on CPU ranks (gloo).
 
 * partition / neighbours / local_row_range cover every global row exactly once;
-* the slab protocol (passes of one or two sweeps over a (rows+4)-row local
-  array -- a two-sweep pass first re-sweeps one halo row on each side --,
-  the first/last two owned rows handed to the neighbours' halo rows after
-  each pass, the residual all-gathered and summed in rank order) reproduces
+* the slab protocol (passes of one, two or four sweeps over a (rows+8)-row
+  local array -- sweep f of an F-sweep pass also re-sweeps F-1-f halo rows on
+  each side --, the first/last four owned rows handed to the neighbours' halo
+  rows after each pass, the residual all-gathered and summed in rank order) reproduces
   the single-domain oracle bit for bit -- the oracle does each rank's sweeps,
   gloo carries the halos;
 * a rank that never reaches the rendezvous makes the other rank fail there
@@ -51,9 +51,11 @@ def test_partition_covers_rows_once():
 
 def _pass_plan(sweeps: int) -> list[int]:
     """Sweeps per pass as the C library schedules them: an even number of
-    two-sweep passes, then the 0-3 sweeps left over one per pass."""
-    fused = (sweeps // 4) * 2
-    return [2] * fused + [1] * (sweeps - 2 * fused)
+    four-sweep passes, an even number of two-sweep passes, then the 0-3 sweeps
+    left over one per pass."""
+    four = (sweeps // 8) * 2
+    two = ((sweeps - 4 * four) // 4) * 2
+    return [4] * four + [2] * two + [1] * (sweeps - 4 * four - 2 * two)
 
 
 def _slab_worker(rank: int, world: int, port: int, G: int, W: int, sweeps: int, res_every: int, q):
@@ -77,13 +79,13 @@ def _slab_worker(rank: int, world: int, port: int, G: int, W: int, sweeps: int, 
     res = []
     k = 0
     for pno, F in enumerate(_pass_plan(sweeps)):
-        # A two-sweep pass first sweeps one halo row beyond each edge (the
-        # second sweep of the owned edge rows reads it), then the owned rows.
+        # Sweep f of an F-sweep pass also sweeps F-1-f halo rows beyond each
+        # edge (the later sweeps of the owned edge rows read them).
         for f in range(F):
             k += 1
             want = res_every > 0 and k % res_every == 0
             ext = F - 1 - f
-            src, dst = (u, v) if f == 0 else (v, u)
+            src, dst = (u, v) if f % 2 == 0 else (v, u)
             oracle.jacobi2d_rows(src, dst, H - ext, H + rows + ext, g0 - H, G)
             rr = oracle.jacobi2d_rows(src, dst, H, H + rows, g0 - H, G, want_res=True) if want else None
             if want:
@@ -96,7 +98,7 @@ def _slab_worker(rank: int, world: int, port: int, G: int, W: int, sweeps: int, 
                 for x in slots:  # rank order, as spmdb200_jacobi2d_slab_residuals sums
                     tot = tot + x
                 res.append(tot)
-        out = v if F == 1 else u
+        out = v if F % 2 == 1 else u
         # halo hand-off after each pass: the first H owned rows up, the last H down
         reqs = []
         if up is not None:
@@ -111,7 +113,7 @@ def _slab_worker(rank: int, world: int, port: int, G: int, W: int, sweeps: int, 
             out[rows + H:rows + 2 * H] = buf.numpy()
         for r in reqs:
             r.wait()
-        if F == 1:
+        if F % 2 == 1:
             u, v = v, u
     parts = [None] * world
     dist.all_gather_object(parts, u[H:rows + H])
@@ -121,8 +123,8 @@ def _slab_worker(rank: int, world: int, port: int, G: int, W: int, sweeps: int, 
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,G,W,sweeps", [(2, 37, 29, 7), (3, 64, 17, 5), (2, 4, 8, 3), (2, 37, 29, 12),
-                                               (4, 41, 13, 9)])
+@pytest.mark.parametrize("world,G,W,sweeps", [(2, 37, 29, 7), (3, 64, 17, 5), (2, 8, 8, 3), (2, 37, 29, 12),
+                                               (4, 41, 13, 9), (2, 50, 21, 22), (3, 40, 9, 17)])
 def test_slab_protocol_matches_single_domain_oracle(oracle_mod, world, G, W, sweeps):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
