@@ -68,7 +68,11 @@ constexpr int kPartialSlots = 8;  // >= 2 x the residuals one pass can produce
 static_assert(kSlabHalo == kMaxF, "slab halos must cover the deepest pass");
 
 // Tile height, ring depth and intermediate buffers per pass depth, chosen by
-// measurement on B200.
+// measurement on B200 (32768^2 x 200 sweeps, four-sweep passes: 40 rows, a
+// 2-deep ring and one intermediate buffer -- 73.7 KB, three CTAs per SM --
+// at 1876 Gcell/s beat 32/48/56 rows (1774-1815), two intermediate buffers
+// (1744, two CTAs per SM) and a 3-deep ring (1726); interleaving two row
+// chains per warp was slower (1856)).
 template <int F>
 struct Cfg;
 template <>
@@ -81,7 +85,7 @@ struct Cfg<2> {
 };
 template <>
 struct Cfg<4> {
-  static constexpr int BH = 40, STAGES = 2, IBUFS = 2;
+  static constexpr int BH = 40, STAGES = 2, IBUFS = 1;
 };
 template <int F>
 struct Geo {
@@ -257,6 +261,28 @@ __device__ __forceinline__ float4 update4(float4 c, float4 n, float4 s, float we
 // global memory at dp (lanes 1..30 hold the tile's 120 columns).  RES adds the
 // squared updates of owned cells (box rows [own_lo, own_hi), lanes 1..30).
 // ---------------------------------------------------------------------------
+// One output row of a straight-line sweep: box row b (its south neighbour at
+// p + (q + 2) * LW), sliding the north/centre window down by one row.
+template <bool TO_GLOBAL, bool RES>
+__device__ __forceinline__ void row_step(const float *p, int q, int b, float4 &n, float4 &c, float *out, int c4,
+                                         float *&dp, long long pitch, bool out_lane, int own_lo, int own_hi,
+                                         double &acc) {
+  const float4 s = lds4(p + (q + 2) * LW);
+  const float wv = __shfl_up_sync(0xffffffffu, c.w, 1);
+  const float ev = __shfl_down_sync(0xffffffffu, c.x, 1);
+  const float4 o = stencil4(c, n, s, wv, ev);
+  if (TO_GLOBAL) {
+    if (out_lane) *reinterpret_cast<float4 *>(dp) = o;
+    dp += pitch;
+    if (RES && out_lane) acc = acc_sq4(acc, o, c);
+  } else {
+    sts4(out + b * LW + c4, o);
+    if (RES && out_lane && b >= own_lo && b < own_hi) acc = acc_sq4(acc, o, c);
+  }
+  n = c;
+  c = s;
+}
+
 template <int ROWS, bool TO_GLOBAL, bool RES>
 __device__ __forceinline__ void rows_fast(const float *in, float *out, int b0, int c4, float *dp, long long pitch,
                                           bool out_lane, int own_lo, int own_hi, double &acc) {
@@ -264,22 +290,8 @@ __device__ __forceinline__ void rows_fast(const float *in, float *out, int b0, i
   float4 n = lds4(p);
   float4 c = lds4(p + LW);
 #pragma unroll
-  for (int q = 0; q < ROWS; ++q) {
-    const float4 s = lds4(p + (q + 2) * LW);
-    const float wv = __shfl_up_sync(0xffffffffu, c.w, 1);
-    const float ev = __shfl_down_sync(0xffffffffu, c.x, 1);
-    const float4 o = stencil4(c, n, s, wv, ev);
-    if (TO_GLOBAL) {
-      if (out_lane) *reinterpret_cast<float4 *>(dp) = o;
-      dp += pitch;
-      if (RES && out_lane) acc = acc_sq4(acc, o, c);
-    } else {
-      sts4(out + (b0 + q) * LW + c4, o);
-      if (RES && out_lane && b0 + q >= own_lo && b0 + q < own_hi) acc = acc_sq4(acc, o, c);
-    }
-    n = c;
-    c = s;
-  }
+  for (int q = 0; q < ROWS; ++q)
+    row_step<TO_GLOBAL, RES>(p, q, b0 + q, n, c, out, c4, dp, pitch, out_lane, own_lo, own_hi, acc);
 }
 
 // Per-tile context of the general (boundary) rows.
