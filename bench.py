@@ -8,16 +8,16 @@ f32 row slab per GPU (weak scaling: the global grid is (32768*N) x 32768),
 interior uniform [0,1) from seed 4, zero boundary rows/columns, 1000 ping-pong
 sweeps, a global L2 residual every 10 sweeps.  Inputs are device-resident when
 the timed region starts (4 GiB per grid, far above the 126 MB L2, so no L2
-flush is needed between steps).  At N > 1 the slabs exchange two halo rows per
-neighbour per two-sweep pass over NVLink inside the persistent kernel.
+flush is needed between steps).  At N > 1 the slabs exchange four halo rows per
+neighbour per pass over NVLink inside the persistent kernel.
 
 `value` is device time (CUDA events, max over ranks); `e2e` runs the same job
 through the host-buffer C entry (pinned host grid in, result grid out, both
 copies inside the timed region).  `roofline` uses the algorithmic bytes of
 the sweep kernel against the measured HBM copy bandwidth: each pass over the
 grid reads every cell once and writes it once (8 B per cell per pass), and a
-pass advances two sweeps (the 0-3 sweeps left over run one per pass), so
-1000 sweeps cost 4 B per cell update.  `cpu_baseline` times the oracle (the C/OpenMP restatement of the
+pass advances four sweeps (two or one for the 0-7 sweeps left over), so 1000
+sweeps cost 2 B per cell update.  `cpu_baseline` times the oracle (the C/OpenMP restatement of the
 reference's SPMDToOpenMP lowering) on a bounded sample of the same grid.
 `--impl reference` times that CPU path alone (the reference itself needs
 MLIR/LLVM 20 to build and cannot run here).
@@ -47,15 +47,16 @@ RES_EVERY = 10
 BYTES_PER_CELL_PASS = 8  # algorithmic: each pass reads u[i,j] once and writes v[i,j] once
 
 
-def sweep_passes(sweeps: int) -> tuple[int, int]:
-    """(two-sweep passes, single-sweep passes) the Jacobi-2D kernel runs."""
-    fused = (sweeps // 4) * 2
-    return fused, sweeps - 2 * fused
+def sweep_passes(sweeps: int) -> tuple[int, int, int]:
+    """(four-sweep, two-sweep, single-sweep) passes the Jacobi-2D kernel runs:
+    even counts of the first two, then the 0-3 sweeps left over."""
+    four = (sweeps // 8) * 2
+    two = ((sweeps - 4 * four) // 4) * 2
+    return four, two, sweeps - 4 * four - 2 * two
 
 
 def bytes_per_update(sweeps: int) -> float:
-    fused, single = sweep_passes(sweeps)
-    return BYTES_PER_CELL_PASS * (fused + single) / sweeps
+    return BYTES_PER_CELL_PASS * sum(sweep_passes(sweeps)) / sweeps
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -398,17 +399,17 @@ def run_spmd_arm(args) -> None:
         e2e = slab.e2e_measure(job, SWEEPS) if hasattr(slab, "e2e_measure") else None
 
     # ---- roofline of the dominant kernel (the persistent sweep kernel) --------------
-    fused, single = sweep_passes(SWEEPS)
+    plan = sweep_passes(SWEEPS)
     alg_bytes = rows * GRID * SWEEPS * bytes_per_update(SWEEPS)
     achieved = alg_bytes / (ms_kernel * 1e-3) / 1e9
-    kname = "jacobi2d_persistent_kernel<2>" if fused else "jacobi2d_persistent_kernel<1>"
+    kname = "jacobi2d_persistent_kernel<%d>" % next(f for f, n in zip((4, 2, 1), plan) if n)
     tpu = profile_traffic_per_update(kname)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4),
                 "traffic": (round(tpu * rows * GRID * SWEEPS) if tpu else None),
-                "traffic_source": "profiles/jacobi2d_persistent_f2_16384x16384.md (bytes per update x updates)",
+                "traffic_source": "profiles/jacobi2d_persistent_f4_16384x16384.md (bytes per update x updates)",
                 "kernel": kname, "peak_kind": f"{peak_kind} hbm_gbs (copy bandwidth)",
-                "passes_per_launch": {"two_sweep": fused, "single_sweep": single},
+                "passes_per_step": {"four_sweep": plan[0], "two_sweep": plan[1], "single_sweep": plan[2]},
                 "algorithmic_bytes_per_update": bytes_per_update(SWEEPS),
                 "algorithmic_bytes_per_launch": round(alg_bytes)}
 
@@ -432,7 +433,7 @@ def run_spmd_arm(args) -> None:
                        "res_every": RES_EVERY, "parallelism": f"row-slab x{world}",
                        "l2": "inputs (4 GiB per grid) larger than L2; no flush needed"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": args.steps * ((fused > 0) + (single > 0)),
+            "gpu_launches": args.steps * sum(1 for n in plan if n),
             "clocks": clocks, "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
