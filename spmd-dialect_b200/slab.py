@@ -2,8 +2,9 @@
 
 torch.distributed is plumbing only (exchanging CUDA IPC handles, the
 rendezvous before each launch, gathering results for tests).  The data path --
-one halo row up and one down per sweep, and the residual all-gather every
-`res_every` sweeps -- runs inside the persistent kernel over NVLink
+four halo rows up and four down per pass (a pass advances up to four sweeps),
+and the residual all-gather every `res_every` sweeps -- runs inside the
+persistent kernel over NVLink
 (spmdb200_jacobi2d_slab): no NCCL call sits between sweeps.
 
 Decomposition: the G x W global grid is cut into contiguous row blocks; rank p
