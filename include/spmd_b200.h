@@ -273,6 +273,28 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U_aligned, int64_t U_offset, in
                            void *ws, float *up_u, float *up_v, void *up_ws, int64_t up_rows,
                            float *dn_u, float *dn_v, void *dn_ws,
                            int rank, int nranks, void *const *all_ws, void *stream);
+/* Jacobi-3D over z-slabs on several GPUs (one process per GPU).  No reference
+ * counterpart.  The global grid has D planes of H x W; this rank owns global
+ * planes [z_first, z_first + Z), Z >= 1.  U and V are (Z + 2) x H x W local
+ * arrays (descriptor sizes (Z+2, H, W), x contiguous, 16-byte aligned rows and
+ * planes): local plane 0 is the halo plane above (global z_first - 1), planes
+ * 1..Z are owned, plane Z+1 is the halo plane below.  The kernel stores its
+ * first / last owned plane straight into the neighbour's halo plane over
+ * NVLink every sweep; up_planes is the number of planes the neighbour above
+ * owns (our first owned plane lands in its local plane up_planes + 1).  All
+ * ranks' arrays share H, W and the row and plane strides.
+ * Neighbour, workspace, residual and ping-pong semantics are those of
+ * spmdb200_jacobi2d_slab (spmdb200_jacobi2d_slab_residuals reads the
+ * all-gathered residuals); global planes 0 and D-1, rows 0 and H-1 and
+ * columns 0 and W-1 are fixed. */
+int spmdb200_jacobi3d_slab(float *U_base, float *U_aligned, int64_t U_offset, int64_t U_size0, int64_t U_size1,
+                           int64_t U_size2, int64_t U_stride0, int64_t U_stride1, int64_t U_stride2,
+                           float *V_base, float *V_aligned, int64_t V_offset, int64_t V_size0, int64_t V_size1,
+                           int64_t V_size2, int64_t V_stride0, int64_t V_stride1, int64_t V_stride2,
+                           int64_t z_first, int64_t D, int64_t sweeps, int64_t res_every, double *res_out,
+                           void *ws, float *up_u, float *up_v, void *up_ws, int64_t up_planes,
+                           float *dn_u, float *dn_v, void *dn_ws,
+                           int rank, int nranks, void *const *all_ws, void *stream);
 /* Clears the 256-byte header of a Jacobi workspace on `stream`. */
 int spmdb200_jacobi_ws_reset(void *ws, void *stream);
 /* After every rank's slab run has finished: res_host[r] = sum over ranks q
@@ -297,6 +319,12 @@ int spmdb200_ipc_close(void *dev_ptr);
  * exchange at start-up. */
 int spmdb200_fill_jacobi_input(float *p, int64_t pitch, int64_t rows, int64_t W, int64_t g_row0, int64_t G,
                                uint64_t seed, void *stream);
+/* The 3-D counterpart: `planes` planes of an H x W grid (strides plane_stride,
+ * row_stride, x contiguous), local plane 0 = global plane g_z0 of D; cell
+ * (gz, y, x) is uniform [0,1) from the hash of (seed, gz * H + y, x), global
+ * boundary cells and planes outside [0, D) are 0. */
+int spmdb200_fill_jacobi3d_input(float *p, int64_t plane_stride, int64_t row_stride, int64_t planes, int64_t H,
+                                 int64_t W, int64_t g_z0, int64_t D, uint64_t seed, void *stream);
 
 /* ---- Jacobi-3D 7-point --------------------------------------------------- */
 /* One sweep over the D x H x W grid (index order [z][y][x]):

@@ -35,6 +35,7 @@ _SIGS = {
     "oracle_jacobi2d_rows": (None, [c_p, c_p, c_i, c_i, c_i, c_i, c_i, c_i, c_p]),
     "oracle_jacobi2d": (None, D2 + D2 + [c_i, c_i, c_p]),
     "oracle_jacobi3d_planes": (None, [c_p, c_p, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_p]),
+    "oracle_jacobi3d_slab_planes": (None, [c_p, c_p, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_p]),
     "oracle_jacobi3d": (None, D3 + D3 + [c_i, c_i, c_p]),
     "oracle_num_threads": (ctypes.c_int, []),
 }
@@ -167,3 +168,14 @@ def jacobi3d(U0: np.ndarray, sweeps: int, res_every: int = 0) -> tuple[np.ndarra
     res = np.zeros(max(nres, 1), dtype=np.float64)
     lib().oracle_jacobi3d(*_d3(U), *_d3(V), c_i(sweeps), c_i(res_every), _p(res))
     return (U if sweeps % 2 == 0 else V), res[:nres]
+
+
+def jacobi3d_planes(u: np.ndarray, v: np.ndarray, z_lo: int, z_hi: int, g_z0: int, D: int,
+                    want_res: bool = False) -> np.ndarray | None:
+    """One sweep over local planes [z_lo, z_hi) of u into v (a z-slab of a D-plane
+    grid whose local plane 0 is global plane g_z0; u, v C-contiguous)."""
+    pr = np.zeros(max(z_hi - z_lo, 1), dtype=np.float64) if want_res else None
+    lib().oracle_jacobi3d_slab_planes(_p(u), _p(v), c_i(g_z0), c_i(D), c_i(u.shape[1]), c_i(u.shape[2]),
+                                      c_i(u.strides[0] // 4), c_i(u.strides[1] // 4), c_i(z_lo), c_i(z_hi),
+                                      _p(pr) if want_res else None)
+    return pr

@@ -343,18 +343,21 @@ EXPORT void oracle_jacobi2d(float *U_base, float *U, int64_t U_off, int64_t H, i
  *   ((((((c + xm) + xp) + ym) + yp) + zm) + zp) * (1.0f/7.0f)
  * with the constant rounded to f32 once.  plane_res[z - z_lo] (when non-NULL)
  * = per-plane sum of squared updates, rows left to right, planes in order.
+ * The arrays may hold a z-slab of a larger grid: local plane z is global plane
+ * g_z0 + z of D (the boundary test is on the global index).
  * ------------------------------------------------------------------------- */
-EXPORT void oracle_jacobi3d_planes(const float *u, float *v, int64_t D, int64_t H, int64_t W,
-                                   int64_t sz, int64_t sy, int64_t z_lo, int64_t z_hi,
-                                   double *plane_res) {
+EXPORT void oracle_jacobi3d_slab_planes(const float *u, float *v, int64_t g_z0, int64_t D, int64_t H,
+                                        int64_t W, int64_t sz, int64_t sy, int64_t z_lo, int64_t z_hi,
+                                        double *plane_res) {
   const float k = 1.0f / 7.0f;
 #pragma omp parallel for schedule(static)
   for (int64_t z = z_lo; z < z_hi; ++z) {
     double pacc = 0.0;
+    const int64_t gz = g_z0 + z;
     for (int64_t y = 0; y < H; ++y) {
       const float *uc = u + z * sz + y * sy;
       float *vr = v + z * sz + y * sy;
-      if (z == 0 || z == D - 1 || y == 0 || y == H - 1) {
+      if (gz == 0 || gz == D - 1 || y == 0 || y == H - 1) {
         for (int64_t x = 0; x < W; ++x) vr[x] = uc[x];
         continue;
       }
@@ -381,6 +384,12 @@ EXPORT void oracle_jacobi3d_planes(const float *u, float *v, int64_t D, int64_t 
     }
     if (plane_res) plane_res[z - z_lo] = pacc;
   }
+}
+
+EXPORT void oracle_jacobi3d_planes(const float *u, float *v, int64_t D, int64_t H, int64_t W,
+                                   int64_t sz, int64_t sy, int64_t z_lo, int64_t z_hi,
+                                   double *plane_res) {
+  oracle_jacobi3d_slab_planes(u, v, 0, D, H, W, sz, sy, z_lo, z_hi, plane_res);
 }
 
 EXPORT void oracle_jacobi3d(float *U_base, float *U, int64_t U_off, int64_t D, int64_t H, int64_t W,

@@ -65,6 +65,8 @@ _SIGS = {
     # multi-GPU row slabs
     "spmdb200_jacobi2d_slab": (ctypes.c_int, D2 + D2 + [c_i, c_i, c_i, c_i, c_p, c_p, c_p, c_p, c_p, c_i, c_p, c_p,
                                                        c_p, ctypes.c_int, ctypes.c_int, c_p, c_p]),
+    "spmdb200_jacobi3d_slab": (ctypes.c_int, D3 + D3 + [c_i, c_i, c_i, c_i, c_p, c_p, c_p, c_p, c_p, c_i, c_p, c_p,
+                                                       c_p, ctypes.c_int, ctypes.c_int, c_p, c_p]),
     "spmdb200_jacobi_ws_reset": (ctypes.c_int, [c_p, c_p]),
     "spmdb200_jacobi2d_slab_residuals": (ctypes.c_int, [c_p, ctypes.c_int, c_i, c_p]),
     "spmdb200_dev_alloc": (ctypes.c_int, [c_sz, ctypes.POINTER(c_p)]),
@@ -74,6 +76,7 @@ _SIGS = {
     "spmdb200_ipc_open": (ctypes.c_int, [c_p, ctypes.POINTER(c_p)]),
     "spmdb200_ipc_close": (ctypes.c_int, [c_p]),
     "spmdb200_fill_jacobi_input": (ctypes.c_int, [c_p, c_i, c_i, c_i, c_i, c_i, ctypes.c_uint64, c_p]),
+    "spmdb200_fill_jacobi3d_input": (ctypes.c_int, [c_p, c_i, c_i, c_i, c_i, c_i, c_i, c_i, ctypes.c_uint64, c_p]),
     # family C: end-to-end host entries
     "spmdb200_axpy_host": (ctypes.c_int, [c_f] + D1 + D1 + [c_i]),
     "spmdb200_sum_f32_host": (ctypes.c_int, D1 + D0 + [c_i]),

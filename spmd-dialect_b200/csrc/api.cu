@@ -481,7 +481,7 @@ int spmdb200_jacobi3d(float *U_base, float *U, int64_t U_off, int64_t U_n0, int6
   p.ws = w;
   if (jacobi3d_tma_ok(p)) {
     int grid = 0;
-    CUDA_TRY(launch_jacobi3d_persistent(p, s, &grid));
+    CUDA_TRY(launch_jacobi3d_persistent(p, SlabPeers{}, s, &grid));
   } else {
     CUDA_TRY(launch_jacobi3d_generic(p, s));
   }
@@ -565,6 +565,80 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   return ok();
 }
 
+int spmdb200_jacobi3d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0, int64_t U_n1, int64_t U_n2,
+                           int64_t U_s0, int64_t U_s1, int64_t U_s2, float *V_base, float *V, int64_t V_off,
+                           int64_t V_n0, int64_t V_n1, int64_t V_n2, int64_t V_s0, int64_t V_s1, int64_t V_s2,
+                           int64_t z_first, int64_t D, int64_t sweeps, int64_t res_every, double *res_out,
+                           void *ws, float *up_u, float *up_v, void *up_ws, int64_t up_planes, float *dn_u,
+                           float *dn_v, void *dn_ws, int rank, int nranks, void *const *all_ws, void *stream) {
+  (void)U_base; (void)V_base;
+  CHECK(check3("U", U, U_off, U_n0, U_n1, U_n2, U_s0, U_s1, U_s2));
+  CHECK(check3("V", V, V_off, V_n0, V_n1, V_n2, V_s0, V_s1, V_s2));
+  if (U_n0 != V_n0 || U_n1 != V_n1 || U_n2 != V_n2 || U_s0 != V_s0 || U_s1 != V_s1 || U_s2 != V_s2)
+    return fail(SPMDB200_ERR_INVALID_ARG, "U and V must have identical sizes and strides");
+  const int64_t H = kSlabHalo3;
+  if (U_n0 < 1 + 2 * H || U_n1 < 1 || U_n2 < 1)
+    return fail(SPMDB200_ERR_INVALID_ARG, "a z-slab needs >= 1 owned plane plus %lld halo plane(s) on each side",
+                (long long)H);
+  const int64_t Z = U_n0 - 2 * H;
+  if (z_first < 0 || D < 1 || z_first + Z > D)
+    return fail(SPMDB200_ERR_INVALID_ARG, "owned planes [%lld, %lld) outside the %lld global planes",
+                (long long)z_first, (long long)(z_first + Z), (long long)D);
+  if (nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks)
+    return fail(SPMDB200_ERR_INVALID_ARG, "rank %d of %d (at most %d ranks)", rank, nranks, kMaxRanks);
+  if ((z_first > 0) != (up_u != nullptr) || (z_first + Z < D) != (dn_u != nullptr))
+    return fail(SPMDB200_ERR_INVALID_ARG, "neighbour pointers must be given exactly where a neighbour exists");
+  if ((up_u && (!up_v || !up_ws)) || (dn_u && (!dn_v || !dn_ws)))
+    return fail(SPMDB200_ERR_INVALID_ARG, "incomplete neighbour (U, V, workspace)");
+  if (up_u && (up_planes < 1 || up_planes > z_first))
+    return fail(SPMDB200_ERR_INVALID_ARG, "neighbour above owns %lld planes: must be in [1, %lld]",
+                (long long)up_planes, (long long)z_first);
+  if (nranks > 1 && !all_ws) return fail(SPMDB200_ERR_INVALID_ARG, "all_ws is required for nranks > 1");
+  if (sweeps < 0 || res_every < 0) return fail(SPMDB200_ERR_INVALID_ARG, "negative sweeps / res_every");
+  if (res_every > 0 && sweeps / res_every > kMaxResSlots)
+    return fail(SPMDB200_ERR_UNSUPPORTED, "at most %d residuals per slab run", kMaxResSlots);
+  CHECK(check_jacobi_ws(ws, sizeof(JacobiWs)));
+  if (sweeps == 0) return ok();
+  Jacobi3dProblem p{};
+  p.u = U + U_off;
+  p.v = V + V_off;
+  p.d = U_n0;
+  p.h = U_n1;
+  p.w = U_n2;
+  p.sz = U_s0;
+  p.sy = U_s1;
+  p.sx = U_s2;
+  p.sweeps = sweeps;
+  p.res_every = res_every;
+  p.res_out = res_out;
+  p.ws = static_cast<JacobiWs *>(ws);
+  p.z_lo = H;
+  p.z_hi = Z + H;
+  p.g_z0 = z_first - H;
+  p.g_d = D;
+  p.halo = (int)H;
+  if (!jacobi3d_tma_ok(p))
+    return fail(SPMDB200_ERR_UNSUPPORTED,
+                "z-slab arrays need contiguous x and 16-byte aligned rows and planes (pitch multiple of 4 floats)");
+  SlabPeers peers;
+  peers.up_u = up_u;
+  peers.up_v = up_v;
+  peers.dn_u = dn_u;
+  peers.dn_v = dn_v;
+  peers.up_row = up_planes + H;  // our first owned plane is the bottom halo plane of the rank above
+  peers.dn_row = 0;              // our last owned plane is the top halo plane of the rank below
+  peers.up_flag = up_ws ? &static_cast<JacobiWs *>(up_ws)->from_below : nullptr;
+  peers.dn_flag = dn_ws ? &static_cast<JacobiWs *>(dn_ws)->from_above : nullptr;
+  peers.rank = rank;
+  peers.nranks = nranks;
+  for (int q = 0; q < nranks; ++q)
+    peers.peer_ws[q] = static_cast<JacobiWs *>(all_ws ? all_ws[q] : (q == rank ? ws : nullptr));
+  if (!peers.peer_ws[rank]) peers.peer_ws[rank] = static_cast<JacobiWs *>(ws);
+  int grid = 0;
+  CUDA_TRY(launch_jacobi3d_persistent(p, peers, (cudaStream_t)stream, &grid));
+  return ok();
+}
+
 int spmdb200_jacobi2d_slab_residuals(void *ws, int nranks, int64_t nres, double *res_host) {
   if (!ws) return fail(SPMDB200_ERR_WORKSPACE, "null workspace");
   if (nranks < 1 || nranks > kMaxRanks || nres < 0 || nres > kMaxResSlots || (nres > 0 && !res_host))
@@ -616,6 +690,15 @@ int spmdb200_ipc_open(const void *handle64, void **dev_ptr_out) {
 }
 int spmdb200_ipc_close(void *dev_ptr) {
   if (dev_ptr) CUDA_TRY(cudaIpcCloseMemHandle(dev_ptr));
+  return ok();
+}
+int spmdb200_fill_jacobi3d_input(float *p, int64_t plane_stride, int64_t row_stride, int64_t planes, int64_t H,
+                                 int64_t W, int64_t g_z0, int64_t D, uint64_t seed, void *stream) {
+  if (planes < 0 || H < 0 || W < 0 || row_stride < W || plane_stride < row_stride * H ||
+      (planes > 0 && H > 0 && W > 0 && !p))
+    return fail(SPMDB200_ERR_INVALID_ARG, "bad fill arguments");
+  CUDA_TRY(launch_fill_jacobi3d_input(p, plane_stride, row_stride, planes, H, W, g_z0, D, seed,
+                                      (cudaStream_t)stream));
   return ok();
 }
 int spmdb200_fill_jacobi_input(float *p, int64_t pitch, int64_t rows, int64_t W, int64_t g_row0, int64_t G,

@@ -177,6 +177,19 @@ __device__ __forceinline__ void st_f4(float *p, float4 v) {
                : "memory");
 }
 
+// ---- seeded synthetic input ---------------------------------------------------
+// splitmix64 finaliser over (seed, row, column): a counter-based generator, so
+// any rank can produce any global cell without coordination.
+__device__ __forceinline__ float hash_uniform(uint64_t seed, uint64_t g, uint64_t c) {
+  uint64_t x = seed * 0x9E3779B97F4A7C15ull + g * 0xD1B54A32D192ED03ull + c * 0x8CB92BA72F3D8DD7ull;
+  x ^= x >> 30;
+  x *= 0xBF58476D1CE4E5B9ull;
+  x ^= x >> 27;
+  x *= 0x94D049BB133111EBull;
+  x ^= x >> 31;
+  return (float)(x >> 40) * (1.0f / 16777216.0f);  // 24 random bits -> [0, 1)
+}
+
 // ---- reductions -----------------------------------------------------------------
 __device__ __forceinline__ double warp_sum_f64(double v) {
 #pragma unroll

@@ -77,9 +77,11 @@ struct Jacobi2dProblem {
   int halo = 0;       // slab mode: halo rows on each side (rows exchanged per neighbour per pass)
 };
 
-// Halo depth of the multi-GPU slab layout: two rows on each side, so a pass
-// may fuse two sweeps.
-constexpr int kSlabHalo = 4;  // rows; the deepest pass advances 4 sweeps
+// Halo depth of the multi-GPU Jacobi-2D slab layout: four rows on each side,
+// so a pass may fuse four sweeps.
+constexpr int kSlabHalo = 4;
+// Halo depth of the multi-GPU Jacobi-3D z-slab layout (one sweep per pass).
+constexpr int kSlabHalo3 = 1;
 
 bool jacobi2d_tma_ok(const Jacobi2dProblem &p);
 // Passes the persistent path runs for `sweeps` sweeps: plan[0] four-sweep,
@@ -98,15 +100,25 @@ cudaError_t launch_jacobi2d_generic(const Jacobi2dProblem &p, int64_t stride1, c
 
 struct Jacobi3dProblem {
   float *u, *v;
-  int64_t d, h, w;     // sizes [z][y][x]
+  int64_t d, h, w;     // sizes [z][y][x] of the (local) arrays
   int64_t sz, sy, sx;  // strides
   int64_t sweeps, res_every;
   double *res_out;
   JacobiWs *ws;
+  // z-slab mode (multi-GPU): local planes [z_lo, z_hi) are updated, local
+  // plane 0 is global plane g_z0, the global grid has g_d planes, and `halo`
+  // planes on each side mirror the neighbours.  One GPU: [0, d), 0, d, 0.
+  int64_t z_lo = 0, z_hi = -1, g_z0 = 0, g_d = -1;
+  int halo = 0;
 };
 bool jacobi3d_tma_ok(const Jacobi3dProblem &p);
-cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, cudaStream_t s, int *grid_out);
+// SlabPeers.up_row / dn_row are plane indices here.
+cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, const SlabPeers &peers, cudaStream_t s,
+                                       int *grid_out);
 cudaError_t launch_jacobi3d_generic(const Jacobi3dProblem &p, cudaStream_t s);
+// Seeded synthetic 3-D Jacobi input (counter hash of (seed, gz * h + y, x)).
+cudaError_t launch_fill_jacobi3d_input(float *p, int64_t sz, int64_t sy, int64_t planes, int64_t h, int64_t w,
+                                       int64_t g_z0, int64_t g_d, uint64_t seed, cudaStream_t s);
 
 // ---- driver entry points resolved at run time (no link-time libcuda) ----------------
 // Encodes a row-major f32 tensor map (innermost dimension first).  Returns 0 on success.

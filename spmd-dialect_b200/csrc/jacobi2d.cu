@@ -694,18 +694,6 @@ __global__ void __launch_bounds__(256) jacobi2d_sweep_generic_kernel(
   }
 }
 
-// splitmix64 finaliser over (seed, row, column): a counter-based generator, so
-// any rank can produce any global cell without coordination.
-__device__ __forceinline__ float hash_uniform(uint64_t seed, uint64_t g, uint64_t c) {
-  uint64_t x = seed * 0x9E3779B97F4A7C15ull + g * 0xD1B54A32D192ED03ull + c * 0x8CB92BA72F3D8DD7ull;
-  x ^= x >> 30;
-  x *= 0xBF58476D1CE4E5B9ull;
-  x ^= x >> 27;
-  x *= 0x94D049BB133111EBull;
-  x ^= x >> 31;
-  return (float)(x >> 40) * (1.0f / 16777216.0f);  // 24 random bits -> [0, 1)
-}
-
 __global__ void __launch_bounds__(256) fill_jacobi_input_kernel(float *p, long long pitch, long long rows,
                                                                 long long w, long long g_row0, long long g_rows,
                                                                 uint64_t seed) {

@@ -15,6 +15,14 @@
 // split grid barrier as the 2-D kernel (consumers arrive, the producer waits),
 // every wait is bounded, and out-of-grid box cells are zero-filled by TMA.
 //
+// z-slabs across GPUs (SlabPeers, halo = 1 plane): a rank updates local planes
+// [z_lo, z_hi) and mirrors one plane of each neighbour.  The work items that
+// compute the first (last) owned plane also store it into the neighbour's halo
+// plane over NVLink, and each consumer warp then bumps the neighbour's
+// delivery counter with a release at system scope; the producer acquires that
+// counter before it stages a halo plane.  Those edge items come first in
+// every sweep.  TMA only ever reads this GPU's own memory.
+//
 // Generic path: one launch per sweep, one thread per cell (x fastest), any
 // strides; residual partials combined by the last block in block order.
 #include <cuda.h>
@@ -81,7 +89,36 @@ __global__ void __launch_bounds__(256) jacobi3d_sweep_generic_kernel(
   }
 }
 
+// Seeded synthetic 3-D input: cell (gz, y, x) of the global g_d x h x w grid
+// is uniform [0, 1) from the counter hash of (seed, gz * h + y, x); global
+// boundary cells and planes outside [0, g_d) are 0.
+__global__ void __launch_bounds__(256) fill_jacobi3d_input_kernel(float *p, long long sz, long long sy,
+                                                                  long long planes, long long h, long long w,
+                                                                  long long g_z0, long long g_d, uint64_t seed) {
+  const long long nth = (long long)gridDim.x * blockDim.x;
+  const long long total = planes * h * w;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += nth) {
+    const long long z = idx / (h * w), rem = idx - z * h * w;
+    const long long y = rem / w, x = rem - y * w;
+    const long long gz = g_z0 + z;
+    const bool interior = gz > 0 && gz < g_d - 1 && y > 0 && y < h - 1 && x > 0 && x < w - 1;
+    p[z * sz + y * sy + x] = interior ? hash_uniform(seed, (uint64_t)(gz * h + y), (uint64_t)x) : 0.0f;
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_fill_jacobi3d_input(float *p, int64_t sz, int64_t sy, int64_t planes, int64_t h, int64_t w,
+                                       int64_t g_z0, int64_t g_d, uint64_t seed, cudaStream_t s) {
+  if (planes <= 0 || h <= 0 || w <= 0) return cudaSuccess;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  long long g = (planes * h * w + 255) / 256;
+  const long long cap = (long long)num_sms(dev) * 8;
+  if (g > cap) g = cap;
+  fill_jacobi3d_input_kernel<<<(unsigned)g, 256, 0, s>>>(p, sz, sy, planes, h, w, g_z0, g_d, seed);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_jacobi3d_generic(const Jacobi3dProblem &p, cudaStream_t s) {
   int dev = 0;
@@ -146,13 +183,55 @@ constexpr size_t SMEM3_BYTES = (size_t)ST3 * PLANE_STRIDE + sizeof(Smem3Tail) + 
 struct J3Kernel {
   float *u, *v;
   long long sy, sz;  // strides in elements (x contiguous)
-  int d, h, w;
+  int d, h, w;       // local planes, rows, columns
+  int z_lo, z_hi;    // local planes updated by a sweep
+  long long g_z0, g_d;  // global plane of local plane 0, global plane count
   int tiles_x, tiles_y, zchunks;
   int sweeps, res_every;
   double *res_out;
   JacobiWs *ws;
-  unsigned long long budget_ns;
+  unsigned long long budget_ns, peer_budget_ns;
+  SlabPeers peers;
+  int halo;  // 1 in z-slab mode, 0 on one GPU
 };
+
+// Work item t -> (zc, tx, ty).  One GPU: z-chunk fastest.  z-slab mode: the
+// first and last z-chunks (the items a neighbour waits for) come first.
+__device__ __forceinline__ void item_coords3(const J3Kernel &k, int t, int &zc, int &tx, int &ty) {
+  const int txy = k.tiles_x * k.tiles_y;
+  int rest;
+  if (k.halo > 0 && k.zchunks > 2) {
+    if (t < 2 * txy) {
+      zc = t < txy ? 0 : k.zchunks - 1;
+      rest = t < txy ? t : t - txy;
+    } else {
+      const int u = t - 2 * txy;
+      zc = 1 + u % (k.zchunks - 2);
+      rest = u / (k.zchunks - 2);
+    }
+  } else {
+    zc = t % k.zchunks;
+    rest = t / k.zchunks;
+  }
+  tx = rest % k.tiles_x;
+  ty = rest / k.tiles_x;
+}
+
+// Residual r: the CTA partials in CTA order (producer warp of CTA 0); in
+// z-slab mode also all-gathered into every rank's slot array.
+__device__ __forceinline__ void combine3(const J3Kernel &k, int r, int lane) {
+  double p = 0.0;
+  for (int i = lane; i < (int)gridDim.x; i += 32) p = __dadd_rn(p, __ldcg(&k.ws->partial[r & 1][i]));
+  p = warp_sum_f64(p);
+  if (lane == 0) {
+    if (k.res_out) k.res_out[r] = p;
+    if (k.peers.peer_ws[0] && r < kMaxResSlots) {
+      for (int q = 0; q < k.peers.nranks; ++q)
+        if (k.peers.peer_ws[q]) k.peers.peer_ws[q]->res_slots[r][k.peers.rank] = p;
+      __threadfence_system();
+    }
+  }
+}
 
 __device__ __forceinline__ void record3(JacobiWs *ws, volatile int *abort, int code) {
   atomicCAS(&ws->status, 0, code);
@@ -160,10 +239,10 @@ __device__ __forceinline__ void record3(JacobiWs *ws, volatile int *abort, int c
 }
 
 __device__ __forceinline__ bool wait_counter3(const unsigned *p, unsigned target, volatile int *abort,
-                                              unsigned long long budget, const JacobiWs *ws) {
+                                              unsigned long long budget, const JacobiWs *ws, bool sys = false) {
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t i = 0;; ++i) {
-    if ((int)(ld_acquire_gpu(p) - target) >= 0) return true;
+    if ((int)((sys ? ld_acquire_sys(p) : ld_acquire_gpu(p)) - target) >= 0) return true;
     if (*abort) return false;
     if ((i & 7u) == 7u && *reinterpret_cast<const volatile int *>(&ws->status) != 0) return false;
     if (globaltimer_ns() - t0 > budget) return false;
@@ -186,6 +265,17 @@ __device__ __forceinline__ bool consumers3_any(bool pred) {
 
 __device__ __forceinline__ float4 ld4s(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 
+// Stores the 4 cells at columns gx0..gx0+3 of a row, masked to the grid width.
+__device__ __forceinline__ void store4_w(float *p, int gx0, int w, float4 o) {
+  if (gx0 + 3 < w) {
+    st_f4(p, o);
+  } else {
+    if (gx0 < w) p[0] = o.x;
+    if (gx0 + 1 < w) p[1] = o.y;
+    if (gx0 + 2 < w) p[2] = o.z;
+  }
+}
+
 __device__ __forceinline__ float j7(float c, float xm, float xp, float ym, float yp, float zm, float zp) {
   float t = __fadd_rn(c, xm);
   t = __fadd_rn(t, xp);
@@ -196,17 +286,22 @@ __device__ __forceinline__ float j7(float c, float xm, float xp, float ym, float
   return __fmul_rn(t, 1.0f / 7.0f);
 }
 
+// SLAB: z-slab mode (peer waits, halo deliveries); the one-GPU instantiation
+// carries none of that code.
+template <bool SLAB>
 __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
     const __grid_constant__ CUtensorMap map_u, const __grid_constant__ CUtensorMap map_v,
     const __grid_constant__ J3Kernel k) {
   extern __shared__ __align__(128) unsigned char smem3_raw[];
-  unsigned char *smem = reinterpret_cast<unsigned char *>(
-      (reinterpret_cast<uintptr_t>(smem3_raw) + 127) & ~uintptr_t(127));
+  // Aligned by pointer arithmetic on the shared array, so shared-space
+  // addressing (LDS) survives for everything derived from it.
+  unsigned char *smem = smem3_raw + ((128u - (smem_u32(smem3_raw) & 127u)) & 127u);
   Smem3Tail *tail = reinterpret_cast<Smem3Tail *>(smem + (size_t)ST3 * PLANE_STRIDE);
   volatile int *abort = &tail->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x;
   const int T = k.tiles_x * k.tiles_y * k.zchunks;
+  const unsigned per_sweep = (unsigned)(k.tiles_x * k.tiles_y * CW3);  // deliveries per neighbour per sweep
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST3; ++i) {
@@ -236,19 +331,32 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
-        if (blockIdx.x == 0 && k.res_every > 0 && s % k.res_every == 0) {
-          const int r = s / k.res_every - 1;
-          double p = 0.0;
-          for (int i = lane; i < G; i += 32) p = __dadd_rn(p, __ldcg(&k.ws->partial[r & 1][i]));
-          p = warp_sum_f64(p);
-          if (lane == 0 && k.res_out) k.res_out[r] = p;
-        }
+        if (blockIdx.x == 0 && k.res_every > 0 && s % k.res_every == 0) combine3(k, s / k.res_every - 1, lane);
       }
       if (lane == 0) {
         for (int t = blockIdx.x; t < T && ok; t += G) {
-          const int zc = t % k.zchunks, rest = t / k.zchunks;
-          const int tx = rest % k.tiles_x, ty = rest / k.tiles_x;
-          const int z0 = zc * BZ3;
+          int zc, tx, ty;
+          item_coords3(k, t, zc, tx, ty);
+          const int z0 = k.z_lo + zc * BZ3;
+          if constexpr (SLAB) {
+            // a halo plane is staged only once the neighbour delivered it for
+            // every earlier sweep; the proxy fence orders that acquire before
+            // the TMA (async-proxy) read of the peer-written plane
+            const unsigned need = (unsigned)s * per_sweep;
+            const bool wait_up = k.peers.up_flag && z0 - 1 < k.z_lo;
+            const bool wait_dn = k.peers.dn_flag && z0 + BZ3 >= k.z_hi;
+            if (wait_up && !wait_counter3(&k.ws->from_above, need, abort, k.peer_budget_ns, k.ws, true)) {
+              record3(k.ws, abort, kDevTimeoutPeer);
+              ok = false;
+              break;
+            }
+            if (wait_dn && !wait_counter3(&k.ws->from_below, need, abort, k.peer_budget_ns, k.ws, true)) {
+              record3(k.ws, abort, kDevTimeoutPeer);
+              ok = false;
+              break;
+            }
+            if (wait_up || wait_dn) fence_proxy_async_global();
+          }
           for (int l = 0; l < BZ3 + 2; ++l) {
             const uint32_t st = pc % ST3, ph = (pc / ST3) & 1u;
             if (!mbar_wait_bounded(&tail->empty[st], ph ^ 1u, abort)) {
@@ -273,13 +381,7 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
         ok = false;
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (ok) {
-        const int r = k.sweeps / k.res_every - 1;
-        double p = 0.0;
-        for (int i = lane; i < G; i += 32) p = __dadd_rn(p, __ldcg(&k.ws->partial[r & 1][i]));
-        p = warp_sum_f64(p);
-        if (lane == 0 && k.res_out) k.res_out[r] = p;
-      }
+      if (ok) combine3(k, k.sweeps / k.res_every - 1, lane);
     }
     if (!ok && lane == 0) {
       const uint32_t n = pc < (uint32_t)ST3 ? pc : (uint32_t)ST3;
@@ -300,12 +402,13 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
   double acc = 0.0;
   for (int s = 0; s < k.sweeps; ++s) {
     float *dst = (s & 1) ? k.u : k.v;
+    const bool has_up = SLAB && k.peers.up_u != nullptr, has_dn = SLAB && k.peers.dn_u != nullptr;
     const bool want = k.res_every > 0 && ((s + 1) % k.res_every == 0);
     bool ok = true;
     for (int t = blockIdx.x; t < T && ok; t += G) {
-      const int zc = t % k.zchunks, rest = t / k.zchunks;
-      const int tx = rest % k.tiles_x, ty = rest / k.tiles_x;
-      const int z0 = zc * BZ3;
+      int zc, tx, ty;
+      item_coords3(k, t, zc, tx, ty);
+      const int z0 = k.z_lo + zc * BZ3;
       const int gx0 = tx * BW3 + 4 * lane;
       const int y0 = ty * BH3 + r0;
       // planes 0 (z0-1) and 1 (z0) of this item
@@ -342,8 +445,10 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
         float4 zp[RPW3];
 #pragma unroll
         for (int q = 0; q < RPW3; ++q) zp[q] = ld4s(Pp + (r0 + q + 1) * BOXW3 + sc);
-        if (z < k.d) {
-          const bool zb = (z == 0 || z == k.d - 1);
+        const bool to_up = has_up && z == k.z_lo, to_dn = has_dn && z == k.z_hi - 1;
+        if (z < k.z_hi) {
+          const long long gz = k.g_z0 + z;
+          const bool zb = (gz == 0 || gz == k.g_d - 1);
 #pragma unroll
           for (int q = 0; q < RPW3; ++q) {
             const int y = y0 + q;
@@ -371,19 +476,35 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
                 if (gx0 + 2 == wl) o.z = cc.z;
                 if (gx0 + 3 == wl) o.w = cc.w;
               }
-              float *drow = dst + (long long)z * k.sz + (long long)y * k.sy + gx0;
-              if (gx0 + 3 < k.w) {
-                st_f4(drow, o);
-              } else {
-                if (gx0 < k.w) drow[0] = o.x;
-                if (gx0 + 1 < k.w) drow[1] = o.y;
-                if (gx0 + 2 < k.w) drow[2] = o.z;
-              }
+              store4_w(dst + (long long)z * k.sz + (long long)y * k.sy + gx0, gx0, k.w, o);
               if (want) {
                 if (gx0 < k.w) acc = __dadd_rn(acc, __dmul_rn(__dsub_rn((double)o.x, (double)cc.x), __dsub_rn((double)o.x, (double)cc.x)));
                 if (gx0 + 1 < k.w) acc = __dadd_rn(acc, __dmul_rn(__dsub_rn((double)o.y, (double)cc.y), __dsub_rn((double)o.y, (double)cc.y)));
                 if (gx0 + 2 < k.w) acc = __dadd_rn(acc, __dmul_rn(__dsub_rn((double)o.z, (double)cc.z), __dsub_rn((double)o.z, (double)cc.z)));
                 if (gx0 + 3 < k.w) acc = __dadd_rn(acc, __dmul_rn(__dsub_rn((double)o.w, (double)cc.w), __dsub_rn((double)o.w, (double)cc.w)));
+              }
+            }
+          }
+          if constexpr (SLAB) {
+            if (to_up || to_dn) {
+              // An edge plane of the slab: copy the cells this thread just
+              // stored (its own writes, L2-resident) into the neighbour's halo
+              // plane; the plane loop above stays free of peer-store tests.
+              float *up_dst = (s & 1) ? k.peers.up_u : k.peers.up_v;
+              float *dn_dst = (s & 1) ? k.peers.dn_u : k.peers.dn_v;
+#pragma unroll 1
+              for (int q = 0; q < RPW3; ++q) {
+                const int y = y0 + q;
+                if (y >= k.h || gx0 >= k.w) continue;
+                const long long yo = (long long)y * k.sy + gx0;
+                const float *mine = dst + (long long)z * k.sz + yo;
+                float4 o;
+                o.x = mine[0];
+                o.y = gx0 + 1 < k.w ? mine[1] : 0.0f;
+                o.z = gx0 + 2 < k.w ? mine[2] : 0.0f;
+                o.w = gx0 + 3 < k.w ? mine[3] : 0.0f;
+                if (to_up) store4_w(up_dst + k.peers.up_row * k.sz + yo, gx0, k.w, o);
+                if (to_dn) store4_w(dn_dst + k.peers.dn_row * k.sz + yo, gx0, k.w, o);
               }
             }
           }
@@ -394,7 +515,14 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
           c[q] = zp[q];
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tail->empty[(pz - 1) % ST3]);  // plane z-1 is no longer needed
+        if (lane == 0) {
+          mbar_arrive(&tail->empty[(pz - 1) % ST3]);  // plane z-1 is no longer needed
+          if (SLAB && (to_up || to_dn)) {  // this warp's rows of a neighbour's halo plane are stored
+            __threadfence_system();
+            if (to_up) red_release_sys_add(k.peers.up_flag, 1u);
+            if (to_dn) red_release_sys_add(k.peers.dn_flag, 1u);
+          }
+        }
       }
       if (!ok) break;
       __syncwarp();
@@ -409,6 +537,7 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
       if (lane == 0) tail->wsum[s & 1][cw] = wv;
       acc = 0.0;
     }
+    fence_proxy_async_global();  // this sweep's stores before the next sweep's TMA reads
     __syncwarp();
     const bool fail = consumers3_any(!ok || *abort);
     if (fail) break;
@@ -433,7 +562,8 @@ bool jacobi3d_tma_ok(const Jacobi3dProblem &p) {
          p.d < (1ll << 30) && p.sz < (1ll << 37) && p.sweeps <= (1ll << 30);
 }
 
-cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, cudaStream_t s, int *grid_out) {
+cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, const SlabPeers &peers, cudaStream_t s,
+                                       int *grid_out) {
   CUtensorMap mu, mv;
   const uint64_t dims[3] = {(uint64_t)p.w, (uint64_t)p.h, (uint64_t)p.d};
   const uint64_t strides[2] = {(uint64_t)p.sy * 4u, (uint64_t)p.sz * 4u};
@@ -448,27 +578,35 @@ cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, cudaStream_t s,
   k.d = (int)p.d;
   k.h = (int)p.h;
   k.w = (int)p.w;
+  k.z_lo = (int)p.z_lo;
+  k.z_hi = (int)(p.z_hi < 0 ? p.d : p.z_hi);
+  k.g_z0 = p.g_z0;
+  k.g_d = p.g_d < 0 ? p.d : p.g_d;
+  k.halo = p.halo;
+  k.peers = peers;
   k.tiles_x = (int)((p.w + BW3 - 1) / BW3);
   k.tiles_y = (int)((p.h + BH3 - 1) / BH3);
-  k.zchunks = (int)((p.d + BZ3 - 1) / BZ3);
+  k.zchunks = (k.z_hi - k.z_lo + BZ3 - 1) / BZ3;
   k.sweeps = (int)p.sweeps;
   k.res_every = (int)p.res_every;
   k.res_out = p.res_out;
   k.ws = p.ws;
   k.budget_ns = wait_budget_ns(false);
+  k.peer_budget_ns = wait_budget_ns(true);
 
-  static thread_local int configured_dev = -1;
+  const bool slab = peers.up_u != nullptr || peers.dn_u != nullptr;  // a neighbour exists
+  auto kernel = slab ? jacobi3d_persistent_kernel<true> : jacobi3d_persistent_kernel<false>;
+  static thread_local int configured_dev[2] = {-1, -1};
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t e;
-  if (configured_dev != dev) {
-    e = cudaFuncSetAttribute(jacobi3d_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)SMEM3_BYTES);
+  if (configured_dev[slab] != dev) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM3_BYTES);
     if (e != cudaSuccess) return e;
-    configured_dev = dev;
+    configured_dev[slab] = dev;
   }
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, jacobi3d_persistent_kernel, THREADS3, SMEM3_BYTES);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, THREADS3, SMEM3_BYTES);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   long long g = (long long)per_sm * num_sms(dev);
@@ -486,7 +624,7 @@ cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, cudaStream_t s,
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, jacobi3d_persistent_kernel, mu, mv, k);
+  return cudaLaunchKernelEx(&cfg, kernel, mu, mv, k);
 }
 
 }  // namespace spmdb200

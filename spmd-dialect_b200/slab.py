@@ -1,16 +1,21 @@
-"""Row-slab Jacobi-2D on several GPUs: one process per GPU.
+"""Slab decompositions across GPUs: row slabs for Jacobi-2D, plane (z) slabs
+for Jacobi-3D.  One process per GPU.
 
 torch.distributed is plumbing only (exchanging CUDA IPC handles, the
 rendezvous before each launch, gathering results for tests).  The data path --
-four halo rows up and four down per pass (a pass advances up to four sweeps),
-and the residual all-gather every `res_every` sweeps -- runs inside the
-persistent kernel over NVLink
-(spmdb200_jacobi2d_slab): no NCCL call sits between sweeps.
+the halo exchange and the residual all-gather every `res_every` sweeps -- runs
+inside the persistent kernels over NVLink (spmdb200_jacobi2d_slab,
+spmdb200_jacobi3d_slab): no NCCL call sits between sweeps.
 
-Decomposition: the G x W global grid is cut into contiguous row blocks; rank p
-owns global rows [g_first, g_first + rows) and keeps a (rows + 8) x pitch local
-array whose first and last HALO = 4 rows mirror the neighbours' edge rows (four
-rows deep, because the kernel fuses up to four sweeps per pass).
+Jacobi-2D: the G x W global grid is cut into contiguous row blocks; rank p owns
+global rows [g_first, g_first + rows) and keeps a (rows + 8) x pitch local
+array whose first and last HALO = 4 rows mirror the neighbours' edge rows
+(four rows deep, because the kernel fuses up to four sweeps per pass; four
+rows move up and four down per pass).
+
+Jacobi-3D: the D x H x W grid is cut into contiguous plane blocks; rank p owns
+planes [g_first, g_first + planes) plus HALO3 = 1 halo plane on each side (one
+sweep per pass, one plane up and one down per sweep).
 """
 from __future__ import annotations
 
@@ -21,7 +26,8 @@ import numpy as np
 
 from ._lib import c_i, c_p, call, lib
 
-HALO = 4  # halo rows on each side of a slab (kSlabHalo in the C library)
+HALO = 4  # halo rows on each side of a 2-D slab (kSlabHalo in the C library)
+HALO3 = 1  # halo planes on each side of a 3-D slab (kSlabHalo3)
 
 
 # ---------------------------------------------------------------- decomposition
@@ -99,42 +105,37 @@ def rendezvous() -> None:
         d.barrier()
 
 
-class SlabJacobi2D:
-    """This rank's share of a multi-GPU Jacobi-2D run.
+class _SlabJob:
+    """Plumbing shared by the row-slab (2-D) and plane-slab (3-D) jobs: the split
+    axis holds `G` global units (rows or planes); this rank owns `rows` of them
+    from `g_first` and keeps `local_rows = rows + 2 * halo` units locally, each
+    `unit_shape` floats (a padded row, or a plane of padded rows)."""
 
-    G x cols global grid (G defaults to rows_per_rank * world: weak scaling).
-    `init` is None (seeded synthetic input generated on the device, identical
-    to what a single-GPU run of the same global grid would see) or the full
-    global grid as a numpy array (tests)."""
+    halo: int
+    entry: str
+    unit_shape: tuple
 
-    def __init__(self, cols: int, rows_per_rank: int | None = None, G: int | None = None, seed: int = 4,
-                 res_every: int = 10, init: np.ndarray | None = None):
+    def _setup(self, G: int, res_every: int, seed: int, init: np.ndarray | None) -> None:
         import torch
         d = _dist()
         self.rank = d.get_rank() if d else 0
         self.world = d.get_world_size() if d else 1
-        if G is None:
-            if rows_per_rank is None:
-                raise ValueError("give rows_per_rank or G")
-            G = rows_per_rank * self.world
-        self.G, self.cols, self.res_every = G, cols, res_every
+        self.G, self.res_every = G, res_every
         self.g_first, self.rows = partition(G, self.world, self.rank)
-        if self.rows < HALO:
-            raise ValueError(f"each rank needs >= {HALO} rows (rank {self.rank} has {self.rows})")
-        self.pitch = pitch_for(cols)
-        self.local_rows = self.rows + 2 * HALO
-        nbytes = self.local_rows * self.pitch * 4
+        if self.rows < self.halo:
+            raise ValueError(f"each rank needs >= {self.halo} units (rank {self.rank} has {self.rows})")
+        self.local_rows = self.rows + 2 * self.halo
+        self.unit_floats = int(np.prod(self.unit_shape))
+        nbytes = self.local_rows * self.unit_floats * 4
         self._u = DeviceBuffer(nbytes)
         self._v = DeviceBuffer(nbytes)
         self._ws = DeviceBuffer(int(lib().spmdb200_jacobi_workspace_bytes()))
         self.sweeps_done = 0
         self._nres_last = 0
-        stream = c_p(torch.cuda.current_stream().cuda_stream)
         if init is None:
-            call("spmdb200_fill_jacobi_input", c_p(self._u.ptr), c_i(self.pitch), c_i(self.local_rows),
-                 c_i(cols), c_i(self.g_first - HALO), c_i(G), ctypes.c_uint64(seed), stream)
-            call("spmdb200_fill_jacobi_input", c_p(self._v.ptr), c_i(self.pitch), c_i(self.local_rows),
-                 c_i(cols), c_i(self.g_first - HALO), c_i(G), ctypes.c_uint64(seed), stream)
+            stream = c_p(torch.cuda.current_stream().cuda_stream)
+            for buf in (self._u, self._v):
+                self._fill(buf.ptr, seed, stream)
         else:
             self.load_global(init)
         torch.cuda.current_stream().synchronize()
@@ -166,25 +167,29 @@ class SlabJacobi2D:
         return p
 
     # ---------------------------------------------------------------- data movement
-    def _desc(self, ptr: int) -> tuple:
-        p = c_p(ptr)
-        return (p, p, c_i(0), c_i(self.local_rows), c_i(self.cols), c_i(self.pitch), c_i(1))
+    def _trim(self, local: np.ndarray) -> np.ndarray:
+        """Owned units of a host copy of the local array, padding columns removed."""
+        raise NotImplementedError
+
+    def _pad(self, block: np.ndarray) -> np.ndarray:
+        """Global units (unpadded) -> the local layout's padded units."""
+        raise NotImplementedError
 
     def load_global(self, grid: np.ndarray) -> None:
-        """Copies this rank's rows (+ halos) of a global G x cols grid into U (and V)."""
-        lo, hi = local_row_range(self.G, self.world, self.rank)
-        local = np.zeros((self.local_rows, self.pitch), np.float32)
+        """Copies this rank's units (+ halos) of the global grid into U (and V)."""
+        lo, hi = self.g_first - self.halo, self.g_first + self.rows + self.halo
+        local = np.zeros((self.local_rows,) + self.unit_shape, np.float32)
         src_lo, src_hi = max(lo, 0), min(hi, self.G)
-        local[src_lo - lo:src_hi - lo, :self.cols] = grid[src_lo:src_hi]
+        local[src_lo - lo:src_hi - lo] = self._pad(np.asarray(grid[src_lo:src_hi], np.float32))
         for buf in (self._u, self._v):
             call("spmdb200_memcpy", c_p(buf.ptr), local.ctypes.data_as(c_p), ctypes.c_size_t(local.nbytes), None)
         self.sweeps_done = 0
 
     def local_owned(self) -> np.ndarray:
-        """This rank's owned rows of the current grid (host copy)."""
-        local = np.empty((self.local_rows, self.pitch), np.float32)
+        """This rank's owned units of the current grid (host copy)."""
+        local = np.empty((self.local_rows,) + self.unit_shape, np.float32)
         call("spmdb200_memcpy", local.ctypes.data_as(c_p), c_p(self._u.ptr), ctypes.c_size_t(local.nbytes), None)
-        return local[HALO:HALO + self.rows, :self.cols].copy()
+        return self._trim(local[self.halo:self.halo + self.rows])
 
     def gather(self) -> np.ndarray | None:
         """The full global grid on rank 0 (None elsewhere)."""
@@ -205,7 +210,7 @@ class SlabJacobi2D:
         torch.cuda.current_stream().synchronize()
         rendezvous()  # every workspace is clear before any kernel can deliver a halo
         up, dn = self._up, self._dn
-        call("spmdb200_jacobi2d_slab", *self._desc(self._u.ptr), *self._desc(self._v.ptr), c_i(self.g_first),
+        call(self.entry, *self._desc(self._u.ptr), *self._desc(self._v.ptr), c_i(self.g_first),
              c_i(self.G), c_i(sweeps), c_i(self.res_every), c_p(0), c_p(self._ws.ptr),
              c_p(up.u or None), c_p(up.v or None), c_p(up.ws or None), c_i(self._up_rows),
              c_p(dn.u or None), c_p(dn.v or None), c_p(dn.ws or None),
@@ -236,19 +241,19 @@ class SlabJacobi2D:
         return out[:self._nres_last]
 
     def run_host(self, host_local: np.ndarray, sweeps: int) -> np.ndarray:
-        """End to end on host memory: host_local is this rank's (rows + 8) x pitch
-        slab (pinned for full speed); copied in, `sweeps` sweeps, owned rows
-        copied back into host_local[HALO:HALO + rows]."""
-        if host_local.shape != (self.local_rows, self.pitch) or host_local.dtype != np.float32:
-            raise ValueError("host slab must be (rows + 2 * HALO) x pitch float32")
-        # Only U needs the input: V's owned rows are all written by sweep 0 and
-        # its halo rows by the neighbours before anyone reads them.
+        """End to end on host memory: host_local is this rank's local array
+        (local_rows x unit_shape, pinned for full speed); copied in, `sweeps`
+        sweeps, owned units copied back into host_local[halo:halo + rows]."""
+        if host_local.shape != (self.local_rows,) + self.unit_shape or host_local.dtype != np.float32:
+            raise ValueError(f"host slab must be {(self.local_rows,) + self.unit_shape} float32")
+        # Only U needs the input: V's owned units are all written by the first
+        # sweep and its halo units by the neighbours before anyone reads them.
         call("spmdb200_memcpy", c_p(self._u.ptr), host_local.ctypes.data_as(c_p),
              ctypes.c_size_t(host_local.nbytes), None)
         self.run(sweeps, check=True)
-        row = self.pitch * 4
-        call("spmdb200_memcpy", c_p(host_local.ctypes.data + HALO * row), c_p(self._u.ptr + HALO * row),
-             ctypes.c_size_t(self.rows * row), None)
+        unit = self.unit_floats * 4
+        call("spmdb200_memcpy", c_p(host_local.ctypes.data + self.halo * unit), c_p(self._u.ptr + self.halo * unit),
+             ctypes.c_size_t(self.rows * unit), None)
         return host_local
 
     def close(self) -> None:
@@ -263,14 +268,99 @@ class SlabJacobi2D:
             b.close()
 
 
-def e2e_measure(job: SlabJacobi2D, sweeps: int, reps: int = 2) -> dict:
+class SlabJacobi2D(_SlabJob):
+    """This rank's share of a multi-GPU Jacobi-2D run (row slabs, spmdb200_jacobi2d_slab).
+
+    G x cols global grid (G defaults to rows_per_rank * world: weak scaling).
+    `init` is None (seeded synthetic input generated on the device, identical
+    to what a single-GPU run of the same global grid would see) or the full
+    global grid as a numpy array (tests)."""
+
+    halo = HALO
+    entry = "spmdb200_jacobi2d_slab"
+
+    def __init__(self, cols: int, rows_per_rank: int | None = None, G: int | None = None, seed: int = 4,
+                 res_every: int = 10, init: np.ndarray | None = None):
+        d = _dist()
+        world = d.get_world_size() if d else 1
+        if G is None:
+            if rows_per_rank is None:
+                raise ValueError("give rows_per_rank or G")
+            G = rows_per_rank * world
+        self.cols = cols
+        self.pitch = pitch_for(cols)
+        self.unit_shape = (self.pitch,)
+        self._setup(G, res_every, seed, init)
+
+    def _fill(self, ptr: int, seed: int, stream) -> None:
+        call("spmdb200_fill_jacobi_input", c_p(ptr), c_i(self.pitch), c_i(self.local_rows), c_i(self.cols),
+             c_i(self.g_first - self.halo), c_i(self.G), ctypes.c_uint64(seed), stream)
+
+    def _desc(self, ptr: int) -> tuple:
+        p = c_p(ptr)
+        return (p, p, c_i(0), c_i(self.local_rows), c_i(self.cols), c_i(self.pitch), c_i(1))
+
+    def _trim(self, local: np.ndarray) -> np.ndarray:
+        return local[:, :self.cols].copy()
+
+    def _pad(self, block: np.ndarray) -> np.ndarray:
+        out = np.zeros((block.shape[0], self.pitch), np.float32)
+        out[:, :self.cols] = block
+        return out
+
+
+class SlabJacobi3D(_SlabJob):
+    """This rank's share of a multi-GPU Jacobi-3D run (z-slabs,
+    spmdb200_jacobi3d_slab): D x H x W global grid split into contiguous plane
+    blocks, one halo plane on each side (HALO3).  Same API as SlabJacobi2D."""
+
+    halo = HALO3
+    entry = "spmdb200_jacobi3d_slab"
+
+    def __init__(self, H: int, W: int, planes_per_rank: int | None = None, D: int | None = None, seed: int = 3,
+                 res_every: int = 10, init: np.ndarray | None = None):
+        d = _dist()
+        world = d.get_world_size() if d else 1
+        if D is None:
+            if planes_per_rank is None:
+                raise ValueError("give planes_per_rank or D")
+            D = planes_per_rank * world
+        self.H, self.cols = H, W
+        self.pitch = pitch_for(W)
+        self.unit_shape = (H, self.pitch)
+        self._setup(D, res_every, seed, init)
+
+    @property
+    def planes(self) -> int:
+        return self.rows
+
+    def _fill(self, ptr: int, seed: int, stream) -> None:
+        call("spmdb200_fill_jacobi3d_input", c_p(ptr), c_i(self.H * self.pitch), c_i(self.pitch),
+             c_i(self.local_rows), c_i(self.H), c_i(self.cols), c_i(self.g_first - self.halo), c_i(self.G),
+             ctypes.c_uint64(seed), stream)
+
+    def _desc(self, ptr: int) -> tuple:
+        p = c_p(ptr)
+        return (p, p, c_i(0), c_i(self.local_rows), c_i(self.H), c_i(self.cols), c_i(self.H * self.pitch),
+                c_i(self.pitch), c_i(1))
+
+    def _trim(self, local: np.ndarray) -> np.ndarray:
+        return local[:, :, :self.cols].copy()
+
+    def _pad(self, block: np.ndarray) -> np.ndarray:
+        out = np.zeros((block.shape[0], self.H, self.pitch), np.float32)
+        out[:, :, :self.cols] = block
+        return out
+
+
+def e2e_measure(job: _SlabJob, sweeps: int, reps: int = 2) -> dict:
     """Whole-job end-to-end rate through SlabJacobi2D.run_host with pinned host
     slabs (H2D + sweeps + D2H timed on every rank, max over ranks)."""
     import time
 
     import torch
     d = _dist()
-    host = torch.empty((job.local_rows, job.pitch), dtype=torch.float32, pin_memory=True)
+    host = torch.empty((job.local_rows,) + job.unit_shape, dtype=torch.float32, pin_memory=True)
     arr = host.numpy()
     arr[:] = 0.0
     job.run_host(arr, 2)  # warm-up
@@ -284,7 +374,8 @@ def e2e_measure(job: SlabJacobi2D, sweeps: int, reps: int = 2) -> dict:
     if d is not None and job.world > 1:
         d.all_reduce(t, op=d.ReduceOp.MAX)
     secs = float(t.item())
-    return {"value": round(job.G * job.cols * sweeps / secs / 1e9, 3), "unit": "Gcell-updates/s",
-            "h2d_bytes_per_step": job.local_rows * job.pitch * 4,
-            "d2h_bytes_per_step": job.rows * job.pitch * 4,
-            "entry": "SlabJacobi2D.run_host (pinned host slab per rank)"}
+    cells = job.G * job.cols * (job.H if isinstance(job, SlabJacobi3D) else 1)
+    return {"value": round(cells * sweeps / secs / 1e9, 3), "unit": "Gcell-updates/s",
+            "h2d_bytes_per_step": job.local_rows * job.unit_floats * 4,
+            "d2h_bytes_per_step": job.rows * job.unit_floats * 4,
+            "entry": f"{type(job).__name__}.run_host (pinned host slab per rank)"}

@@ -1,9 +1,9 @@
 """One rank of the 2-GPU slab parity test (launched by test_gpu_slab.py via torchrun).
 
-Every rank builds the same seeded global grid, runs its row slab on its own
-GPU (halo rows stored into the neighbour over NVLink inside the kernel), and
-rank 0 compares the gathered grid and the all-gathered residuals with the
-single-domain oracle."""
+Every rank builds the same seeded global grid, runs its row slab (Jacobi-2D)
+or plane slab (Jacobi-3D) on its own GPU (halo rows / planes stored into the
+neighbour over NVLink inside the kernel), and rank 0 compares the gathered
+grid and the all-gathered residuals with the single-domain oracle."""
 from __future__ import annotations
 
 import os
@@ -43,6 +43,22 @@ def main() -> None:
             same = np.array_equal(grid.view(np.uint32), want.view(np.uint32))
             rel = np.max(np.abs(res - wres) / np.abs(wres)) if wres.size else 0.0
             print(f"G={G} W={W} sweeps={sweeps}: grid bit-exact={same} residual max rel err={rel:.3g}", flush=True)
+            ok = ok and same and rel <= 1e-12
+    # Jacobi-3D z-slabs: one halo plane each side, one plane up and down per sweep.
+    for (D, H, W, sweeps, res_every) in [(37, 20, 150, 7, 2), (64, 64, 130, 10, 5), (5, 9, 11, 3, 1)]:
+        u0 = jacobi_init((D, H, W), 3)
+        job = slab.SlabJacobi3D(H=H, W=W, D=D, res_every=res_every, init=u0)
+        job.run(sweeps)
+        res = job.residuals()
+        grid = job.gather()
+        job.close()
+        if rank == 0:
+            from oracle import oracle
+            want, wres = oracle.jacobi3d(u0, sweeps, res_every)
+            same = np.array_equal(grid.view(np.uint32), want.view(np.uint32))
+            rel = np.max(np.abs(res - wres) / np.abs(wres)) if wres.size else 0.0
+            print(f"D={D} H={H} W={W} sweeps={sweeps}: grid bit-exact={same} residual max rel err={rel:.3g}",
+                  flush=True)
             ok = ok and same and rel <= 1e-12
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.broadcast(flag, 0)

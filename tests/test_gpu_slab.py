@@ -4,8 +4,10 @@
 * a bounded peer wait that nothing satisfies (a neighbour whose delivery
   counter is never bumped) ends the kernel with SPMDB200_ERR_TIMEOUT, and the
   context stays usable for the next launch;
+* the same for Jacobi-3D z-slabs (one rank; a fake neighbour below);
 * with >= 2 GPUs, 2 ranks (torchrun, NCCL plumbing, NVLink halo stores inside
-  the kernel) reproduce the single-domain oracle bit for bit."""
+  the kernel) reproduce the single-domain oracle bit for bit, for row slabs
+  and z-slabs."""
 from __future__ import annotations
 
 import ctypes
@@ -46,6 +48,31 @@ def test_single_rank_seeded_fill_is_deterministic(kernels):
     assert 0.4 < float(ga[1:-1, 1:-1].mean()) < 0.6
 
 
+def test_single_rank_zslab_matches_oracle(kernels, oracle_mod):
+    slab = spmd_mod("slab")
+    u0 = jacobi_init((21, 40, 300), 3)
+    job = slab.SlabJacobi3D(H=40, W=300, D=21, res_every=3, init=u0)
+    job.run(7)
+    res = job.residuals()
+    got = job.gather()
+    job.close()
+    want, wres = oracle_mod.jacobi3d(u0, 7, 3)
+    assert_bits_equal(got, want, "z-slab world=1")
+    np.testing.assert_allclose(res, wres, rtol=1e-12)
+
+
+def test_zslab_seeded_fill_is_deterministic(kernels):
+    slab = spmd_mod("slab")
+    a = slab.SlabJacobi3D(H=17, W=33, D=9, seed=3)
+    b = slab.SlabJacobi3D(H=17, W=33, D=9, seed=3)
+    ga, gb = a.gather(), b.gather()
+    a.close()
+    b.close()
+    assert_bits_equal(ga, gb)
+    assert ga[0].max() == 0 and ga[-1].max() == 0 and ga[:, 0].max() == 0 and ga[:, :, -1].max() == 0
+    assert 0.4 < float(ga[1:-1, 1:-1, 1:-1].mean()) < 0.6
+
+
 def test_peer_wait_runs_out_and_reports_timeout(kernels):
     """A fake neighbour above (local buffers) whose deliveries never arrive."""
     import torch
@@ -83,6 +110,45 @@ def test_peer_wait_runs_out_and_reports_timeout(kernels):
     # The context survived: a normal run still works.
     a = torch.rand((64, 128), device="cuda")
     fin, _ = kernels.jacobi2d(a, torch.empty_like(a), 2, 0)
+    torch.cuda.synchronize()
+
+
+def test_zslab_peer_wait_runs_out_and_reports_timeout(kernels):
+    """Jacobi-3D: a fake neighbour below (local buffers) that never delivers."""
+    import torch
+    L = spmd_mod("_lib")
+    lib = L.lib()
+    c_i, c_p = ctypes.c_int64, ctypes.c_void_p
+    planes, H, W = 6, 16, 128
+    u = torch.zeros((planes + 2, H, W), device="cuda")
+    v = torch.zeros_like(u)
+    fake_u, fake_v = torch.zeros_like(u), torch.zeros_like(u)
+    nbytes = int(lib.spmdb200_jacobi_workspace_bytes())
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    fake_ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+
+    def d(t):
+        p = c_p(t.data_ptr())
+        return (p, p, c_i(0), c_i(planes + 2), c_i(H), c_i(W), c_i(H * W), c_i(W), c_i(1))
+
+    s = c_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.spmdb200_set_wait_budget_ms(c_i(2000), c_i(300)) == 0
+    try:
+        assert lib.spmdb200_jacobi_ws_reset(c_p(ws.data_ptr()), s) == 0
+        # this rank owns global planes [0, 6) of 12: a neighbour below, none above
+        st = lib.spmdb200_jacobi3d_slab(*d(u), *d(v), c_i(0), c_i(2 * planes), c_i(3), c_i(0), None,
+                                        c_p(ws.data_ptr()), None, None, None, c_i(0),
+                                        c_p(fake_u.data_ptr()), c_p(fake_v.data_ptr()), c_p(fake_ws.data_ptr()),
+                                        ctypes.c_int(0), ctypes.c_int(2),
+                                        (c_p * 2)(c_p(ws.data_ptr()), c_p(fake_ws.data_ptr())), s)
+        assert st == 0, lib.spmdb200_last_error_message()
+        st = lib.spmdb200_workspace_status(c_p(ws.data_ptr()), s)
+        assert st == -3, "the unsatisfiable peer wait must end in SPMDB200_ERR_TIMEOUT"
+        assert b"peer" in lib.spmdb200_last_error_message()
+    finally:
+        assert lib.spmdb200_set_wait_budget_ms(c_i(4000), c_i(20000)) == 0
+    a = torch.rand((8, 16, 128), device="cuda")
+    kernels.jacobi3d(a, torch.empty_like(a), 2, 0)
     torch.cuda.synchronize()
 
 

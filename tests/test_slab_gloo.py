@@ -141,6 +141,80 @@ def test_slab_protocol_matches_single_domain_oracle(oracle_mod, world, G, W, swe
     np.testing.assert_allclose(res, wres, rtol=1e-12)
 
 
+def _zslab_worker(rank: int, world: int, port: int, D: int, H: int, W: int, sweeps: int, res_every: int, q):
+    """Jacobi-3D z-slab protocol: one halo plane each side, the first/last owned
+    plane handed to the neighbours after every sweep, residuals summed in rank
+    order."""
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "tests"))
+    import torch
+    import torch.distributed as dist
+    from oracle import oracle
+    from conftest import spmd_mod as _m
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    slab = _m("slab")
+    h = slab.HALO3
+    u0 = jacobi_init((D, H, W), 3)
+    z0, planes = slab.partition(D, world, rank)
+    lo, hi = z0 - h, z0 + planes + h
+    u = np.zeros((planes + 2 * h, H, W), np.float32)
+    u[max(lo, 0) - lo:min(hi, D) - lo] = u0[max(lo, 0):min(hi, D)]
+    v = np.zeros_like(u)
+    up, dn = slab.neighbours(D, world, rank)
+    res = []
+    for k in range(1, sweeps + 1):
+        want = res_every > 0 and k % res_every == 0
+        pr = oracle.jacobi3d_planes(u, v, h, h + planes, z0 - h, D, want_res=want)
+        reqs = []
+        if up is not None:
+            reqs.append(dist.isend(torch.from_numpy(v[h].copy()), up, tag=2 * k))
+            buf = torch.empty((H, W))
+            dist.recv(buf, up, tag=2 * k + 1)
+            v[0] = buf.numpy()
+        if dn is not None:
+            reqs.append(dist.isend(torch.from_numpy(v[planes].copy()), dn, tag=2 * k + 1))
+            buf = torch.empty((H, W))
+            dist.recv(buf, dn, tag=2 * k)
+            v[planes + h] = buf.numpy()
+        for r in reqs:
+            r.wait()
+        if want:
+            mine = 0.0
+            for x in pr:
+                mine = mine + float(x)
+            slots = [None] * world
+            dist.all_gather_object(slots, mine)
+            tot = 0.0
+            for x in slots:
+                tot = tot + x
+            res.append(tot)
+        u, v = v, u
+    parts = [None] * world
+    dist.all_gather_object(parts, u[h:h + planes])
+    if rank == 0:
+        q.put((np.concatenate(parts, 0), np.array(res)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,D,H,W,sweeps", [(2, 9, 6, 7, 5), (3, 13, 5, 9, 4), (4, 4, 3, 5, 3)])
+def test_zslab_protocol_matches_single_domain_oracle(oracle_mod, world, D, H, W, sweeps):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_zslab_worker, args=(r, world, port, D, H, W, sweeps, 1, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    grid, res = q.get(timeout=120)
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want, wres = oracle_mod.jacobi3d(jacobi_init((D, H, W), 3), sweeps, 1)
+    assert np.array_equal(grid.view(np.uint32), want.view(np.uint32))
+    np.testing.assert_allclose(res, wres, rtol=1e-12)
+
+
 def _dead_rank_worker(rank: int, port: int, q):
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "tests"))
