@@ -136,6 +136,45 @@ int spmdb200_stencil3pt(float *A_base, float *A_aligned, int64_t A_offset, int64
                         int64_t B_stride0, int64_t B_stride1,
                         int64_t N, int64_t M, void *stream);
 
+/* ---- general promoted-tile stencil (rank 1-3) ------------------------------ */
+/* Promotion decision for one operand, restating computePromotionPlan
+ * (lib/Analysis/PromotionPlanAnalysis.cpp:53-164) on explicit inputs: per
+ * dimension d < rank the tile size, the original loop step (NULL: 1) and the
+ * min / max constant read offset.  footprint[d] = (tile - 1) * step + max - min
+ * + 1 (tile_dims_out[d], when the offsets are bounded), footprint bytes =
+ * elem_bytes * prod(footprint).  Returns SPMDB200_PLAN_PROMOTE, a
+ * SPMDB200_PLAN_SKIP_* reason (in the reference's check order: unbounded
+ * offsets, read-write operand, footprint above max_group_bytes, no reuse
+ * because every offset is equal), or a negative status.  Host only. */
+#define SPMDB200_PLAN_PROMOTE 0
+#define SPMDB200_PLAN_SKIP_UNBOUNDED 1
+#define SPMDB200_PLAN_SKIP_READ_WRITE 2
+#define SPMDB200_PLAN_SKIP_FOOTPRINT 3
+#define SPMDB200_PLAN_SKIP_NO_REUSE 4
+#define SPMDB200_DEFAULT_GROUP_MEM_BYTES 49152 /* TargetDescriptor.h:26-37 maxGroupMemBytes */
+int spmdb200_promotion_plan(int rank, const int64_t *tile_sizes, const int64_t *steps,
+                            const int64_t *min_offsets, const int64_t *max_offsets, int64_t elem_bytes,
+                            int64_t max_group_bytes, int read_only, int64_t *tile_dims_out,
+                            int64_t *footprint_bytes_out);
+
+/* B[p] = s * (((w0 * A[p + off0]) + w1 * A[p + off1]) + ...) for every output
+ * point p = (k0 * step0, ...) inside B's sizes (rank 1-3; sizes / strides /
+ * steps / tile sizes are host arrays of `rank` entries, strides in elements;
+ * offsets is ntaps x rank, 1 <= ntaps <= 64).  weights NULL means every w = 1
+ * and no multiply; scale 1.0f means no final multiply; arithmetic in the
+ * given order with no contraction.  Reads outside A's sizes are 0.  With
+ * policy 0 (prefer_group) the promotion plan above decides whether each
+ * tile's footprint is staged in shared memory (max_group_bytes <= 0: the
+ * reference's 48 KB; at most 227 KB); policy 1 (no_promotion) reads global
+ * memory directly.  A and B must not overlap.  *promoted_out (optional)
+ * reports the path taken.  The general form of the promoted stencil behind
+ * PromoteGroupMemory.cpp:113-314. */
+int spmdb200_stencil_nd(int rank, const float *A, const int64_t *A_sizes, const int64_t *A_strides,
+                        float *B, const int64_t *B_sizes, const int64_t *B_strides,
+                        int ntaps, const int64_t *offsets, const float *weights, float scale,
+                        const int64_t *tile_sizes, const int64_t *steps, int64_t max_group_bytes,
+                        int policy, int *promoted_out, void *stream);
+
 /* Bytes of device workspace spmdb200_sum_f32 needs for N elements. */
 size_t spmdb200_sum_workspace_bytes(int64_t N);
 

@@ -38,6 +38,7 @@ _SIGS = {
     "oracle_jacobi3d_slab_planes": (None, [c_p, c_p, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_p]),
     "oracle_jacobi3d": (None, D3 + D3 + [c_i, c_i, c_p]),
     "oracle_num_threads": (ctypes.c_int, []),
+    "oracle_stencil_nd": (None, [ctypes.c_int, c_p, c_p, c_p, c_p, c_p, c_p, ctypes.c_int, c_p, c_p, c_f, c_p]),
 }
 
 _lib = None
@@ -179,3 +180,21 @@ def jacobi3d_planes(u: np.ndarray, v: np.ndarray, z_lo: int, z_hi: int, g_z0: in
                                       c_i(u.strides[0] // 4), c_i(u.strides[1] // 4), c_i(z_lo), c_i(z_hi),
                                       _p(pr) if want_res else None)
     return pr
+
+
+def stencil_nd(A: np.ndarray, out_shape: tuple, offsets, weights=None, scale: float = 1.0, steps=None,
+               out: np.ndarray | None = None) -> np.ndarray:
+    """The general linear stencil on host arrays (see oracle_stencil_nd); B
+    starts as `out` (or zeros) and only the step lattice is written."""
+    A = np.ascontiguousarray(A, dtype=np.float32)
+    rank = A.ndim
+    B = np.zeros(out_shape, np.float32) if out is None else np.array(out, np.float32, copy=True)
+    off = np.ascontiguousarray(np.asarray(offsets, dtype=np.int64).reshape(-1, rank))
+    i64 = lambda v: np.ascontiguousarray(np.asarray(v, dtype=np.int64))
+    a_size, a_str = i64(A.shape), i64([s // 4 for s in A.strides])
+    b_size, b_str = i64(B.shape), i64([s // 4 for s in B.strides])
+    w = None if weights is None else np.ascontiguousarray(np.asarray(weights, np.float32))
+    st = None if steps is None else i64(steps)
+    lib().oracle_stencil_nd(rank, _p(A), _p(a_size), _p(a_str), _p(B), _p(b_size), _p(b_str), off.shape[0],
+                            _p(off), _p(w) if w is not None else None, c_f(scale), _p(st) if st is not None else None)
+    return B

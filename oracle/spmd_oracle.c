@@ -413,3 +413,46 @@ EXPORT void oracle_jacobi3d(float *U_base, float *U, int64_t U_off, int64_t D, i
   }
   free(pres);
 }
+
+/* ---------------------------------------------------------------------------
+ * General linear stencil, rank 1-3 (the body behind PromoteGroupMemory's
+ * promoted tiles, lib/Transforms/PromoteGroupMemory.cpp:113-314, evaluated on
+ * the original arrays since promotion only changes where values are read,
+ * rewriteLoadsToTile :62-97):  for every output point p = (k0*step0, ...)
+ * inside B's sizes, in row-major order,
+ *   t = w0*A[p+off0]; t = t + wk*A[p+offk] (k = 1..); B[p] = t*scale
+ * with no multiply when weights == NULL (all 1) or scale == 1.  Reads outside
+ * A's sizes are 0.  Strides in elements.
+ * ------------------------------------------------------------------------- */
+EXPORT void oracle_stencil_nd(int rank, const float *A, const int64_t *a_size, const int64_t *a_stride,
+                              float *B, const int64_t *b_size, const int64_t *b_stride, int ntaps,
+                              const int64_t *off, const float *w, float scale, const int64_t *step) {
+  int64_t npts[3] = {1, 1, 1}, st[3] = {1, 1, 1};
+  for (int d = 0; d < rank; ++d) {
+    st[d] = step ? step[d] : 1;
+    npts[d] = (b_size[d] + st[d] - 1) / st[d];
+  }
+  const int64_t total = npts[0] * npts[1] * npts[2];
+  for (int64_t q = 0; q < total; ++q) {
+    int64_t r = q, o[3] = {0, 0, 0}, boff = 0;
+    for (int d = rank - 1; d >= 0; --d) {
+      o[d] = (r % npts[d]) * st[d];
+      r /= npts[d];
+      boff += o[d] * b_stride[d];
+    }
+    float t = 0.0f;
+    for (int j = 0; j < ntaps; ++j) {
+      int64_t aoff = 0;
+      int in = 1;
+      for (int d = 0; d < rank; ++d) {
+        const int64_t g = o[d] + off[j * rank + d];
+        in = in && g >= 0 && g < a_size[d];
+        aoff += g * a_stride[d];
+      }
+      float v = in ? A[aoff] : 0.0f;
+      if (w) v = w[j] * v;
+      t = j == 0 ? v : t + v;
+    }
+    B[boff] = scale != 1.0f ? t * scale : t;
+  }
+}

@@ -57,6 +57,9 @@ _SIGS = {
     "spmdb200_reduction_status": (ctypes.c_int, []),
     "spmdb200_reduce_f32": (ctypes.c_int, [ctypes.c_int] + D1 + D0 + [c_i, c_f, c_p, c_sz, c_p]),
     "spmdb200_reduce_i32": (ctypes.c_int, [ctypes.c_int] + D1 + D0 + [c_i, ctypes.c_int32, c_p, c_sz, c_p]),
+    "spmdb200_promotion_plan": (ctypes.c_int, [ctypes.c_int, c_p, c_p, c_p, c_p, c_i, c_i, ctypes.c_int, c_p, c_p]),
+    "spmdb200_stencil_nd": (ctypes.c_int, [ctypes.c_int, c_p, c_p, c_p, c_p, c_p, c_p, ctypes.c_int, c_p, c_p, c_f,
+                                           c_p, c_p, c_i, ctypes.c_int, c_p, c_p]),
     "spmdb200_jacobi_workspace_bytes": (c_sz, []),
     "spmdb200_jacobi2d": (ctypes.c_int, D2 + D2 + [c_i, c_i, c_p, c_p, c_sz, c_p]),
     "spmdb200_jacobi3d": (ctypes.c_int, D3 + D3 + [c_i, c_i, c_p, c_p, c_sz, c_p]),

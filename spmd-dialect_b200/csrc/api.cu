@@ -313,6 +313,79 @@ int spmdb200_stencil3pt(float *A_base, float *A, int64_t A_off, int64_t A_n0, in
   return ok();
 }
 
+int spmdb200_promotion_plan(int rank, const int64_t *tile_sizes, const int64_t *steps,
+                            const int64_t *min_offsets, const int64_t *max_offsets, int64_t elem_bytes,
+                            int64_t max_group_bytes, int read_only, int64_t *tile_dims_out,
+                            int64_t *footprint_bytes_out) {
+  const int r = promotion_plan(rank, tile_sizes, steps, min_offsets, max_offsets, elem_bytes, max_group_bytes,
+                               read_only, tile_dims_out, footprint_bytes_out);
+  if (r < 0) return fail(SPMDB200_ERR_INVALID_ARG, "promotion plan: rank 1-3, non-null sizes, elem_bytes >= 1");
+  ok();
+  return r;
+}
+
+int spmdb200_stencil_nd(int rank, const float *A, const int64_t *A_sizes, const int64_t *A_strides, float *B,
+                        const int64_t *B_sizes, const int64_t *B_strides, int ntaps, const int64_t *offsets,
+                        const float *weights, float scale, const int64_t *tile_sizes, const int64_t *steps,
+                        int64_t max_group_bytes, int policy, int *promoted_out, void *stream) {
+  if (promoted_out) *promoted_out = 0;
+  if (rank < 1 || rank > 3) return fail(SPMDB200_ERR_INVALID_ARG, "rank %d: must be 1, 2 or 3", rank);
+  if (ntaps < 1 || ntaps > kNdMaxTaps) return fail(SPMDB200_ERR_INVALID_ARG, "ntaps %d: 1..%d", ntaps, kNdMaxTaps);
+  if (!A_sizes || !A_strides || !B_sizes || !B_strides || !offsets || !tile_sizes)
+    return fail(SPMDB200_ERR_INVALID_ARG, "null size / stride / offset / tile array");
+  if (policy != 0 && policy != 1) return fail(SPMDB200_ERR_INVALID_ARG, "policy must be 0 or 1");
+  if (max_group_bytes <= 0) max_group_bytes = SPMDB200_DEFAULT_GROUP_MEM_BYTES;
+  if (max_group_bytes > 227 * 1024) return fail(SPMDB200_ERR_UNSUPPORTED, "max_group_bytes above 227 KB");
+  StencilNdProblem p{};
+  p.rank = rank;
+  p.ntaps = ntaps;
+  p.a = A;
+  p.b = B;
+  p.offsets = offsets;
+  p.weights = weights;
+  p.scale = scale;
+  int64_t a_cells = 1, b_cells = 1, a_span = 1, b_span = 1, mn[3], mx[3];
+  for (int d = 0; d < rank; ++d) {
+    if (A_sizes[d] < 0 || B_sizes[d] < 0 || A_strides[d] < 0 || B_strides[d] < 0)
+      return fail(SPMDB200_ERR_INVALID_ARG, "negative size or stride in dimension %d", d);
+    if (tile_sizes[d] < 1 || tile_sizes[d] > 1024 || (steps && (steps[d] < 1 || steps[d] > (1 << 20))))
+      return fail(SPMDB200_ERR_INVALID_ARG, "tile size 1..1024 and step 1..2^20 in dimension %d", d);
+    p.a_size[d] = A_sizes[d];
+    p.a_stride[d] = A_strides[d];
+    p.b_size[d] = B_sizes[d];
+    p.b_stride[d] = B_strides[d];
+    p.tile[d] = tile_sizes[d];
+    p.step[d] = steps ? steps[d] : 1;
+    a_cells *= A_sizes[d];
+    b_cells *= B_sizes[d];
+    a_span += (A_sizes[d] > 0 ? A_sizes[d] - 1 : 0) * A_strides[d];
+    b_span += (B_sizes[d] > 0 ? B_sizes[d] - 1 : 0) * B_strides[d];
+    mn[d] = mx[d] = offsets[d];
+  }
+  for (int j = 0; j < ntaps; ++j)
+    for (int d = 0; d < rank; ++d) {
+      const int64_t o = offsets[j * rank + d];
+      if (o < -(1 << 20) || o > (1 << 20)) return fail(SPMDB200_ERR_INVALID_ARG, "offset %lld out of range", (long long)o);
+      mn[d] = o < mn[d] ? o : mn[d];
+      mx[d] = o > mx[d] ? o : mx[d];
+    }
+  if (b_cells == 0) return ok();
+  if (!B || (a_cells > 0 && !A)) return fail(SPMDB200_ERR_INVALID_ARG, "null A or B");
+  const bool overlap = a_cells > 0 && (const void *)A < (const void *)(B + b_span) && (const void *)B < (const void *)(A + a_span);
+  if (overlap) return fail(SPMDB200_ERR_INVALID_ARG, "A and B overlap (the stencil's input must be read-only)");
+  if (a_cells == 0) {
+    p.a = B;  // every read is outside A: reads return 0 without touching memory
+    for (int d = 0; d < rank; ++d) p.a_size[d] = 0;
+  }
+  int64_t dims[3], bytes = 0;
+  const int plan = policy == 0 ? promotion_plan(rank, tile_sizes, steps, mn, mx, 4, max_group_bytes, 1, dims, &bytes)
+                               : kPlanSkipNoReuse;
+  const int promote = plan == kPlanPromote ? 1 : 0;
+  CUDA_TRY(launch_stencil_nd(p, promote, (cudaStream_t)stream));
+  if (promoted_out) *promoted_out = promote;
+  return ok();
+}
+
 size_t spmdb200_sum_workspace_bytes(int64_t N) { return sum_f32_workspace_bytes(N); }
 
 int spmdb200_sum_f32(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st,

@@ -120,6 +120,32 @@ cudaError_t launch_jacobi3d_generic(const Jacobi3dProblem &p, cudaStream_t s);
 cudaError_t launch_fill_jacobi3d_input(float *p, int64_t sz, int64_t sy, int64_t planes, int64_t h, int64_t w,
                                        int64_t g_z0, int64_t g_d, uint64_t seed, cudaStream_t s);
 
+// ---- general N-D promoted-tile stencil (stencil_nd.cu) ------------------------------
+constexpr int kNdMaxTaps = 64;
+enum PlanCode : int {  // promotion decision (PromotionPlanAnalysis.cpp:53-164)
+  kPlanPromote = 0,
+  kPlanSkipUnbounded = 1,
+  kPlanSkipReadWrite = 2,
+  kPlanSkipFootprint = 3,
+  kPlanSkipNoReuse = 4,
+};
+// Returns a PlanCode (or -1 for bad arguments); tile_dims_out / footprint
+// bytes are filled whenever the offsets are bounded.
+int promotion_plan(int rank, const int64_t *tile_sizes, const int64_t *steps, const int64_t *min_off,
+                   const int64_t *max_off, int64_t elem_bytes, int64_t max_group_bytes, int read_only,
+                   int64_t *tile_dims_out, int64_t *footprint_bytes_out);
+struct StencilNdProblem {
+  int rank, ntaps;
+  const float *a;
+  float *b;
+  int64_t a_size[3], a_stride[3], b_size[3], b_stride[3];
+  int64_t step[3], tile[3];
+  const int64_t *offsets;  // ntaps x rank
+  const float *weights;    // ntaps, or null (all 1)
+  float scale;             // 1: no final multiply
+};
+cudaError_t launch_stencil_nd(const StencilNdProblem &p, int promote, cudaStream_t s);
+
 // ---- driver entry points resolved at run time (no link-time libcuda) ----------------
 // Encodes a row-major f32 tensor map (innermost dimension first).  Returns 0 on success.
 int encode_tensor_map_f32(void *tmap /*CUtensorMap*/, void *gaddr, int rank, const uint64_t *dims,

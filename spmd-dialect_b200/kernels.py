@@ -54,6 +54,51 @@ def stencil3pt(a: torch.Tensor, out: torch.Tensor, n: int | None = None, m: int 
     return out
 
 
+PLAN_REASONS = {0: "promote", 1: "unbounded offsets", 2: "read-write operand", 3: "footprint too large",
+                4: "no reuse"}
+
+
+def _i64(vals) -> ctypes.Array:
+    vals = [int(v) for v in vals]
+    return (ctypes.c_int64 * max(len(vals), 1))(*vals)
+
+
+def promotion_plan(tile_sizes, min_offsets, max_offsets, steps=None, elem_bytes: int = 4,
+                   max_group_bytes: int = 49152, read_only: bool = True) -> tuple[int, tuple, int]:
+    """(plan code, footprint extents, footprint bytes) of one operand, as the
+    reference's computePromotionPlan decides it (host only, no GPU needed)."""
+    rank = len(tile_sizes)
+    dims = (ctypes.c_int64 * 3)()
+    nbytes = ctypes.c_int64(0)
+    code = lib().spmdb200_promotion_plan(rank, _i64(tile_sizes), _i64(steps) if steps is not None else None,
+                                         _i64(min_offsets), _i64(max_offsets), c_i(elem_bytes),
+                                         c_i(max_group_bytes), int(bool(read_only)), dims, ctypes.byref(nbytes))
+    if code < 0:
+        from ._lib import check
+        check("spmdb200_promotion_plan", code)  # raises with the library's message
+    return int(code), tuple(int(dims[d]) for d in range(rank)), int(nbytes.value)
+
+
+def stencil_nd(a: torch.Tensor, out: torch.Tensor, offsets, weights=None, scale: float = 1.0, tile_sizes=None,
+               steps=None, max_group_bytes: int = 0, policy: int = 0, stream=None) -> bool:
+    """out[p] = scale * sum_k w_k * a[p + offsets[k]] in order, for p on the step
+    lattice inside out's shape (reads off `a` are 0).  Returns True when the
+    promotion plan staged tiles in shared memory."""
+    rank = a.dim()
+    if out.dim() != rank or not (1 <= rank <= 3):
+        raise ValueError("a and out must have the same rank, 1-3")
+    offs = [int(v) for row in offsets for v in (row if hasattr(row, "__len__") else [row])]
+    ntaps = len(offs) // rank
+    tile_sizes = tile_sizes or ([256] if rank == 1 else [32, 8] if rank == 2 else [8, 8, 4])
+    w = None if weights is None else (ctypes.c_float * ntaps)(*[float(x) for x in weights])
+    promoted = ctypes.c_int(0)
+    call("spmdb200_stencil_nd", rank, c_p(a.data_ptr()), _i64(a.shape), _i64(a.stride()), c_p(out.data_ptr()),
+         _i64(out.shape), _i64(out.stride()), ntaps, _i64(offs), w, ctypes.c_float(scale), _i64(tile_sizes),
+         _i64(steps) if steps is not None else None, c_i(max_group_bytes), policy, ctypes.byref(promoted),
+         _stream(stream))
+    return bool(promoted.value)
+
+
 def sum_workspace(n: int, device=None) -> torch.Tensor:
     """Zero-filled workspace for sum_f32 (reusable: every call leaves it zeroed)."""
     nbytes = int(lib().spmdb200_sum_workspace_bytes(c_i(n)))

@@ -201,6 +201,32 @@ class _SlabJob:
         d.gather_object(mine, parts, dst=0)
         return np.concatenate(parts, axis=0) if self.rank == 0 else None
 
+    # ---------------------------------------------------------------- checkpoint / resume
+    def save(self, path: str) -> None:
+        """Checkpoint: rank 0 writes the header, then every rank writes its owned
+        units of the current grid at their offset (collective: all ranks call)."""
+        from . import checkpoint as ck
+        if self.rank == 0:
+            ck.write_header(path, (self.G,) + self._global_unit_shape(), self.sweeps_done, self.res_every)
+        rendezvous()
+        ck.write_block(path, self.g_first, self.local_owned())
+        rendezvous()
+
+    def restore(self, path: str) -> None:
+        """Loads this rank's units (+ halos) of a checkpointed grid into U and V and
+        takes over its sweep count.  The checkpoint may come from any number of ranks."""
+        from . import checkpoint as ck
+        info = ck.read_header(path)
+        want = (self.G,) + self._global_unit_shape()
+        if tuple(info.shape) != want:
+            raise ValueError(f"checkpoint grid {info.shape} does not match this job's grid {want}")
+        block = ck.read_block(path, self.g_first - self.halo, self.g_first + self.rows + self.halo)
+        local = np.ascontiguousarray(self._pad(block))
+        for buf in (self._u, self._v):
+            call("spmdb200_memcpy", c_p(buf.ptr), local.ctypes.data_as(c_p), ctypes.c_size_t(local.nbytes), None)
+        self.sweeps_done = info.sweeps
+        rendezvous()
+
     # ---------------------------------------------------------------- running
     def run(self, sweeps: int, check: bool = True) -> None:
         """`sweeps` sweeps on every rank (all ranks must call with the same count)."""
@@ -292,6 +318,9 @@ class SlabJacobi2D(_SlabJob):
         self.unit_shape = (self.pitch,)
         self._setup(G, res_every, seed, init)
 
+    def _global_unit_shape(self) -> tuple:
+        return (self.cols,)
+
     def _fill(self, ptr: int, seed: int, stream) -> None:
         call("spmdb200_fill_jacobi_input", c_p(ptr), c_i(self.pitch), c_i(self.local_rows), c_i(self.cols),
              c_i(self.g_first - self.halo), c_i(self.G), ctypes.c_uint64(seed), stream)
@@ -333,6 +362,9 @@ class SlabJacobi3D(_SlabJob):
     @property
     def planes(self) -> int:
         return self.rows
+
+    def _global_unit_shape(self) -> tuple:
+        return (self.H, self.cols)
 
     def _fill(self, ptr: int, seed: int, stream) -> None:
         call("spmdb200_fill_jacobi3d_input", c_p(ptr), c_i(self.H * self.pitch), c_i(self.pitch),

@@ -61,6 +61,36 @@ def test_single_rank_zslab_matches_oracle(kernels, oracle_mod):
     np.testing.assert_allclose(res, wres, rtol=1e-12)
 
 
+def test_checkpoint_resume_matches_uninterrupted(kernels, oracle_mod, tmp_path):
+    """Run 7 sweeps, save, resume in a fresh job (other seed), run 6: equals 13."""
+    slab = spmd_mod("slab")
+    u0 = jacobi_init((130, 300), 4)
+    a = slab.SlabJacobi2D(cols=300, G=130, res_every=0, init=u0)
+    a.run(7)
+    a.save(str(tmp_path / "j2.ckpt"))
+    a.close()
+    b = slab.SlabJacobi2D(cols=300, G=130, res_every=0, seed=99)
+    b.restore(str(tmp_path / "j2.ckpt"))
+    assert b.sweeps_done == 7
+    b.run(6)
+    got = b.gather()
+    b.close()
+    want, _ = oracle_mod.jacobi2d(u0, 13, 0)
+    assert_bits_equal(got, want, "2-D resume")
+    u3 = jacobi_init((13, 20, 150), 3)
+    c = slab.SlabJacobi3D(H=20, W=150, D=13, res_every=0, init=u3)
+    c.run(3)
+    c.save(str(tmp_path / "j3.ckpt"))
+    c.close()
+    d = slab.SlabJacobi3D(H=20, W=150, D=13, res_every=0, seed=5)
+    d.restore(str(tmp_path / "j3.ckpt"))
+    d.run(4)
+    got3 = d.gather()
+    d.close()
+    want3, _ = oracle_mod.jacobi3d(u3, 7, 0)
+    assert_bits_equal(got3, want3, "3-D resume")
+
+
 def test_zslab_seeded_fill_is_deterministic(kernels):
     slab = spmd_mod("slab")
     a = slab.SlabJacobi3D(H=17, W=33, D=9, seed=3)
