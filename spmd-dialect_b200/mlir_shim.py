@@ -1,0 +1,590 @@
+"""Textual-MLIR shim: maps `spmd.kernel` functions written with `spmd.forall` /
+`spmd.reduce` onto this library's C entries, so code (and orchestration)
+written against the dialect runs here without MLIR, LLVM or a PTX toolchain.
+
+It reads the generic operation form the dialect's tests use
+("spmd.forall"(lbs, ubs, steps) ({ ^bb0(ivs): ... }) {attrs}), evaluates the
+index arithmetic symbolically, and recognises the lowered shapes of the hot
+path:
+
+* elementwise foralls: C[i] = A[i] + B[i] (the ewise kernel,
+  test/SPMD/lower-to-gpu-nvptx.mlir:54-71) and Y[i] = a * X[i] + Y[i];
+* linear stencils: B[p] = s * (w0 A[p + o0] + w1 A[p + o1] + ...) in source
+  order (a left fold of arith.addf), any rank 1-3, with the group forall's
+  `spmd.tile_sizes`, the lane step and `spmd.memory_policy` handed to the
+  promotion plan (lib/Analysis/PromotionPlanAnalysis.cpp:53-164) -- e.g. the
+  promoted 3-point stencil (test/SPMD/lower-to-gpu-nvptx-promoted.mlir:32-67);
+* reductions: an `spmd.reduce` (any kind, include/spmd/IR/SPMDAttrs.td:74-80)
+  of one memref, combined into a rank-0 memref with memref.atomic_rmw (the
+  hierarchical sum, SPMDToGPU.cpp:249-415) or one atomic per element (the
+  atomic baseline).
+
+`load(text)` returns callables taking the function's own arguments (CUDA
+tensors for memrefs, ints for index, floats for f32).  The command line adds
+stand-ins for the two build steps of the reference's differential script
+(scripts/run-differential.sh:108-140 `_compile_so`, scripts/gen-ptx.sh):
+
+    python mlir_shim.py describe kernels.mlir
+    python mlir_shim.py so  kernels.mlir scf|omp out.so     # host entries (ewise, stencil_cpu, ...)
+    python mlir_shim.py ptx kernels.mlir ewise|promoted|hierarchical out.ptx [sm]
+
+`so` and `ptx` check that every kernel in the file has an entry of the same
+name and calling convention in this library, then write the library (or the
+kernel module, loadable by cuModuleLoadData like PTX) to the output path;
+anything the shim does not recognise is reported, not guessed.
+"""
+from __future__ import annotations
+
+import json
+import re
+import shutil
+import sys
+from dataclasses import dataclass, field
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+
+
+class ShimError(ValueError):
+    """The MLIR text uses a form or pattern the shim does not map."""
+
+
+# ----------------------------------------------------------------------------- parsing
+@dataclass
+class Op:
+    name: str                  # e.g. "arith.addf", "spmd.forall"
+    result: str | None
+    operands: list
+    attrs: str = ""            # raw attribute text
+    extra: str = ""            # predicate / reduction kind / memref index list
+    region: list = field(default_factory=list)
+    block_args: list = field(default_factory=list)
+    type: str = ""
+
+
+@dataclass
+class Arg:
+    name: str
+    kind: str                  # "memref", "index", "f32", "i32"
+    rank: int = 0
+    elem: str = ""
+
+
+@dataclass
+class Func:
+    name: str
+    args: list
+    ops: list
+    kernel: bool
+
+
+_REGION_OP = re.compile(r'(?:(%[\w.#]+)\s*=\s*)?"(spmd\.\w+)"\(([^)]*)\)\s*\(\{')
+_SIG = re.compile(r'\s*:\s*\(([^)]*)\)\s*->\s*(\(\)|[^\s,}]+)')
+_FUNC = re.compile(r'func\.func\s+(?:private\s+)?@([\w.]+)\s*\(([^)]*)\)\s*(?:->\s*[^{]*?)?\s*(attributes\s*\{[^}]*\})?\s*\{')
+
+
+def _strip_comments(text: str) -> str:
+    return "\n".join(line.split("//", 1)[0] for line in text.splitlines())
+
+
+def _match_brace(s: str, i: int) -> int:
+    """Index of the brace closing the one at s[i]."""
+    depth = 0
+    for j in range(i, len(s)):
+        if s[j] == "{":
+            depth += 1
+        elif s[j] == "}":
+            depth -= 1
+            if depth == 0:
+                return j
+    raise ShimError("unbalanced braces")
+
+
+def _vals(s: str) -> list:
+    return [v.strip() for v in s.split(",") if v.strip()]
+
+
+def _parse_simple(line: str) -> Op:
+    m = re.match(r'(?:(%[\w.#]+)\s*=\s*)?([\w.]+|"[\w.]+")\s*(.*)$', line)
+    if not m:
+        return Op("unknown", None, [], extra=line)
+    res, name, rest = m.group(1), m.group(2).strip('"'), m.group(3)
+    if name == "arith.constant":
+        v, t = rest.rsplit(":", 1)
+        return Op(name, res, [], extra=v.strip(), type=t.strip())
+    if name in ("arith.cmpi", "arith.cmpf"):
+        pred, rest2 = rest.split(",", 1)
+        ops, t = rest2.rsplit(":", 1)
+        return Op(name, res, _vals(ops), extra=pred.strip(), type=t.strip())
+    if name == "memref.load":
+        mm = re.match(r'(%[\w.#]+)\[([^\]]*)\]\s*:\s*(.*)$', rest)
+        return Op(name, res, [mm.group(1)], extra=mm.group(2), type=mm.group(3).strip())
+    if name == "memref.store":
+        mm = re.match(r'(%[\w.#]+)\s*,\s*(%[\w.#]+)\[([^\]]*)\]\s*:\s*(.*)$', rest)
+        return Op(name, None, [mm.group(1), mm.group(2)], extra=mm.group(3), type=mm.group(4).strip())
+    if name == "memref.atomic_rmw":
+        mm = re.match(r'(\w+)\s+(%[\w.#]+)\s*,\s*(%[\w.#]+)\[([^\]]*)\]', rest)
+        return Op(name, res, [mm.group(2), mm.group(3)], extra=mm.group(1), attrs=mm.group(4))
+    if name in ("spmd.yield", "spmd.barrier"):
+        mm = re.match(r'\(([^)]*)\)', rest)
+        return Op(name, None, _vals(mm.group(1)) if mm else [])
+    if name in ("func.return", "return"):
+        return Op("func.return", None, [])
+    if name.startswith("arith."):
+        ops, t = rest.rsplit(":", 1)
+        return Op(name, res, _vals(ops), type=t.strip())
+    return Op("unknown", res, [], extra=line)
+
+
+def _parse_ops(s: str) -> list:
+    ops, pos = [], 0
+    while pos < len(s):
+        while pos < len(s) and s[pos].isspace():
+            pos += 1
+        if pos >= len(s):
+            break
+        m = _REGION_OP.match(s, pos)
+        if m:
+            brace = m.end() - 1
+            close = _match_brace(s, brace)
+            inner = s[brace + 1:close]
+            bb = re.match(r'\s*\^bb\d+\(([^)]*)\)\s*:', inner)
+            block_args = [a.split(":")[0].strip() for a in _vals(bb.group(1))] if bb else []
+            region = _parse_ops(inner[bb.end():] if bb else inner)
+            pos = close + 1
+            while s[pos].isspace():
+                pos += 1
+            if s[pos] != ")":
+                raise ShimError(f"{m.group(2)}: expected ')' after its region")
+            pos += 1
+            while pos < len(s) and s[pos].isspace():
+                pos += 1
+            attrs = ""
+            if pos < len(s) and s[pos] == "{":
+                aend = _match_brace(s, pos)
+                attrs = s[pos + 1:aend]
+                pos = aend + 1
+            sig = _SIG.match(s, pos)
+            if sig:
+                pos = sig.end()
+            ops.append(Op(m.group(2), m.group(1), _vals(m.group(3)), attrs=attrs, region=region,
+                          block_args=block_args))
+            continue
+        eol = s.find("\n", pos)
+        eol = len(s) if eol < 0 else eol
+        line = s[pos:eol].strip()
+        pos = eol + 1
+        if line:
+            ops.append(_parse_simple(line))
+    return ops
+
+
+def _parse_arg(a: str) -> Arg:
+    name, t = [x.strip() for x in a.split(":", 1)]
+    mm = re.match(r'memref<(.*)>$', t)
+    if mm:
+        dims = mm.group(1).split("x")
+        elem = dims[-1].split(",")[0].strip()
+        return Arg(name, "memref", len(dims) - 1, elem)
+    return Arg(name, t if t in ("index", "f32", "i32") else t)
+
+
+def parse_module(text: str) -> list:
+    """Every func.func of the module (kernels marked by `spmd.kernel`)."""
+    text = _strip_comments(text)
+    funcs = []
+    for m in _FUNC.finditer(text):
+        start = m.end() - 1
+        body = text[start + 1:_match_brace(text, start)]
+        args = [_parse_arg(a) for a in _vals(m.group(2))]
+        funcs.append(Func(m.group(1), args, _parse_ops(body), bool(m.group(3) and "spmd.kernel" in m.group(3))))
+    return funcs
+
+
+# ----------------------------------------------------------------------------- analysis
+class _Aff:
+    """An index value: sum of coeff * symbol + const (symbols: ivs and index args)."""
+
+    def __init__(self, terms=None, const=0):
+        self.terms = dict(terms or {})
+        self.const = const
+
+    def __add__(self, o):
+        t = dict(self.terms)
+        for k, v in o.terms.items():
+            t[k] = t.get(k, 0) + v
+        return _Aff({k: v for k, v in t.items() if v}, self.const + o.const)
+
+    def __sub__(self, o):
+        return self + o.scale(-1)
+
+    def scale(self, c):
+        return _Aff({k: v * c for k, v in self.terms.items()}, self.const * c)
+
+
+def _attr_ints(attrs: str, key: str) -> list | None:
+    m = re.search(r'"?' + re.escape(key) + r'"?\s*=\s*array<i64:\s*([^>]*)>', attrs)
+    return [int(x) for x in _vals(m.group(1))] if m else None
+
+
+def _attr_enum(attrs: str, key: str) -> str | None:
+    m = re.search(r'"?' + re.escape(key) + r'"?\s*=\s*#spmd\.\w+<(\w+)>', attrs)
+    return m.group(1) if m else None
+
+
+def _segments(op: Op) -> tuple:
+    seg = re.search(r'operandSegmentSizes\s*=\s*array<i32:\s*([^>]*)>', op.attrs)
+    if seg:
+        n = [int(x) for x in _vals(seg.group(1))]
+    else:
+        r = len(op.operands) // 3
+        n = [r, r, r]
+    o = op.operands
+    return o[:n[0]], o[n[0]:n[0] + n[1]], o[n[0] + n[1]:n[0] + n[1] + n[2]]
+
+
+@dataclass
+class Mapping:
+    """How one spmd.kernel function maps onto the library."""
+    name: str
+    pattern: str               # "ewise" | "axpy" | "stencil" | "reduce"
+    entry: str                 # C entry called
+    detail: dict
+
+    def to_json(self) -> dict:
+        return {"function": self.name, "pattern": self.pattern, "entry": self.entry, **self.detail}
+
+
+class _Env:
+    def __init__(self, func: Func):
+        self.func = func
+        self.idx: dict = {}      # ssa -> _Aff
+        self.consts: dict = {}   # ssa -> python number
+        self.defs: dict = {}     # ssa -> Op
+        for a in func.args:
+            if a.kind == "index":
+                self.idx[a.name] = _Aff({a.name: 1})
+
+    def index(self, v: str) -> _Aff:
+        if v in self.idx:
+            return self.idx[v]
+        raise ShimError(f"{self.func.name}: index value {v} is not an affine function of the loop indices")
+
+    def visit(self, op: Op) -> None:
+        if op.result:
+            self.defs[op.result] = op
+        if op.name == "arith.constant":
+            val = float(op.extra) if op.type in ("f32", "f64") else int(op.extra)
+            self.consts[op.result] = val
+            if op.type == "index":
+                self.idx[op.result] = _Aff({}, val)
+        elif op.name in ("arith.addi", "arith.subi", "arith.muli") and op.type == "index":
+            try:
+                a, b = self.index(op.operands[0]), self.index(op.operands[1])
+            except ShimError:
+                return  # not affine: any load through it makes the function unmappable
+            if op.name == "arith.addi":
+                self.idx[op.result] = a + b
+            elif op.name == "arith.subi":
+                self.idx[op.result] = a - b
+            elif not a.terms:
+                self.idx[op.result] = b.scale(a.const)
+            elif not b.terms:
+                self.idx[op.result] = a.scale(b.const)
+
+
+def _walk(ops, env: _Env, path=()):
+    """Yields (op, enclosing spmd ops) depth first, feeding env."""
+    for op in ops:
+        env.visit(op)
+        yield op, path
+        if op.region:
+            for a in op.block_args:
+                env.idx[a] = _Aff({a: 1})
+            yield from _walk(op.region, env, path + (op,))
+
+
+def _fold(env: _Env, v: str, loads: list) -> tuple:
+    """(taps, scale): v as a left fold t = w0 x0; t = t + wk xk; then t * s."""
+    op = env.defs.get(v)
+    if op is None:
+        raise ShimError(f"{env.func.name}: value {v} has no definition the shim understands")
+    if op.name == "memref.load":
+        loads.append(op)
+        return [(None, op)], None
+    if op.name == "arith.mulf":
+        a, b = op.operands
+        const, other = (a, b) if a in env.consts else (b, a) if b in env.consts else (None, None)
+        if const is None:
+            raise ShimError(f"{env.func.name}: product of two non-constant values")
+        inner = env.defs.get(other)
+        if inner is not None and inner.name == "memref.load":
+            loads.append(inner)
+            return [(env.consts[const], inner)], None
+        taps, scale = _fold(env, other, loads)
+        if scale is not None:
+            raise ShimError(f"{env.func.name}: more than one final scale")
+        return taps, env.consts[const]
+    if op.name == "arith.addf":
+        a, b = op.operands
+        left, ls = _fold(env, a, loads)
+        right, rs = _fold(env, b, loads)
+        if ls is not None or rs is not None or len(right) != 1:
+            raise ShimError(f"{env.func.name}: the sum is not a left fold in source order")
+        return left + right, None
+    raise ShimError(f"{env.func.name}: {op.name} is not part of a linear stencil")
+
+
+def analyse(func: Func) -> Mapping:
+    """Recognises the function's pattern; raises ShimError when it maps to nothing."""
+    env = _Env(func)
+    nodes = list(_walk(func.ops, env))
+    unknown = [op.extra for op, _ in nodes if op.name == "unknown"]
+    if unknown:
+        raise ShimError(f"{func.name}: unsupported operation: {unknown[0]}")
+    args = {a.name: a for a in func.args}
+    foralls = [op for op, _ in nodes if op.name == "spmd.forall"]
+    reduces = [(op, p) for op, p in nodes if op.name == "spmd.reduce"]
+    atomics = [(op, p) for op, p in nodes if op.name == "memref.atomic_rmw"]
+    stores = [(op, p) for op, p in nodes if op.name == "memref.store"]
+    if not foralls:
+        raise ShimError(f"{func.name}: no spmd.forall")
+    group = foralls[0]
+    lbs, ubs, steps = _segments(group)
+    tile = _attr_ints(group.attrs, "spmd.tile_sizes")
+    policy = _attr_enum(group.attrs, "spmd.memory_policy")
+
+    if atomics:  # ---------------------------------------------------------- reductions
+        at, _ = atomics[0]
+        val, out = at.operands
+        if args.get(out) is None or args[out].rank != 0:
+            raise ShimError(f"{func.name}: atomic_rmw target must be a rank-0 memref argument")
+        if reduces:
+            red, _ = reduces[0]
+            kind = _attr_enum(red.attrs, "spmd.kind") or "add"
+            yields = [o for o in red.region if o.name == "spmd.yield"]
+            y = env.defs.get(yields[-1].operands[0]) if yields and yields[-1].operands else None
+            while y is not None and y.name == "arith.select":
+                y = env.defs.get(y.operands[1])
+            if y is None or y.name != "memref.load":
+                raise ShimError(f"{func.name}: spmd.reduce body must yield one (masked) load")
+            src = y.operands[0]
+        else:
+            kind = {"addf": "add", "addi": "add"}.get(at.extra)
+            v = env.defs.get(val)
+            if kind is None or v is None or v.name != "memref.load":
+                raise ShimError(f"{func.name}: atomic_rmw of a loaded element expected")
+            src = v.operands[0]
+        if at.extra not in ("addf", "addi") and not reduces:
+            raise ShimError(f"{func.name}: unsupported atomic kind {at.extra}")
+        n_arg = ubs[0] if ubs and ubs[0] in args else None
+        elem = args[src].elem
+        if elem == "f32" and kind == "add":
+            entry = "spmdb200_hierarchical_sum" if reduces else "spmdb200_sum_f32"
+        else:
+            entry = f"spmdb200_reduce_{elem}"
+        return Mapping(func.name, "reduce", entry, {"kind": kind, "input": src, "output": out, "n": n_arg,
+                                                    "combine": at.extra, "elem": elem})
+
+    if len(stores) != 1:
+        raise ShimError(f"{func.name}: expected exactly one memref.store, found {len(stores)}")
+    st, _ = stores[0]
+    val, dst = st.operands
+    dst_idx = [env.index(v) for v in _vals(st.extra)]
+    rank = len(dst_idx)
+    loads: list = []
+    taps, scale = _fold(env, val, loads)
+    srcs = {ld.operands[0] for _, ld in taps}
+    # offsets of every load relative to the store's index
+    offsets = []
+    for w, ld in taps:
+        li = [env.index(v) for v in _vals(ld.extra)]
+        if len(li) != rank:
+            raise ShimError(f"{func.name}: load rank differs from the store's")
+        off = []
+        for a, b in zip(li, dst_idx):
+            d = a - b
+            if d.terms:
+                raise ShimError(f"{func.name}: load index is not the store index plus a constant")
+            off.append(d.const)
+        offsets.append(off)
+    # iteration domain: the group forall's upper bounds; lane step from the store index
+    ub = [u for u in ubs[:rank]]
+    lane_steps = []
+    inner = foralls[1] if len(foralls) > 1 else None
+    for d in range(rank):
+        coeffs = sorted(v for k, v in dst_idx[d].terms.items() if inner is None or k in inner.block_args)
+        lane_steps.append(coeffs[0] if coeffs else 1)
+    lower = []
+    for v in lbs[:rank]:
+        a = env.index(v)
+        if len(a.terms) > 1 or any(c != 1 for c in a.terms.values()) or (a.terms and a.const):
+            raise ShimError(f"{func.name}: lower bound {v} must be a constant or an index argument")
+        lower.append(next(iter(a.terms)) if a.terms else a.const)
+    if rank == 1 and lower == [0] and len(srcs) >= 1 and all(o == [0] for o in offsets):
+        ws = [w for w, _ in taps]
+        if len(taps) == 2 and ws == [None, None] and scale is None and len(srcs) == 2:
+            a, b = [ld.operands[0] for _, ld in taps]
+            return Mapping(func.name, "ewise", "spmdb200_ewise", {"a": a, "b": b, "c": dst, "n": ub[0]})
+        if len(taps) == 2 and ws[0] is not None and ws[1] is None and scale is None:
+            x, y = [ld.operands[0] for _, ld in taps]
+            if y == dst:
+                return Mapping(func.name, "axpy", "spmdb200_axpy", {"alpha": ws[0], "x": x, "y": dst, "n": ub[0]})
+    if len(srcs) != 1:
+        raise ShimError(f"{func.name}: a stencil reads exactly one memref (found {sorted(srcs)})")
+    (src,) = srcs
+    if src == dst:
+        raise ShimError(f"{func.name}: the stencil's input is also its output (not read-only)")
+    weights = None if all(w is None for w, _ in taps) else [1.0 if w is None else w for w, _ in taps]
+    return Mapping(func.name, "stencil", "spmdb200_stencil_nd", {
+        "rank": rank, "input": src, "output": dst, "domain": ub, "offsets": offsets, "weights": weights,
+        "scale": scale, "tile_sizes": tile or [1] * rank, "steps": lane_steps, "lower": lower,
+        "memory_policy": policy or "none"})
+
+
+# ----------------------------------------------------------------------------- binding
+class BoundKernel:
+    """Calls the mapped entry with the MLIR function's own argument list."""
+
+    def __init__(self, func: Func, mapping: Mapping):
+        self.func, self.mapping = func, mapping
+        self.names = [a.name for a in func.args]
+
+    def __repr__(self) -> str:
+        return f"BoundKernel({self.mapping.name} -> {self.mapping.entry})"
+
+    def __call__(self, *vals, stream=None):
+        import importlib
+        k = importlib.import_module(__package__ + ".kernels") if __package__ else importlib.import_module("kernels")
+        if len(vals) != len(self.names):
+            raise TypeError(f"{self.func.name} takes {len(self.names)} arguments")
+        env = dict(zip(self.names, vals))
+        m, d = self.mapping, self.mapping.detail
+
+        def num(v):
+            return int(env[v]) if v in env else int(v) if str(v).lstrip("-").isdigit() else None
+
+        if m.pattern == "ewise":
+            n = num(d["n"])
+            return k.ewise(env[d["a"]][:n], env[d["b"]][:n], out=env[d["c"]][:n], stream=stream)
+        if m.pattern == "axpy":
+            n = num(d["n"])
+            return k.axpy(d["alpha"], env[d["x"]][:n], env[d["y"]][:n], stream=stream)
+        if m.pattern == "stencil":
+            dom = [num(u) if u in env else self._const(u) for u in d["domain"]]
+            lo = [int(env[v]) if isinstance(v, str) else int(v) for v in d["lower"]]
+            # Output point q of the view is global point lo + q: shift the reads by lo.
+            out = env[d["output"]][tuple(slice(a, max(a, b)) for a, b in zip(lo, dom))]
+            offs = [[o + a for o, a in zip(off, lo)] for off in d["offsets"]]
+            policy = 0 if d["memory_policy"] == "prefer_group" else 1
+            return k.stencil_nd(env[d["input"]], out, offs, weights=d["weights"],
+                                scale=1.0 if d["scale"] is None else d["scale"], tile_sizes=d["tile_sizes"],
+                                steps=d["steps"], policy=policy, stream=stream)
+        if m.pattern == "reduce":
+            n = num(d["n"]) if d["n"] else env[d["input"]].shape[0]
+            a, out = env[d["input"]][:n], env[d["output"]].reshape(1)
+            if m.entry == "spmdb200_hierarchical_sum":
+                return k.hierarchical_sum(a, out, stream=stream)
+            if m.entry == "spmdb200_sum_f32":
+                return k.sum_f32(a, out, stream=stream)
+            init = out.item()  # the combine folds the old value in, as atomic_rmw does
+            return k.reduce(d["kind"], a, init, out=out, stream=stream)
+        raise ShimError(f"unbound pattern {m.pattern}")
+
+    def _const(self, v):
+        for op in _iter_ops(self.func.ops):
+            if op.result == v and op.name == "arith.constant":
+                return int(op.extra)
+        raise ShimError(f"{self.func.name}: domain bound {v} is neither an argument nor a constant")
+
+
+def _iter_ops(ops):
+    for op in ops:
+        yield op
+        yield from _iter_ops(op.region)
+
+
+def load(text: str, skip_unmapped: bool = False) -> dict:
+    """name -> BoundKernel for the module's spmd.kernel functions; a function
+    the shim cannot map raises ShimError unless skip_unmapped."""
+    out = {}
+    for f in parse_module(text):
+        if not f.kernel:
+            continue
+        try:
+            out[f.name] = BoundKernel(f, analyse(f))
+        except ShimError:
+            if not skip_unmapped:
+                raise
+    return out
+
+
+def describe(text: str) -> list:
+    res = []
+    for f in parse_module(text):
+        if not f.kernel:
+            continue
+        try:
+            res.append(analyse(f).to_json())
+        except ShimError as e:
+            res.append({"function": f.name, "pattern": None, "error": str(e)})
+    return res
+
+
+# ----------------------------------------------------------------------------- build stand-ins
+# Host entries with the reference's names and signatures (harness/run_host.py)
+# and the kernel names a reference PTX module carries (func name + "_kernel").
+HOST_ENTRIES = {"ewise", "stencil_cpu", "atomic_sum", "hierarchical_sum"}
+MODULE_KERNELS = {"ewise": "ewise_kernel", "promoted_stencil": "promoted_stencil_kernel",
+                  "atomic_sum": "atomic_sum_kernel", "hierarchical_sum": "hierarchical_sum_kernel"}
+
+
+def build_so(text: str, out: str) -> list:
+    names = [f.name for f in parse_module(text) if f.kernel]
+    missing = [n for n in names if n not in HOST_ENTRIES]
+    if not names or missing:
+        raise ShimError(f"no host entry of this name in the library: {missing or '(no spmd.kernel function)'}")
+    lib = HERE / "libspmdb200.so"
+    if not lib.exists():
+        raise ShimError("libspmdb200.so is not built (run spmd-dialect_b200/build.py)")
+    shutil.copyfile(lib, out)
+    return names
+
+
+def build_module(text: str, out: str) -> list:
+    names = [f.name for f in parse_module(text) if f.kernel]
+    missing = [n for n in names if n not in MODULE_KERNELS]
+    if not names or missing:
+        raise ShimError(f"no kernel of this name in the module: {missing or '(no spmd.kernel function)'}")
+    mod = HERE / "spmdb200_kernels.cubin"
+    if not mod.exists():
+        raise ShimError("spmdb200_kernels.cubin is not built (run spmd-dialect_b200/build.py)")
+    shutil.copyfile(mod, out)
+    return [MODULE_KERNELS[n] for n in names]
+
+
+def main(argv=None) -> int:
+    argv = sys.argv[1:] if argv is None else argv
+    if len(argv) < 2 or argv[0] not in ("describe", "so", "ptx"):
+        print(__doc__.split("\n\n")[-2], file=sys.stderr)
+        return 2
+    text = Path(argv[1]).read_text()
+    try:
+        if argv[0] == "describe":
+            print(json.dumps(describe(text), indent=1))
+        elif argv[0] == "so":
+            if len(argv) != 4 or argv[2] not in ("scf", "omp"):
+                raise ShimError("usage: so FILE scf|omp OUT.so")
+            print("host entries:", ", ".join(build_so(text, argv[3])))
+        else:
+            if len(argv) < 4 or argv[2] not in ("ewise", "promoted", "hierarchical"):
+                raise ShimError("usage: ptx FILE ewise|promoted|hierarchical OUT [sm]")
+            print("kernels:", ", ".join(build_module(text, argv[3])))
+    except ShimError as e:
+        print(f"ERROR: {e}", file=sys.stderr)
+        return 1
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

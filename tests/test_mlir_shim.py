@@ -1,0 +1,92 @@
+"""The textual-MLIR shim on the host: parsing the dialect's generic form,
+recognising the hot-path patterns, reporting what it cannot map, and the
+build stand-ins of the differential script.  When the reference checkout is
+present, its own kernel files are mapped too."""
+from __future__ import annotations
+
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+from conftest import ROOT, spmd_mod
+
+MLIR = ROOT / "tests" / "mlir" / "kernels.mlir"
+REFERENCE = Path("/root/reference/test/SPMD")
+
+
+def _by_name():
+    shim = spmd_mod("mlir_shim")
+    return {d["function"]: d for d in shim.describe(MLIR.read_text())}
+
+
+def test_patterns_recognised():
+    d = _by_name()
+    assert d["ewise"]["entry"] == "spmdb200_ewise"
+    assert d["axpy"]["pattern"] == "axpy" and d["axpy"]["alpha"] == 2.5
+    ps = d["promoted_stencil"]
+    assert ps["offsets"] == [[0, 0], [0, 1], [1, 0]] and ps["tile_sizes"] == [32, 8]
+    assert ps["memory_policy"] == "prefer_group" and ps["scale"] is None and ps["weights"] is None
+    jac = d["jacobi_interior"]
+    assert jac["offsets"] == [[0, 0], [-1, 0], [1, 0], [0, 1], [0, -1]] and jac["scale"] == pytest.approx(0.2)
+    assert d["pairs_stepped"]["steps"] == [2] and d["pairs_stepped"]["offsets"] == [[0], [1]]
+    assert d["smooth_interior"]["lower"] == [1] and d["smooth_interior"]["weights"] == [0.5, 0.5]
+    assert d["hierarchical_sum"]["entry"] == "spmdb200_hierarchical_sum"
+    assert d["max_i32"]["entry"] == "spmdb200_reduce_i32" and d["max_i32"]["kind"] == "max"
+
+
+def test_unmappable_functions_are_reported_not_guessed():
+    d = _by_name()
+    assert d["gather_unsupported"]["pattern"] is None
+    assert "affine" in d["gather_unsupported"]["error"]
+    shim = spmd_mod("mlir_shim")
+    with pytest.raises(shim.ShimError):
+        shim.load(MLIR.read_text())  # load() maps every kernel or fails
+
+
+def test_plan_of_mapped_stencils():
+    """The mapped tile sizes / offsets drive the same promotion plan."""
+    k = spmd_mod("kernels")
+    ps = _by_name()["promoted_stencil"]
+    mn = [min(o[d] for o in ps["offsets"]) for d in range(2)]
+    mx = [max(o[d] for o in ps["offsets"]) for d in range(2)]
+    assert k.promotion_plan(ps["tile_sizes"], mn, mx, steps=ps["steps"])[:2] == (0, (33, 9))
+
+
+def test_build_stand_ins(tmp_path):
+    shim = spmd_mod("mlir_shim")
+    one = tmp_path / "ewise.mlir"
+    text = MLIR.read_text()
+    one.write_text(text[:text.index("func.func @axpy")])
+    so = tmp_path / "ewise_scf.so"
+    r = subprocess.run([sys.executable, str(ROOT / "spmd-dialect_b200" / "mlir_shim.py"), "so", str(one), "scf",
+                        str(so)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    import ctypes
+    assert hasattr(ctypes.CDLL(str(so)), "ewise")  # the reference's host entry name
+    mod = tmp_path / "ewise.ptx"
+    r = subprocess.run([sys.executable, str(ROOT / "spmd-dialect_b200" / "mlir_shim.py"), "ptx", str(one), "ewise",
+                        str(mod), "sm_100"], capture_output=True, text=True)
+    assert r.returncode == 0 and "ewise_kernel" in r.stdout and mod.stat().st_size > 0
+    with pytest.raises(shim.ShimError):
+        shim.build_so(text, str(tmp_path / "all.so"))  # axpy etc. have no reference host entry
+
+
+@pytest.mark.skipif(not REFERENCE.exists(), reason="reference checkout not present")
+def test_reference_kernel_files_map():
+    shim = spmd_mod("mlir_shim")
+    want = {
+        "lower-to-gpu-nvptx.mlir": {"ewise": "spmdb200_ewise"},
+        "lower-to-gpu-nvptx-promoted.mlir": {"promoted_stencil": "spmdb200_stencil_nd"},
+        "lower-to-gpu-nvptx-reduction.mlir": {"atomic_sum": "spmdb200_sum_f32"},
+        "lower-to-gpu-nvptx-hierarchical-reduction.mlir": {"hierarchical_sum": "spmdb200_hierarchical_sum"},
+        "differential-stencil.mlir": {"stencil_cpu": "spmdb200_stencil_nd"},
+    }
+    for f, names in want.items():
+        got = {d["function"]: d.get("entry") for d in shim.describe((REFERENCE / f).read_text())}
+        for n, e in names.items():
+            assert got.get(n) == e, (f, n, got)
+    steps = {d["function"]: (d["offsets"], d["steps"]) for d in shim.describe((REFERENCE / "promotion.mlir").read_text())}
+    assert steps["stencil1d_stepped"] == ([[0], [1]], [2])
+    assert steps["stencil_pos_halo"][0] == [[1], [2]] and steps["stencil_neg_halo"][0] == [[-1], [-2]]
