@@ -410,6 +410,10 @@ def run_spmd_arm(args) -> None:
                 "traffic_source": "profiles/jacobi2d_persistent_f4_16384x16384.md (bytes per update x updates)",
                 "kernel": kname, "peak_kind": f"{peak_kind} hbm_gbs (copy bandwidth)",
                 "passes_per_step": {"four_sweep": plan[0], "two_sweep": plan[1], "single_sweep": plan[2]},
+                "limiter": ("SM issue/latency, not HBM: four sweeps per pass move 2.1 B/update (ncu), DRAM "
+                            "under half busy, issue ~60 percent active, leading stall shared-memory latency "
+                            "(profiles/jacobi2d_persistent_f4_16384x16384.md); the one-sweep-per-pass ceiling "
+                            f"at 8 B/update would be {hbm_peak / 8.0:.0f} Gcell/s"),
                 "algorithmic_bytes_per_update": bytes_per_update(SWEEPS),
                 "algorithmic_bytes_per_launch": round(alg_bytes)}
 
