@@ -190,6 +190,13 @@ int spmdb200_sum_f32(float *A_base, float *A_aligned, int64_t A_offset, int64_t 
                      float *out_base, float *out_aligned, int64_t out_offset,
                      int64_t N, void *ws, size_t ws_bytes, void *stream);
 
+/* *partial (device f64) = the unrounded f64 total of A[0..N) in the same
+ * deterministic order as spmdb200_sum_f32: one rank's share of a sum split
+ * across GPUs, combined by the caller in rank order before the single f32
+ * rounding.  Same workspace as spmdb200_sum_f32.  No reference entry. */
+int spmdb200_sum_f32_partial(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
+                             int64_t N, double *partial, void *ws, size_t ws_bytes, void *stream);
+
 /* The same deterministic sum as spmdb200_sum_f32 for callers that cannot
  * allocate device memory: code inside a stream capture that must not
  * allocate, a plugin whose host application owns every device allocation, or

@@ -60,6 +60,7 @@ _SIGS = {
     "spmdb200_promotion_plan": (ctypes.c_int, [ctypes.c_int, c_p, c_p, c_p, c_p, c_i, c_i, ctypes.c_int, c_p, c_p]),
     "spmdb200_stencil_nd": (ctypes.c_int, [ctypes.c_int, c_p, c_p, c_p, c_p, c_p, c_p, ctypes.c_int, c_p, c_p, c_f,
                                            c_p, c_p, c_i, ctypes.c_int, c_p, c_p]),
+    "spmdb200_sum_f32_partial": (ctypes.c_int, D1 + [c_i, c_p, c_p, c_sz, c_p]),
     "spmdb200_jacobi_workspace_bytes": (c_sz, []),
     "spmdb200_jacobi2d": (ctypes.c_int, D2 + D2 + [c_i, c_i, c_p, c_p, c_sz, c_p]),
     "spmdb200_jacobi3d": (ctypes.c_int, D3 + D3 + [c_i, c_i, c_p, c_p, c_sz, c_p]),

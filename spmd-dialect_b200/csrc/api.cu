@@ -400,6 +400,18 @@ int spmdb200_sum_f32(float *A_base, float *A, int64_t A_off, int64_t A_size, int
   return ok();
 }
 
+int spmdb200_sum_f32_partial(float *A_base, float *A, int64_t A_off, int64_t A_size, int64_t A_st, int64_t N,
+                             double *partial, void *ws, size_t ws_bytes, void *stream) {
+  (void)A_base;
+  CHECK(check1("A", A, A_off, A_size, A_st, N));
+  if (!partial) return fail(SPMDB200_ERR_INVALID_ARG, "partial: null pointer");
+  if (!ws || ((uintptr_t)ws & 255u) != 0 || ws_bytes < sum_f32_workspace_bytes(N))
+    return fail(SPMDB200_ERR_WORKSPACE, "workspace must be >= %zu bytes and 256-byte aligned",
+                sum_f32_workspace_bytes(N));
+  CUDA_TRY(launch_sum_f32(View1{A ? A + A_off : nullptr, N, A_st}, nullptr, N, ws, (cudaStream_t)stream, partial));
+  return ok();
+}
+
 int spmdb200_sum_i32(int32_t *A_base, int32_t *A, int64_t A_off, int64_t A_size, int64_t A_st,
                      int32_t *o_base, int32_t *o, int64_t o_off, int64_t N, void *stream) {
   (void)A_base; (void)o_base;

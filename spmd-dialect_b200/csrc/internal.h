@@ -19,7 +19,8 @@ cudaError_t launch_axpy(float alpha, View1 x, View1 y, int64_t n, cudaStream_t s
 // Workspace of the deterministic f32 sum: [ticket u32 | pad to 256 B | f64 partials].
 size_t sum_f32_workspace_bytes(int64_t n);
 int sum_f32_grid(int64_t n);
-cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_t s);
+// f64_out set: the unrounded f64 total goes there and `out` is not touched.
+cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_t s, double *f64_out = nullptr);
 cudaError_t launch_sum_i32(const int32_t *a, int64_t stride, int32_t *out, int64_t n, cudaStream_t s);
 cudaError_t launch_hier_sum_f32(View1 a, float *out, int64_t n, cudaStream_t s);
 // Every spmd.reduce kind (0 add, 1 mul, 2 max, 3 min, 4 and, 5 or, 6 xor):

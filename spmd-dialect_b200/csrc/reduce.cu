@@ -43,10 +43,13 @@ size_t sum_f32_workspace_bytes(int64_t n) {
 
 // Deterministic f32 sum: per-block f64 partials, last block (ticket) combines
 // them in index order and performs the single f32 rounding of
-// out = out + total.  The ticket is reset to 0 so the workspace stays reusable.
+// out = out + total -- or, when f64_out is set, stores the f64 total there
+// unrounded (a rank's share of a sum across GPUs).  The ticket is reset to 0
+// so the workspace stays reusable.
 __global__ void __launch_bounds__(kSumThreads, 8) sum_f32_kernel(const float *__restrict__ a, int64_t sa,
                                                               int64_t n, float *out,
-                                                              unsigned *ticket, double *partials) {
+                                                              unsigned *ticket, double *partials,
+                                                              double *f64_out) {
   __shared__ double sh[32];
   __shared__ int last;
   const double b = block_sum_f64(thread_sum_f64(a, sa, n), sh);
@@ -63,8 +66,12 @@ __global__ void __launch_bounds__(kSumThreads, 8) sum_f32_kernel(const float *__
   for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) p = __dadd_rn(p, __ldcg(partials + i));
   const double tot = block_sum_f64(p, sh);
   if (threadIdx.x == 0) {
-    const float o = *out;
-    *out = __double2float_rn(__dadd_rn((double)o, tot));
+    if (f64_out) {
+      *f64_out = tot;
+    } else {
+      const float o = *out;
+      *out = __double2float_rn(__dadd_rn((double)o, tot));
+    }
     *ticket = 0u;
   }
 }
@@ -92,10 +99,12 @@ enum class BulkMode { kF32Det, kI32, kF32Atomic };
 
 template <BulkMode M>
 __global__ void __launch_bounds__(kBulkThreads) sum_bulk_kernel(const void *__restrict__ a, int64_t n, void *out,
-                                                               unsigned *ticket, double *partials) {
+                                                               unsigned *ticket, double *partials,
+                                                               double *f64_out) {
   extern __shared__ __align__(128) unsigned char bulk_raw[];
-  unsigned char *smem =
-      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(bulk_raw) + 127) & ~uintptr_t(127));
+  // Aligned by pointer arithmetic on the shared array, so the stage reads
+  // stay shared-space (LDS) accesses.
+  unsigned char *smem = bulk_raw + ((128u - (smem_u32(bulk_raw) & 127u)) & 127u);
   __shared__ uint64_t full[kBulkStages];
   __shared__ double shd[32];
   __shared__ uint32_t shu[32];
@@ -150,8 +159,12 @@ __global__ void __launch_bounds__(kBulkThreads) sum_bulk_kernel(const void *__re
       for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) p = __dadd_rn(p, __ldcg(partials + i));
       const double tot = block_sum_f64(p, shd);
       if (threadIdx.x == 0) {
-        float *o = static_cast<float *>(out);
-        *o = __double2float_rn(__dadd_rn((double)*o, tot));
+        if (f64_out) {
+          *f64_out = tot;
+        } else {
+          float *o = static_cast<float *>(out);
+          *o = __double2float_rn(__dadd_rn((double)*o, tot));
+        }
         *ticket = 0u;
       }
     }
@@ -192,15 +205,15 @@ int sum_f32_grid(int64_t n) {
   return a > b ? a : b;
 }
 
-cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_t s) {
+cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_t s, double *f64_out) {
   unsigned *ticket = static_cast<unsigned *>(ws);
   double *partials = reinterpret_cast<double *>(static_cast<char *>(ws) + kSumWsHeader);
   if (bulk_ok(a.p, a.s)) {
     sum_bulk_kernel<BulkMode::kF32Det><<<bulk_grid<BulkMode::kF32Det>(n), kBulkThreads, kBulkSmem, s>>>(
-        a.p, n, out, ticket, partials);
+        a.p, n, out, ticket, partials, f64_out);
   } else {
     sum_f32_kernel<<<reduce_grid(sum_f32_kernel, g_f32_cache, n), kSumThreads, 0, s>>>(a.p, a.s, n, out, ticket,
-                                                                                       partials);
+                                                                                       partials, f64_out);
   }
   return cudaGetLastError();
 }
@@ -208,8 +221,8 @@ cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_
 cudaError_t launch_sum_i32(const int32_t *a, int64_t stride, int32_t *out, int64_t n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   if (bulk_ok(a, stride))
-    sum_bulk_kernel<BulkMode::kI32><<<bulk_grid<BulkMode::kI32>(n), kBulkThreads, kBulkSmem, s>>>(a, n, out,
-                                                                                                 nullptr, nullptr);
+    sum_bulk_kernel<BulkMode::kI32><<<bulk_grid<BulkMode::kI32>(n), kBulkThreads, kBulkSmem, s>>>(
+        a, n, out, nullptr, nullptr, nullptr);
   else
     sum_i32_kernel<<<reduce_grid(sum_i32_kernel, g_i32_cache, n), kSumThreads, 0, s>>>(a, stride, n, out);
   return cudaGetLastError();
@@ -219,7 +232,7 @@ cudaError_t launch_hier_sum_f32(View1 a, float *out, int64_t n, cudaStream_t s) 
   if (n <= 0) return cudaSuccess;
   if (bulk_ok(a.p, a.s))
     sum_bulk_kernel<BulkMode::kF32Atomic><<<bulk_grid<BulkMode::kF32Atomic>(n), kBulkThreads, kBulkSmem, s>>>(
-        a.p, n, out, nullptr, nullptr);
+        a.p, n, out, nullptr, nullptr, nullptr);
   else
     hier_sum_f32_kernel<<<reduce_grid(hier_sum_f32_kernel, g_hier_cache, n), kSumThreads, 0, s>>>(a.p, a.s, n,
                                                                                                   out);

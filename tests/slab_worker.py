@@ -60,6 +60,40 @@ def main() -> None:
             print(f"D={D} H={H} W={W} sweeps={sweeps}: grid bit-exact={same} residual max rel err={rel:.3g}",
                   flush=True)
             ok = ok and same and rel <= 1e-12
+    # Reductions and axpy split across the ranks (one exchange for the sums).
+    sh = spmd_mod("shard")
+    n = (1 << 22) + 5
+    x = np.random.RandomState(0).random_sample(n).astype(np.float32)
+    lo, hi = sh.shard_range(n, dist.get_world_size(), rank)
+    xl = torch.from_numpy(x[lo:hi]).cuda()
+    s1, s2 = sh.sum_f32(xl, init=0.5), sh.sum_f32(xl, init=0.5)
+    v = np.random.RandomState(1).randint(0, 100, size=n).astype(np.int32)
+    si = sh.sum_i32(torch.from_numpy(v[lo:hi]).cuda(), init=-7)
+    y = np.random.RandomState(2).random_sample(n).astype(np.float32)
+    yl = torch.from_numpy(y[lo:hi]).cuda()
+    sh.axpy(2.5, xl, yl)
+    mine = yl.cpu().numpy()
+    parts = [None] * dist.get_world_size()
+    dist.all_gather_object(parts, (float(s1), int(si)))
+    if rank == 0:
+        from oracle import oracle
+        exact = 0.5 + oracle.sum_f64(x)
+        same_all = all(p_ == parts[0] for p_ in parts)
+        ok_sum = abs(float(s1) - exact) <= 1e-6 * abs(exact) and s1 == s2 and same_all
+        ok_i32 = si == int(v.astype(np.int64).sum()) - 7
+        print(f"sharded sums: f32 rel err {abs(float(s1) - exact) / exact:.3g} deterministic={s1 == s2} "
+              f"same on every rank={same_all} i32 exact={ok_i32}", flush=True)
+        ok = ok and ok_sum and ok_i32
+    want_y = None
+    if True:
+        from oracle import oracle
+        want_y = oracle.axpy(2.5, x[lo:hi], y[lo:hi])
+    ok_axpy = np.array_equal(mine.view(np.uint32), want_y.view(np.uint32))
+    flag_axpy = torch.tensor([1 if ok_axpy else 0], device="cuda")
+    dist.all_reduce(flag_axpy, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        print(f"sharded axpy bit-exact on every rank={bool(flag_axpy.item())}", flush=True)
+        ok = ok and bool(flag_axpy.item())
     # Checkpoint from both ranks, resume in a fresh 2-rank job.
     import tempfile
     ck_dir = tempfile.mkdtemp() if rank == 0 else None

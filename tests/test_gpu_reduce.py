@@ -13,7 +13,7 @@ import json
 import numpy as np
 import pytest
 
-from conftest import GOLDEN
+from conftest import GOLDEN, spmd_mod
 
 pytestmark = pytest.mark.gpu
 
@@ -119,3 +119,16 @@ def test_i32_sum_wraps_like_addi(kernels, oracle_mod):
     out = torch.zeros(1, dtype=torch.int32, device="cuda")
     kernels.sum_i32(_t(a), out)
     assert int(out.item()) == oracle_mod.sum_i32(a)
+
+
+def test_partial_sum_is_the_unrounded_f64_total(kernels, oracle_mod):
+    """spmdb200_sum_f32_partial: f64 total of a rank's block, both kernel paths."""
+    import torch
+    shard = spmd_mod("shard")
+    for n, stride in ((1 << 20, 1), (100003, 1), (77777, 3)):
+        x = np.random.RandomState(n).random_sample(n * stride).astype(np.float32)
+        t = torch.from_numpy(x).cuda()[::stride]
+        p = float(shard.partial_sum_f32(t).item())
+        exact = oracle_mod.sum_f64(np.ascontiguousarray(x[::stride]))
+        assert abs(p - exact) <= 1e-12 * abs(exact)
+        assert shard.sum_f32(t, init=1.0) == np.float32(1.0 + p)
