@@ -415,7 +415,12 @@ def run_spmd_arm(args) -> None:
                             "(profiles/jacobi2d_persistent_f4_16384x16384.md); the one-sweep-per-pass ceiling "
                             f"at 8 B/update would be {hbm_peak / 8.0:.0f} Gcell/s"),
                 "algorithmic_bytes_per_update": bytes_per_update(SWEEPS),
-                "algorithmic_bytes_per_launch": round(alg_bytes)}
+                "algorithmic_bytes_per_launch": round(alg_bytes),
+                # The same time against one-sweep-per-pass traffic (read u, write v: 8 B per update),
+                # i.e. how far past the ceiling of any kernel without temporal blocking it runs.
+                "single_sweep_bytes_per_update": 8,
+                "frac_vs_single_sweep_ceiling": round(rows * GRID * SWEEPS * 8 / (ms_kernel * 1e-3) / 1e9
+                                                      / hbm_peak, 4)}
 
     cpu = None
     secondary = None
