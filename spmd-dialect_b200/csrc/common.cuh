@@ -177,6 +177,31 @@ __device__ __forceinline__ void st_f4(float *p, float4 v) {
                : "memory");
 }
 
+// ---- programmatic dependent launch -----------------------------------------------
+// A kernel launched with launch_pdl() may start while the previous kernel of
+// its stream is finishing (its launch and prologue overlap that kernel's
+// tail); pdl_wait() then blocks until the previous kernel has completed and
+// its memory is visible, so nothing may touch global memory before it.
+// pdl_trigger() lets the next such launch start early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                              cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---- seeded synthetic input ---------------------------------------------------
 // splitmix64 finaliser over (seed, row, column): a counter-based generator, so
 // any rank can produce any global cell without coordination.

@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(kSumThreads, 8) sum_f32_kernel(const float *__
                                                               double *f64_out) {
   __shared__ double sh[32];
   __shared__ int last;
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
   const double b = block_sum_f64(thread_sum_f64(a, sa, n), sh);
   if (threadIdx.x == 0) {
     partials[blockIdx.x] = b;
@@ -79,6 +81,8 @@ __global__ void __launch_bounds__(kSumThreads, 8) sum_f32_kernel(const float *__
 __global__ void __launch_bounds__(kSumThreads) sum_i32_kernel(const int32_t *__restrict__ a, int64_t sa,
                                                               int64_t n, int32_t *out) {
   __shared__ uint32_t sh[32];
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
   const uint32_t b = block_sum_u32(thread_sum_u32(a, sa, n), sh);
   if (threadIdx.x == 0 && b != 0u) atomicAdd(reinterpret_cast<unsigned *>(out), b);
 }
@@ -86,6 +90,8 @@ __global__ void __launch_bounds__(kSumThreads) sum_i32_kernel(const int32_t *__r
 __global__ void __launch_bounds__(kSumThreads, 8) hier_sum_f32_kernel(const float *__restrict__ a, int64_t sa,
                                                                    int64_t n, float *out) {
   __shared__ double sh[32];
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
   const double b = block_sum_f64(thread_sum_f64(a, sa, n), sh);
   if (threadIdx.x == 0) atomicAdd(out, __double2float_rn(b));
 }
@@ -115,6 +121,8 @@ __global__ void __launch_bounds__(kBulkThreads) sum_bulk_kernel(const void *__re
     mbar_fence_init();
   }
   __syncthreads();
+  pdl_wait();  // the previous kernel of the stream is complete (it may have written the input)
+  if (threadIdx.x == 0) pdl_trigger();
   const int64_t units = n >> 2;  // 16-byte units; the last n % 4 elements are the tail
   int64_t lo, hi;
   cta_range(units, lo, hi);
@@ -208,35 +216,31 @@ int sum_f32_grid(int64_t n) {
 cudaError_t launch_sum_f32(View1 a, float *out, int64_t n, void *ws, cudaStream_t s, double *f64_out) {
   unsigned *ticket = static_cast<unsigned *>(ws);
   double *partials = reinterpret_cast<double *>(static_cast<char *>(ws) + kSumWsHeader);
-  if (bulk_ok(a.p, a.s)) {
-    sum_bulk_kernel<BulkMode::kF32Det><<<bulk_grid<BulkMode::kF32Det>(n), kBulkThreads, kBulkSmem, s>>>(
-        a.p, n, out, ticket, partials, f64_out);
-  } else {
-    sum_f32_kernel<<<reduce_grid(sum_f32_kernel, g_f32_cache, n), kSumThreads, 0, s>>>(a.p, a.s, n, out, ticket,
-                                                                                       partials, f64_out);
-  }
-  return cudaGetLastError();
+  // Launched with programmatic dependent launch: back-to-back reductions
+  // overlap each launch and prologue with the previous kernel's tail.
+  if (bulk_ok(a.p, a.s))
+    return launch_pdl(sum_bulk_kernel<BulkMode::kF32Det>, bulk_grid<BulkMode::kF32Det>(n), kBulkThreads, kBulkSmem,
+                      s, a.p, n, out, ticket, partials, f64_out);
+  return launch_pdl(sum_f32_kernel, reduce_grid(sum_f32_kernel, g_f32_cache, n), kSumThreads, 0, s, a.p, a.s, n, out,
+                    ticket, partials, f64_out);
 }
 
 cudaError_t launch_sum_i32(const int32_t *a, int64_t stride, int32_t *out, int64_t n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   if (bulk_ok(a, stride))
-    sum_bulk_kernel<BulkMode::kI32><<<bulk_grid<BulkMode::kI32>(n), kBulkThreads, kBulkSmem, s>>>(
-        a, n, out, nullptr, nullptr, nullptr);
-  else
-    sum_i32_kernel<<<reduce_grid(sum_i32_kernel, g_i32_cache, n), kSumThreads, 0, s>>>(a, stride, n, out);
-  return cudaGetLastError();
+    return launch_pdl(sum_bulk_kernel<BulkMode::kI32>, bulk_grid<BulkMode::kI32>(n), kBulkThreads, kBulkSmem, s, a,
+                      n, out, nullptr, nullptr, nullptr);
+  return launch_pdl(sum_i32_kernel, reduce_grid(sum_i32_kernel, g_i32_cache, n), kSumThreads, 0, s, a, stride, n,
+                    out);
 }
 
 cudaError_t launch_hier_sum_f32(View1 a, float *out, int64_t n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   if (bulk_ok(a.p, a.s))
-    sum_bulk_kernel<BulkMode::kF32Atomic><<<bulk_grid<BulkMode::kF32Atomic>(n), kBulkThreads, kBulkSmem, s>>>(
-        a.p, n, out, nullptr, nullptr, nullptr);
-  else
-    hier_sum_f32_kernel<<<reduce_grid(hier_sum_f32_kernel, g_hier_cache, n), kSumThreads, 0, s>>>(a.p, a.s, n,
-                                                                                                  out);
-  return cudaGetLastError();
+    return launch_pdl(sum_bulk_kernel<BulkMode::kF32Atomic>, bulk_grid<BulkMode::kF32Atomic>(n), kBulkThreads,
+                      kBulkSmem, s, a.p, n, out, nullptr, nullptr, nullptr);
+  return launch_pdl(hier_sum_f32_kernel, reduce_grid(hier_sum_f32_kernel, g_hier_cache, n), kSumThreads, 0, s, a.p,
+                    a.s, n, out);
 }
 
 }  // namespace spmdb200

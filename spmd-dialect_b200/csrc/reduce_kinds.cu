@@ -105,6 +105,8 @@ __global__ void __launch_bounds__(kKindThreads) reduce_kind_kernel(const T *__re
   __shared__ A sh[32];
   __shared__ int last;
   A *partials = static_cast<A *>(partials_raw);
+  pdl_wait();  // launched with programmatic dependent launch: nothing global before this
+  if (threadIdx.x == 0) pdl_trigger();
   const int64_t nth = (int64_t)gridDim.x * blockDim.x;
   A acc = O::id();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += nth) acc = O::op(acc, O::in(a[i * sa]));
@@ -158,8 +160,7 @@ cudaError_t launch_kind(const T *a, int64_t sa, int64_t n, T *out, T init, void 
   if (g > kMaxCtas) g = kMaxCtas;
   unsigned *ticket = static_cast<unsigned *>(ws);
   void *partials = static_cast<char *>(ws) + 256;
-  reduce_kind_kernel<T, K><<<(unsigned)g, kKindThreads, 0, s>>>(a, sa, n, out, init, ticket, partials);
-  return cudaGetLastError();
+  return launch_pdl(reduce_kind_kernel<T, K>, (unsigned)g, kKindThreads, 0, s, a, sa, n, out, init, ticket, partials);
 }
 
 }  // namespace
