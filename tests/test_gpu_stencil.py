@@ -157,8 +157,8 @@ def _run_j3(kernels, u0, sweeps, res_every):
                                          # x-contiguous rows of a multiple of 16 bytes: persistent TMA path
                                          ((33, 17, 132), 5, 1), ((5, 3, 4), 3, 1), ((17, 50, 136), 4, 2),
                                          ((40, 33, 260), 7, 7), ((1, 1, 4), 2, 1),
-                                         # two-sweep passes (4+ sweeps on the persistent path), residuals
-                                         # on either sweep of a pass, ragged and exact tile shapes
+                                         # longer runs on the persistent path: residuals at odd and even
+                                         # sweeps, ragged and exact tile shapes
                                          ((37, 45, 300), 9, 2), ((20, 29, 132), 8, 1), ((5, 16, 128), 4, 4),
                                          ((64, 30, 260), 12, 3), ((17, 14, 120), 6, 5), ((33, 3, 8), 5, 1),
                                          ((3, 40, 244), 4, 1)])
