@@ -445,7 +445,6 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
         float4 zp[RPW3];
 #pragma unroll
         for (int q = 0; q < RPW3; ++q) zp[q] = ld4s(Pp + (r0 + q + 1) * BOXW3 + sc);
-        const bool to_up = has_up && z == k.z_lo, to_dn = has_dn && z == k.z_hi - 1;
         if (z < k.z_hi) {
           const long long gz = k.g_z0 + z;
           const bool zb = (gz == 0 || gz == k.g_d - 1);
@@ -485,29 +484,6 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
               }
             }
           }
-          if constexpr (SLAB) {
-            if (to_up || to_dn) {
-              // An edge plane of the slab: copy the cells this thread just
-              // stored (its own writes, L2-resident) into the neighbour's halo
-              // plane; the plane loop above stays free of peer-store tests.
-              float *up_dst = (s & 1) ? k.peers.up_u : k.peers.up_v;
-              float *dn_dst = (s & 1) ? k.peers.dn_u : k.peers.dn_v;
-#pragma unroll 1
-              for (int q = 0; q < RPW3; ++q) {
-                const int y = y0 + q;
-                if (y >= k.h || gx0 >= k.w) continue;
-                const long long yo = (long long)y * k.sy + gx0;
-                const float *mine = dst + (long long)z * k.sz + yo;
-                float4 o;
-                o.x = mine[0];
-                o.y = gx0 + 1 < k.w ? mine[1] : 0.0f;
-                o.z = gx0 + 2 < k.w ? mine[2] : 0.0f;
-                o.w = gx0 + 3 < k.w ? mine[3] : 0.0f;
-                if (to_up) store4_w(up_dst + k.peers.up_row * k.sz + yo, gx0, k.w, o);
-                if (to_dn) store4_w(dn_dst + k.peers.dn_row * k.sz + yo, gx0, k.w, o);
-              }
-            }
-          }
         }
 #pragma unroll
         for (int q = 0; q < RPW3; ++q) {
@@ -515,16 +491,45 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
           c[q] = zp[q];
         }
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&tail->empty[(pz - 1) % ST3]);  // plane z-1 is no longer needed
-          if (SLAB && (to_up || to_dn)) {  // this warp's rows of a neighbour's halo plane are stored
+        if (lane == 0) mbar_arrive(&tail->empty[(pz - 1) % ST3]);  // plane z-1 is no longer needed
+      }
+      if (!ok) break;
+      if constexpr (SLAB) {
+        // An edge item of the slab: copy this warp's rows of the first / last
+        // owned plane (its own stores, L2-resident) into the neighbour's halo
+        // plane, then count the delivery.  Done once per item, outside the
+        // plane loop, which keeps that loop the one-GPU loop.
+        const bool up_item = has_up && zc == 0, dn_item = has_dn && zc == k.zchunks - 1;
+        if (up_item || dn_item) {
+          float *up_dst = (s & 1) ? k.peers.up_u : k.peers.up_v;
+          float *dn_dst = (s & 1) ? k.peers.dn_u : k.peers.dn_v;
+#pragma unroll 1
+          for (int e = 0; e < 2; ++e) {
+            if (e == 0 ? !up_item : !dn_item) continue;
+            const int z = e == 0 ? k.z_lo : k.z_hi - 1;
+            float *to = e == 0 ? up_dst + k.peers.up_row * k.sz : dn_dst + k.peers.dn_row * k.sz;
+#pragma unroll 1
+            for (int q = 0; q < RPW3; ++q) {
+              const int y = y0 + q;
+              if (y >= k.h || gx0 >= k.w) continue;
+              const long long yo = (long long)y * k.sy + gx0;
+              const float *mine = dst + (long long)z * k.sz + yo;
+              float4 o;
+              o.x = mine[0];
+              o.y = gx0 + 1 < k.w ? mine[1] : 0.0f;
+              o.z = gx0 + 2 < k.w ? mine[2] : 0.0f;
+              o.w = gx0 + 3 < k.w ? mine[3] : 0.0f;
+              store4_w(to + yo, gx0, k.w, o);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) {
             __threadfence_system();
-            if (to_up) red_release_sys_add(k.peers.up_flag, 1u);
-            if (to_dn) red_release_sys_add(k.peers.dn_flag, 1u);
+            if (up_item) red_release_sys_add(k.peers.up_flag, 1u);
+            if (dn_item) red_release_sys_add(k.peers.dn_flag, 1u);
           }
         }
       }
-      if (!ok) break;
       __syncwarp();
       if (lane == 0) {  // the item's last two planes
         mbar_arrive(&tail->empty[(pc + BZ3) % ST3]);
