@@ -30,7 +30,8 @@ def main() -> None:
     slab = spmd_mod("slab")
     rank = dist.get_rank()
     ok = True
-    for (G, W, sweeps, res_every) in [(514, 1000, 13, 3), (67, 130, 8, 1), (4096, 4096, 20, 10)]:
+    for (G, W, sweeps, res_every) in [(514, 1000, 13, 3), (67, 130, 8, 1), (4096, 4096, 20, 10),
+                                      (9, 300, 9, 1)]:  # 5 and 4 rows: a rank owns exactly one halo's depth
         u0 = jacobi_init((G, W), 4)
         job = slab.SlabJacobi2D(cols=W, G=G, res_every=res_every, init=u0)
         job.run(sweeps)

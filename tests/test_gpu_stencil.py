@@ -85,6 +85,12 @@ J2_CASES = [
     (333, 777, 12, 4, 780),
     (520, 1300, 17, 3, None),
     (130, 245, 16, 5, 248),
+    # tiny grids through four-sweep passes: boxes reach far past every edge
+    (5, 9, 8, 1, 12),
+    (3, 3, 9, 1, 4),
+    (1, 5, 8, 2, 8),
+    (2, 130, 16, 4, None),
+    (41, 121, 13, 13, 124),
 ]
 
 
