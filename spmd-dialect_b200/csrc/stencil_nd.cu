@@ -25,8 +25,8 @@ namespace {
 
 constexpr int kNdThreads = 256;
 constexpr int kNdWarps = kNdThreads / 32;
-// Footprint budget of one staged tile chosen by the kernel: the six blocks of
-// 256 threads the register file holds per SM fit its shared memory.
+// Footprint budget of one staged tile chosen by the kernel (a block holds two):
+// three blocks of 256 threads fit one SM's shared memory.
 constexpr int kNdTileBytes = 36 * 1024;
 
 // Launch parameters.  Dimensions are outermost first and padded to 3 with
@@ -45,8 +45,19 @@ struct NdStencil {
   int fdim[3];  // footprint extent per dimension of one kernel tile
   int min_off[3], max_off[3];
   int vsplit;   // segments per tile row
+  // Staged footprint layout (promoted): cell (i0, i1, c) at pad + i0 * pitch0
+  // + i1 * pitch1 + c of a buffer of buf_cells floats.  With unit contiguous
+  // strides the pitches are congruent to A's strides mod 4 and pad is the
+  // element address of cell (0, 0, 0) mod 4, so every 16-byte chunk of A
+  // lands on a 16-byte boundary of shared memory; otherwise the pitches are
+  // dense and pad is 0.
+  int pitch0, pitch1, buf_cells;
+  // Promoted: offsets inside one tile fit 32 bits (checked on the host).
+  int as0, as1;  // A strides of the two outer dimensions
+  int bs0, bs1;  // B distance between neighbouring point rows (step * stride)
+  int gstep[3];  // the grid size as tile coordinates (mixed radix tiles[0..2])
   int off[kNdMaxTaps][3];
-  int tap_lin[kNdMaxTaps];         // (off_j - min_off) flattened over the footprint's extents
+  int tap_lin[kNdMaxTaps];         // (off_j - min_off) . (pitch0, pitch1, 1)
   long long tap_goff[kNdMaxTaps];  // off_j . a_stride
   float w[kNdMaxTaps];
 };
@@ -54,16 +65,36 @@ struct NdStencil {
 __device__ __forceinline__ void cp_async4(uint32_t dst, const float *src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }
-
-// Tile t -> tile coordinates (the contiguous dimension fastest); tile counts
-// fit 32 bits (checked on the host).
-__device__ __forceinline__ void tile_coords(const NdStencil &k, unsigned t, long long *tc) {
-  const unsigned n2 = (unsigned)k.tiles[2], n1 = (unsigned)k.tiles[1];
-  const unsigned q = t / n2;
-  tc[2] = t - q * n2;
-  tc[1] = q % n1;
-  tc[0] = q / n1;
+__device__ __forceinline__ void cp_async16(uint32_t dst, const float *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
+
+// A block's current tile: its index t and coordinates (the contiguous
+// dimension fastest).  Blocks step through the tiles by the grid size, added
+// as a mixed-radix number so no division runs per tile; tile counts fit 32
+// bits (checked on the host).
+struct TileIter {
+  unsigned t;
+  int c[3];
+  __device__ __forceinline__ void start(const NdStencil &k, unsigned t0) {
+    const unsigned n2 = (unsigned)k.tiles[2], n1 = (unsigned)k.tiles[1];
+    const unsigned q = t0 / n2;
+    t = t0;
+    c[2] = (int)(t0 - q * n2);
+    c[1] = (int)(q % n1);
+    c[0] = (int)(q / n1);
+  }
+  __device__ __forceinline__ void advance(const NdStencil &k) {
+    t += gridDim.x;
+    c[2] += k.gstep[2];
+    int carry = c[2] >= (int)k.tiles[2];
+    c[2] -= carry ? (int)k.tiles[2] : 0;
+    c[1] += k.gstep[1] + carry;
+    carry = c[1] >= (int)k.tiles[1];
+    c[1] -= carry ? (int)k.tiles[1] : 0;
+    c[0] += k.gstep[0] + carry;
+  }
+};
 
 // A warp's contiguous share of a tile's units, as (i0, i1, seg) of its first
 // unit and a count; the same for every tile, so decoded once per launch.
@@ -92,8 +123,16 @@ __device__ __forceinline__ void next_unit(const NdStencil &k, int &i0, int &i1, 
   }
 }
 
-// One footprint row into shared memory: cp.async for the cells inside A
-// (columns [c_lo, c_hi) of a row inside A), a plain 0 store for the rest.
+// [lo, hi): the footprint cells of one dimension that lie inside A.
+__device__ __forceinline__ void inside_range(long long base, long long size, int f, int &lo, int &hi) {
+  lo = base >= 0 ? 0 : (int)(-base < f ? -base : f);
+  const long long h = size - base;
+  hi = h < 0 ? 0 : (h > f ? f : (int)h);
+}
+
+// One footprint row into shared memory, 4 bytes per copy (any contiguous
+// stride): cp.async for the cells inside A (columns [c_lo, c_hi) of a row
+// inside A), a plain 0 store for the rest.
 __device__ __forceinline__ void stage_row(float *srow, const float *__restrict__ A, long long arow, long long s2a,
                                           int f2, int c_lo, int c_hi, bool row_in, int c0, int cstep) {
   if (!row_in) {
@@ -110,6 +149,29 @@ __device__ __forceinline__ void stage_row(float *srow, const float *__restrict__
         srow[c] = 0.0f;
     }
   }
+}
+
+// The same with unit stride, in 16-byte chunks: the cells before A's first
+// 16-byte boundary in the row and after its last one go 4 bytes at a time
+// (at most 3 each).  phase = element address of the row's cell 0, mod 4;
+// srow + c and A + arow + c share their 16-byte phase.
+__device__ __forceinline__ void stage_row16(float *srow, const float *__restrict__ A, long long arow, int phase,
+                                            int f2, int c_lo, int c_hi, bool row_in, int c0, int cstep) {
+  if (!row_in || c_hi <= c_lo) {
+    for (int c = c0; c < f2; c += cstep) srow[c] = 0.0f;
+    return;
+  }
+  for (int c = c0; c < c_lo; c += cstep) srow[c] = 0.0f;
+  for (int c = c_hi + c0; c < f2; c += cstep) srow[c] = 0.0f;
+  int h1 = c_lo + ((4 - ((phase + c_lo) & 3)) & 3);
+  h1 = h1 < c_hi ? h1 : c_hi;
+  const int nch = (c_hi - h1) >> 2, b1 = h1 + 4 * nch;
+  if (c0 < h1 - c_lo) cp_async4(smem_u32(srow + c_lo + c0), A + (arow + c_lo + c0));
+  if (c0 < c_hi - b1) cp_async4(smem_u32(srow + b1 + c0), A + (arow + b1 + c0));
+  uint32_t dst = smem_u32(srow + h1) + 16u * c0;
+  const float *src = A + (arow + h1 + 4 * c0);
+#pragma unroll 2
+  for (int q = c0; q < nch; q += cstep, dst += 16u * cstep, src += 4 * cstep) cp_async16(dst, src);
 }
 
 // Left fold of the taps in source order for CPL points 32 apart; `live`
@@ -143,84 +205,151 @@ __device__ __forceinline__ void store_points(const NdStencil &k, float *bp, long
     if (!GUARD || u < nlive) bp[u * bstep] = k.has_scale ? __fmul_rn(acc[u], k.scale) : acc[u];
 }
 
-// Promoted: each block iteration stages one kernel tile's footprint in shared
-// memory (cooperative guarded copy, wait, barrier) and computes the tile's
-// points from it.  UNIT: unit contiguous strides of A and B and step 1 along
-// the contiguous dimension.
+__device__ __forceinline__ void tile_base(const NdStencil &k, const TileIter &it, long long *base) {
+#pragma unroll
+  for (int d = 0; d < 3; ++d) base[d] = (long long)it.c[d] * k.kt[d] * k.step[d] + k.min_off[d];
+}
+
+// Stages a tile's footprint into buf (cooperative, bounds-guarded copy) and
+// returns the tile's pad.  Footprint rows go to warps (warp w: rows w, w + 8,
+// ...; (r0, r1) is the warp's first row as (i0, i1)); a single row is spread
+// over the whole block.
+template <bool UNIT>
+__device__ __forceinline__ int stage_tile(const NdStencil &k, const float *__restrict__ A, const TileIter &it,
+                                          float *buf, int r0, int r1) {
+  const int f0 = k.fdim[0], f1 = k.fdim[1], f2 = k.fdim[2];
+  const long long s2a = UNIT ? 1 : k.a_stride[2];
+  long long base[3];  // A index of footprint cell (0, 0, 0)
+  tile_base(k, it, base);
+  int lo0, hi0, lo1, hi1, c_lo, c_hi;
+  inside_range(base[0], k.a_size[0], f0, lo0, hi0);
+  inside_range(base[1], k.a_size[1], f1, lo1, hi1);
+  inside_range(base[2], k.a_size[2], f2, c_lo, c_hi);
+  const long long a_cell0 = base[0] * k.a_stride[0] + base[1] * k.a_stride[1] + base[2] * s2a;
+  const int pad = UNIT ? (int)(((long long)(reinterpret_cast<uintptr_t>(A) >> 2) + a_cell0) & 3) : 0;
+  buf += pad;
+  const bool flat = f0 * f1 == 1;
+  const int c0 = flat ? (int)threadIdx.x : (int)(threadIdx.x & 31), cstep = flat ? kNdThreads : 32;
+  for (int i0 = flat ? 0 : r0, i1 = flat ? 0 : r1; i0 < f0;) {
+    const bool in = i0 >= lo0 && i0 < hi0 && i1 >= lo1 && i1 < hi1;
+    const int roff = i0 * k.as0 + i1 * k.as1;
+    float *srow = buf + i0 * k.pitch0 + i1 * k.pitch1;
+    if (UNIT)
+      stage_row16(srow, A, a_cell0 + roff, (pad + roff) & 3, f2, c_lo, c_hi, in, c0, cstep);
+    else
+      stage_row(srow, A, a_cell0 + roff, s2a, f2, c_lo, c_hi, in, c0, cstep);
+    if (flat) break;
+    for (i1 += kNdWarps; i1 >= f1; i1 -= f1) ++i0;
+  }
+  return pad;
+}
+
+// CPL points 32 apart from the staged tile: a left fold of the taps in
+// source order per point, then the optional scale.
+template <int CPL, int ST2, bool GUARD>
+__device__ __forceinline__ void fold_staged(const NdStencil &k, const float *sp, int st2, int nlive, float *acc) {
+  const int cs = 32 * (ST2 > 0 ? ST2 : st2);
+  const float *q = sp + k.tap_lin[0];
+  if (!k.has_w) {
+#pragma unroll
+    for (int u = 0; u < CPL; ++u) acc[u] = (!GUARD || u < nlive) ? q[u * cs] : 0.0f;
+    for (int j = 1; j < k.ntaps; ++j) {
+      q = sp + k.tap_lin[j];
+#pragma unroll
+      for (int u = 0; u < CPL; ++u) acc[u] = __fadd_rn(acc[u], (!GUARD || u < nlive) ? q[u * cs] : 0.0f);
+    }
+  } else {
+    float w = k.w[0];
+#pragma unroll
+    for (int u = 0; u < CPL; ++u) acc[u] = __fmul_rn(w, (!GUARD || u < nlive) ? q[u * cs] : 0.0f);
+    for (int j = 1; j < k.ntaps; ++j) {
+      q = sp + k.tap_lin[j];
+      w = k.w[j];
+#pragma unroll
+      for (int u = 0; u < CPL; ++u)
+        acc[u] = __fadd_rn(acc[u], __fmul_rn(w, (!GUARD || u < nlive) ? q[u * cs] : 0.0f));
+    }
+  }
+  if (k.has_scale) {
+#pragma unroll
+    for (int u = 0; u < CPL; ++u) acc[u] = __fmul_rn(acc[u], k.scale);
+  }
+}
+
+// Promoted: a block stages its tiles' footprints in shared memory and
+// computes each tile's points from there.  Two buffers: the next tile's copy
+// is in flight while the current tile is computed.  UNIT: unit contiguous
+// strides of A and B and step 1 along the contiguous dimension.
 template <bool UNIT, int CPL>
-__global__ void __launch_bounds__(kNdThreads, 5) stencil_nd_promoted_kernel(const float *__restrict__ A,
-                                                                         float *__restrict__ B,
-                                                                         const __grid_constant__ NdStencil k) {
-  extern __shared__ float tile_buf[];
+__global__ void __launch_bounds__(kNdThreads, 3) stencil_nd_promoted_kernel(const float *__restrict__ A,
+                                                                            float *__restrict__ B,
+                                                                            const __grid_constant__ NdStencil k) {
+  extern __shared__ __align__(16) float tile_buf[];
   constexpr int SEG = 32 * CPL;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int f1 = k.fdim[1], f2 = k.fdim[2];
-  const int frows = k.fdim[0] * f1, kcols = k.kt[2];
-  const long long s2a = UNIT ? 1 : k.a_stride[2], s2b = UNIT ? 1 : k.b_stride[2];
+  const int kcols = k.kt[2];
   const int st2 = UNIT ? 1 : k.step[2];
-  const long long bs0 = (long long)k.step[0] * k.b_stride[0], bs1 = (long long)k.step[1] * k.b_stride[1];
-  const long long bcol = (long long)st2 * s2b;              // B distance between neighbouring points
-  const int ss0 = k.step[0] * f1 * f2, ss1 = k.step[1] * f2;  // tile_buf distance between point rows
+  const int bcol = UNIT ? 1 : (int)(k.step[2] * k.b_stride[2]);  // B distance between neighbouring points
+  const int ss0 = k.step[0] * k.pitch0, ss1 = k.step[1] * k.pitch1;  // tile_buf distance between point rows
   const UnitRange ur = warp_units(k, warp);
-  for (unsigned t = blockIdx.x; t < (unsigned)k.ntiles; t += gridDim.x) {
-    long long tc[3];
-    tile_coords(k, t, tc);
-    long long base[3];  // A index of footprint cell 0
-#pragma unroll
-    for (int d = 0; d < 3; ++d) base[d] = tc[d] * k.kt[d] * k.step[d] + k.min_off[d];
-    const long long gc0 = base[2];
-    const int c_lo = gc0 >= 0 ? 0 : (int)(-gc0 < f2 ? -gc0 : f2);  // first column inside A
-    const long long c_hi_l = k.a_size[2] - gc0;
-    const int c_hi = c_hi_l < 0 ? 0 : (c_hi_l > f2 ? f2 : (int)c_hi_l);  // one past the last
-    if (frows == 1) {  // one footprint row: the whole block spreads over it
-      const bool in = base[0] >= 0 && base[0] < k.a_size[0] && base[1] >= 0 && base[1] < k.a_size[1];
-      stage_row(tile_buf, A, base[0] * k.a_stride[0] + base[1] * k.a_stride[1] + gc0 * s2a, s2a, f2, c_lo, c_hi,
-                in, threadIdx.x, kNdThreads);
-    } else {
-      for (int fr = warp; fr < frows; fr += kNdWarps) {
-        const int i0 = fr / f1, i1 = fr - i0 * f1;
-        const long long g0 = base[0] + i0, g1 = base[1] + i1;
-        const bool in = g0 >= 0 && g0 < k.a_size[0] && g1 >= 0 && g1 < k.a_size[1];
-        stage_row(tile_buf + fr * f2, A, g0 * k.a_stride[0] + g1 * k.a_stride[1] + gc0 * s2a, s2a, f2, c_lo, c_hi,
-                  in, lane, 32);
-      }
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
+  const int r0 = warp / k.fdim[1], r1 = warp - r0 * k.fdim[1];  // this warp's first footprint row
+  const unsigned ntiles = (unsigned)k.ntiles;
+  TileIter cur, next;  // the tile computed in this iteration; the one staged during it
+  cur.start(k, blockIdx.x);
+  int pad = 0, pad_next = 0;
+  if (cur.t < ntiles) pad = stage_tile<UNIT>(k, A, cur, tile_buf, r0, r1);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  next = cur;
+  next.advance(k);
+  for (int b = 0; cur.t < ntiles; b ^= 1) {
+    if (next.t < ntiles) pad_next = stage_tile<UNIT>(k, A, next, tile_buf + (b ^ 1) * k.buf_cells, r0, r1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // cur's copies (all but the newest group)
     __syncthreads();
-    const long long pc0 = tc[2] * kcols;  // first output column of the tile
+    const float *buf = tile_buf + b * k.buf_cells + pad;
+    const long long pc0 = (long long)cur.c[2] * kcols;  // first output column of the tile
     const int ncols = k.npts[2] - pc0 < kcols ? (int)(k.npts[2] - pc0) : kcols;
-    const long long p0t = tc[0] * k.kt[0], p1t = tc[1] * k.kt[1];
-    float *btile = B + p0t * bs0 + p1t * bs1 + pc0 * bcol;
+    const long long p0t = (long long)cur.c[0] * k.kt[0], p1t = (long long)cur.c[1] * k.kt[1];
+    const int rows0 = k.npts[0] - p0t < k.kt[0] ? (int)(k.npts[0] - p0t) : k.kt[0];  // point rows in the tile
+    const int rows1 = k.npts[1] - p1t < k.kt[1] ? (int)(k.npts[1] - p1t) : k.kt[1];
+    float *btile = B + (p0t * k.bs0 + p1t * k.bs1 + pc0 * bcol);
     int i0 = ur.i0, i1 = ur.i1, seg = ur.seg;
     for (int n = 0; n < ur.n; ++n, next_unit(k, i0, i1, seg)) {
-      if (p0t + i0 >= k.npts[0] || p1t + i1 >= k.npts[1]) continue;
+      if (i0 >= rows0 || i1 >= rows1) continue;
       const int cb = seg * SEG + lane;  // this lane's first column in the tile
-      const float *sp = tile_buf + i0 * ss0 + i1 * ss1 + cb * st2;
-      float *bp = btile + i0 * bs0 + i1 * bs1 + cb * bcol;
-      // points of this lane before the tile's last column: lane + 32u < ncols - seg*SEG
-      const int rem = ncols - seg * SEG - lane;
-      const int nlive = rem <= 0 ? 0 : (rem + 31) / 32;
-      auto ld = [&](int j, int u) { return sp[k.tap_lin[j] + u * 32 * st2]; };
+      const float *sp = buf + i0 * ss0 + i1 * ss1 + cb * st2;
+      float *bp = btile + (i0 * k.bs0 + i1 * k.bs1 + cb * bcol);
       float acc[CPL];
       if (ncols - seg * SEG >= SEG) {
-        fold_taps<CPL, false>(k, ld, CPL, acc);
-        store_points<CPL, false>(k, bp, 32 * bcol, CPL, acc);
-      } else if (nlive > 0) {
-        fold_taps<CPL, true>(k, ld, nlive, acc);
-        store_points<CPL, true>(k, bp, 32 * bcol, nlive, acc);
+        fold_staged<CPL, UNIT ? 1 : 0, false>(k, sp, st2, CPL, acc);
+#pragma unroll
+        for (int u = 0; u < CPL; ++u) bp[u * 32 * bcol] = acc[u];
+      } else {
+        // points of this lane before the tile's last column: lane + 32u < ncols - seg*SEG
+        const int rem = ncols - seg * SEG - lane;
+        const int nlive = rem <= 0 ? 0 : (rem + 31) / 32;
+        if (nlive == 0) continue;
+        fold_staged<CPL, UNIT ? 1 : 0, true>(k, sp, st2, nlive, acc);
+#pragma unroll
+        for (int u = 0; u < CPL; ++u)
+          if (u < nlive) bp[u * 32 * bcol] = acc[u];
       }
     }
-    __syncthreads();
+    __syncthreads();  // every warp is done with this buffer before it is refilled
+    cur = next;
+    pad = pad_next;
+    next.advance(k);
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // Not promoted: the same tiles, units and fold, every tap read from global
 // memory (the caches catch the neighbours' reuse).  Units whose taps all land
 // inside A read without per-point bounds checks.
 template <bool UNIT, int CPL>
-__global__ void __launch_bounds__(kNdThreads) stencil_nd_direct_kernel(const float *__restrict__ A,
-                                                                       float *__restrict__ B,
-                                                                       const __grid_constant__ NdStencil k) {
+__global__ void __launch_bounds__(kNdThreads, 4) stencil_nd_direct_kernel(const float *__restrict__ A,
+                                                                          float *__restrict__ B,
+                                                                          const __grid_constant__ NdStencil k) {
   constexpr int SEG = 32 * CPL;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kcols = k.kt[2];
@@ -228,14 +357,14 @@ __global__ void __launch_bounds__(kNdThreads) stencil_nd_direct_kernel(const flo
   const int st2 = UNIT ? 1 : k.step[2];
   const long long bcol = (long long)st2 * s2b, acol = (long long)st2 * s2a;
   const UnitRange ur = warp_units(k, warp);
-  for (unsigned t = blockIdx.x; t < (unsigned)k.ntiles; t += gridDim.x) {
-    long long tc[3];
-    tile_coords(k, t, tc);
-    const long long pc0 = tc[2] * kcols;
+  TileIter it;
+  it.start(k, blockIdx.x);
+  for (; it.t < (unsigned)k.ntiles; it.advance(k)) {
+    const long long pc0 = (long long)it.c[2] * kcols;
     const int ncols = k.npts[2] - pc0 < kcols ? (int)(k.npts[2] - pc0) : kcols;
     int i0 = ur.i0, i1 = ur.i1, seg = ur.seg;
     for (int n = 0; n < ur.n; ++n, next_unit(k, i0, i1, seg)) {
-      const long long p0 = tc[0] * k.kt[0] + i0, p1 = tc[1] * k.kt[1] + i1;
+      const long long p0 = (long long)it.c[0] * k.kt[0] + i0, p1 = (long long)it.c[1] * k.kt[1] + i1;
       if (p0 >= k.npts[0] || p1 >= k.npts[1]) continue;
       const long long o0 = p0 * k.step[0], o1 = p1 * k.step[1];
       const long long c_first = pc0 + seg * SEG;  // the unit's first output column
@@ -282,7 +411,11 @@ cudaError_t launch_grid(K kern, const NdStencil &k, size_t smem, const float *a,
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   const long long cap = (long long)per_sm * num_sms(dev);
   const long long g = k.ntiles < cap ? (k.ntiles > 0 ? k.ntiles : 1) : cap;
-  kern<<<(unsigned)g, kNdThreads, smem, s>>>(a, b, k);
+  NdStencil kl = k;
+  kl.gstep[2] = (int)(g % kl.tiles[2]);
+  kl.gstep[1] = (int)((g / kl.tiles[2]) % kl.tiles[1]);
+  kl.gstep[0] = (int)(g / (kl.tiles[2] * kl.tiles[1]));
+  kern<<<(unsigned)g, kNdThreads, smem, s>>>(a, b, kl);
   return cudaGetLastError();
 }
 
@@ -351,18 +484,21 @@ cudaError_t launch_stencil_nd(const StencilNdProblem &p, int promote, cudaStream
     k.w[j] = p.weights ? p.weights[j] : 1.0f;
     k.tap_goff[j] = k.off[j][0] * k.a_stride[0] + k.off[j][1] * k.a_stride[1] + k.off[j][2] * k.a_stride[2];
   }
-  // Kernel tile: rows of 256 contiguous points (128 for rank 3) and ~4K points
-  // per tile; halved, outer dimensions first, while the footprint exceeds the
-  // budget (promoted only), and never larger than the grid of output points.
-  const int cpl = p.rank == 3 ? 4 : 8;
-  static const int kDefault[3][3] = {{1, 1, 4096}, {1, 16, 256}, {4, 8, 128}};
+  const bool unit = k.a_stride[2] == 1 && k.b_stride[2] == 1 && k.step[2] == 1;
+  // Kernel tile: ~8K points per promoted tile (rows of 512 points, 16 per
+  // lane; rank 3: 4 x 8 rows of 128), ~4K per direct one; never larger than
+  // the grid of output points.  A promoted tile shrinks, outer dimensions
+  // first, until its footprint fits the budget.
+  static const int kPromoted[3][3] = {{1, 1, 8192}, {1, 16, 512}, {4, 8, 128}};
+  static const int kDirect[3][3] = {{1, 1, 4096}, {1, 16, 256}, {4, 8, 128}};
+  const int cpl = p.rank == 3 ? 4 : (promote ? 16 : 8);
   for (int d = 0; d < 3; ++d) {
-    const long long want = kDefault[p.rank - 1][d];
+    const long long want = (promote ? kPromoted : kDirect)[p.rank - 1][d];
     k.kt[d] = (int)(k.npts[d] < want ? (k.npts[d] > 0 ? k.npts[d] : 1) : want);
   }
   if (promote) {
     // A promoted plan's footprint fits group memory on the caller's tile, so
-    // the footprint of a one-point tile (the halving's floor) fits too.
+    // the footprint of a one-point tile (the shrinking's floor) fits too.
     int one[3] = {1, 1, 1};
     const long long floor_cells = footprint_cells(one, k.step, span);
     const long long budget_cells = floor_cells * 4 > kNdTileBytes ? floor_cells : kNdTileBytes / 4;
@@ -370,11 +506,33 @@ cudaError_t launch_stencil_nd(const StencilNdProblem &p, int promote, cudaStream
       int d = 0;
       while (d < 3 && k.kt[d] == 1) ++d;
       if (d == 3) break;
-      k.kt[d] = (k.kt[d] + 1) / 2;
+      k.kt[d] = d < 2 ? k.kt[d] - 1 : (k.kt[d] + 1) / 2;
     }
     for (int d = 0; d < 3; ++d) k.fdim[d] = (int)((long long)(k.kt[d] - 1) * k.step[d] + span[d] + 1);
+    // Offsets inside a tile must fit 32 bits; otherwise read A directly
+    // (identical values, no staging).
+    const long long a_ext = (k.fdim[0] - 1) * k.a_stride[0] + (k.fdim[1] - 1) * k.a_stride[1] +
+                            (long long)k.fdim[2] * k.a_stride[2];
+    const long long b_ext = (long long)(k.kt[0] - 1) * k.step[0] * k.b_stride[0] +
+                            (long long)(k.kt[1] - 1) * k.step[1] * k.b_stride[1] +
+                            (long long)k.kt[2] * k.step[2] * k.b_stride[2];
+    if (a_ext >= 0x7fffffffLL || b_ext >= 0x7fffffffLL) return launch_stencil_nd(p, 0, s);
+    k.as0 = (int)k.a_stride[0];
+    k.as1 = (int)k.a_stride[1];
+    k.bs0 = (int)(k.step[0] * k.b_stride[0]);
+    k.bs1 = (int)(k.step[1] * k.b_stride[1]);
+    if (unit) {  // pitches congruent to A's strides mod 4 (see NdStencil); 3 cells of pad slack
+      k.pitch1 = k.fdim[2] + (int)((((k.a_stride[1] - k.fdim[2]) % 4) + 4) % 4);
+      const long long rows = (long long)k.fdim[1] * k.pitch1;
+      k.pitch0 = (int)(rows + (((k.a_stride[0] - rows) % 4) + 4) % 4);
+      k.buf_cells = (k.fdim[0] * k.pitch0 + 3 + 3) & ~3;
+    } else {
+      k.pitch1 = k.fdim[2];
+      k.pitch0 = k.fdim[1] * k.fdim[2];
+      k.buf_cells = (k.fdim[0] * k.pitch0 + 3) & ~3;
+    }
     for (int j = 0; j < p.ntaps; ++j)
-      k.tap_lin[j] = ((k.off[j][0] - k.min_off[0]) * k.fdim[1] + (k.off[j][1] - k.min_off[1])) * k.fdim[2] +
+      k.tap_lin[j] = (k.off[j][0] - k.min_off[0]) * k.pitch0 + (k.off[j][1] - k.min_off[1]) * k.pitch1 +
                      (k.off[j][2] - k.min_off[2]);
   }
   k.vsplit = (k.kt[2] + 32 * cpl - 1) / (32 * cpl);
@@ -385,16 +543,19 @@ cudaError_t launch_stencil_nd(const StencilNdProblem &p, int promote, cudaStream
   }
   if (k.ntiles == 0) return cudaSuccess;
   if (k.ntiles > 0x7fffffffLL) return cudaErrorInvalidValue;  // tile indices are 32-bit in the kernels
-  const bool unit = k.a_stride[2] == 1 && k.b_stride[2] == 1 && k.step[2] == 1;
-  const size_t smem = promote ? (size_t)footprint_cells(k.kt, k.step, span) * sizeof(float) : 0;
-#define SPMD_ND_LAUNCH(KERN)                                                                     \
-  (cpl == 8 ? (unit ? launch_grid(KERN<true, 8>, k, smem, p.a, p.b, s)                           \
-                    : launch_grid(KERN<false, 8>, k, smem, p.a, p.b, s))                         \
-            : (unit ? launch_grid(KERN<true, 4>, k, smem, p.a, p.b, s)                           \
-                    : launch_grid(KERN<false, 4>, k, smem, p.a, p.b, s)))
-  const cudaError_t e = promote ? SPMD_ND_LAUNCH(stencil_nd_promoted_kernel) : SPMD_ND_LAUNCH(stencil_nd_direct_kernel);
-#undef SPMD_ND_LAUNCH
-  return e;
+  if (promote) {
+    const size_t smem = 2 * (size_t)k.buf_cells * sizeof(float);  // two buffers
+    if (cpl == 16)
+      return unit ? launch_grid(stencil_nd_promoted_kernel<true, 16>, k, smem, p.a, p.b, s)
+                  : launch_grid(stencil_nd_promoted_kernel<false, 16>, k, smem, p.a, p.b, s);
+    return unit ? launch_grid(stencil_nd_promoted_kernel<true, 4>, k, smem, p.a, p.b, s)
+                : launch_grid(stencil_nd_promoted_kernel<false, 4>, k, smem, p.a, p.b, s);
+  }
+  if (cpl == 8)
+    return unit ? launch_grid(stencil_nd_direct_kernel<true, 8>, k, 0, p.a, p.b, s)
+                : launch_grid(stencil_nd_direct_kernel<false, 8>, k, 0, p.a, p.b, s);
+  return unit ? launch_grid(stencil_nd_direct_kernel<true, 4>, k, 0, p.a, p.b, s)
+              : launch_grid(stencil_nd_direct_kernel<false, 4>, k, 0, p.a, p.b, s);
 }
 
 }  // namespace spmdb200
