@@ -1,21 +1,36 @@
-// stencil3.cu -- library launch of the promoted 3-point stencil.
+// stencil3.cu -- library launch of the promoted 3-point stencil
+//   B[i,j] = (A[i,j] + A[i,j+1]) + A[i+1,j],  0 <= i < n, 0 <= j < m
+// (test/SPMD/lower-to-gpu-nvptx-promoted.mlir:32-67).  It is the general
+// promoted-tile stencil with the offsets (0,0), (0,1), (1,0) in that order:
+// footprint cells outside A read as 0 and stores stay inside n x m, exactly
+// as stencil3_body does for the reference-signature kernel.
 #include "internal.h"
-#include "stencil3.cuh"
 
 namespace spmdb200 {
 
-__global__ void __launch_bounds__(256) stencil3_kernel(View2 a, View2 b, int64_t n, int64_t m) {
-  __shared__ Stencil3Smem sm;
-  stencil3_body(a, b, n, m, 1, kChR, kChC, sm);
-}
-
 cudaError_t launch_stencil3(View2 a, View2 b, int64_t n, int64_t m, cudaStream_t s) {
   if (n <= 0 || m <= 0) return cudaSuccess;
-  const int64_t gx = (n + kChR - 1) / kChR, gy = (m + kChC - 1) / kChC;
-  // grid.y is limited to 65535; the body's tile loop covers what the grid does not.
-  dim3 grid((unsigned)(gx < 2147483647 ? gx : 2147483647), (unsigned)(gy < 65535 ? gy : 65535));
-  stencil3_kernel<<<grid, 256, 0, s>>>(a, b, n, m);
-  return cudaGetLastError();
+  static const int64_t kOffsets[6] = {0, 0, 0, 1, 1, 0};
+  StencilNdProblem p{};
+  p.rank = 2;
+  p.ntaps = 3;
+  p.a = a.p;
+  p.b = b.p;
+  p.a_size[0] = a.n0;
+  p.a_size[1] = a.n1;
+  p.a_stride[0] = a.s0;
+  p.a_stride[1] = a.s1;
+  p.b_size[0] = n;
+  p.b_size[1] = m;
+  p.b_stride[0] = b.s0;
+  p.b_stride[1] = b.s1;
+  p.step[0] = p.step[1] = 1;
+  p.tile[0] = 32;  // the reference's group tile; the kernel stages larger ones
+  p.tile[1] = 8;
+  p.offsets = kOffsets;
+  p.weights = nullptr;
+  p.scale = 1.0f;
+  return launch_stencil_nd(p, 1, s);
 }
 
 }  // namespace spmdb200
