@@ -216,7 +216,9 @@ def run_reference_arm(args) -> None:
 # ------------------------------------------------------------------ GPU legs
 def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
     """The other configurations at N=1 (rank 0): f32/i32 sum 2^24, axpy 2^28,
-    Jacobi-2D 4096^2 x 100, Jacobi-3D 512^3 x 50.  L2 flushed between reps."""
+    the promoted 3-point stencil at 4096^2 and 8192^2, the general stencil
+    (5-point) at 8192^2, Jacobi-2D 4096^2 x 100, Jacobi-3D 512^3 x 50.  L2
+    flushed between reps."""
     out = {}
     dev = torch.device("cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MiB > 126 MB L2
@@ -281,6 +283,25 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
     gbs = n * 12 / ms / 1e6
     out["axpy_2^28"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3)}
     del x, y
+    # Promoted 3-point stencil B = (A + A east) + A south on the harness layout
+    # (A is (N+1) x (N+1)): 4096^2 is the reference's own configuration, 8192^2
+    # the same above the L2 size.  Bytes: A read once, B written once.
+    for nn in (4096, 8192):
+        a = torch.rand((nn + 1, nn + 1), device=dev, generator=g)
+        b = torch.empty((nn, nn), device=dev)
+        ms = timed(lambda: kernels.stencil3pt(a, b))
+        gbs = (a.numel() + b.numel()) * 4 / ms / 1e6
+        out[f"stencil3pt_{nn}^2"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
+                                     "frac_of_hbm": round(gbs / hbm_peak, 3)}
+        del a, b
+    # General promoted-tile stencil: Jacobi-2D 5-point, one sweep, 8192^2.
+    a = torch.rand((8192, 8192), device=dev, generator=g)
+    b = torch.empty_like(a)
+    j5 = [[0, 0], [-1, 0], [1, 0], [0, 1], [0, -1]]
+    ms = timed(lambda: kernels.stencil_nd(a, b, j5, scale=0.2, tile_sizes=[16, 32]))
+    gbs = 2 * a.numel() * 4 / ms / 1e6
+    out["stencil_nd_5pt_8192^2"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3)}
+    del a, b
     u = torch.rand((4096, 4096), device=dev, generator=g)
     u[0] = 0; u[-1] = 0; u[:, 0] = 0; u[:, -1] = 0
     v = torch.empty_like(u)
