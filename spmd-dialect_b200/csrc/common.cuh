@@ -184,9 +184,16 @@ __device__ __forceinline__ void st_f4(float *p, float4 v) {
 // A kernel launched with launch_pdl() may start while the previous kernel of
 // its stream is finishing (its launch and prologue overlap that kernel's
 // tail); pdl_wait() then blocks until the previous kernel has completed and
-// its memory is visible, so nothing may touch global memory before it.
+// its memory is visible, so nothing may read or write global memory before
+// it (an L2 prefetch, which returns no data, may run earlier).
 // pdl_trigger() lets the next such launch start early.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned *p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 template <class... KArgs, class... Args>

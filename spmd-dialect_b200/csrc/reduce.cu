@@ -120,13 +120,20 @@ __global__ void __launch_bounds__(kBulkThreads) sum_bulk_kernel(const void *__re
     abort_flag = 0;
     mbar_fence_init();
   }
-  __syncthreads();
-  pdl_wait();  // the previous kernel of the stream is complete (it may have written the input)
-  if (threadIdx.x == 0) pdl_trigger();
   const int64_t units = n >> 2;  // 16-byte units; the last n % 4 elements are the tail
   int64_t lo, hi;
   cta_range(units, lo, hi);
   const uint4 *base = reinterpret_cast<const uint4 *>(a);
+  // While the previous kernel finishes, warm L2 with this CTA's first chunks.
+  if (threadIdx.x == 0) bulk_prefetch_head(base, lo, hi);
+  __syncthreads();
+  pdl_wait();  // the previous kernel of the stream is complete (it may have written the input)
+  if (threadIdx.x == 0) pdl_trigger();
+  // The value the sum adds to, read now so the last block's final store does
+  // not wait on it (nothing else writes *out while this kernel runs).
+  double init = 0.0;
+  if constexpr (M == BulkMode::kF32Det)
+    if (threadIdx.x == 0 && !f64_out) init = (double)*static_cast<const float *>(out);
   if constexpr (M == BulkMode::kI32) {
     uint32_t acc = 0;
     const bool ok = bulk_stream(base, lo, hi, smem, full, &abort_flag,
@@ -157,22 +164,21 @@ __global__ void __launch_bounds__(kBulkThreads) sum_bulk_kernel(const void *__re
     } else {
       if (threadIdx.x == 0) {
         partials[blockIdx.x] = b;
-        __threadfence();
-        last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+        // acq_rel: the partial is visible before the ticket moves, and the
+        // last block's reads below come after every other block's partial.
+        last = (atom_add_acq_rel_gpu(ticket, 1u) == gridDim.x - 1);
       }
       __syncthreads();
       if (!last) return;
-      __threadfence();
+      fence_acq_rel_gpu();
       double p = 0.0;
       for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) p = __dadd_rn(p, __ldcg(partials + i));
       const double tot = block_sum_f64(p, shd);
       if (threadIdx.x == 0) {
-        if (f64_out) {
+        if (f64_out)
           *f64_out = tot;
-        } else {
-          float *o = static_cast<float *>(out);
-          *o = __double2float_rn(__dadd_rn((double)*o, tot));
-        }
+        else
+          *static_cast<float *>(out) = __double2float_rn(__dadd_rn(init, tot));
         *ticket = 0u;
       }
     }

@@ -33,6 +33,20 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
       : "memory");
 }
 
+// L2 prefetch of the first kBulkStages chunks of [u_lo, u_hi).  A prefetch
+// returns no data, so it may run before griddepcontrol.wait: lines that the
+// previous kernel still writes are updated in L2, the point of coherence, and
+// the stage loads after the wait read them from there.
+__device__ __forceinline__ void bulk_prefetch_head(const uint4 *base, int64_t u_lo, int64_t u_hi) {
+  constexpr int kUnits = kBulkChunk / 16;
+  for (int s = 0; s < kBulkStages; ++s) {
+    const int64_t c0 = u_lo + (int64_t)s * kUnits;
+    if (c0 >= u_hi) break;
+    const uint32_t bytes = (uint32_t)(min((int64_t)kUnits, u_hi - c0) * 16);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + c0), "r"(bytes) : "memory");
+  }
+}
+
 // Streams the 16-byte units [u_lo, u_hi) of `base` through shared memory and
 // calls f(float4 as the element type's 16 bytes) for every unit, each thread
 // seeing a fixed, deterministic subset.  Returns false if a wait timed out.

@@ -56,6 +56,14 @@ struct NdStencil {
   int as0, as1;  // A strides of the two outer dimensions
   int bs0, bs1;  // B distance between neighbouring point rows (step * stride)
   int gstep[3];  // the grid size as tile coordinates (mixed radix tiles[0..2])
+  // Rank-3 z-streaming (promoted, unit strides, z step 1): a work item is
+  // kt[1] x kt[2] points of kz consecutive planes; its input planes pass
+  // through a ring of `ring` slots of slot_cells floats, slot_cells
+  // congruent to A's plane stride mod 4 and ring a multiple of 4, so the
+  // 16-byte phase of every staged cell again matches A's.
+  int kz, ring, slot_cells;
+  int tap_dz[kNdMaxTaps];  // off_j[0] - min_off[0]
+  int tap_in[kNdMaxTaps];  // (off_j[1] - min_off[1]) * pitch1 + off_j[2] - min_off[2]
   int off[kNdMaxTaps][3];
   int tap_lin[kNdMaxTaps];         // (off_j - min_off) . (pitch0, pitch1, 1)
   long long tap_goff[kNdMaxTaps];  // off_j . a_stride
@@ -246,15 +254,20 @@ __device__ __forceinline__ int stage_tile(const NdStencil &k, const float *__res
 
 // CPL points 32 apart from the staged tile: a left fold of the taps in
 // source order per point, then the optional scale.
-template <int CPL, int ST2, bool GUARD>
-__device__ __forceinline__ void fold_staged(const NdStencil &k, const float *sp, int st2, int nlive, float *acc) {
+struct ParamTaps {  // tap offsets of the tiled kernels (kernel parameters)
+  const NdStencil &k;
+  __device__ __forceinline__ int operator()(int j) const { return k.tap_lin[j]; }
+};
+template <int CPL, int ST2, bool GUARD, typename Taps = ParamTaps>
+__device__ __forceinline__ void fold_staged(const NdStencil &k, const float *sp, int st2, int nlive, float *acc,
+                                            Taps taps) {
   const int cs = 32 * (ST2 > 0 ? ST2 : st2);
-  const float *q = sp + k.tap_lin[0];
+  const float *q = sp + taps(0);
   if (!k.has_w) {
 #pragma unroll
     for (int u = 0; u < CPL; ++u) acc[u] = (!GUARD || u < nlive) ? q[u * cs] : 0.0f;
     for (int j = 1; j < k.ntaps; ++j) {
-      q = sp + k.tap_lin[j];
+      q = sp + taps(j);
 #pragma unroll
       for (int u = 0; u < CPL; ++u) acc[u] = __fadd_rn(acc[u], (!GUARD || u < nlive) ? q[u * cs] : 0.0f);
     }
@@ -263,7 +276,7 @@ __device__ __forceinline__ void fold_staged(const NdStencil &k, const float *sp,
 #pragma unroll
     for (int u = 0; u < CPL; ++u) acc[u] = __fmul_rn(w, (!GUARD || u < nlive) ? q[u * cs] : 0.0f);
     for (int j = 1; j < k.ntaps; ++j) {
-      q = sp + k.tap_lin[j];
+      q = sp + taps(j);
       w = k.w[j];
 #pragma unroll
       for (int u = 0; u < CPL; ++u)
@@ -321,7 +334,7 @@ __global__ void __launch_bounds__(kNdThreads, 3) stencil_nd_promoted_kernel(cons
       float *bp = btile + (i0 * k.bs0 + i1 * k.bs1 + cb * bcol);
       float acc[CPL];
       if (ncols - seg * SEG >= SEG) {
-        fold_staged<CPL, UNIT ? 1 : 0, false>(k, sp, st2, CPL, acc);
+        fold_staged<CPL, UNIT ? 1 : 0, false>(k, sp, st2, CPL, acc, ParamTaps{k});
 #pragma unroll
         for (int u = 0; u < CPL; ++u) bp[u * 32 * bcol] = acc[u];
       } else {
@@ -329,7 +342,7 @@ __global__ void __launch_bounds__(kNdThreads, 3) stencil_nd_promoted_kernel(cons
         const int rem = ncols - seg * SEG - lane;
         const int nlive = rem <= 0 ? 0 : (rem + 31) / 32;
         if (nlive == 0) continue;
-        fold_staged<CPL, UNIT ? 1 : 0, true>(k, sp, st2, nlive, acc);
+        fold_staged<CPL, UNIT ? 1 : 0, true>(k, sp, st2, nlive, acc, ParamTaps{k});
 #pragma unroll
         for (int u = 0; u < CPL; ++u)
           if (u < nlive) bp[u * 32 * bcol] = acc[u];
@@ -341,6 +354,111 @@ __global__ void __launch_bounds__(kNdThreads, 3) stencil_nd_promoted_kernel(cons
     next.advance(k);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Rank 3, promoted, unit strides, z step 1: each work item streams its
+// input planes through a ring of shared-memory slots (cp.async 16-byte
+// staging, one commit group per plane, PF planes in flight while one output
+// plane is computed from the span0 + 1 planes in the ring).  A plane's
+// halo rows and columns are staged once per plane rather than once per
+// z-extent of a tile, so the staged cells per point drop from ~1.9 (tiles of
+// 4 x 8 x 128) to ~1.16.
+template <int CPL, int PF>
+__global__ void __launch_bounds__(kNdThreads, 4) stencil_nd_stream3_kernel(const float *__restrict__ A,
+                                                                           float *__restrict__ B,
+                                                                           const __grid_constant__ NdStencil k) {
+  extern __shared__ __align__(16) float ring[];
+  // Tap offsets for each ring position of the output plane: s_toff[r][j] =
+  // ((r + dz_j) mod ring) * slot_cells + in-plane offset of tap j.
+  __shared__ int s_toff[16][kNdMaxTaps];
+  constexpr int SEG = 32 * CPL;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int fy = k.fdim[1], fx = k.fdim[2], kcols = k.kt[2];
+  const int R1 = k.ring - 1, S = k.slot_cells, span0 = k.max_off[0] - k.min_off[0];
+  for (int i = threadIdx.x; i < k.ring * k.ntaps; i += kNdThreads) {
+    const int r = i / k.ntaps, j = i - r * k.ntaps;
+    s_toff[r][j] = ((r + k.tap_dz[j]) & R1) * S + k.tap_in[j];
+  }
+  const int ss1 = k.step[1] * k.pitch1;
+  const long long bs0 = k.b_stride[0];
+  // This warp's contiguous share of a plane's units (rows x segments).
+  const int units = k.kt[1] * k.vsplit, per = (units + kNdWarps - 1) / kNdWarps, u0 = warp * per;
+  const int nu = units - u0 < per ? (units - u0 > 0 ? units - u0 : 0) : per;
+  const int row0 = u0 / k.vsplit, seg0 = u0 - row0 * k.vsplit;
+  const int a0m4 = (int)(k.a_stride[0] & 3);
+  TileIter it;
+  it.start(k, blockIdx.x);
+  for (; it.t < (unsigned)k.ntiles; it.advance(k)) {
+    const long long z0 = (long long)it.c[0] * k.kz;  // first output plane of the item
+    const int nz = k.npts[0] - z0 < k.kz ? (int)(k.npts[0] - z0) : k.kz;
+    const long long gz0 = z0 + k.min_off[0];
+    const long long gy0 = (long long)it.c[1] * k.kt[1] * k.step[1] + k.min_off[1];
+    const long long gx0 = (long long)it.c[2] * kcols + k.min_off[2];
+    int lo1, hi1, c_lo, c_hi;
+    inside_range(gy0, k.a_size[1], fy, lo1, hi1);
+    inside_range(gx0, k.a_size[2], fx, c_lo, c_hi);
+    const long long a_cell0 = gz0 * k.a_stride[0] + gy0 * k.a_stride[1] + gx0;
+    const int pad = (int)(((long long)(reinterpret_cast<uintptr_t>(A) >> 2) + a_cell0) & 3);
+    const int np = nz + span0;  // input planes of the item
+    auto stage_plane = [&](int p) {
+      const long long gz = gz0 + p;
+      const bool pin = gz >= 0 && gz < k.a_size[0];
+      float *slot = ring + (p & R1) * S + pad;
+      const long long aplane = a_cell0 + p * k.a_stride[0];
+      const int pphase = pad + ((p * a0m4) & 3);
+      for (int r = warp; r < fy; r += kNdWarps) {
+        const bool in = pin && r >= lo1 && r < hi1;
+        const int roff = r * k.as1;
+        stage_row16(slot + r * k.pitch1, A, aplane + roff, (pphase + roff) & 3, fx, c_lo, c_hi, in, lane, 32);
+      }
+    };
+    for (int p = 0; p < span0 + PF; ++p) {  // one commit group per plane, empty past the item
+      if (p < np) stage_plane(p);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    const long long p1t = (long long)it.c[1] * k.kt[1], pc0 = (long long)it.c[2] * kcols;
+    const int rows1 = k.npts[1] - p1t < k.kt[1] ? (int)(k.npts[1] - p1t) : k.kt[1];
+    const int ncols = k.npts[2] - pc0 < kcols ? (int)(k.npts[2] - pc0) : kcols;
+    float *bplane = B + (z0 * bs0 + p1t * k.bs1 + pc0);
+    for (int zo = 0; zo < nz; ++zo, bplane += bs0) {
+      if (zo + span0 + PF < np) stage_plane(zo + span0 + PF);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      asm volatile("cp.async.wait_group %0;" ::"n"(PF) : "memory");  // planes up to zo + span0 have landed
+      __syncthreads();
+      const int *toff = s_toff[zo & R1];
+      auto taps = [toff](int j) { return toff[j]; };
+      int i1 = row0, seg = seg0;
+      for (int n = 0; n < nu; ++n) {
+        if (i1 < rows1) {
+          const int cb = seg * SEG + lane;
+          const float *sp = ring + pad + i1 * ss1 + cb;
+          float *bp = bplane + (i1 * k.bs1 + cb);
+          float acc[CPL];
+          if (ncols - seg * SEG >= SEG) {
+            fold_staged<CPL, 1, false>(k, sp, 1, CPL, acc, taps);
+#pragma unroll
+            for (int u = 0; u < CPL; ++u) bp[u * 32] = acc[u];
+          } else {
+            const int rem = ncols - seg * SEG - lane;
+            const int nlive = rem <= 0 ? 0 : ((rem + 31) >> 5);
+            if (nlive > 0) {
+              fold_staged<CPL, 1, true>(k, sp, 1, nlive, acc, taps);
+#pragma unroll
+              for (int u = 0; u < CPL; ++u)
+                if (u < nlive) bp[u * 32] = acc[u];
+            }
+          }
+        }
+        if (++seg == k.vsplit) {
+          seg = 0;
+          ++i1;
+        }
+      }
+      __syncthreads();  // plane zo's slot is refilled in the next iteration
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+  }
 }
 
 // Not promoted: the same tiles, units and fold, every tap read from global
@@ -425,6 +543,79 @@ long long footprint_cells(const int *kt, const int *step, const int *span) {
   return n;
 }
 
+// Rank-3 z-streaming launch (see stencil_nd_stream3_kernel); returns
+// cudaErrorNotSupported when the problem does not fit it.
+#ifndef SPMDB200_STREAM3_PREFETCH
+#define SPMDB200_STREAM3_PREFETCH 1  // planes in flight per block (2-4 measured slower: a larger ring costs blocks)
+#endif
+#ifndef SPMDB200_STREAM3_ROWS
+#define SPMDB200_STREAM3_ROWS 16  // output rows of a work item
+#endif
+cudaError_t launch_stream3(NdStencil k, const int *span, const float *a, float *b, cudaStream_t s) {
+  // Row segments of 128 or 256 points (4 or 8 per lane): the wider one when
+  // it wastes no more of the last column tile (512^3 7-point: 2.9 vs
+  // 2.4 TB/s; 320^3: 1.4 vs 1.8 TB/s, whose 320-point rows fill 128-point
+  // tiles better).
+  const long long nx = k.npts[2];
+  const long long waste4 = ((nx + 127) / 128) * 128 - nx, waste8 = ((nx + 255) / 256) * 256 - nx;
+  const int kCpl = waste8 <= waste4 ? 8 : 4;
+  constexpr int kPf = SPMDB200_STREAM3_PREFETCH;
+  // span0 + 1 planes read + kPf in flight, rounded up to a power of two >= 4
+  // (slot indices are masked; a multiple of 4 keeps the 16-byte phase).
+  const int need = span[0] + 1 + kPf;
+  k.ring = need <= 4 ? 4 : (need <= 8 ? 8 : 16);
+  k.kt[1] = (int)(k.npts[1] < SPMDB200_STREAM3_ROWS ? k.npts[1] : SPMDB200_STREAM3_ROWS);
+  k.kt[2] = (int)(k.npts[2] < 32 * kCpl ? k.npts[2] : 32 * kCpl);
+  for (;;) {
+    k.fdim[1] = (k.kt[1] - 1) * k.step[1] + span[1] + 1;
+    k.fdim[2] = k.kt[2] + span[2];
+    k.pitch1 = k.fdim[2] + (int)((((k.a_stride[1] - k.fdim[2]) % 4) + 4) % 4);
+    long long cells = (long long)k.fdim[1] * k.pitch1 + 3;
+    cells += (((k.a_stride[0] - cells) % 4) + 4) % 4;
+    k.slot_cells = (int)cells;
+    if (cells * k.ring * 4 <= 64 * 1024) break;
+    if (k.kt[1] > 1)
+      k.kt[1] = (k.kt[1] + 1) / 2;
+    else if (k.kt[2] > 1)
+      k.kt[2] = (k.kt[2] + 1) / 2;
+    else
+      return cudaErrorNotSupported;
+  }
+  const long long a_ext = (long long)k.fdim[1] * k.a_stride[1] + k.pitch1;
+  const long long b_ext = (long long)k.kt[1] * k.step[1] * k.b_stride[1] + k.kt[2];
+  if (a_ext >= 0x7fffffffLL || b_ext >= 0x7fffffffLL) return cudaErrorNotSupported;
+  k.as1 = (int)k.a_stride[1];
+  k.bs1 = (int)(k.step[1] * k.b_stride[1]);
+  k.fdim[0] = 1;
+  k.kt[0] = 1;
+  k.vsplit = (k.kt[2] + 32 * kCpl - 1) / (32 * kCpl);
+  for (int j = 0; j < k.ntaps; ++j) {
+    k.tap_dz[j] = k.off[j][0] - k.min_off[0];
+    k.tap_in[j] = (k.off[j][1] - k.min_off[1]) * k.pitch1 + (k.off[j][2] - k.min_off[2]);
+  }
+  // Planes per item: long enough to amortise the span0-plane prologue, short
+  // enough for about two items per resident block.
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const long long tiles_yx = ((k.npts[1] + k.kt[1] - 1) / k.kt[1]) * ((k.npts[2] + k.kt[2] - 1) / k.kt[2]);
+  const long long want_items = 2LL * 4 * num_sms(dev);
+  long long kz = (k.npts[0] * tiles_yx + want_items - 1) / want_items;
+  if (kz < 4LL * (span[0] + 1)) kz = 4LL * (span[0] + 1);
+  if (kz > 64) kz = 64;
+  if (kz > k.npts[0]) kz = k.npts[0];
+  k.kz = (int)(kz > 0 ? kz : 1);
+  k.tiles[0] = (k.npts[0] + k.kz - 1) / k.kz;
+  k.tiles[1] = (k.npts[1] + k.kt[1] - 1) / k.kt[1];
+  k.tiles[2] = (k.npts[2] + k.kt[2] - 1) / k.kt[2];
+  k.ntiles = k.tiles[0] * k.tiles[1] * k.tiles[2];
+  if (k.ntiles == 0) return cudaSuccess;
+  if (k.ntiles > 0x7fffffffLL) return cudaErrorNotSupported;
+  const size_t smem = (size_t)k.slot_cells * k.ring * sizeof(float);
+  return kCpl == 8 ? launch_grid(stencil_nd_stream3_kernel<8, kPf>, k, smem, a, b, s)
+                   : launch_grid(stencil_nd_stream3_kernel<4, kPf>, k, smem, a, b, s);
+}
+
 }  // namespace
 
 int promotion_plan(int rank, const int64_t *tile_sizes, const int64_t *steps, const int64_t *min_off,
@@ -485,6 +676,10 @@ cudaError_t launch_stencil_nd(const StencilNdProblem &p, int promote, cudaStream
     k.tap_goff[j] = k.off[j][0] * k.a_stride[0] + k.off[j][1] * k.a_stride[1] + k.off[j][2] * k.a_stride[2];
   }
   const bool unit = k.a_stride[2] == 1 && k.b_stride[2] == 1 && k.step[2] == 1;
+  if (promote && p.rank == 3 && unit && k.step[0] == 1 && span[0] <= 6) {
+    const cudaError_t e = launch_stream3(k, span, p.a, p.b, s);
+    if (e != cudaErrorNotSupported) return e;
+  }
   // Kernel tile: ~8K points per promoted tile (rows of 512 points, 16 per
   // lane; rank 3: 4 x 8 rows of 128), ~4K per direct one; never larger than
   // the grid of output points.  A promoted tile shrinks, outer dimensions

@@ -103,3 +103,27 @@ def test_rejects_overlap_and_bad_arguments(kernels):
         kernels.stencil_nd(t, t, THREE_POINT)
     with pytest.raises(L.SpmdError):
         kernels.stencil_nd(t, torch.zeros((64, 64), device="cuda"), [[0, 0]] * 65)
+
+
+@pytest.mark.parametrize("shape,offsets,weights,steps,shift", [
+    ((9, 20, 140), JACOBI7, None, None, 0),                                       # one ring of 4 planes
+    ((13, 7, 33), [[2, 1, -3], [-3, 0, 2], [0, 0, 0]], [0.5, 0.25, 2.0], None, 1),  # z span 5: ring of 8
+    ((30, 18, 40), [[0, 0, 0], [1, 1, 1]], None, [1, 2, 1], 2),                    # y step 2
+    ((5, 3, 6), [[6, 0, 0], [0, 0, 0]], None, None, 3),                           # z span 6, planes past A
+    ((70, 37, 261), JACOBI7, None, None, 1),                                      # several z items, ragged x
+    ((6, 5, 512), JACOBI7, None, None, 2),                                        # 256-point row segments
+    ((11, 9, 1030), [[0, 0, 0], [1, -1, 2], [-1, 1, -2]], [1.0, -0.5, 0.5], None, 3),  # 256-point, ragged
+])
+def test_rank3_z_streaming(kernels, oracle_mod, shape, offsets, weights, steps, shift):
+    """Rank 3, unit strides, z step 1: the z-streaming kernel (a ring of
+    planes), A starting at every 4-byte phase of a 16-byte line."""
+    base = torch.from_numpy(_rand(int(np.prod(shape)) + 3, 11)).cuda()
+    ta = base[shift:shift + int(np.prod(shape))].view(shape)
+    b_shape = tuple(shape)
+    tb = torch.zeros(b_shape, device="cuda")
+    scale = np.float32(1.0 / 7.0) if offsets is JACOBI7 else 1.0
+    promoted = kernels.stencil_nd(ta, tb, offsets, weights=weights, scale=scale, tile_sizes=[2, 4, 8], steps=steps)
+    torch.cuda.synchronize()
+    assert promoted
+    want = oracle_mod.stencil_nd(ta.cpu().numpy(), b_shape, offsets, weights=weights, scale=scale, steps=steps)
+    assert_bits_equal(tb.cpu().numpy(), want, f"z-streaming {shape}")
