@@ -266,7 +266,11 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
     o = torch.zeros(1, device=dev)
     oi = torch.zeros(1, device=dev, dtype=torch.int32)
     ws = kernels.sum_workspace(n)
+    # sum_f32: the deterministic sum (one f32 rounding, identical bits on every
+    # call); hierarchical_sum_f32: the reference's own semantics (one f32
+    # atomic per block, SPMDToGPU.cpp's grid combine), no last-block combine.
     for key, fn_i in (("sum_f32_2^24", lambda i: kernels.sum_f32(bufs[i % 4], o, ws)),
+                      ("hierarchical_sum_f32_2^24", lambda i: kernels.hierarchical_sum(bufs[i % 4], o)),
                       ("sum_i32_2^24", lambda i: kernels.sum_i32(ibufs[i % 4], oi))):
         ms = batch(fn_i)
         it = iter(range(1 << 30))
