@@ -859,7 +859,7 @@ static int sum_host_impl(float *A, int64_t A_off, int64_t A_size, int64_t A_st, 
   CHECK(staging(2, wsb, &dws));
   CHECK(h2d_1d(da, A ? A + A_off : nullptr, N, A_st, 4));
   CUDA_TRY(cudaMemcpy(dout, o + o_off, 4, cudaMemcpyHostToDevice));
-  CUDA_TRY(cudaMemset(dws, 0, 256));
+  CUDA_TRY(cudaMemset(dws, 0, wsb));  // the whole workspace: ticket and partial words start at zero
   CUDA_TRY(launch_sum_f32(View1{(float *)da, N, 1}, (float *)dout, N, dws, 0));
   CUDA_TRY(cudaMemcpy(o + o_off, dout, 4, cudaMemcpyDeviceToHost));
   return ok();

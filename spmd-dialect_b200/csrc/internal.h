@@ -16,7 +16,10 @@ cudaError_t launch_ewise_add(View1 a, View1 b, View1 c, int64_t n, cudaStream_t 
 cudaError_t launch_axpy(float alpha, View1 x, View1 y, int64_t n, cudaStream_t s);
 
 // ---- reductions (reduce.cu) ---------------------------------------------------
-// Workspace of the deterministic f32 sum: [ticket u32 | pad to 256 B | f64 partials].
+// Workspace of the deterministic f32 sum: [ticket u32 | pad to 256 B | 8-byte
+// partials].  All-zero between calls: every kernel that uses it clears the
+// ticket and the partial words it wrote (the staged sum reads a non-zero word
+// as a written partial).
 size_t sum_f32_workspace_bytes(int64_t n);
 int sum_f32_grid(int64_t n);
 // f64_out set: the unrounded f64 total goes there and `out` is not touched.

@@ -44,8 +44,9 @@ size_t sum_f32_workspace_bytes(int64_t n) {
 // Deterministic f32 sum: per-block f64 partials, last block (ticket) combines
 // them in index order and performs the single f32 rounding of
 // out = out + total -- or, when f64_out is set, stores the f64 total there
-// unrounded (a rank's share of a sum across GPUs).  The ticket is reset to 0
-// so the workspace stays reusable.
+// unrounded (a rank's share of a sum across GPUs).  The ticket and every
+// partial read are reset to 0, so the workspace is all-zero again for the
+// next call (the staged sum below relies on that).
 __global__ void __launch_bounds__(kSumThreads, 8) sum_f32_kernel(const float *__restrict__ a, int64_t sa,
                                                               int64_t n, float *out,
                                                               unsigned *ticket, double *partials,
@@ -65,7 +66,10 @@ __global__ void __launch_bounds__(kSumThreads, 8) sum_f32_kernel(const float *__
   if (!last) return;
   __threadfence();
   double p = 0.0;
-  for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) p = __dadd_rn(p, __ldcg(partials + i));
+  for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
+    p = __dadd_rn(p, __ldcg(partials + i));
+    partials[i] = 0.0;  // the staged sum reads a non-zero word as a written partial
+  }
   const double tot = block_sum_f64(p, sh);
   if (threadIdx.x == 0) {
     if (f64_out) {
@@ -101,6 +105,35 @@ __global__ void __launch_bounds__(kSumThreads, 8) hier_sum_f32_kernel(const floa
 // spmdb200_reduction_status).
 __device__ int g_reduce_timeout;
 
+// Block partials of the staged deterministic sum travel as one 64-bit word
+// each: the f64 bits XOR a signalling-NaN key.  Every partial is the result of
+// __dadd_rn (a number or the canonical quiet NaN), never the key itself, so a
+// stored word is never 0 and 0 means "not written yet".  One word carries the
+// value and its presence, so the writer needs no fence and the combiner no
+// ticket: it polls the words and sees each partial one store latency after
+// it is written.
+constexpr unsigned long long kPartialKey = 0x7FF0DEADBEEF0001ull;
+
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait for a non-zero word; returns 0 if the wait budget ran out.
+__device__ __forceinline__ unsigned long long poll_partial(const unsigned long long *p) {
+  unsigned long long v = ld_relaxed_u64(p);
+  if (v) return v;
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    v = ld_relaxed_u64(p);
+    if (v) return v;
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) return 0ull;
+  }
+}
+
 enum class BulkMode { kF32Det, kI32, kF32Atomic };
 
 template <BulkMode M>
@@ -115,6 +148,7 @@ __global__ void __launch_bounds__(kBulkThreads) sum_bulk_kernel(const void *__re
   __shared__ double shd[32];
   __shared__ uint32_t shu[32];
   __shared__ int last, abort_flag;
+  __shared__ double own;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kBulkStages; ++s) mbar_init(&full[s], 1);
     abort_flag = 0;
@@ -132,8 +166,17 @@ __global__ void __launch_bounds__(kBulkThreads) sum_bulk_kernel(const void *__re
   // The value the sum adds to, read now so the last block's final store does
   // not wait on it (nothing else writes *out while this kernel runs).
   double init = 0.0;
-  if constexpr (M == BulkMode::kF32Det)
-    if (threadIdx.x == 0 && !f64_out) init = (double)*static_cast<const float *>(out);
+  // Start ticket: the block that takes the last one combines the partials.
+  // Every other block has started by then, so its polls wait only on blocks
+  // that are already running.  The atomic's result is first needed after the
+  // stream loop, so its round trip overlaps the loads.
+  unsigned start = 0;
+  if constexpr (M == BulkMode::kF32Det) {
+    if (threadIdx.x == 0) {
+      start = atomicAdd(ticket, 1u);
+      if (!f64_out) init = (double)*static_cast<const float *>(out);
+    }
+  }
   if constexpr (M == BulkMode::kI32) {
     uint32_t acc = 0;
     const bool ok = bulk_stream(base, lo, hi, smem, full, &abort_flag,
@@ -162,17 +205,31 @@ __global__ void __launch_bounds__(kBulkThreads) sum_bulk_kernel(const void *__re
     if constexpr (M == BulkMode::kF32Atomic) {
       if (threadIdx.x == 0) atomicAdd(static_cast<float *>(out), __double2float_rn(b));
     } else {
+      unsigned long long *words = reinterpret_cast<unsigned long long *>(partials);
       if (threadIdx.x == 0) {
-        partials[blockIdx.x] = b;
-        // acq_rel: the partial is visible before the ticket moves, and the
-        // last block's reads below come after every other block's partial.
-        last = (atom_add_acq_rel_gpu(ticket, 1u) == gridDim.x - 1);
+        last = (start == gridDim.x - 1);
+        if (last)
+          own = b;
+        else
+          st_relaxed_u64(words + blockIdx.x, (unsigned long long)__double_as_longlong(b) ^ kPartialKey);
       }
       __syncthreads();
       if (!last) return;
-      fence_acq_rel_gpu();
+      // Combine in block-index order (the same fixed tree for every call);
+      // each word read is cleared again, so the workspace stays all-zero.
       double p = 0.0;
-      for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) p = __dadd_rn(p, __ldcg(partials + i));
+      bool lost = false;
+      for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
+        double v = own;
+        if (i != (int)blockIdx.x) {
+          const unsigned long long w = poll_partial(words + i);
+          lost |= (w == 0ull);
+          v = w ? __longlong_as_double((long long)(w ^ kPartialKey)) : 0.0;
+          st_relaxed_u64(words + i, 0ull);
+        }
+        p = __dadd_rn(p, v);
+      }
+      if (lost) atomicExch(&g_reduce_timeout, 1);
       const double tot = block_sum_f64(p, shd);
       if (threadIdx.x == 0) {
         if (f64_out)

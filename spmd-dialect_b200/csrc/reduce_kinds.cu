@@ -127,7 +127,10 @@ __global__ void __launch_bounds__(kKindThreads) reduce_kind_kernel(const T *__re
   __threadfence();
   if (warp == 0) {
     A p = O::id();
-    for (int i = lane; i < (int)gridDim.x; i += 32) p = O::op(p, __ldcg(partials + i));
+    for (int i = lane; i < (int)gridDim.x; i += 32) {
+      p = O::op(p, __ldcg(partials + i));
+      partials[i] = A(0);  // the workspace is shared with the sums, which read a non-zero word as written
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) p = O::op(p, shfl_xor(p, o));
     if (lane == 0) {

@@ -132,3 +132,41 @@ def test_partial_sum_is_the_unrounded_f64_total(kernels, oracle_mod):
         exact = oracle_mod.sum_f64(np.ascontiguousarray(x[::stride]))
         assert abs(p - exact) <= 1e-12 * abs(exact)
         assert shard.sum_f32(t, init=1.0) == np.float32(1.0 + p)
+
+
+def test_shared_workspace_stays_zero_across_entries(kernels, oracle_mod):
+    """One workspace serves the staged sum, the strided sum and every reduce
+    kind.  The staged sum reads a non-zero partial word as written, so every
+    entry must leave the workspace all-zero; interleaving them on one
+    workspace must not change any result."""
+    import torch
+    from conftest import spmd_pkg
+
+    a = np.random.RandomState(7).random_sample((1 << 20) + 3).astype(np.float32)
+    ia = np.random.RandomState(8).randint(-1000, 1000, 70001, dtype=np.int32)
+    ta, tia = _t(a), _t(ia)
+    ws = kernels.sum_workspace(a.size)
+    f64 = oracle_mod.sum_f64(a)
+
+    def staged():
+        v = float(kernels.sum_f32(ta, _zero_out(), ws).item())
+        assert abs(v - f64) / f64 <= REL_F32
+        return v
+
+    first = staged()
+    assert int(torch.count_nonzero(ws)) == 0
+    strided = float(kernels.sum_f32(ta[::2], _zero_out(), ws).item())
+    want = oracle_mod.sum_f64(a[::2])
+    assert abs(strided - want) / want <= REL_F32
+    assert int(torch.count_nonzero(ws)) == 0
+    assert float(kernels.reduce("max", ta, -1.0, ws=ws).item()) == float(a.max())
+    assert int(torch.count_nonzero(ws)) == 0
+    got_add = float(kernels.reduce("add", ta, 0.0, ws=ws).item())
+    assert abs(got_add - f64) / f64 <= REL_F32
+    assert int(torch.count_nonzero(ws)) == 0
+    x = int(np.bitwise_xor.reduce(ia))
+    assert int(kernels.reduce("xor", tia, 0, ws=ws).item()) == x
+    assert int(torch.count_nonzero(ws)) == 0
+    assert staged() == first
+    assert int(torch.count_nonzero(ws)) == 0
+    assert spmd_pkg().lib().spmdb200_reduction_status() == 0
