@@ -291,6 +291,22 @@ int spmdb200_jacobi2d_host(float *U_base, float *U_aligned, int64_t U_offset, in
                            int64_t U_stride0, int64_t U_stride1,
                            int64_t sweeps, int64_t res_every, double *res_out);
 
+/* The same job on a batch of `count` independent HOST grids that share one
+ * shape and row pitch: grid k is U_aligned[k] + U_offset (H x W, row pitch
+ * stride0 elements, stride1 == 1); its residuals go to res_out[k] (res_out may
+ * be NULL when res_every == 0).  Each grid is swept in place exactly as
+ * spmdb200_jacobi2d_host would sweep it.  The grids run one after another on
+ * the GPU through two device slots.  Grid k+1's upload and grid k-1's download
+ * run on their own streams while grid k is swept, so the PCIe copies overlap
+ * the sweeps.  With pinned host grids, the batch costs the sweeps plus one
+ * upload and one download.  Pageable grids give the same results, but their
+ * copies do not overlap.  The grids must not overlap one another in host
+ * memory.  Synchronous.  No reference counterpart (the reference has no
+ * Jacobi entry); it serves a stream of independent grids. */
+int spmdb200_jacobi2d_host_batch(int64_t count, float *const *U_aligned, int64_t U_offset, int64_t U_size0,
+                                 int64_t U_size1, int64_t U_stride0, int64_t U_stride1,
+                                 int64_t sweeps, int64_t res_every, double *const *res_out);
+
 /* ---- Jacobi-2D over row slabs on several GPUs (one process per GPU) ------ */
 /* No reference counterpart: the reference runs on one GPU.  The global grid
  * has G rows; this rank owns global rows [g_first, g_first + R), R >= 4.  U

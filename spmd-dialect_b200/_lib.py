@@ -86,6 +86,7 @@ _SIGS = {
     "spmdb200_sum_f32_host": (ctypes.c_int, D1 + D0 + [c_i]),
     "spmdb200_sum_i32_host": (ctypes.c_int, D1 + D0 + [c_i]),
     "spmdb200_jacobi2d_host": (ctypes.c_int, D2 + [c_i, c_i, c_p]),
+    "spmdb200_jacobi2d_host_batch": (ctypes.c_int, [c_i, c_p, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_p]),
     # utilities
     "spmdb200_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "spmdb200_last_error": (ctypes.c_int, []),

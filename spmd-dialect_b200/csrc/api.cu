@@ -944,4 +944,92 @@ int spmdb200_jacobi2d_host(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   return ok();
 }
 
+// A batch of independent host grids through two device slots.  Grid k uses
+// slot k % 2.  Uploads run on `in`, sweeps on `comp`, downloads on `out`.
+// Grid k's upload waits for grid k-2's download, which was the last reader of
+// that slot.  So grid k+1's upload and grid k-1's download overlap grid k's
+// sweeps: PCIe copies both ways while HBM serves the sweep kernel.  Residuals
+// and status words come back through a pinned host buffer: a download into
+// pageable memory would block this thread and serialise the pipeline.
+int spmdb200_jacobi2d_host_batch(int64_t count, float *const *U, int64_t U_off, int64_t U_n0, int64_t U_n1,
+                                 int64_t U_s0, int64_t U_s1, int64_t sweeps, int64_t res_every,
+                                 double *const *res_out) {
+  if (count < 0 || (count > 0 && !U)) return fail(SPMDB200_ERR_INVALID_ARG, "negative count or null grid list");
+  if (U_s1 != 1) return fail(SPMDB200_ERR_UNSUPPORTED, "batch grids need contiguous rows (stride1 == 1)");
+  const int64_t nres = res_every > 0 ? sweeps / res_every : 0;
+  for (int64_t k = 0; k < count; ++k) {
+    CHECK(check2("U", U[k], U_off, U_n0, U_n1, U_s0, U_s1));
+    CHECK(check_res(sweeps, res_every, res_out ? res_out[k] : nullptr));
+    if (U_n0 > 0 && U_n1 > 0 && U_s0 < U_n1) return fail(SPMDB200_ERR_INVALID_ARG, "U: row pitch below the row length");
+  }
+  if (count == 0 || U_n0 == 0 || U_n1 == 0) return ok();
+  CHECK(have_device());
+  const int64_t dp = round_up4(U_n1);
+  const size_t grid_bytes = (size_t)U_n0 * dp * 4, rows_bytes = (size_t)U_n1 * 4;
+  void *du[2], *dv[2], *dws[2], *dres[2];
+  for (int j = 0; j < 2; ++j) {  // staging slots 8..15: apart from the single-grid entries' slots
+    CHECK(staging(8 + 4 * j, grid_bytes, &du[j]));
+    CHECK(staging(9 + 4 * j, grid_bytes, &dv[j]));
+    CHECK(staging(10 + 4 * j, sizeof(JacobiWs), &dws[j]));
+    CHECK(staging(11 + 4 * j, (size_t)(nres > 0 ? nres : 1) * 8, &dres[j]));
+  }
+  cudaStream_t in = nullptr, comp = nullptr, out = nullptr;
+  cudaEvent_t ev[6] = {};  // in_done[2], comp_done[2], out_done[2]
+  char *pin = nullptr;     // per grid: status word (8 B) + residuals
+  const size_t per_grid = 8 + (size_t)nres * 8;
+  int st = SPMDB200_OK;
+  auto body = [&]() -> int {
+    CUDA_TRY(cudaStreamCreateWithFlags(&in, cudaStreamNonBlocking));
+    CUDA_TRY(cudaStreamCreateWithFlags(&comp, cudaStreamNonBlocking));
+    CUDA_TRY(cudaStreamCreateWithFlags(&out, cudaStreamNonBlocking));
+    for (auto &e : ev) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    CUDA_TRY(cudaHostAlloc((void **)&pin, per_grid * (size_t)count, cudaHostAllocDefault));
+    // Status words read as OK when a grid runs no sweep (zero sweeps launch nothing).
+    for (int j = 0; j < 2; ++j) CUDA_TRY(cudaMemsetAsync(dws[j], 0, 256, comp));
+    for (int64_t k = 0; k < count; ++k) {
+      const int j = (int)(k & 1);
+      float *hu = U[k] + U_off;
+      if (k >= 2) CUDA_TRY(cudaStreamWaitEvent(in, ev[4 + j], 0));
+      CUDA_TRY(cudaMemcpy2DAsync(du[j], (size_t)dp * 4, hu, (size_t)U_s0 * 4, rows_bytes, (size_t)U_n0,
+                                 cudaMemcpyHostToDevice, in));
+      CUDA_TRY(cudaEventRecord(ev[j], in));
+      CUDA_TRY(cudaStreamWaitEvent(comp, ev[j], 0));
+      CHECK(spmdb200_jacobi2d(nullptr, (float *)du[j], 0, U_n0, U_n1, dp, 1, nullptr, (float *)dv[j], 0, U_n0, U_n1,
+                              dp, 1, sweeps, res_every, (double *)dres[j], dws[j], sizeof(JacobiWs), comp));
+      CUDA_TRY(cudaEventRecord(ev[2 + j], comp));
+      CUDA_TRY(cudaStreamWaitEvent(out, ev[2 + j], 0));
+      const void *fin = (sweeps % 2 == 0) ? du[j] : dv[j];
+      CUDA_TRY(cudaMemcpy2DAsync(hu, (size_t)U_s0 * 4, fin, (size_t)dp * 4, rows_bytes, (size_t)U_n0,
+                                 cudaMemcpyDeviceToHost, out));
+      char *slot = pin + per_grid * (size_t)k;
+      CUDA_TRY(cudaMemcpyAsync(slot, &static_cast<JacobiWs *>(dws[j])->status, sizeof(int), cudaMemcpyDeviceToHost,
+                               out));
+      if (nres > 0) CUDA_TRY(cudaMemcpyAsync(slot + 8, dres[j], (size_t)nres * 8, cudaMemcpyDeviceToHost, out));
+      CUDA_TRY(cudaEventRecord(ev[4 + j], out));
+    }
+    CUDA_TRY(cudaStreamSynchronize(out));
+    for (int64_t k = 0; k < count; ++k) {
+      const char *slot = pin + per_grid * (size_t)k;
+      int dev_status = 0;
+      std::memcpy(&dev_status, slot, sizeof(int));
+      if (dev_status != kDevOk)
+        return fail(SPMDB200_ERR_TIMEOUT, "grid %lld: a bounded device wait expired (status %d)", (long long)k,
+                    dev_status);
+      if (nres > 0 && res_out && res_out[k]) std::memcpy(res_out[k], slot + 8, (size_t)nres * 8);
+    }
+    return SPMDB200_OK;
+  };
+  st = body();
+  // Every stream drains before its resources go, on success and on error.
+  for (cudaStream_t s : {in, comp, out})
+    if (s) cudaStreamSynchronize(s);
+  for (cudaStream_t s : {in, comp, out})
+    if (s) cudaStreamDestroy(s);
+  for (auto e : ev)
+    if (e) cudaEventDestroy(e);
+  if (pin) cudaFreeHost(pin);
+  if (st != SPMDB200_OK) return st;
+  return ok();
+}
+
 }  // extern "C"

@@ -101,3 +101,26 @@ def jacobi2d_host(U: np.ndarray, sweeps: int, res_every: int = 0) -> tuple[np.nd
     res = np.zeros(max(nres, 1), dtype=np.float64)
     call("spmdb200_jacobi2d_host", *desc2d(U), c_i(sweeps), c_i(res_every), _ptr(res))
     return U, (res[:nres] if nres else None)
+
+
+def jacobi2d_host_batch(grids: list[np.ndarray], sweeps: int, res_every: int = 0) -> list:
+    """Runs `sweeps` sweeps on each host grid in place, the copies of one grid
+    overlapping the sweeps of its neighbours in the list (pinned grids, e.g.
+    torch.empty(..., pin_memory=True).numpy(), overlap; pageable ones do not).
+    Every grid has the same shape and row pitch.  Returns one residual array
+    (or None) per grid."""
+    if not grids:
+        return []
+    g0 = grids[0]
+    if g0.ndim != 2 or g0.dtype != np.float32 or g0.strides[1] != 4 or g0.strides[0] % 4:
+        raise ValueError("float32 grids with contiguous rows expected")
+    for g in grids:
+        if g.shape != g0.shape or g.strides != g0.strides or g.dtype != g0.dtype:
+            raise ValueError("every grid of a batch must share shape, strides and dtype")
+    nres = sweeps // res_every if res_every > 0 else 0
+    res = [np.zeros(max(nres, 1), dtype=np.float64) for _ in grids]
+    ptrs = (c_p * len(grids))(*[g.ctypes.data for g in grids])
+    rptr = (c_p * len(grids))(*[r.ctypes.data for r in res])
+    call("spmdb200_jacobi2d_host_batch", c_i(len(grids)), ctypes.cast(ptrs, c_p), c_i(0), c_i(g0.shape[0]),
+         c_i(g0.shape[1]), c_i(g0.strides[0] // 4), c_i(1), c_i(sweeps), c_i(res_every), ctypes.cast(rptr, c_p))
+    return [r[:nres] if nres else None for r in res]

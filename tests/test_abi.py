@@ -122,3 +122,31 @@ def test_no_silent_cpu_fallback_without_gpu():
     with pytest.raises(spmd_mod("_lib").SpmdError):
         host.ewise(a, b, c)
     assert not c.any(), "output written without a GPU"
+
+
+def test_jacobi2d_host_batch_validates_and_never_falls_back():
+    """The batch host entry checks its arguments before any CUDA call, and with
+    no usable GPU reports an error instead of sweeping on the CPU."""
+    import numpy as np
+    import torch
+    lib = spmd_mod("_lib").lib()
+    c_i = ctypes.c_int64
+    fake = (ctypes.c_void_p * 1)(0x1000)
+    grids = ctypes.cast(fake, ctypes.c_void_p)
+    assert lib.spmdb200_jacobi2d_host_batch(c_i(-1), grids, c_i(0), c_i(8), c_i(8), c_i(8), c_i(1), c_i(1), c_i(0),
+                                            None) == -1
+    assert lib.spmdb200_jacobi2d_host_batch(c_i(1), None, c_i(0), c_i(8), c_i(8), c_i(8), c_i(1), c_i(1), c_i(0),
+                                            None) == -1
+    assert lib.spmdb200_jacobi2d_host_batch(c_i(1), grids, c_i(0), c_i(8), c_i(8), c_i(8), c_i(2), c_i(1), c_i(0),
+                                            None) == -4  # rows must be contiguous
+    assert lib.spmdb200_jacobi2d_host_batch(c_i(1), grids, c_i(0), c_i(8), c_i(8), c_i(4), c_i(1), c_i(1), c_i(0),
+                                            None) == -1  # row pitch below the row length
+    assert lib.spmdb200_jacobi2d_host_batch(c_i(1), grids, c_i(0), c_i(8), c_i(8), c_i(8), c_i(1), c_i(4), c_i(2),
+                                            None) == -1  # residuals due but nowhere to put them
+    if torch.cuda.is_available():
+        return
+    host = spmd_mod("host")
+    gs = [np.ones((6, 8), np.float32) for _ in range(2)]
+    with pytest.raises(spmd_mod("_lib").SpmdError):
+        host.jacobi2d_host_batch(gs, 3)
+    assert all((g == 1).all() for g in gs), "grid changed without a GPU"

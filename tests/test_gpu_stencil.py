@@ -193,3 +193,38 @@ def test_jacobi3d_config_512_50_sweeps(kernels, oracle_mod):
     want, wres = oracle_mod.jacobi3d(u0, 50, 10)
     assert_bits_equal(fin, want, "J3 512^3 x 50")
     np.testing.assert_allclose(res, wres, rtol=RES_RTOL)
+
+
+@pytest.mark.parametrize("pinned", [True, False])
+def test_jacobi2d_host_batch_matches_oracle(host_api, oracle_mod, pinned):
+    """Five independent grids through the batch host entry (two device slots,
+    each reused twice; pinned grids overlap their copies with the sweeps,
+    pageable ones do not): every grid and its residuals equal the oracle's,
+    including a row pitch that is not a multiple of four and a padded one."""
+    import torch
+    for shape, pitch in (((97, 517), 517), ((64, 130), 160)):
+        inits = [jacobi_init(shape, seed) for seed in range(10, 15)]
+        grids = []
+        for u0 in inits:
+            if pinned:
+                buf = torch.empty((shape[0], pitch), dtype=torch.float32, pin_memory=True).numpy()
+            else:
+                buf = np.empty((shape[0], pitch), np.float32)
+            g = buf[:, :shape[1]]
+            g[...] = u0
+            grids.append(g)
+        res = host_api.jacobi2d_host_batch(grids, 9, 3)
+        for k, (g, u0, r) in enumerate(zip(grids, inits, res)):
+            want, wres = oracle_mod.jacobi2d(u0, 9, 3)
+            assert_bits_equal(g, want, f"batch grid {k} {shape} pitch {pitch}")
+            assert np.max(np.abs(r - wres) / np.abs(wres)) <= 1e-12
+    # Residual-free batch of one grid equals the single-grid host entry.
+    u0 = jacobi_init((33, 40), 21)
+    a, b = u0.copy(), u0.copy()
+    assert host_api.jacobi2d_host_batch([a], 6) == [None]
+    host_api.jacobi2d_host(b, 6, 0)
+    assert_bits_equal(a, b, "batch of one vs jacobi2d_host")
+    # Zero sweeps: the grids come back unchanged.
+    c = u0.copy()
+    assert host_api.jacobi2d_host_batch([c, c.copy()], 0) == [None, None]
+    assert_bits_equal(c, u0, "zero-sweep batch")
