@@ -222,16 +222,28 @@ class _SlabJob:
             raise ValueError(f"checkpoint grid {info.shape} does not match this job's grid {want}")
         block = ck.read_block(path, self.g_first - self.halo, self.g_first + self.rows + self.halo)
         local = np.ascontiguousarray(self._pad(block))
+        self._quiesce()
         for buf in (self._u, self._v):
             call("spmdb200_memcpy", c_p(buf.ptr), local.ctypes.data_as(c_p), ctypes.c_size_t(local.nbytes), None)
         self.sweeps_done = info.sweeps
         rendezvous()
 
     # ---------------------------------------------------------------- running
+    def _quiesce(self) -> None:
+        """Returns once every rank's previous launch is complete.  A launch's
+        last pass still stores halo rows (the next launch's input) into the
+        neighbours' memory and bumps their delivery counters after a
+        neighbour's own kernel may have ended; nothing may clear those counters
+        or overwrite those rows before then."""
+        import torch
+        torch.cuda.current_stream().synchronize()
+        rendezvous()
+
     def run(self, sweeps: int, check: bool = True) -> None:
         """`sweeps` sweeps on every rank (all ranks must call with the same count)."""
         import torch
         stream = c_p(torch.cuda.current_stream().cuda_stream)
+        self._quiesce()
         call("spmdb200_jacobi_ws_reset", c_p(self._ws.ptr), stream)
         torch.cuda.current_stream().synchronize()
         rendezvous()  # every workspace is clear before any kernel can deliver a halo
@@ -274,6 +286,7 @@ class _SlabJob:
             raise ValueError(f"host slab must be {(self.local_rows,) + self.unit_shape} float32")
         # Only U needs the input: V's owned units are all written by the first
         # sweep and its halo units by the neighbours before anyone reads them.
+        self._quiesce()
         call("spmdb200_memcpy", c_p(self._u.ptr), host_local.ctypes.data_as(c_p),
              ctypes.c_size_t(host_local.nbytes), None)
         self.run(sweeps, check=True)

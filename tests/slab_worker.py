@@ -95,6 +95,40 @@ def main() -> None:
     if rank == 0:
         print(f"sharded axpy bit-exact on every rank={bool(flag_axpy.item())}", flush=True)
         ok = ok and bool(flag_axpy.item())
+    # Back-to-back launches: a launch's last pass still delivers halo rows into
+    # the neighbour after that neighbour's kernel may have ended, so each run
+    # (and each host-buffer run, which overwrites the slab) must wait for every
+    # rank's previous launch before clearing counters or writing the slab.
+    G, W = 2048, 4096
+    u0 = jacobi_init((G, W), 5)
+    job = slab.SlabJacobi2D(cols=W, G=G, res_every=0, init=u0)
+    for _ in range(4):
+        job.run(9, check=False)
+    job.check()
+    grid = job.gather()
+    host_ok = True
+    lo, hi = job.g_first - job.halo, job.g_first + job.rows + job.halo
+    from oracle import oracle as orc
+    want6, _ = orc.jacobi2d(u0, 6, 0)
+    for _ in range(2):  # fresh input each call, as the end-to-end benchmark does
+        local = np.zeros((job.local_rows,) + job.unit_shape, np.float32)
+        s_lo, s_hi = max(lo, 0), min(hi, G)
+        local[s_lo - lo:s_hi - lo] = job._pad(u0[s_lo:s_hi])
+        host = torch.empty(local.shape, dtype=torch.float32, pin_memory=True).numpy()
+        host[...] = local
+        job.run_host(host, 6)
+        got = job._trim(host[job.halo:job.halo + job.rows])
+        mine6 = want6[job.g_first:job.g_first + job.rows]
+        host_ok = host_ok and np.array_equal(got.view(np.uint32), mine6.view(np.uint32))
+    job.close()
+    flag_host = torch.tensor([1 if host_ok else 0], device="cuda")
+    dist.all_reduce(flag_host, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        want36, _ = orc.jacobi2d(u0, 36, 0)
+        same = np.array_equal(grid.view(np.uint32), want36.view(np.uint32))
+        print(f"4 back-to-back runs of 9 sweeps: bit-exact={same}; two host-buffer runs: bit-exact="
+              f"{bool(flag_host.item())}", flush=True)
+        ok = ok and same and bool(flag_host.item())
     # Checkpoint from both ranks, resume in a fresh 2-rank job.
     import tempfile
     ck_dir = tempfile.mkdtemp() if rank == 0 else None
