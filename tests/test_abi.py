@@ -150,3 +150,17 @@ def test_jacobi2d_host_batch_validates_and_never_falls_back():
     with pytest.raises(spmd_mod("_lib").SpmdError):
         host.jacobi2d_host_batch(gs, 3)
     assert all((g == 1).all() for g in gs), "grid changed without a GPU"
+
+
+def test_jacobi2d_host_batch_wrapper_checks_layout():
+    """Every grid of a batch shares one shape and row pitch, rows contiguous."""
+    import numpy as np
+    host = spmd_mod("host")
+    a = np.zeros((6, 8), np.float32)
+    assert host.jacobi2d_host_batch([], 3) == []
+    for bad in ([a, np.zeros((6, 9), np.float32)],            # shape differs
+                [a, np.zeros((6, 16), np.float32)[:, :8]],    # row pitch differs
+                [np.zeros((6, 16), np.float32)[:, ::2]],      # rows not contiguous
+                [a.astype(np.float64)]):                       # not float32
+        with pytest.raises(ValueError):
+            host.jacobi2d_host_batch(bad, 3)
