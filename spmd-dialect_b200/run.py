@@ -28,7 +28,7 @@ sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["ewise", "axpy", "sum_f32", "sum_i32", "hierarchical_sum", "stencil3",
-                                       "jacobi2d", "jacobi3d", "reduce_f32", "reduce_i32"])
+                                       "stencil_nd", "jacobi2d", "jacobi3d", "reduce_f32", "reduce_i32"])
     ap.add_argument("--kind", default="max", help="reduction kind for reduce_f32 / reduce_i32")
     ap.add_argument("--size", type=int, default=1 << 24)
     ap.add_argument("--shape", default="4096x4096")
@@ -80,6 +80,20 @@ def main() -> None:
         out = torch.empty((n, m), device=dev)
         fn = lambda: k.stencil3pt(x, out)  # noqa: E731
         work_bytes = 8 * n * m
+    elif a.kernel == "stencil_nd":
+        # The general promoted-tile stencil: the 5-point (rank 2) or 7-point
+        # (rank 3) star in source order, scaled, output the size of the input.
+        x = torch.rand(shape, device=dev, generator=g)
+        out = torch.empty_like(x)
+        r = len(shape)
+        taps = [[0] * r]
+        for d in range(r):
+            for o in (-1, 1):
+                t = [0] * r
+                t[d] = o
+                taps.append(t)
+        fn = lambda: k.stencil_nd(x, out, taps, scale=1.0 / len(taps))  # noqa: E731
+        work_bytes = 8 * x.numel()
     else:
         u = torch.rand(shape, device=dev, generator=g)
         v = torch.empty_like(u)
