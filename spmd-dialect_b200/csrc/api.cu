@@ -464,9 +464,9 @@ int spmdb200_reduce_i32(int kind, int32_t *A_base, int32_t *A, int64_t A_off, in
 
 int spmdb200_reduction_status(void) {
   CUDA_TRY(cudaDeviceSynchronize());
-  const int f = reduction_timeout_flag(true);
-  if (f < 0) return fail(SPMDB200_ERR_CUDA, "reading the reduction status flag failed");
-  if (f) return fail(SPMDB200_ERR_TIMEOUT, "a staged reduction's bounded wait expired; its result is invalid");
+  const int f0 = reduction_timeout_flag(true), f1 = kind_timeout_flag(true);
+  if (f0 < 0 || f1 < 0) return fail(SPMDB200_ERR_CUDA, "reading the reduction status flag failed");
+  if (f0 || f1) return fail(SPMDB200_ERR_TIMEOUT, "a staged reduction's bounded wait expired; its result is invalid");
   return ok();
 }
 

@@ -32,8 +32,10 @@ cudaError_t launch_reduce_f32(int kind, const float *a, int64_t sa, int64_t n, f
                               cudaStream_t s);
 cudaError_t launch_reduce_i32(int kind, const int32_t *a, int64_t sa, int64_t n, int32_t *out, int32_t init,
                               void *ws, cudaStream_t s);
-// Device flag set when a bounded wait of a staged reduction expired (-1 on error).
+// Device flags set when a bounded wait of a staged sum / staged kind reduction
+// expired (-1 on error).
 int reduction_timeout_flag(bool clear);
+int kind_timeout_flag(bool clear);
 
 // ---- 3-point promoted stencil (stencil3.cu) -----------------------------------------
 cudaError_t launch_stencil3(View2 a, View2 b, int64_t n, int64_t m, cudaStream_t s);

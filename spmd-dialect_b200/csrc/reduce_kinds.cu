@@ -16,8 +16,10 @@
 // and -0 orders below +0.  i32 max/min are signed (arith.maxsi / minsi); i32
 // add/mul wrap like arith.addi / muli.
 #include <cmath>
+#include <type_traits>
 
 #include "internal.h"
+#include "reduce_bulk.cuh"
 #include "reduction.cuh"
 
 namespace spmdb200 {
@@ -140,8 +142,143 @@ __global__ void __launch_bounds__(kKindThreads) reduce_kind_kernel(const T *__re
   }
 }
 
+// Set when a bounded wait of a staged kind reduction expires (read with the
+// sums' flag by spmdb200_reduction_status).
+__device__ int g_kind_timeout;
+
+__device__ __forceinline__ float elem_as(float, uint32_t u) { return __uint_as_float(u); }
+
+// Order-preserving integer key of an f32 (an involution): keys of non-NaN
+// values compare like the values, with -0 below +0 (arith.maximumf /
+// minimumf order).  NaNs of either sign fall outside [key(-inf), key(+inf)].
+__device__ __forceinline__ int32_t f32_key(uint32_t bits) {
+  const int32_t s = (int32_t)bits;
+  return s ^ ((s >> 31) & 0x7fffffff);
+}
+__device__ __forceinline__ float f32_from_key(int32_t k) { return __int_as_float(k ^ ((k >> 31) & 0x7fffffff)); }
+__device__ __forceinline__ int32_t elem_as(int32_t, uint32_t u) { return (int32_t)u; }
+
+// Unit stride, 16-byte aligned input: the sums' shared-memory staging (each
+// CTA, one per SM, pulls one contiguous range through the cp.async.bulk ring)
+// with this kind's combine per thread, then the same warp / block / last-block
+// tree as reduce_kind_kernel.  Each thread combines a fixed subset in a fixed
+// order, so the result is deterministic for a given device.
+template <typename T, int K>
+__global__ void __launch_bounds__(kBulkThreads) reduce_kind_bulk_kernel(const T *__restrict__ a, int64_t n, T *out,
+                                                                       T init, unsigned *ticket, void *partials_raw) {
+  using O = KindOp<T, K>;
+  using A = typename O::A;
+  extern __shared__ __align__(128) unsigned char bulk_raw[];
+  unsigned char *smem = bulk_raw + ((128u - (smem_u32(bulk_raw) & 127u)) & 127u);
+  __shared__ uint64_t full[kBulkStages];
+  __shared__ A sh[32];
+  __shared__ int last, abort_flag;
+  A *partials = static_cast<A *>(partials_raw);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBulkStages; ++s) mbar_init(&full[s], 1);
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  const int64_t units = n >> 2;
+  int64_t lo, hi;
+  cta_range(units, lo, hi);
+  const uint4 *base = reinterpret_cast<const uint4 *>(a);
+  if (threadIdx.x == 0) bulk_prefetch_head(base, lo, hi);
+  __syncthreads();
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
+  // Four independent chains (one per element of a 16-byte unit): the f32
+  // max/min combine is a long dependent sequence, and a single chain held
+  // each stage long enough to slow the stream.  Combined in a fixed order.
+  A acc;
+  bool ok;
+  if constexpr (std::is_same<T, float>::value && (K == 2 || K == 3)) {
+    // f32 max / min as integer max and min over keys: the largest key (max)
+    // or smallest (min) is the result unless a NaN was seen, which shows as
+    // a key above key(+inf) or below key(-inf).
+    int32_t hi_k = f32_key(0xff800000u), lo_k = f32_key(0x7f800000u);  // key(-inf), key(+inf)
+    ok = bulk_stream(base, lo, hi, smem, full, &abort_flag, [&](uint4 v) {
+      const int32_t a0 = f32_key(v.x), a1 = f32_key(v.y), a2 = f32_key(v.z), a3 = f32_key(v.w);
+      hi_k = max(hi_k, max(max(a0, a1), max(a2, a3)));
+      lo_k = min(lo_k, min(min(a0, a1), min(a2, a3)));
+    });
+    const bool nan = hi_k > f32_key(0x7f800000u) || lo_k < f32_key(0xff800000u);
+    acc = nan ? __int_as_float(0x7fc00000) : f32_from_key(K == 2 ? hi_k : lo_k);
+  } else {
+    A acc0 = O::id(), acc1 = O::id(), acc2 = O::id(), acc3 = O::id();
+    ok = bulk_stream(base, lo, hi, smem, full, &abort_flag, [&](uint4 v) {
+      acc0 = O::op(acc0, O::in(elem_as(T(), v.x)));
+      acc1 = O::op(acc1, O::in(elem_as(T(), v.y)));
+      acc2 = O::op(acc2, O::in(elem_as(T(), v.z)));
+      acc3 = O::op(acc3, O::in(elem_as(T(), v.w)));
+    });
+    acc = O::op(O::op(acc0, acc1), O::op(acc2, acc3));
+  }
+  if (!ok && threadIdx.x == 0) atomicExch(&g_kind_timeout, 1);
+  if (blockIdx.x == gridDim.x - 1) {  // the n % 4 elements past the last 16-byte unit
+    const int64_t t = (units << 2) + threadIdx.x;
+    if (t < n) acc = O::op(acc, O::in(a[t]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc = O::op(acc, shfl_xor(acc, o));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) sh[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    A b = O::id();
+    for (int w = 0; w < kBulkThreads / 32; ++w) b = O::op(b, sh[w]);
+    partials[blockIdx.x] = b;
+    __threadfence();
+    last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (warp == 0) {
+    A p = O::id();
+    for (int i = lane; i < (int)gridDim.x; i += 32) {
+      p = O::op(p, __ldcg(partials + i));
+      partials[i] = A(0);  // the workspace is shared with the sums, which read a non-zero word as written
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) p = O::op(p, shfl_xor(p, o));
+    if (lane == 0) {
+      *out = O::fin(init, p);
+      *ticket = 0u;
+    }
+  }
+}
+
+template <typename T, int K>
+cudaError_t launch_kind_bulk(const T *a, int64_t n, T *out, T init, void *ws, cudaStream_t s) {
+  static int cache[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (cache[dev] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(reduce_kind_bulk_kernel<T, K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kBulkSmem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reduce_kind_bulk_kernel<T, K>, kBulkThreads,
+                                                      kBulkSmem) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    cache[dev] = per_sm * num_sms(dev);
+  }
+  const int64_t chunks = ((n >> 2) * 16 + kBulkChunk - 1) / kBulkChunk;  // at least one chunk per CTA
+  int64_t g = chunks < 1 ? 1 : chunks;
+  if (g > cache[dev]) g = cache[dev];
+  if (g > kMaxCtas) g = kMaxCtas;
+  unsigned *ticket = static_cast<unsigned *>(ws);
+  void *partials = static_cast<char *>(ws) + 256;
+  return launch_pdl(reduce_kind_bulk_kernel<T, K>, (unsigned)g, kBulkThreads, kBulkSmem, s, a, n, out, init, ticket,
+                    partials);
+}
+
 template <typename T, int K>
 cudaError_t launch_kind(const T *a, int64_t sa, int64_t n, T *out, T init, void *ws, cudaStream_t s) {
+  if (sa == 1 && (reinterpret_cast<uintptr_t>(a) & 15u) == 0) return launch_kind_bulk<T, K>(a, n, out, init, ws, s);
   static int cache[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -167,6 +304,16 @@ cudaError_t launch_kind(const T *a, int64_t sa, int64_t n, T *out, T init, void 
 }
 
 }  // namespace
+
+int kind_timeout_flag(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_kind_timeout, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_kind_timeout, &zero, sizeof(int));
+  }
+  return v;
+}
 
 cudaError_t launch_reduce_f32(int kind, const float *a, int64_t sa, int64_t n, float *out, float init, void *ws,
                               cudaStream_t s) {
