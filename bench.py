@@ -215,7 +215,8 @@ def run_reference_arm(args) -> None:
 
 # ------------------------------------------------------------------ GPU legs
 def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
-    """The other configurations at N=1 (rank 0): f32/i32 sum 2^24, axpy 2^28,
+    """The other configurations at N=1 (rank 0): f32/i32 sum 2^24, f32 max and
+    i32 xor reductions 2^24, axpy 2^28,
     the promoted 3-point stencil at 4096^2 and 8192^2, the general stencil
     (5-point) at 8192^2, Jacobi-2D 4096^2 x 100, Jacobi-3D 512^3 x 50.  L2
     flushed between reps."""
@@ -279,6 +280,16 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
         out[key] = {"ms": round(ms, 5), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3),
                     "ms_single_launch": round(ms1, 5), "l2": "4 rotating 64 MiB inputs",
                     "timing": "mean of 40 back-to-back launches"}
+    # Other spmd.reduce kinds on the same inputs (f32 max: integer max over
+    # order-preserving keys; i32 xor), same timing.
+    ok_ = torch.zeros(1, device=dev)
+    oki = torch.zeros(1, device=dev, dtype=torch.int32)
+    for key, fn_i in (("reduce_max_f32_2^24", lambda i: kernels.reduce("max", bufs[i % 4], 0.0, ok_, ws)),
+                      ("reduce_xor_i32_2^24", lambda i: kernels.reduce("xor", ibufs[i % 4], 0, oki, ws))):
+        ms = batch(fn_i)
+        gbs = n * 4 / ms / 1e6
+        out[key] = {"ms": round(ms, 5), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3),
+                    "l2": "4 rotating 64 MiB inputs", "timing": "mean of 40 back-to-back launches"}
     del bufs, ibufs
     n = 1 << 28
     x = torch.rand(n, device=dev, generator=g) * 2 - 1

@@ -105,35 +105,6 @@ __global__ void __launch_bounds__(kSumThreads, 8) hier_sum_f32_kernel(const floa
 // spmdb200_reduction_status).
 __device__ int g_reduce_timeout;
 
-// Block partials of the staged deterministic sum travel as one 64-bit word
-// each: the f64 bits XOR a signalling-NaN key.  Every partial is the result of
-// __dadd_rn (a number or the canonical quiet NaN), never the key itself, so a
-// stored word is never 0 and 0 means "not written yet".  One word carries the
-// value and its presence, so the writer needs no fence and the combiner no
-// ticket: it polls the words and sees each partial one store latency after
-// it is written.
-constexpr unsigned long long kPartialKey = 0x7FF0DEADBEEF0001ull;
-
-__device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v) {
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-// Bounded wait for a non-zero word; returns 0 if the wait budget ran out.
-__device__ __forceinline__ unsigned long long poll_partial(const unsigned long long *p) {
-  unsigned long long v = ld_relaxed_u64(p);
-  if (v) return v;
-  const unsigned long long t0 = globaltimer_ns();
-  for (;;) {
-    v = ld_relaxed_u64(p);
-    if (v) return v;
-    if (globaltimer_ns() - t0 > kWaitBudgetNs) return 0ull;
-  }
-}
-
 enum class BulkMode { kF32Det, kI32, kF32Atomic };
 
 template <BulkMode M>

@@ -98,6 +98,46 @@ __device__ __forceinline__ bool bulk_stream(const uint4 *base, int64_t u_lo, int
   return failed_at < 0;
 }
 
+// Block partials of the staged reductions travel as one 64-bit word each.
+// An f64 partial is stored as its bits XOR a signalling-NaN key: the f64 bits XOR a signalling-NaN key.  Every partial is the result of
+// __dadd_rn (a number or the canonical quiet NaN), never the key itself, so a
+// stored word is never 0 and 0 means "not written yet".  One word carries the
+// value and its presence, so the writer needs no fence and the combiner no
+// ticket: it polls the words and sees each partial one store latency after
+// it is written.
+constexpr unsigned long long kPartialKey = 0x7FF0DEADBEEF0001ull;
+
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// A 4-byte partial (f32 or i32 bits) is stored with bit 32 set.
+__device__ __forceinline__ unsigned long long partial_word(double v) {
+  return (unsigned long long)__double_as_longlong(v) ^ kPartialKey;
+}
+__device__ __forceinline__ unsigned long long partial_word(float v) { return (1ull << 32) | __float_as_uint(v); }
+__device__ __forceinline__ unsigned long long partial_word(uint32_t v) { return (1ull << 32) | v; }
+__device__ __forceinline__ void partial_value(unsigned long long w, double &v) {
+  v = __longlong_as_double((long long)(w ^ kPartialKey));
+}
+__device__ __forceinline__ void partial_value(unsigned long long w, float &v) { v = __uint_as_float((uint32_t)w); }
+__device__ __forceinline__ void partial_value(unsigned long long w, uint32_t &v) { v = (uint32_t)w; }
+// Bounded wait for a non-zero word; returns 0 if the wait budget ran out.
+__device__ __forceinline__ unsigned long long poll_partial(const unsigned long long *p) {
+  unsigned long long v = ld_relaxed_u64(p);
+  if (v) return v;
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    v = ld_relaxed_u64(p);
+    if (v) return v;
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) return 0ull;
+  }
+}
+
 // This CTA's contiguous share [lo, hi) of `total` units (equal split).
 __device__ __forceinline__ void cta_range(int64_t total, int64_t &lo, int64_t &hi) {
   lo = total * (int64_t)blockIdx.x / gridDim.x;

@@ -172,8 +172,9 @@ __global__ void __launch_bounds__(kBulkThreads) reduce_kind_bulk_kernel(const T 
   unsigned char *smem = bulk_raw + ((128u - (smem_u32(bulk_raw) & 127u)) & 127u);
   __shared__ uint64_t full[kBulkStages];
   __shared__ A sh[32];
+  __shared__ A own;
   __shared__ int last, abort_flag;
-  A *partials = static_cast<A *>(partials_raw);
+  unsigned long long *words = static_cast<unsigned long long *>(partials_raw);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kBulkStages; ++s) mbar_init(&full[s], 1);
     abort_flag = 0;
@@ -187,6 +188,9 @@ __global__ void __launch_bounds__(kBulkThreads) reduce_kind_bulk_kernel(const T 
   __syncthreads();
   pdl_wait();
   if (threadIdx.x == 0) pdl_trigger();
+  // Start ticket: the block that starts last combines (see the staged sum).
+  unsigned start = 0;
+  if (threadIdx.x == 0) start = atomicAdd(ticket, 1u);
   // Four independent chains (one per element of a 16-byte unit): the f32
   // max/min combine is a long dependent sequence, and a single chain held
   // each stage long enough to slow the stream.  Combined in a fixed order.
@@ -227,25 +231,43 @@ __global__ void __launch_bounds__(kBulkThreads) reduce_kind_bulk_kernel(const T 
   if (threadIdx.x == 0) {
     A b = O::id();
     for (int w = 0; w < kBulkThreads / 32; ++w) b = O::op(b, sh[w]);
-    partials[blockIdx.x] = b;
-    __threadfence();
-    last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+    last = (start == gridDim.x - 1);
+    if (last)
+      own = b;
+    else
+      st_relaxed_u64(words + blockIdx.x, partial_word(b));  // value and presence in one word: no fence
   }
   __syncthreads();
   if (!last) return;
-  __threadfence();
-  if (warp == 0) {
-    A p = O::id();
-    for (int i = lane; i < (int)gridDim.x; i += 32) {
-      p = O::op(p, __ldcg(partials + i));
-      partials[i] = A(0);  // the workspace is shared with the sums, which read a non-zero word as written
+  // The combiner: one thread per block partial polls its word, then the same
+  // fixed tree (per-thread order, warp shuffles, warps in order); every word
+  // read is cleared, so the workspace stays all-zero.
+  A p = O::id();
+  bool lost = false;
+  for (int i = threadIdx.x; i < (int)gridDim.x; i += kBulkThreads) {
+    A v = own;
+    if (i != (int)blockIdx.x) {
+      const unsigned long long w = poll_partial(words + i);
+      lost |= (w == 0ull);
+      if (w)
+        partial_value(w, v);
+      else
+        v = O::id();
+      st_relaxed_u64(words + i, 0ull);
     }
+    p = O::op(p, v);
+  }
+  if (lost) atomicExch(&g_kind_timeout, 1);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) p = O::op(p, shfl_xor(p, o));
-    if (lane == 0) {
-      *out = O::fin(init, p);
-      *ticket = 0u;
-    }
+  for (int o = 16; o > 0; o >>= 1) p = O::op(p, shfl_xor(p, o));
+  __syncthreads();  // thread 0 has finished reading sh[] above
+  if (lane == 0) sh[warp] = p;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    A t = O::id();
+    for (int w = 0; w < kBulkThreads / 32; ++w) t = O::op(t, sh[w]);
+    *out = O::fin(init, t);
+    *ticket = 0u;
   }
 }
 
