@@ -12,13 +12,26 @@ flush is needed between steps).  At N > 1 the slabs exchange four halo rows per
 neighbour per pass over NVLink inside the persistent kernel.
 
 `value` is device time (CUDA events, max over ranks); `e2e` runs the same job
-through the host-buffer C entry (pinned host grid in, result grid out, both
-copies inside the timed region).  `roofline` uses the algorithmic bytes of
+through the host-buffer C entries (pinned host grids in, result grids out,
+every copy inside the timed region).  `roofline` uses the algorithmic bytes of
 the sweep kernel against the measured HBM copy bandwidth: each pass over the
 grid reads every cell once and writes it once (8 B per cell per pass), and a
 pass advances four sweeps (two or one for the 0-7 sweeps left over), so 1000
-sweeps cost 2 B per cell update.  `cpu_baseline` times the oracle (the C/OpenMP restatement of the
-reference's SPMDToOpenMP lowering) on a bounded sample of the same grid.
+sweeps cost 2 B per cell update.
+
+Before anything is timed the run checks its own results (`parity`, and a
+non-zero exit on any mismatch): at N = 1 the timed kernel on a 2048 x 32768
+slab of RandomState(4) input for the full 1000 sweeps against the oracle; at
+N > 1 a gathered row-slab grid and a gathered z-slab grid against the
+single-domain oracle, and the sharded sums against the f64 sum.
+
+At N > 1 the line also carries the configured global grid split across the
+GPUs (`strong`: 32768 x 32768 in 32768/N-row slabs), the sharded f32/i32 sums
+(2^24 elements per GPU) and the Jacobi-3D z-slab run (512^3 per GPU).
+
+`cpu_baseline` times the oracle (the C/OpenMP restatement of the reference's
+SPMDToOpenMP lowering) on a bounded sample of the same grid, on every host core
+(set explicitly: launchers export OMP_NUM_THREADS=1), before torch is loaded.
 `--impl reference` times that CPU path alone (the reference itself needs
 MLIR/LLVM 20 to build and cannot run here).
 """
@@ -27,6 +40,7 @@ from __future__ import annotations
 import argparse
 import importlib
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -45,6 +59,13 @@ GRID = 32768
 SWEEPS = 1000
 RES_EVERY = 10
 BYTES_PER_CELL_PASS = 8  # algorithmic: each pass reads u[i,j] once and writes v[i,j] once
+FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) per cell update of the four-sweep Jacobi-2D kernel,
+# measured by ncu on a 16384^2 grid (the benchmark grid is too large for a
+# multi-pass capture; traffic grows with cells x sweeps).
+TRAFFIC_BYTES_PER_UPDATE = {"jacobi2d_persistent_kernel<4>": 2.10}
+# Parity slab of the headline kernel: rows x columns of RandomState(4) input.
+PARITY_ROWS = 2048
 
 
 def sweep_passes(sweeps: int) -> tuple[int, int, int]:
@@ -57,7 +78,6 @@ def sweep_passes(sweeps: int) -> tuple[int, int, int]:
 
 def bytes_per_update(sweeps: int) -> float:
     return BYTES_PER_CELL_PASS * sum(sweep_passes(sweeps)) / sweeps
-FALLBACK_HBM_GBS = 6650.0
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -70,16 +90,25 @@ def measured_peaks() -> tuple[float, str]:
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic_per_update(kernel: str) -> float | None:
-    """DRAM bytes per cell update from the committed ncu summary, if one exists."""
-    for f in sorted((ROOT / "profiles").glob("*.md")):
-        for line in f.read_text().splitlines():
-            if line.startswith(f"traffic_bytes_per_update[{kernel}]:"):
-                try:
-                    return float(line.split(":", 1)[1].split()[0])
-                except ValueError:
-                    return None
-    return None
+def jacobi_init(shape, seed: int) -> np.ndarray:
+    """Interior uniform [0,1) from RandomState(seed), boundary cells 0."""
+    u = np.random.RandomState(seed).random_sample(shape).astype(np.float32)
+    if u.ndim == 2:
+        u[0, :] = 0; u[-1, :] = 0; u[:, 0] = 0; u[:, -1] = 0
+    else:
+        u[0] = 0; u[-1] = 0; u[:, 0] = 0; u[:, -1] = 0; u[:, :, 0] = 0; u[:, :, -1] = 0
+    return u
+
+
+def same_bits(a: np.ndarray, b: np.ndarray) -> bool:
+    a, b = np.ascontiguousarray(a), np.ascontiguousarray(b)
+    return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def max_rel(a: np.ndarray, b: np.ndarray) -> float:
+    if b.size == 0:
+        return 0.0
+    return float(np.max(np.abs(np.asarray(a) - b) / np.maximum(np.abs(b), 1e-300)))
 
 
 # ------------------------------------------------------------------ clocks sampler
@@ -156,18 +185,18 @@ def cpu_count() -> int:
         return os.cpu_count() or 1
 
 
-# ------------------------------------------------------------------ CPU (oracle) leg
+# ------------------------------------------------------------------ CPU (oracle) legs
 def cpu_jacobi_sample(target_s: float = 12.0, rows: int = 2048, cols: int = GRID) -> dict:
     """Oracle Jacobi-2D sweeps over a rows x cols slab of the workload grid (same
-    row width), repeated until ~target_s of CPU work; Gcell-updates/s."""
+    row width) on every host core, repeated until ~target_s of CPU work;
+    Gcell-updates/s."""
     from oracle import oracle
-    threads = oracle.num_threads()
-    rng = np.random.RandomState(4)
-    u = rng.random_sample((rows, cols)).astype(np.float32)
-    u[0] = 0; u[-1] = 0; u[:, 0] = 0; u[:, -1] = 0
+    threads = oracle.set_num_threads(cpu_count())
+    u = jacobi_init((rows, cols), 4)
     v = np.empty_like(u)
     rr = np.zeros(rows, np.float64)
-    oracle.jacobi2d_rows(u, v, 0, rows, 0, rows)  # warm-up (page faults, thread pool)
+    for _ in range(2):  # warm-up (page faults, thread pool)
+        oracle.jacobi2d_rows(u, v, 0, rows, 0, rows)
     sweeps, t0 = 0, time.perf_counter()
     while True:
         want = (sweeps + 1) % RES_EVERY == 0
@@ -181,7 +210,19 @@ def cpu_jacobi_sample(target_s: float = 12.0, rows: int = 2048, cols: int = GRID
     gcell = rows * cols * sweeps / el / 1e9
     return {"value": round(gcell, 4), "unit": "Gcell-updates/s", "cores": threads, "kind": "port",
             "sample": f"{rows}x{cols} rows of the workload grid, {sweeps} sweeps (residual every {RES_EVERY}), "
-                      f"{el:.1f} s, OpenMP threads={threads}, host cpus={cpu_count()}"}
+                      f"{el:.1f} s, OpenMP threads={threads} (set explicitly), host cpus={cpu_count()}"}
+
+
+def oracle_headline_parity() -> tuple[np.ndarray, np.ndarray, np.ndarray, float]:
+    """(input, oracle grid, oracle residuals, seconds) of the headline kernel's
+    parity case: a PARITY_ROWS x 32768 RandomState(4) slab, 1000 sweeps,
+    residual every 10."""
+    from oracle import oracle
+    oracle.set_num_threads(cpu_count())
+    u0 = jacobi_init((PARITY_ROWS, GRID), 4)
+    t0 = time.perf_counter()
+    want, wres = oracle.jacobi2d(u0, SWEEPS, RES_EVERY)
+    return u0, want, wres, time.perf_counter() - t0
 
 
 def run_reference_arm(args) -> None:
@@ -192,6 +233,7 @@ def run_reference_arm(args) -> None:
     for _ in range(args.warmup):
         cpu_jacobi_sample(target_s=2.0)
     vals, times = [], []
+    r = None
     for _ in range(args.steps):
         t0 = time.perf_counter()
         r = cpu_jacobi_sample(target_s=6.0)
@@ -214,12 +256,110 @@ def run_reference_arm(args) -> None:
 
 
 # ------------------------------------------------------------------ GPU legs
+def refabi_benchmarks(torch, hbm_peak: float) -> dict:
+    """The reference-named kernels of spmdb200_kernels.cubin, loaded with
+    cuModuleLoadData and launched with the reference harness's own launch
+    shapes, sizes and timing methods: ewise_kernel (tile 32, N = 1e7, wall
+    clock per launch over 20 asynchronous launches, harness/run_ewise.py:127-132),
+    promoted_stencil_kernel (32 x 8 tile, 297 threads, 4096^2, wall clock over 10
+    launches, harness/run_promoted_stencil.py:184-188) and
+    hierarchical_sum_kernel (tile 256, 2^24, CUDA events around each launch
+    after a memset of the output, mean of 10, harness/run_reduction.py:307-315)."""
+    cd = importlib.import_module("spmd-dialect_b200.cuda_driver")
+    lib_mod = importlib.import_module("spmd-dialect_b200._lib")
+    cd.init(torch.cuda.current_device())
+    mod = cd.load_cubin(str(lib_mod.CUBIN_PATH))
+    out = {}
+    rng = np.random.default_rng(0)
+
+    def wall(launch, reps):
+        for _ in range(3):
+            launch()
+        cd.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            launch()
+        cd.synchronize()
+        return (time.perf_counter() - t0) / reps * 1e3
+
+    n = 10_000_000
+    a = rng.random(n, dtype=np.float32)
+    b = rng.random(n, dtype=np.float32)
+    ad, bd, cdv = cd.alloc(a.nbytes), cd.alloc(b.nbytes), cd.alloc(a.nbytes)
+    cd.memcpy_h2d(ad, a)
+    cd.memcpy_h2d(bd, b)
+    fn = cd.get_function(mod, "ewise_kernel")
+    tile = 32
+    ms = wall(lambda: cd.launch(fn, (math.ceil(n / tile), 1, 1), (tile, 1, 1), tile, n, ad, ad, 0, n, 1,
+                                bd, bd, 0, n, 1, cdv, cdv, 0, n, 1), 20)
+    c = np.empty(n, np.float32)
+    cd.memcpy_d2h(c, cdv)
+    for p in (ad, bd, cdv):
+        p.free()
+    gbs = n * 12 / ms / 1e6
+    out["ewise_kernel_1e7"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3),
+                               "reference_ms": 0.206, "launch": "grid ceil(N/32), block 32",
+                               "timing": "wall clock per launch, 20 async launches (run_ewise.py)",
+                               "max_abs_err": float(np.max(np.abs(c - (a + b))))}
+    N = M = 4096
+    tr, tc = 32, 8
+    a = rng.random((N, M), dtype=np.float32)
+    ad, bd = cd.alloc(a.nbytes), cd.alloc(a.nbytes)
+    cd.memcpy_h2d(ad, a)
+    fn = cd.get_function(mod, "promoted_stencil_kernel")
+    grid = (math.ceil(N / tr), math.ceil(M / tc), 1)
+    ms = wall(lambda: cd.launch(fn, grid, ((tr + 1) * (tc + 1), 1, 1), tr, tc, ad, ad, 0, N, M, M, 1, 1,
+                                bd, bd, 0, N, M, M, 1), 10)
+    bh = np.zeros((N, M), np.float32)
+    cd.memcpy_d2h(bh, bd)
+    ad.free()
+    bd.free()
+    ref = a[:-1, :-1] + a[:-1, 1:] + a[1:, :-1]
+    gbs = 2 * N * M * 4 / ms / 1e6
+    out["promoted_stencil_kernel_4096^2"] = {
+        "ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3), "reference_ms": 0.285,
+        "launch": "grid (128, 512), block 297 (33 x 9)", "timing": "wall clock per launch, 10 async launches "
+        "(run_promoted_stencil.py)", "max_abs_err": float(np.max(np.abs(bh[:-1, :-1] - ref)))}
+    n = 1 << 24
+    a = rng.random(n, dtype=np.float32)
+    ad, od = cd.alloc(a.nbytes), cd.alloc(4)
+    cd.memcpy_h2d(ad, a)
+    fn = cd.get_function(mod, "hierarchical_sum_kernel")
+    e0, e1 = cd.event_create(), cd.event_create()
+    for _ in range(3):
+        cd.memset(od, 0, 4)
+        cd.launch(fn, (n // 256, 1, 1), (256, 1, 1), 256, n, ad, od)
+    cd.synchronize()
+    tot = 0.0
+    for _ in range(10):
+        cd.memset(od, 0, 4)
+        cd.event_record(e0)
+        cd.launch(fn, (n // 256, 1, 1), (256, 1, 1), 256, n, ad, od)
+        cd.event_record(e1)
+        tot += cd.event_elapsed_ms(e0, e1)
+    ms = tot / 10
+    r = np.zeros(1, np.float32)
+    cd.memcpy_d2h(r, od)
+    cd.event_destroy(e0)
+    cd.event_destroy(e1)
+    ad.free()
+    od.free()
+    f64 = float(np.sum(a.astype(np.float64)))
+    gbs = n * 4 / ms / 1e6
+    out["hierarchical_sum_kernel_2^24"] = {
+        "ms": round(ms, 5), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3), "reference_ms": 0.112,
+        "launch": "grid 65536, block 256", "timing": "CUDA events per launch, mean of 10 (run_reduction.py)",
+        "rel_err_vs_f64": abs(float(r[0]) - f64) / f64, "l2": "input may be L2-resident, as in the reference's run"}
+    return out
+
+
 def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
     """The other configurations at N=1 (rank 0): f32/i32 sum 2^24, f32 max and
     i32 xor reductions 2^24, axpy 2^28,
     the promoted 3-point stencil at 4096^2 and 8192^2, the general stencil
-    (5-point) at 8192^2, Jacobi-2D 4096^2 x 100, Jacobi-3D 512^3 x 50.  L2
-    flushed between reps."""
+    (5-point) at 8192^2, Jacobi-2D 4096^2 x 100, Jacobi-3D 512^3 x 50, and the
+    reference-named kernels at the reference's launch shapes.  L2 flushed
+    between reps unless stated."""
     out = {}
     dev = torch.device("cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MiB > 126 MB L2
@@ -243,10 +383,11 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
 
     # Reductions: 2^24 elements (64 MiB) is below the 126 MB L2, so consecutive
     # launches read different ones of 4 copies (256 MiB rotation): every read
-    # comes from HBM and no flush write-back is charged to the kernel.  A single
-    # launch between two events carries ~6 us of launch latency on this system
-    # (a one-element torch kernel measures the same), so the kernel rate is taken
-    # from 40 back-to-back launches; the single-launch time is reported beside it.
+    # comes from HBM and no flush write-back is charged to the kernel.  Two
+    # figures: one launch between two events (the stream kept busy so the
+    # host's launch latency stays outside), and the mean of 40 back-to-back
+    # launches (programmatic dependent launch overlaps each prologue with the
+    # previous kernel's tail).
     def batch(fn_i, n_launch=40):
         for i in range(3):
             fn_i(i)
@@ -278,8 +419,10 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
         ms1 = timed(lambda: fn_i(next(it)), reps=20, flush_l2=False)
         gbs = n * 4 / ms / 1e6
         out[key] = {"ms": round(ms, 5), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3),
-                    "ms_single_launch": round(ms1, 5), "l2": "4 rotating 64 MiB inputs",
-                    "timing": "mean of 40 back-to-back launches"}
+                    "ms_single_launch": round(ms1, 5),
+                    "frac_of_hbm_single_launch": round(n * 4 / ms1 / 1e6 / hbm_peak, 3),
+                    "l2": "4 rotating 64 MiB inputs", "timing": "mean of 40 back-to-back launches; single launch: "
+                    "median of 20, CUDA events around one launch"}
     # Other spmd.reduce kinds on the same inputs (f32 max: integer max over
     # order-preserving keys; i32 xor), same timing.
     ok_ = torch.zeros(1, device=dev)
@@ -339,14 +482,182 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
                                  "frac_of_hbm": round(gc * 8 / hbm_peak, 3)}  # 8 B per update: one sweep per pass
     del u, v, flush
     torch.cuda.empty_cache()
+    out.update(refabi_benchmarks(torch, hbm_peak))
     return out
 
 
+def headline_parity(kernels, torch, dev, u0, want, wres) -> dict:
+    """The timed kernel (same path, same row width, same 250 four-sweep passes)
+    on the PARITY_ROWS x 32768 slab against the oracle."""
+    u = torch.from_numpy(u0).to(dev)
+    v = torch.empty_like(u)
+    fin, res = kernels.jacobi2d(u, v, SWEEPS, RES_EVERY)
+    got = fin.cpu().numpy()
+    gres = res.cpu().numpy()
+    bit_exact = same_bits(got, want)
+    rel = max_rel(gres, wres)
+    return {"case": f"{PARITY_ROWS}x{GRID} RandomState(4), {SWEEPS} sweeps, residual every {RES_EVERY}",
+            "bit_exact": bit_exact, "residual_max_rel": rel, "ok": bool(bit_exact and rel <= 1e-12)}
+
+
+def slab_parity(slab, torch, dist, rank: int, world: int) -> dict:
+    """Row slabs and z-slabs across the ranks, gathered on rank 0 and compared
+    with the single-domain oracle: an uneven row split that runs four-, two-
+    and one-sweep passes, and an uneven plane split."""
+    out = {}
+    G, W, sweeps, res_every = 64 * world + 5, 4100, 13, 3
+    u0 = jacobi_init((G, W), 4)
+    job = slab.SlabJacobi2D(cols=W, G=G, res_every=res_every, init=u0)
+    job.run(sweeps)
+    res = job.residuals()
+    grid = job.gather()
+    job.close()
+    ok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    if rank == 0:
+        from oracle import oracle
+        want, wres = oracle.jacobi2d(u0, sweeps, res_every)
+        be, rel = same_bits(grid, want), max_rel(res, wres)
+        out["slab2d"] = {"case": f"{G}x{W} over {world} ranks, {sweeps} sweeps, residual every {res_every}",
+                         "bit_exact": be, "residual_max_rel": rel, "ok": bool(be and rel <= 1e-12)}
+    D, H, W3, sweeps3, res3 = 8 * world + 3, 36, 130, 7, 2
+    u0 = jacobi_init((D, H, W3), 3)
+    job = slab.SlabJacobi3D(H=H, W=W3, D=D, res_every=res3, init=u0)
+    job.run(sweeps3)
+    res = job.residuals()
+    grid = job.gather()
+    job.close()
+    if rank == 0:
+        from oracle import oracle
+        want, wres = oracle.jacobi3d(u0, sweeps3, res3)
+        be, rel = same_bits(grid, want), max_rel(res, wres)
+        out["slab3d"] = {"case": f"{D}x{H}x{W3} over {world} ranks, {sweeps3} sweeps, residual every {res3}",
+                         "bit_exact": be, "residual_max_rel": rel, "ok": bool(be and rel <= 1e-12)}
+        ok.fill_(int(out["slab2d"]["ok"] and out["slab3d"]["ok"]))
+    dist.broadcast(ok, 0)
+    return out
+
+
+def timed_steps(step, steps: int, warmup: int, world: int, dist, torch, finish=None,
+                region=None) -> tuple[float, float]:
+    """(ms per step over the whole timed region, mean per-step event time), max
+    over ranks; W untimed steps first, barrier + synchronize on both sides.
+    `region` (a context manager, e.g. the clock sampler) brackets the timed
+    steps only."""
+    import contextlib
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        step()
+    if finish:
+        finish()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    with region if region is not None else contextlib.nullcontext():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        evs[0].record(stream)
+        for k in range(steps):
+            step()
+            evs[k + 1].record(stream)
+        torch.cuda.synchronize()
+    if finish:
+        finish()
+    per_step = [evs[k].elapsed_time(evs[k + 1]) for k in range(steps)]
+    t = torch.tensor([evs[0].elapsed_time(evs[-1]) / steps, statistics.mean(per_step)], dtype=torch.float64,
+                     device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0]), float(t[1])
+
+
+def multi_gpu_records(slab, shard, kernels, torch, dist, rank: int, world: int, args, hbm_peak: float) -> dict:
+    """N > 1: the configured 32768^2 global grid split over the ranks (strong
+    scaling), the sharded sums at 2^24 elements per GPU, and Jacobi-3D z-slabs
+    at 512^3 per GPU."""
+    out = {}
+    steps, warm = max(3, args.steps), 3
+    # ---- strong: 32768 x 32768 global, 32768/N rows per rank
+    job = slab.SlabJacobi2D(cols=GRID, G=GRID, seed=4, res_every=RES_EVERY)
+    ms, _ = timed_steps(lambda: job.run(SWEEPS, check=False), steps, warm, world, dist, torch, job.check)
+    job.close()
+    out["strong"] = {"workload": "jacobi2d 32768x32768 global (the configured grid) in 32768/N-row slabs, "
+                                 "1000 sweeps, residual every 10",
+                     "value": round(GRID * GRID * SWEEPS / (ms * 1e-3) / 1e9, 3), "unit": "Gcell-updates/s",
+                     "ms_per_step": round(ms, 3), "rows_per_rank": GRID // world, "steps": steps}
+    # ---- sharded sums: 2^24 elements per rank (weak), one all-gather / all-reduce
+    n = 1 << 24
+    rs = np.random.RandomState(100 + rank)
+    xf = torch.from_numpy(rs.random_sample(n).astype(np.float32)).cuda()
+    xi = torch.from_numpy(rs.randint(0, 100, n).astype(np.int32)).cuda()
+    local64 = torch.tensor([float(np.sum(xf.cpu().numpy().astype(np.float64))),
+                            float(xi.cpu().numpy().astype(np.int64).sum())], dtype=torch.float64, device="cuda")
+    dist.all_reduce(local64)
+    ws = kernels.sum_workspace(n)
+    got_f = shard.sum_f32(xf, ws=ws)
+    got_i = shard.sum_i32(xi)
+    exact_f, exact_i = float(local64[0]), int(local64[1])
+    ok_f = abs(float(got_f) - exact_f) <= 1e-6 * exact_f
+    ok_i = got_i == shard.combine_i32([exact_i])  # the int32 wrap of the exact total
+    stream = torch.cuda.current_stream()
+    oi = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def med_ms(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ts = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        t = torch.tensor([statistics.median(ts)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    recs = {}
+    for key, fn, local_fn in (("sum_f32", lambda: shard.sum_f32(xf, ws=ws), lambda: shard.partial_sum_f32(xf, ws)),
+                              ("sum_i32", lambda: shard.sum_i32(xi), lambda: kernels.sum_i32(xi, oi))):
+        ms = med_ms(fn)  # local kernel + NCCL exchange + the host read of the combined result
+        ms_k = med_ms(local_fn)  # this rank's kernel alone
+        recs[key] = {"ms": round(ms, 5), "GB/s_total": round(world * n * 4 / ms / 1e6, 1),
+                     "ms_local_kernel": round(ms_k, 5),
+                     "GB/s_per_gpu_kernel": round(n * 4 / ms_k / 1e6, 1),
+                     "frac_of_hbm_per_gpu_kernel": round(n * 4 / ms_k / 1e6 / hbm_peak, 3)}
+    out["sharded_sums"] = {"elements_per_gpu": n, **recs,
+                           "timing": "CUDA events around one sharded sum (local kernel, NCCL exchange, host "
+                                     "combine) and around the local kernel alone, median of 20, max over ranks",
+                           "f32_rel_err_vs_f64": abs(float(got_f) - exact_f) / exact_f, "f32_ok": bool(ok_f),
+                           "i32_exact": bool(ok_i)}
+    # ---- Jacobi-3D z-slabs, 512^3 per rank (weak)
+    job3 = slab.SlabJacobi3D(H=512, W=512, planes_per_rank=512, seed=3, res_every=10)
+    ms3, _ = timed_steps(lambda: job3.run(50, check=False), steps, warm, world, dist, torch, job3.check)
+    job3.close()
+    out["jacobi3d_slab"] = {"workload": "jacobi3d 7-point, 512^3 per GPU in z-slabs (global 512N x 512 x 512), "
+                                        "50 sweeps, residual every 10",
+                            "value": round(world * 512 ** 3 * 50 / (ms3 * 1e-3) / 1e9, 3),
+                            "unit": "Gcell-updates/s", "ms_per_step": round(ms3, 3), "steps": steps}
+    return out, bool(ok_f and ok_i)
+
+
 def run_spmd_arm(args) -> None:
+    rank, world, local = dist_env()
+    # ---- CPU work first, before torch is loaded: torch brings its own OpenMP
+    # pool, whose spinning threads would compete with the oracle's.
+    cpu = None
+    headline_case = None
+    if rank == 0 and world == 1:
+        cpu = cpu_jacobi_sample()
+        headline_case = oracle_headline_parity()
+
     import torch
     import torch.distributed as dist
 
-    rank, world, local = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     torch.cuda.set_device(local)
@@ -356,7 +667,23 @@ def run_spmd_arm(args) -> None:
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     kernels = importlib.import_module("spmd-dialect_b200.kernels")
     slab = importlib.import_module("spmd-dialect_b200.slab") if world > 1 else None
+    shard = importlib.import_module("spmd-dialect_b200.shard") if world > 1 else None
     hbm_peak, peak_kind = measured_peaks()
+
+    # ---- parity of what is about to be timed -----------------------------------
+    parity = {}
+    if world == 1:
+        u0, want, wres, oracle_s = headline_case
+        parity["jacobi2d"] = {**headline_parity(kernels, torch, dev, u0, want, wres),
+                              "oracle_s": round(oracle_s, 1)}
+        del u0, want, wres, headline_case
+        parity_ok = parity["jacobi2d"]["ok"]
+    else:
+        parity = slab_parity(slab, torch, dist, rank, world)
+        flag = torch.tensor([1 if (rank != 0 or all(p["ok"] for p in parity.values())) else 0],
+                            dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        parity_ok = bool(flag.item())
 
     # ---- device-resident workload ------------------------------------------------
     rows = GRID
@@ -382,30 +709,8 @@ def run_spmd_arm(args) -> None:
         def finish():
             job.check()
 
-    stream = torch.cuda.current_stream()
-    for _ in range(args.warmup):
-        step()
-    finish()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    with ClockSampler(local) as clk:
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        evs[0].record(stream)
-        for k in range(args.steps):
-            step()
-            evs[k + 1].record(stream)
-        torch.cuda.synchronize()
-    finish()
-    per_step = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
-    ms_local = evs[0].elapsed_time(evs[-1]) / args.steps
-    t = torch.tensor([ms_local, statistics.mean(per_step)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_step, ms_kernel = float(t[0]), float(t[1])
+    clk = ClockSampler(local)
+    ms_step, ms_kernel = timed_steps(step, args.steps, args.warmup, world, dist, torch, finish, region=clk)
     updates = rows * GRID * SWEEPS * world
     value = updates / (ms_step * 1e-3) / 1e9
 
@@ -443,24 +748,20 @@ def run_spmd_arm(args) -> None:
         del hbufs, grids
         getattr(importlib.import_module("spmd-dialect_b200._lib"), "lib")().spmdb200_release_cache()
     else:
-        e2e = slab.e2e_measure(job, SWEEPS) if hasattr(slab, "e2e_measure") else None
+        e2e = slab.e2e_measure(job, SWEEPS)
 
     # ---- roofline of the dominant kernel (the persistent sweep kernel) --------------
     plan = sweep_passes(SWEEPS)
     alg_bytes = rows * GRID * SWEEPS * bytes_per_update(SWEEPS)
     achieved = alg_bytes / (ms_kernel * 1e-3) / 1e9
     kname = "jacobi2d_persistent_kernel<%d>" % next(f for f, n in zip((4, 2, 1), plan) if n)
-    tpu = profile_traffic_per_update(kname)
+    tpu = TRAFFIC_BYTES_PER_UPDATE.get(kname)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4),
                 "traffic": (round(tpu * rows * GRID * SWEEPS) if tpu else None),
-                "traffic_source": "profiles/jacobi2d_persistent_f4_16384x16384.md (bytes per update x updates)",
+                "traffic_basis": "ncu DRAM read+write bytes per cell update on a 16384^2 grid x updates per launch",
                 "kernel": kname, "peak_kind": f"{peak_kind} hbm_gbs (copy bandwidth)",
                 "passes_per_step": {"four_sweep": plan[0], "two_sweep": plan[1], "single_sweep": plan[2]},
-                "limiter": ("SM issue/latency, not HBM: four sweeps per pass move 2.1 B/update (ncu), DRAM "
-                            "under half busy, issue ~60 percent active, leading stall shared-memory latency "
-                            "(profiles/jacobi2d_persistent_f4_16384x16384.md); the one-sweep-per-pass ceiling "
-                            f"at 8 B/update would be {hbm_peak / 8.0:.0f} Gcell/s"),
                 "algorithmic_bytes_per_update": bytes_per_update(SWEEPS),
                 "algorithmic_bytes_per_launch": round(alg_bytes),
                 # The same time against one-sweep-per-pass traffic (read u, write v: 8 B per update),
@@ -469,11 +770,15 @@ def run_spmd_arm(args) -> None:
                 "frac_vs_single_sweep_ceiling": round(rows * GRID * SWEEPS * 8 / (ms_kernel * 1e-3) / 1e9
                                                       / hbm_peak, 4)}
 
-    cpu = None
     secondary = None
-    if rank == 0 and world == 1:
+    multi = None
+    if world == 1:
         secondary = secondary_benchmarks(kernels, torch, hbm_peak)
-        cpu = cpu_jacobi_sample()
+    else:
+        job.close()
+        multi, multi_ok = multi_gpu_records(slab, shard, kernels, torch, dist, rank, world, args, hbm_peak)
+        parity["sharded_sums"] = {"ok": multi_ok}
+        parity_ok = parity_ok and multi_ok
     clocks = clk.summary()
     if world > 1:
         dist.barrier()
@@ -482,22 +787,27 @@ def run_spmd_arm(args) -> None:
             "metric": METRIC, "value": round(value, 3), "unit": "Gcell-updates/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic: torch Philox uniform [0,1) seeded 4 on device, zero boundary",
+            "data": "synthetic: torch Philox uniform [0,1) seeded 4 on device, zero boundary; parity cases "
+                    "numpy RandomState",
             "config": {"workload": "jacobi2d 5-point, 32768x32768 f32 row slab per GPU, 1000 sweeps, "
                                    "residual every 10 (multi-GPU Jacobi-2D config, weak-scaled)",
                        "grid_per_gpu": [rows, GRID], "global_grid": [rows * world, GRID], "sweeps": SWEEPS,
                        "res_every": RES_EVERY, "parallelism": f"row-slab x{world}",
                        "l2": "inputs (4 GiB per grid) larger than L2; no flush needed"},
+            "parity": {**parity, "all_ok": parity_ok},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": args.steps * sum(1 for n in plan if n),
             "clocks": clocks, "secondary": secondary,
         }
+        if multi:
+            line.update(multi)
         print(json.dumps(line), flush=True)
     if world > 1:
-        if slab is not None:
-            job.close()
         dist.barrier()
         dist.destroy_process_group()
+    if not parity_ok:
+        print("PARITY FAILURE: a checked result differs from the oracle", file=sys.stderr, flush=True)
+        sys.exit(3)
 
 
 def main() -> None:

@@ -205,10 +205,14 @@ int spmdb200_sum_f32_partial(float *A_base, float *A_aligned, int64_t A_offset, 
  * __device__ array of 256 + 2048*8 = 16,640 bytes that every GPU loading the
  * library holds until exit; a launch needing more than 2048 block partials is
  * rejected with SPMDB200_ERR_WORKSPACE (the reduction never launches more, so
- * every N >= 0 fits).  The first call on each device looks up the array's
- * device address (cudaGetSymbolAddress) and should come before any stream
- * capture.  Allocates nothing.  All calls share the array and each clears its
- * ticket first: calls that overlap on the GPU race and must be serialised. */
+ * every N >= 0 fits).  The array has one instance per CUDA context: the
+ * first call in each context (the primary context, or one the caller made
+ * current) looks up its device address (cudaGetSymbolAddress) and should come
+ * before any stream capture; after destroying a context that used this entry,
+ * do not call it again in the process (a new context may reuse the handle).
+ * Allocates nothing.  All calls share the array; each clears the header and
+ * the partial words it will use before its launch.  Calls that overlap on the
+ * GPU race on the array and must be serialised by the caller. */
 int spmdb200_sum_f32_noalloc(float *A_base, float *A_aligned, int64_t A_offset, int64_t A_size, int64_t A_stride,
                              float *out_base, float *out_aligned, int64_t out_offset,
                              int64_t N, void *stream);

@@ -38,6 +38,7 @@ _SIGS = {
     "oracle_jacobi3d_slab_planes": (None, [c_p, c_p, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_p]),
     "oracle_jacobi3d": (None, D3 + D3 + [c_i, c_i, c_p]),
     "oracle_num_threads": (ctypes.c_int, []),
+    "oracle_set_num_threads": (ctypes.c_int, [ctypes.c_int]),
     "oracle_stencil_nd": (None, [ctypes.c_int, c_p, c_p, c_p, c_p, c_p, c_p, ctypes.c_int, c_p, c_p, c_f, c_p]),
 }
 
@@ -81,6 +82,12 @@ def _d3(a: np.ndarray) -> tuple:
 
 def num_threads() -> int:
     return int(lib().oracle_num_threads())
+
+
+def set_num_threads(n: int) -> int:
+    """OpenMP threads of later oracle calls on this thread (independent of
+    OMP_NUM_THREADS); returns the count now in effect."""
+    return int(lib().oracle_set_num_threads(int(n)))
 
 
 def ewise(A: np.ndarray, B: np.ndarray) -> np.ndarray:

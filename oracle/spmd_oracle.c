@@ -53,6 +53,19 @@ EXPORT int oracle_num_threads(void) {
 #endif
 }
 
+/* Sets the OpenMP team size of later parallel regions on the calling thread
+ * (launchers such as torchrun export OMP_NUM_THREADS=1; the timed CPU
+ * baseline sets the host's core count explicitly).  Returns the new count. */
+EXPORT int oracle_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n >= 1) omp_set_num_threads(n);
+  return omp_get_max_threads();
+#else
+  (void)n;
+  return 1;
+#endif
+}
+
 /* ---------------------------------------------------------------------------
  * ewise: C[i] = A[i] + B[i]   (test/SPMD/lower-to-gpu-nvptx.mlir:54-71)
  * Group forall over tiles of 32 (spmd.tile_sizes = [32]); OpenMP static over

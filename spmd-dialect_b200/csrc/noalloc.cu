@@ -16,15 +16,23 @@
 // and rejects a launch that would need more.
 //
 // In host code the array's name is only a host-side stand-in, not a device
-// address, so the entry looks the address up with cudaGetSymbolAddress once
-// per device (with that device current) and passes it to the kernel.  That
-// look-up happens on the first call on each device, so the first call on a
-// device should come before any stream capture.
+// address, so the entry looks the address up with cudaGetSymbolAddress with
+// the device current and passes it to the kernel.  A __device__ array has one
+// instance per CUDA context, so the address is cached per context (the
+// primary context, or one a caller created with cuCtxCreate and made
+// current): the first call in each context does the look-up, so that first
+// call should come before any stream capture.  A context that is destroyed
+// and replaced by a new one with the same handle value would reuse the old
+// address, so a caller that destroys contexts must not call this entry again
+// in the process afterwards.
 //
-// All calls share the one array: each call clears the ticket before its
-// launch, and calls that overlap on the GPU (different streams, or different
-// host threads on one device) race on it and must be serialised by the
-// caller.  No cudaMalloc, cudaFree or allocating library routine is called.
+// All calls share the one array.  Each call clears the header and the
+// partial words its launch will use before the launch (a partial that a
+// block stored after a bounded wait gave up would otherwise be read by the
+// next call as already written), and calls that overlap on the GPU
+// (different streams, or different host threads on one device) race on it
+// and must be serialised by the caller.  No cudaMalloc, cudaFree or
+// allocating library routine is called.
 #include <mutex>
 
 #include "../../include/spmd_b200.h"
@@ -39,25 +47,65 @@ constexpr size_t kNoAllocBytes = kNoAllocHeader + sizeof(double) * kNoAllocMaxBl
 
 static __device__ __align__(256) unsigned char g_sum_scratch[kNoAllocBytes];
 
-constexpr int kMaxDevices = 64;
+// Address cache: (CUcontext, address of g_sum_scratch in it).  The runtime
+// resolves the context itself; the driver's cuCtxGetCurrent names it.
+constexpr int kMaxContexts = 64;
 std::mutex g_mu;
-void *g_scratch_addr[kMaxDevices] = {};
+struct CtxAddr {
+  void *ctx;
+  void *addr;
+};
+CtxAddr g_scratch_addr[kMaxContexts] = {};
+int g_scratch_n = 0;
 
-// Device address of g_sum_scratch on the current device (looked up once).
+using CtxGetCurrentFn = int (*)(void **);
+
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    tried = true;
+  }
+  return fn;
+}
+
+// Device address of g_sum_scratch in the current context (looked up once per
+// context).
 cudaError_t scratch_address(void **out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  CtxGetCurrentFn get = ctx_get_current();
+  if (!get) return cudaErrorDeviceUninitialized;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_scratch_addr[dev]) {
-    void *p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_sum_scratch);
-    if (e != cudaSuccess) return e;
-    if (!p) return cudaErrorInvalidSymbol;
-    g_scratch_addr[dev] = p;
+  void *ctx = nullptr;
+  if (get(&ctx) != 0) return cudaErrorDeviceUninitialized;
+  for (int i = 0; ctx && i < g_scratch_n; ++i)
+    if (g_scratch_addr[i].ctx == ctx) {
+      *out = g_scratch_addr[i].addr;
+      return cudaSuccess;
+    }
+  // First call in this context (or on a thread the runtime has not bound to
+  // a context yet: the look-up binds the device's primary context).
+  void *p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_sum_scratch);
+  if (e != cudaSuccess) return e;
+  if (!p) return cudaErrorInvalidSymbol;
+  if (!ctx && (get(&ctx) != 0 || !ctx)) return cudaErrorDeviceUninitialized;
+  bool known = false;
+  for (int i = 0; i < g_scratch_n; ++i) known |= g_scratch_addr[i].ctx == ctx;
+  if (!known) {
+    if (g_scratch_n < kMaxContexts)
+      g_scratch_addr[g_scratch_n++] = CtxAddr{ctx, p};
+    else
+      g_scratch_addr[kMaxContexts - 1] = CtxAddr{ctx, p};  // full: the newest context replaces the last entry
   }
-  *out = g_scratch_addr[dev];
+  *out = p;
   return cudaSuccess;
 }
 
@@ -85,7 +133,8 @@ extern "C" int spmdb200_sum_f32_noalloc(float *A_base, float *A, int64_t A_off, 
     return record_api_status(SPMDB200_ERR_CUDA, "cudaGetSymbolAddress(g_sum_scratch): %s", cudaGetErrorString(e));
   }
   cudaStream_t s = (cudaStream_t)stream;
-  e = cudaMemsetAsync(scratch, 0, sizeof(unsigned), s);  // the ticket starts at zero
+  // The header and every partial word this launch can touch start at zero.
+  e = cudaMemsetAsync(scratch, 0, kNoAllocHeader + sizeof(double) * (size_t)blocks, s);
   if (e == cudaSuccess) e = launch_sum_f32(View1{A ? A + A_off : nullptr, N, A_st}, o + o_off, N, scratch, s);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -93,3 +142,4 @@ extern "C" int spmdb200_sum_f32_noalloc(float *A_base, float *A, int64_t A_off, 
   }
   return record_api_status(SPMDB200_OK, "");
 }
+

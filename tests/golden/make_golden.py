@@ -1,7 +1,8 @@
 """Generates the golden fixtures in tests/golden/ (run where the reference tree
 is available; the fixtures are committed, the tests never read the reference).
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
+    (or SPMD_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py)
 
 What it pins, and against what:
   * The reference's own numpy references, imported from its harness modules
@@ -29,6 +30,7 @@ import hashlib
 import importlib.util
 import io
 import json
+import os
 import sys
 import types
 from pathlib import Path
@@ -112,8 +114,11 @@ def jacobi_init(shape, seed: int) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SPMD_REFERENCE_DIR"),
+                    help="reference checkout (default: $SPMD_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("give --reference or set SPMD_REFERENCE_DIR")
     harness = Path(args.reference) / "harness"
     if not harness.exists():
         raise SystemExit(f"reference harness not found at {harness}")

@@ -1,9 +1,11 @@
 """The textual-MLIR shim on the host: parsing the dialect's generic form,
 recognising the hot-path patterns, reporting what it cannot map, and the
-build stand-ins of the differential script.  When the reference checkout is
-present, its own kernel files are mapped too."""
+build stand-ins of the differential script.  When SPMD_REFERENCE_DIR names a
+checkout of the reference, its own kernel files (test/SPMD/*.mlir) are mapped
+too."""
 from __future__ import annotations
 
+import os
 import subprocess
 import sys
 from pathlib import Path
@@ -13,7 +15,8 @@ import pytest
 from conftest import ROOT, spmd_mod
 
 MLIR = ROOT / "tests" / "mlir" / "kernels.mlir"
-REFERENCE = Path("/root/reference/test/SPMD")
+_REF_DIR = os.environ.get("SPMD_REFERENCE_DIR", "")
+REFERENCE = Path(_REF_DIR) / "test" / "SPMD" if _REF_DIR else None
 
 
 def _by_name():
@@ -73,7 +76,8 @@ def test_build_stand_ins(tmp_path):
         shim.build_so(text, str(tmp_path / "all.so"))  # axpy etc. have no reference host entry
 
 
-@pytest.mark.skipif(not REFERENCE.exists(), reason="reference checkout not present")
+@pytest.mark.skipif(REFERENCE is None or not REFERENCE.exists(),
+                    reason="SPMD_REFERENCE_DIR does not name a reference checkout")
 def test_reference_kernel_files_map():
     shim = spmd_mod("mlir_shim")
     want = {
