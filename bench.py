@@ -8,7 +8,7 @@ f32 row slab per GPU (weak scaling: the global grid is (32768*N) x 32768),
 interior uniform [0,1) from seed 4, zero boundary rows/columns, 1000 ping-pong
 sweeps, a global L2 residual every 10 sweeps.  Inputs are device-resident when
 the timed region starts (4 GiB per grid, far above the 126 MB L2, so no L2
-flush is needed between steps).  At N > 1 the slabs exchange four halo rows per
+flush is needed between steps).  At N > 1 the slabs exchange eight halo rows per
 neighbour per pass over NVLink inside the persistent kernel.
 
 `value` is device time (CUDA events, max over ranks); `e2e` runs the same job
@@ -16,8 +16,8 @@ through the host-buffer C entries (pinned host grids in, result grids out,
 every copy inside the timed region).  `roofline` uses the algorithmic bytes of
 the sweep kernel against the measured HBM copy bandwidth: each pass over the
 grid reads every cell once and writes it once (8 B per cell per pass), and a
-pass advances four sweeps (two or one for the 0-7 sweeps left over), so 1000
-sweeps cost 2 B per cell update.
+pass advances eight sweeps (1000 sweeps with a residual every 10: 124 passes
+of eight and 2 of four), so 1000 sweeps cost 1.008 B per cell update.
 
 Before anything is timed the run checks its own results (`parity`, and a
 non-zero exit on any mismatch): at N = 1 the timed kernel on a 2048 x 32768
@@ -60,24 +60,31 @@ SWEEPS = 1000
 RES_EVERY = 10
 BYTES_PER_CELL_PASS = 8  # algorithmic: each pass reads u[i,j] once and writes v[i,j] once
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) per cell update of the four-sweep Jacobi-2D kernel,
-# measured by ncu on a 16384^2 grid (the benchmark grid is too large for a
-# multi-pass capture; traffic grows with cells x sweeps).
-TRAFFIC_BYTES_PER_UPDATE = {"jacobi2d_persistent_kernel<4>": 2.10}
+# DRAM bytes (read + write) per cell update of the dominant Jacobi-2D kernel,
+# measured by ncu on a 16384^2 grid with 8-sweep passes (the benchmark grid is
+# too large for a multi-pass capture; traffic grows with cells x sweeps).
+TRAFFIC_BYTES_PER_UPDATE = {}
 # Parity slab of the headline kernel: rows x columns of RandomState(4) input.
 PARITY_ROWS = 2048
 
 
-def sweep_passes(sweeps: int) -> tuple[int, int, int]:
-    """(four-sweep, two-sweep, single-sweep) passes the Jacobi-2D kernel runs:
-    even counts of the first two, then the 0-3 sweeps left over."""
-    four = (sweeps // 8) * 2
-    two = ((sweeps - 4 * four) // 4) * 2
-    return four, two, sweeps - 4 * four - 2 * two
+def sweep_passes(sweeps: int, res_every: int) -> dict[int, int]:
+    """{sweeps per pass: passes} as the Jacobi-2D kernel schedules them: even
+    numbers of 8-, 4- and 2-sweep passes (none longer than the residual
+    interval), then the single sweep left over."""
+    fmax = 8
+    while res_every > 0 and fmax > res_every:
+        fmax //= 2
+    plan, left = {}, sweeps
+    for f in (8, 4, 2, 1):
+        n = 0 if f > fmax else left if f == 1 else (left // (2 * f)) * 2
+        plan[f] = n
+        left -= n * f
+    return plan
 
 
-def bytes_per_update(sweeps: int) -> float:
-    return BYTES_PER_CELL_PASS * sum(sweep_passes(sweeps)) / sweeps
+def bytes_per_update(sweeps: int, res_every: int) -> float:
+    return BYTES_PER_CELL_PASS * sum(sweep_passes(sweeps, res_every).values()) / sweeps
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -469,7 +476,7 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
     kernels.workspace_status(jws)
     gc = 4096 * 4096 * 100 / ms / 1e6
     out["jacobi2d_4096^2_x100"] = {"ms": round(ms, 4), "Gcell/s": round(gc, 1),
-                                   "frac_of_hbm": round(gc * bytes_per_update(100) / hbm_peak, 3),
+                                   "frac_of_hbm": round(gc * bytes_per_update(100, 10) / hbm_peak, 3),
                                    "note": "128 MiB working set is L2-sized: fractions above 1 mean L2 reuse"}
     del u, v
     u = torch.rand((512, 512, 512), device=dev, generator=g)
@@ -487,7 +494,7 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
 
 
 def headline_parity(kernels, torch, dev, u0, want, wres) -> dict:
-    """The timed kernel (same path, same row width, same 250 four-sweep passes)
+    """The timed kernel (same path, same row width, same 126 passes of eight and four sweeps)
     on the PARITY_ROWS x 32768 slab against the oracle."""
     u = torch.from_numpy(u0).to(dev)
     v = torch.empty_like(u)
@@ -502,23 +509,32 @@ def headline_parity(kernels, torch, dev, u0, want, wres) -> dict:
 
 def slab_parity(slab, torch, dist, rank: int, world: int) -> dict:
     """Row slabs and z-slabs across the ranks, gathered on rank 0 and compared
-    with the single-domain oracle: an uneven row split that runs four-, two-
-    and one-sweep passes, and an uneven plane split."""
+    with the single-domain oracle: an uneven row split that runs two- and
+    one-sweep passes (residual every 3) and one that runs eight- and four-sweep
+    passes (residual every 8), and an uneven plane split."""
     out = {}
-    G, W, sweeps, res_every = 64 * world + 5, 4100, 13, 3
-    u0 = jacobi_init((G, W), 4)
-    job = slab.SlabJacobi2D(cols=W, G=G, res_every=res_every, init=u0)
-    job.run(sweeps)
-    res = job.residuals()
-    grid = job.gather()
-    job.close()
     ok = torch.zeros(1, dtype=torch.int32, device="cuda")
-    if rank == 0:
-        from oracle import oracle
-        want, wres = oracle.jacobi2d(u0, sweeps, res_every)
-        be, rel = same_bits(grid, want), max_rel(res, wres)
-        out["slab2d"] = {"case": f"{G}x{W} over {world} ranks, {sweeps} sweeps, residual every {res_every}",
-                         "bit_exact": be, "residual_max_rel": rel, "ok": bool(be and rel <= 1e-12)}
+    cases_ok = True
+    for name, (G, W, runs, res_every) in (("slab2d", (64 * world + 5, 4100, (13,), 3)),
+                                          ("slab2d_deep", (200 * world + 3, 3001, (28, 9), 8))):
+        u0 = jacobi_init((G, W), 4)
+        job = slab.SlabJacobi2D(cols=W, G=G, res_every=res_every, init=u0)
+        for n in runs:  # back to back, no host synchronisation between the runs
+            job.run(n, check=False)
+        job.check()
+        res = job.residuals()
+        grid = job.gather()
+        job.close()
+        if rank == 0:
+            from oracle import oracle
+            want, _ = oracle.jacobi2d(u0, sum(runs), 0)
+            _, wres = oracle.jacobi2d(jacobi_init((G, W), 4) if len(runs) == 1 else
+                                      oracle.jacobi2d(u0, sum(runs[:-1]), 0)[0], runs[-1], res_every)
+            be, rel = same_bits(grid, want), max_rel(res, wres)
+            out[name] = {"case": f"{G}x{W} over {world} ranks, runs of {list(runs)} sweeps, residual every "
+                                 f"{res_every}", "bit_exact": be, "residual_max_rel": rel,
+                         "ok": bool(be and rel <= 1e-12)}
+            cases_ok = cases_ok and out[name]["ok"]
     D, H, W3, sweeps3, res3 = 8 * world + 3, 36, 130, 7, 2
     u0 = jacobi_init((D, H, W3), 3)
     job = slab.SlabJacobi3D(H=H, W=W3, D=D, res_every=res3, init=u0)
@@ -532,7 +548,7 @@ def slab_parity(slab, torch, dist, rank: int, world: int) -> dict:
         be, rel = same_bits(grid, want), max_rel(res, wres)
         out["slab3d"] = {"case": f"{D}x{H}x{W3} over {world} ranks, {sweeps3} sweeps, residual every {res3}",
                          "bit_exact": be, "residual_max_rel": rel, "ok": bool(be and rel <= 1e-12)}
-        ok.fill_(int(out["slab2d"]["ok"] and out["slab3d"]["ok"]))
+        ok.fill_(int(cases_ok and out["slab3d"]["ok"]))
     dist.broadcast(ok, 0)
     return out
 
@@ -751,18 +767,18 @@ def run_spmd_arm(args) -> None:
         e2e = slab.e2e_measure(job, SWEEPS)
 
     # ---- roofline of the dominant kernel (the persistent sweep kernel) --------------
-    plan = sweep_passes(SWEEPS)
-    alg_bytes = rows * GRID * SWEEPS * bytes_per_update(SWEEPS)
+    plan = sweep_passes(SWEEPS, RES_EVERY)
+    alg_bytes = rows * GRID * SWEEPS * bytes_per_update(SWEEPS, RES_EVERY)
     achieved = alg_bytes / (ms_kernel * 1e-3) / 1e9
-    kname = "jacobi2d_persistent_kernel<%d>" % next(f for f, n in zip((4, 2, 1), plan) if n)
+    kname = "jacobi2d_wave_kernel<%d>" % max(plan, key=lambda f: plan[f] * f)
     tpu = TRAFFIC_BYTES_PER_UPDATE.get(kname)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4),
                 "traffic": (round(tpu * rows * GRID * SWEEPS) if tpu else None),
                 "traffic_basis": "ncu DRAM read+write bytes per cell update on a 16384^2 grid x updates per launch",
                 "kernel": kname, "peak_kind": f"{peak_kind} hbm_gbs (copy bandwidth)",
-                "passes_per_step": {"four_sweep": plan[0], "two_sweep": plan[1], "single_sweep": plan[2]},
-                "algorithmic_bytes_per_update": bytes_per_update(SWEEPS),
+                "passes_per_step": {f"{f}_sweep": n for f, n in plan.items() if n},
+                "algorithmic_bytes_per_update": round(bytes_per_update(SWEEPS, RES_EVERY), 4),
                 "algorithmic_bytes_per_launch": round(alg_bytes),
                 # The same time against one-sweep-per-pass traffic (read u, write v: 8 B per update),
                 # i.e. how far past the ceiling of any kernel without temporal blocking it runs.
@@ -796,7 +812,7 @@ def run_spmd_arm(args) -> None:
                        "l2": "inputs (4 GiB per grid) larger than L2; no flush needed"},
             "parity": {**parity, "all_ok": parity_ok},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": args.steps * sum(1 for n in plan if n),
+            "gpu_launches": args.steps * sum(1 for n in plan.values() if n),
             "clocks": clocks, "secondary": secondary,
         }
         if multi:

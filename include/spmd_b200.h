@@ -313,24 +313,30 @@ int spmdb200_jacobi2d_host_batch(int64_t count, float *const *U_aligned, int64_t
 
 /* ---- Jacobi-2D over row slabs on several GPUs (one process per GPU) ------ */
 /* No reference counterpart: the reference runs on one GPU.  The global grid
- * has G rows; this rank owns global rows [g_first, g_first + R), R >= 4.  U
- * and V are (R + 8) x W local arrays (descriptor sizes (R+8, W), stride1 == 1,
- * 16-byte aligned rows): local rows 0-3 are the four halo rows above (global
- * g_first - 4 .. g_first - 1), rows 4..R+3 are owned, rows R+4..R+7 are the
- * halo rows below.  Halo rows of U must hold the neighbours' initial rows; the
- * kernel keeps every halo current by storing its first / last four owned rows
- * straight into the neighbour's halo rows over NVLink (up to four sweeps are
- * fused per pass, so four rows are exchanged per pass).  up_* / dn_* are the
- * neighbours' U, V and workspace as mapped in this process (spmdb200_ipc_open),
- * NULL at the global top / bottom; up_rows is the number of rows the neighbour
- * above owns (our first owned rows land in its local rows up_rows + 4 ..
- * up_rows + 7).  all_ws[q] is rank q's workspace as mapped here (all_ws[rank]
- * is `ws`); the residual of every residual sweep is all-gathered into each
- * rank's workspace.  The caller must clear every rank's workspace
- * (spmdb200_jacobi_ws_reset) and make all ranks wait for one another before
- * any rank launches.  res_out (device, optional) receives this rank's local
+ * has G rows; this rank owns global rows [g_first, g_first + R), R >= 8.  U
+ * and V are (R + 16) x W local arrays (descriptor sizes (R+16, W), stride1 ==
+ * 1, 16-byte aligned rows): local rows 0-7 are the eight halo rows above
+ * (global g_first - 8 .. g_first - 1), rows 8..R+7 are owned, rows
+ * R+8..R+15 are the halo rows below.  The kernel fuses up to eight sweeps per
+ * pass and keeps every halo current over NVLink: before its first pass each
+ * run stores its first / last eight owned rows of U into the neighbours' halo
+ * rows, and every pass does the same with the rows it writes (halo rows of
+ * U need not hold anything on entry).  up_* / dn_* are the neighbours' U, V
+ * and workspace as mapped in this process (spmdb200_ipc_open), NULL at the
+ * global top / bottom; up_rows is the number of rows the neighbour above owns
+ * (our first owned rows land in its local rows up_rows + 8 .. up_rows + 15).
+ * all_ws[q] is rank q's workspace as mapped here (all_ws[rank] is `ws`); the
+ * residual of every residual sweep is all-gathered into each rank's
+ * workspace.  *deliveries (host, in/out) counts the halo deliveries this rank
+ * has received from each neighbour since the workspaces were cleared: 0 for
+ * the first run after every rank cleared its workspace
+ * (spmdb200_jacobi_ws_reset) and all ranks waited for one another, then
+ * whatever the previous call left in it.  The kernel waits on these
+ * monotonic counters, so back-to-back runs need no host synchronisation
+ * between them.  res_out (device, optional) receives this rank's local
  * residual contributions.  Sweep semantics and ping-pong are those of
- * spmdb200_jacobi2d; global rows 0 and G-1 and columns 0 and W-1 are fixed. */
+ * spmdb200_jacobi2d; global rows 0 and G-1 and columns 0 and W-1 are
+ * fixed. */
 int spmdb200_jacobi2d_slab(float *U_base, float *U_aligned, int64_t U_offset, int64_t U_size0, int64_t U_size1,
                            int64_t U_stride0, int64_t U_stride1,
                            float *V_base, float *V_aligned, int64_t V_offset, int64_t V_size0, int64_t V_size1,
@@ -338,7 +344,7 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U_aligned, int64_t U_offset, in
                            int64_t g_first, int64_t G, int64_t sweeps, int64_t res_every, double *res_out,
                            void *ws, float *up_u, float *up_v, void *up_ws, int64_t up_rows,
                            float *dn_u, float *dn_v, void *dn_ws,
-                           int rank, int nranks, void *const *all_ws, void *stream);
+                           int rank, int nranks, void *const *all_ws, int64_t *deliveries, void *stream);
 /* Jacobi-3D over z-slabs on several GPUs (one process per GPU).  No reference
  * counterpart.  The global grid has D planes of H x W; this rank owns global
  * planes [z_first, z_first + Z), Z >= 1.  U and V are (Z + 2) x H x W local
@@ -348,11 +354,13 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U_aligned, int64_t U_offset, in
  * first / last owned plane straight into the neighbour's halo plane over
  * NVLink every sweep; up_planes is the number of planes the neighbour above
  * owns (our first owned plane lands in its local plane up_planes + 1).  All
- * ranks' arrays share H, W and the row and plane strides.
- * Neighbour, workspace, residual and ping-pong semantics are those of
- * spmdb200_jacobi2d_slab (spmdb200_jacobi2d_slab_residuals reads the
- * all-gathered residuals); global planes 0 and D-1, rows 0 and H-1 and
- * columns 0 and W-1 are fixed. */
+ * ranks' arrays share H, W and the row and plane strides.  The halo planes
+ * of U must hold the neighbours' planes on the first run (this kernel does
+ * not deliver its input; later runs find the planes the previous run
+ * delivered).  Neighbour, workspace, delivery-count, residual and ping-pong
+ * semantics are those of spmdb200_jacobi2d_slab
+ * (spmdb200_jacobi2d_slab_residuals reads the all-gathered residuals);
+ * global planes 0 and D-1, rows 0 and H-1 and columns 0 and W-1 are fixed. */
 int spmdb200_jacobi3d_slab(float *U_base, float *U_aligned, int64_t U_offset, int64_t U_size0, int64_t U_size1,
                            int64_t U_size2, int64_t U_stride0, int64_t U_stride1, int64_t U_stride2,
                            float *V_base, float *V_aligned, int64_t V_offset, int64_t V_size0, int64_t V_size1,
@@ -360,7 +368,11 @@ int spmdb200_jacobi3d_slab(float *U_base, float *U_aligned, int64_t U_offset, in
                            int64_t z_first, int64_t D, int64_t sweeps, int64_t res_every, double *res_out,
                            void *ws, float *up_u, float *up_v, void *up_ws, int64_t up_planes,
                            float *dn_u, float *dn_v, void *dn_ws,
-                           int rank, int nranks, void *const *all_ws, void *stream);
+                           int rank, int nranks, void *const *all_ws, int64_t *deliveries, void *stream);
+/* Halo depth of the slab layouts: rows on each side of a Jacobi-2D row slab
+ * (dims == 2: 8) or planes on each side of a Jacobi-3D z-slab (dims == 3: 1);
+ * -1 for other dims.  No reference counterpart. */
+int spmdb200_jacobi_slab_halo(int dims);
 /* Clears the 256-byte header of a Jacobi workspace on `stream`. */
 int spmdb200_jacobi_ws_reset(void *ws, void *stream);
 /* After every rank's slab run has finished: res_host[r] = sum over ranks q
@@ -373,6 +385,9 @@ int spmdb200_dev_free(void *p);
 /* Copies `bytes` between any two addresses (host or device; direction from
  * unified addressing) on `stream`, then synchronises it. */
 int spmdb200_memcpy(void *dst, const void *src, size_t bytes, void *stream);
+/* The same copy, asynchronous on `stream` (pinned host memory for overlap;
+ * the caller orders it with events).  No reference counterpart. */
+int spmdb200_memcpy_async(void *dst, const void *src, size_t bytes, void *stream);
 /* 64-byte IPC handle of a spmdb200_dev_alloc pointer. */
 int spmdb200_ipc_handle(void *dev_ptr, void *handle64_out);
 int spmdb200_ipc_open(const void *handle64, void **dev_ptr_out);

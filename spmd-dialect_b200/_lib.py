@@ -68,14 +68,16 @@ _SIGS = {
     "spmdb200_set_wait_budget_ms": (ctypes.c_int, [c_i, c_i]),
     # multi-GPU row slabs
     "spmdb200_jacobi2d_slab": (ctypes.c_int, D2 + D2 + [c_i, c_i, c_i, c_i, c_p, c_p, c_p, c_p, c_p, c_i, c_p, c_p,
-                                                       c_p, ctypes.c_int, ctypes.c_int, c_p, c_p]),
+                                                       c_p, ctypes.c_int, ctypes.c_int, c_p, c_p, c_p]),
     "spmdb200_jacobi3d_slab": (ctypes.c_int, D3 + D3 + [c_i, c_i, c_i, c_i, c_p, c_p, c_p, c_p, c_p, c_i, c_p, c_p,
-                                                       c_p, ctypes.c_int, ctypes.c_int, c_p, c_p]),
+                                                       c_p, ctypes.c_int, ctypes.c_int, c_p, c_p, c_p]),
+    "spmdb200_jacobi_slab_halo": (ctypes.c_int, [ctypes.c_int]),
     "spmdb200_jacobi_ws_reset": (ctypes.c_int, [c_p, c_p]),
     "spmdb200_jacobi2d_slab_residuals": (ctypes.c_int, [c_p, ctypes.c_int, c_i, c_p]),
     "spmdb200_dev_alloc": (ctypes.c_int, [c_sz, ctypes.POINTER(c_p)]),
     "spmdb200_dev_free": (ctypes.c_int, [c_p]),
     "spmdb200_memcpy": (ctypes.c_int, [c_p, c_p, c_sz, c_p]),
+    "spmdb200_memcpy_async": (ctypes.c_int, [c_p, c_p, c_sz, c_p]),
     "spmdb200_ipc_handle": (ctypes.c_int, [c_p, c_p]),
     "spmdb200_ipc_open": (ctypes.c_int, [c_p, ctypes.POINTER(c_p)]),
     "spmdb200_ipc_close": (ctypes.c_int, [c_p]),

@@ -527,8 +527,8 @@ int spmdb200_jacobi2d(float *U_base, float *U, int64_t U_off, int64_t U_n0, int6
   p.res_every = res_every;
   p.res_out = res_out;
   p.ws = w;
-  if (U_s1 == 1 && jacobi2d_tma_ok(p)) {
-    CUDA_TRY(run_jacobi2d_persistent(p, SlabPeers{}, s));
+  if (U_s1 == 1 && jacobi2d_persistent_ok(p)) {
+    CUDA_TRY(run_jacobi2d_persistent(p, SlabPeers{}, 0u, s));
   } else {
     CUDA_TRY(launch_jacobi2d_generic(p, U_s1, s));
   }
@@ -574,6 +574,8 @@ int spmdb200_jacobi3d(float *U_base, float *U, int64_t U_off, int64_t U_n0, int6
 }
 
 // ---------------------------------------------------------------- multi-GPU slabs
+int spmdb200_jacobi_slab_halo(int dims) { return dims == 2 ? kSlabHalo : dims == 3 ? kSlabHalo3 : -1; }
+
 int spmdb200_jacobi_ws_reset(void *ws, void *stream) {
   if (!ws) return fail(SPMDB200_ERR_WORKSPACE, "null workspace");
   CUDA_TRY(cudaMemsetAsync(ws, 0, 256, (cudaStream_t)stream));
@@ -585,7 +587,7 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
                            int64_t V_s0, int64_t V_s1, int64_t g_first, int64_t G, int64_t sweeps,
                            int64_t res_every, double *res_out, void *ws, float *up_u, float *up_v, void *up_ws,
                            int64_t up_rows, float *dn_u, float *dn_v, void *dn_ws, int rank, int nranks,
-                           void *const *all_ws, void *stream) {
+                           void *const *all_ws, int64_t *deliveries, void *stream) {
   (void)U_base; (void)V_base;
   CHECK(check2("U", U, U_off, U_n0, U_n1, U_s0, U_s1));
   CHECK(check2("V", V, V_off, V_n0, V_n1, V_s0, V_s1));
@@ -630,8 +632,9 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   p.res_every = res_every;
   p.res_out = res_out;
   p.ws = static_cast<JacobiWs *>(ws);
-  if (!jacobi2d_tma_ok(p))
+  if (!jacobi2d_persistent_ok(p))
     return fail(SPMDB200_ERR_UNSUPPORTED, "slab arrays need 16-byte aligned rows (pitch multiple of 4 floats)");
+  if (!deliveries) return fail(SPMDB200_ERR_INVALID_ARG, "deliveries (the halo-delivery count) is required");
   SlabPeers peers;
   peers.up_u = up_u;
   peers.up_v = up_v;
@@ -646,7 +649,8 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   for (int q = 0; q < nranks; ++q)
     peers.peer_ws[q] = static_cast<JacobiWs *>(all_ws ? all_ws[q] : (q == rank ? ws : nullptr));
   if (!peers.peer_ws[rank]) peers.peer_ws[rank] = static_cast<JacobiWs *>(ws);
-  CUDA_TRY(run_jacobi2d_persistent(p, peers, (cudaStream_t)stream));
+  CUDA_TRY(run_jacobi2d_persistent(p, peers, (unsigned)*deliveries, (cudaStream_t)stream));
+  *deliveries += jacobi2d_slab_deliveries(sweeps, res_every, U_n1, (int)H);
   return ok();
 }
 
@@ -655,7 +659,8 @@ int spmdb200_jacobi3d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
                            int64_t V_n0, int64_t V_n1, int64_t V_n2, int64_t V_s0, int64_t V_s1, int64_t V_s2,
                            int64_t z_first, int64_t D, int64_t sweeps, int64_t res_every, double *res_out,
                            void *ws, float *up_u, float *up_v, void *up_ws, int64_t up_planes, float *dn_u,
-                           float *dn_v, void *dn_ws, int rank, int nranks, void *const *all_ws, void *stream) {
+                           float *dn_v, void *dn_ws, int rank, int nranks, void *const *all_ws,
+                           int64_t *deliveries, void *stream) {
   (void)U_base; (void)V_base;
   CHECK(check3("U", U, U_off, U_n0, U_n1, U_n2, U_s0, U_s1, U_s2));
   CHECK(check3("V", V, V_off, V_n0, V_n1, V_n2, V_s0, V_s1, V_s2));
@@ -719,8 +724,13 @@ int spmdb200_jacobi3d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   for (int q = 0; q < nranks; ++q)
     peers.peer_ws[q] = static_cast<JacobiWs *>(all_ws ? all_ws[q] : (q == rank ? ws : nullptr));
   if (!peers.peer_ws[rank]) peers.peer_ws[rank] = static_cast<JacobiWs *>(ws);
+  if (!deliveries) return fail(SPMDB200_ERR_INVALID_ARG, "deliveries (the halo-delivery count) is required");
   int grid = 0;
-  CUDA_TRY(launch_jacobi3d_persistent(p, peers, (cudaStream_t)stream, &grid));
+  // Fresh grid barrier for this launch (stream-ordered); the status word and
+  // the delivery counters carry over.
+  CUDA_TRY(cudaMemsetAsync(&p.ws->barrier, 0, sizeof(unsigned), (cudaStream_t)stream));
+  CUDA_TRY(launch_jacobi3d_persistent(p, peers, (cudaStream_t)stream, &grid, (unsigned)*deliveries));
+  *deliveries += jacobi3d_slab_deliveries(sweeps, U_n1, U_n2);
   return ok();
 }
 
@@ -756,6 +766,12 @@ int spmdb200_memcpy(void *dst, const void *src, size_t bytes, void *stream) {
   if (!dst || !src) return fail(SPMDB200_ERR_INVALID_ARG, "null pointer");
   CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, (cudaStream_t)stream));
   CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+  return ok();
+}
+int spmdb200_memcpy_async(void *dst, const void *src, size_t bytes, void *stream) {
+  if (bytes == 0) return ok();
+  if (!dst || !src) return fail(SPMDB200_ERR_INVALID_ARG, "null pointer");
+  CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, (cudaStream_t)stream));
   return ok();
 }
 int spmdb200_ipc_handle(void *dev_ptr, void *handle64_out) {

@@ -44,6 +44,9 @@ cudaError_t launch_stencil3(View2 a, View2 b, int64_t n, int64_t m, cudaStream_t
 constexpr int kMaxCtas = 2048;
 constexpr int kMaxRanks = 8;
 constexpr int kMaxResSlots = 1024;
+// Residual partial slots: at least twice the residuals one pass can produce
+// (a pass fuses up to 8 sweeps).
+constexpr int kJacobiPartialSlots = 16;
 
 // Device workspace of every Jacobi run.  The 256-byte header is cleared by the
 // host before each run.
@@ -54,7 +57,7 @@ struct JacobiWs {
   unsigned from_below; // halo-tile deliveries received from the rank below
   unsigned ticket;     // last-block ticket of the per-sweep (generic) path
   unsigned pad[59];
-  double partial[8][kMaxCtas];                // per-CTA residual partials, slot = residual index % 8
+  double partial[kJacobiPartialSlots][kMaxCtas];  // per-CTA residual partials, slot = residual index % 16
   double res_slots[kMaxResSlots][kMaxRanks];  // residual all-gather target (multi-GPU)
 };
 static_assert(offsetof(JacobiWs, partial) == 256, "JacobiWs header must be 256 bytes");
@@ -83,21 +86,30 @@ struct Jacobi2dProblem {
   int halo = 0;       // slab mode: halo rows on each side (rows exchanged per neighbour per pass)
 };
 
-// Halo depth of the multi-GPU Jacobi-2D slab layout: four rows on each side,
-// so a pass may fuse four sweeps.
-constexpr int kSlabHalo = 4;
+// Halo depth of the multi-GPU Jacobi-2D slab layout: eight rows on each side,
+// so a pass may fuse eight sweeps.
+constexpr int kSlabHalo = 8;
 // Halo depth of the multi-GPU Jacobi-3D z-slab layout (one sweep per pass).
 constexpr int kSlabHalo3 = 1;
 
-bool jacobi2d_tma_ok(const Jacobi2dProblem &p);
-// Passes the persistent path runs for `sweeps` sweeps: plan[0] four-sweep,
-// plan[1] two-sweep and plan[2] single-sweep passes (the first two even).
-void jacobi2d_pass_plan(int64_t sweeps, int64_t plan[3]);
-// Runs p.sweeps sweeps on the persistent TMA path (requires jacobi2d_tma_ok)
-// as jacobi2d_pass_plan lays them out (temporal blocking), so the result
-// lands in u after an even and in v after an odd number of sweeps.  The
-// workspace header must be clear.  Asynchronous.
-cudaError_t run_jacobi2d_persistent(const Jacobi2dProblem &p, const SlabPeers &peers, cudaStream_t s);
+// The persistent (register-wavefront) path needs 16-byte aligned rows.
+bool jacobi2d_persistent_ok(const Jacobi2dProblem &p);
+// Passes the persistent path runs for `sweeps` sweeps: plan[0..3] passes of
+// 8, 4, 2 and 1 sweeps (the first three even; no pass longer than res_every
+// when res_every > 0, so a pass holds at most one residual sweep).
+void jacobi2d_pass_plan(int64_t sweeps, int64_t res_every, int64_t plan[4]);
+// Halo deliveries a slab run of `sweeps` sweeps makes to each neighbour (and
+// receives from it): one per halo row, tile column and pass, plus one pass's
+// worth for the input rows delivered before the first pass.
+int64_t jacobi2d_slab_deliveries(int64_t sweeps, int64_t res_every, int64_t w, int halo);
+// Runs p.sweeps sweeps on the persistent path (requires
+// jacobi2d_persistent_ok) as jacobi2d_pass_plan lays them out (temporal
+// blocking), so the result lands in u after an even and in v after an odd
+// number of sweeps.  Slab mode: flag_base = deliveries already received from
+// each neighbour.  The workspace status word must be clear; the grid barrier
+// is reset here on the stream.  Asynchronous.
+cudaError_t run_jacobi2d_persistent(const Jacobi2dProblem &p, const SlabPeers &peers, unsigned flag_base,
+                                    cudaStream_t s);
 // Seeded synthetic Jacobi input (counter-based hash of (seed, global row, column)).
 cudaError_t launch_fill_jacobi_input(float *p, int64_t pitch, int64_t rows, int64_t w, int64_t g_row0,
                                      int64_t g_rows, uint64_t seed, cudaStream_t s);
@@ -118,9 +130,12 @@ struct Jacobi3dProblem {
   int halo = 0;
 };
 bool jacobi3d_tma_ok(const Jacobi3dProblem &p);
-// SlabPeers.up_row / dn_row are plane indices here.
+// SlabPeers.up_row / dn_row are plane indices here.  z-slab mode: flag_base =
+// halo-plane deliveries already received from each neighbour.
 cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, const SlabPeers &peers, cudaStream_t s,
-                                       int *grid_out);
+                                       int *grid_out, unsigned flag_base = 0);
+// Halo-plane deliveries a z-slab run of `sweeps` sweeps makes to each neighbour.
+int64_t jacobi3d_slab_deliveries(int64_t sweeps, int64_t h, int64_t w);
 cudaError_t launch_jacobi3d_generic(const Jacobi3dProblem &p, cudaStream_t s);
 // Seeded synthetic 3-D Jacobi input (counter hash of (seed, gz * h + y, x)).
 cudaError_t launch_fill_jacobi3d_input(float *p, int64_t sz, int64_t sy, int64_t planes, int64_t h, int64_t w,

@@ -192,7 +192,8 @@ struct J3Kernel {
   JacobiWs *ws;
   unsigned long long budget_ns, peer_budget_ns;
   SlabPeers peers;
-  int halo;  // 1 in z-slab mode, 0 on one GPU
+  int halo;            // 1 in z-slab mode, 0 on one GPU
+  unsigned flag_base;  // halo-plane deliveries already received from each neighbour
 };
 
 // Work item t -> (zc, tx, ty).  One GPU: z-chunk fastest.  z-slab mode: the
@@ -342,7 +343,7 @@ __global__ void __launch_bounds__(THREADS3) jacobi3d_persistent_kernel(
             // a halo plane is staged only once the neighbour delivered it for
             // every earlier sweep; the proxy fence orders that acquire before
             // the TMA (async-proxy) read of the peer-written plane
-            const unsigned need = (unsigned)s * per_sweep;
+            const unsigned need = k.flag_base + (unsigned)s * per_sweep;
             const bool wait_up = k.peers.up_flag && z0 - 1 < k.z_lo;
             const bool wait_dn = k.peers.dn_flag && z0 + BZ3 >= k.z_hi;
             if (wait_up && !wait_counter3(&k.ws->from_above, need, abort, k.peer_budget_ns, k.ws, true)) {
@@ -567,8 +568,12 @@ bool jacobi3d_tma_ok(const Jacobi3dProblem &p) {
          p.d < (1ll << 30) && p.sz < (1ll << 37) && p.sweeps <= (1ll << 30);
 }
 
+int64_t jacobi3d_slab_deliveries(int64_t sweeps, int64_t h, int64_t w) {
+  return sweeps * ((w + BW3 - 1) / BW3) * ((h + BH3 - 1) / BH3) * CW3;
+}
+
 cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, const SlabPeers &peers, cudaStream_t s,
-                                       int *grid_out) {
+                                       int *grid_out, unsigned flag_base) {
   CUtensorMap mu, mv;
   const uint64_t dims[3] = {(uint64_t)p.w, (uint64_t)p.h, (uint64_t)p.d};
   const uint64_t strides[2] = {(uint64_t)p.sy * 4u, (uint64_t)p.sz * 4u};
@@ -598,6 +603,7 @@ cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, const SlabPeers
   k.ws = p.ws;
   k.budget_ns = wait_budget_ns(false);
   k.peer_budget_ns = wait_budget_ns(true);
+  k.flag_base = flag_base;
 
   const bool slab = peers.up_u != nullptr || peers.dn_u != nullptr;  // a neighbour exists
   auto kernel = slab ? jacobi3d_persistent_kernel<true> : jacobi3d_persistent_kernel<false>;

@@ -10,14 +10,130 @@
 //   atomic_sum_kernel       (i64 tile, i64 N, A x5, out x3)             harness/run_reduction.py:32-49
 //   hierarchical_sum_kernel (i64 tile, i64 N, ptr A.aligned, ptr out)   scripts/gen-ptx.sh:116-130
 //
-// Every kernel is correct for any grid/block shape (grid-stride bodies), so
-// the reference launches (grid=ceil(N/tile), block=tile; grid=(N/TR, M/TC),
-// block=(TR+1)(TC+1)) work unchanged.  Memref offsets and strides are honoured.
+// Every kernel is correct for any grid/block shape, so the reference launches
+// (grid = ceil(N/tile), block = tile; grid = (N/TR, M/TC), block =
+// (TR+1)(TC+1)) work unchanged.  Memref offsets and strides are honoured.
+//
+// Those launches are tens or hundreds of thousands of small blocks (65,536
+// blocks for the 2^24 sum and the 4096^2 stencil), and on B200 launching the
+// blocks alone takes ~37 us for 65,536 blocks (an empty kernel of that shape).
+// One block per block of work would also keep only a few KB in flight per SM.
+// So the stencil and the sums work in groups: the first block of every K
+// consecutive blocks does the work of all K (wide contiguous slices, 16-byte
+// loads where aligned) and the other K - 1 return at once.  The elementwise
+// kernel already runs at the launch floor of its shape (312,500 blocks of 32
+// threads for N = 1e7: 0.164 ms empty, 0.165 ms with the work) and keeps its
+// grid-stride body.
 #include "elementwise.cuh"
 #include "reduction.cuh"
-#include "stencil3.cuh"
 
-using spmdb200::View2;
+namespace {
+
+// Linear index of this block in the whole grid, and the grid's block count.
+__device__ __forceinline__ void block_linear(int64_t &L, int64_t &G) {
+  G = (int64_t)gridDim.x * gridDim.y * gridDim.z;
+  L = blockIdx.x + (int64_t)gridDim.x * (blockIdx.y + (int64_t)gridDim.y * blockIdx.z);
+}
+
+// Work slice [c0, c1) of `total` items for this block when every K
+// consecutive blocks pool their shares (ceil(total / G) items each) in the
+// group's first block.  False for the other blocks of the group and for
+// groups past the end.  The groups cover [0, total) exactly once for any grid.
+template <int K>
+__device__ __forceinline__ bool group_slice(int64_t total, int64_t &c0, int64_t &c1) {
+  int64_t L, G;
+  block_linear(L, G);
+  if (L % K != 0 || total <= 0) return false;
+  const int64_t share = (total + G - 1) / G;
+  c0 = L * share;
+  c1 = min(c0 + K * share, total);
+  return c0 < c1;
+}
+
+// f64 sum of a[c0..c1) (stride sa) by this block's threads; valid in thread 0.
+__device__ __forceinline__ double block_slice_sum(const float *a, int64_t sa, int64_t c0, int64_t c1, double *sh) {
+  const int64_t T = blockDim.x;
+  double acc0 = 0.0, acc1 = 0.0;
+  const float *p = a + c0 * sa;
+  const int64_t n = c1 - c0;
+  if (sa == 1 && ((uintptr_t)p & 15u) == 0) {
+    const int64_t n4 = n >> 2;
+    int64_t i = threadIdx.x;
+    for (; i + T < n4; i += 2 * T) {
+      const float4 v0 = spmdb200::ld_stream_f4(p + 4 * i);
+      const float4 v1 = spmdb200::ld_stream_f4(p + 4 * (i + T));
+      acc0 = __dadd_rn(acc0, (double)v0.x);
+      acc1 = __dadd_rn(acc1, (double)v1.x);
+      acc0 = __dadd_rn(acc0, (double)v0.y);
+      acc1 = __dadd_rn(acc1, (double)v1.y);
+      acc0 = __dadd_rn(acc0, (double)v0.z);
+      acc1 = __dadd_rn(acc1, (double)v1.z);
+      acc0 = __dadd_rn(acc0, (double)v0.w);
+      acc1 = __dadd_rn(acc1, (double)v1.w);
+    }
+    if (i < n4) {
+      const float4 v0 = spmdb200::ld_stream_f4(p + 4 * i);
+      acc0 = __dadd_rn(acc0, (double)v0.x);
+      acc0 = __dadd_rn(acc0, (double)v0.y);
+      acc0 = __dadd_rn(acc0, (double)v0.z);
+      acc0 = __dadd_rn(acc0, (double)v0.w);
+    }
+    const int64_t t = (n4 << 2) + threadIdx.x;
+    if (t < n) acc1 = __dadd_rn(acc1, (double)p[t]);
+  } else {
+    for (int64_t i = threadIdx.x; i < n; i += T) acc0 = __dadd_rn(acc0, (double)p[i * sa]);
+  }
+  return spmdb200::block_sum_f64(__dadd_rn(acc0, acc1), sh);
+}
+
+constexpr int kSumGroup = 16;     // blocks pooled per working block of the sums
+constexpr int kStencilGroup = 4;  // ... of the promoted stencil
+
+__device__ __forceinline__ float ld_a(const float *a, long long n0, long long n1, long long s0, long long s1,
+                                      long long i, long long j) {
+  return (i >= 0 && j >= 0 && i < n0 && j < n1) ? a[i * s0 + j * s1] : 0.0f;
+}
+
+// B[i,j] = (A[i,j] + A[i,j+c1]) + A[i+c1,j] over the N x M output in
+// row-major order, K blocks' shares per working block, cut at row ends.
+// Footprint cells outside A read as 0 (the reference leaves those
+// group-memory slots unwritten, PromoteGroupMemory.cpp:268-292).  Staging the
+// footprint in group memory (the reference's promotion) changes only where
+// the values are read from; here the +c1 neighbours come from the L1 cache
+// and the next row from L2 (the block one group later reads it), so the
+// arithmetic and its order are the reference's.
+__device__ __forceinline__ void promoted_stencil_body(const float *A, long long A_n0, long long A_n1, long long A_s0,
+                                                      long long A_s1, long long c1, float *B, long long B_n0,
+                                                      long long B_n1, long long B_s0, long long B_s1) {
+  const long long N = B_n0, M = B_n1;
+  int64_t c0, cend;
+  if (M <= 0 || !group_slice<kStencilGroup>(N * M, c0, cend)) return;
+  while (c0 < cend) {
+    const long long i = c0 / M, j0 = c0 - i * M;
+    const long long len = min((long long)(cend - c0), M - j0);
+    const float *a0 = A + i * A_s0;
+    float *b0 = B + i * B_s0;
+    const bool fast = c1 >= 0 && i + c1 < A_n0 && j0 + len + c1 <= A_n1;  // every read inside A
+#pragma unroll 4
+    for (long long jj = threadIdx.x; jj < len; jj += blockDim.x) {
+      const long long j = j0 + jj;
+      float x, e, s;
+      if (fast) {
+        x = a0[j * A_s1];
+        e = a0[(j + c1) * A_s1];
+        s = a0[c1 * A_s0 + j * A_s1];
+      } else {
+        x = ld_a(A, A_n0, A_n1, A_s0, A_s1, i, j);
+        e = ld_a(A, A_n0, A_n1, A_s0, A_s1, i, j + c1);
+        s = ld_a(A, A_n0, A_n1, A_s0, A_s1, i + c1, j);
+      }
+      b0[j * B_s1] = __fadd_rn(__fadd_rn(x, e), s);
+    }
+    c0 += len;
+  }
+}
+
+}  // namespace
 
 extern "C" __global__ void __launch_bounds__(1024) ewise_kernel(long long tile, long long N,
                                         float *A_base, float *A, long long A_off, long long A_size, long long A_st,
@@ -35,11 +151,8 @@ extern "C" __global__ void __launch_bounds__(1024) promoted_stencil_kernel(long 
                                                    long long c1,
                                                    float *B_base, float *B, long long B_off, long long B_n0,
                                                    long long B_n1, long long B_s0, long long B_s1) {
-  (void)A_base; (void)B_base;
-  __shared__ spmdb200::Stencil3Smem sm;
-  const View2 a{A + A_off, A_n0, A_n1, A_s0, A_s1};
-  const View2 b{B + B_off, B_n0, B_n1, B_s0, B_s1};
-  spmdb200::stencil3_body(a, b, B_n0, B_n1, c1, TR, TC, sm);
+  (void)A_base; (void)B_base; (void)TR; (void)TC;
+  promoted_stencil_body(A + A_off, A_n0, A_n1, A_s0, A_s1, c1, B + B_off, B_n0, B_n1, B_s0, B_s1);
 }
 
 extern "C" __global__ void __launch_bounds__(1024) promoted_stencil_kernel_square(long long T,
@@ -48,28 +161,33 @@ extern "C" __global__ void __launch_bounds__(1024) promoted_stencil_kernel_squar
                                                           long long c1,
                                                           float *B_base, float *B, long long B_off, long long B_n0,
                                                           long long B_n1, long long B_s0, long long B_s1) {
-  (void)A_base; (void)B_base;
-  __shared__ spmdb200::Stencil3Smem sm;
-  const View2 a{A + A_off, A_n0, A_n1, A_s0, A_s1};
-  const View2 b{B + B_off, B_n0, B_n1, B_s0, B_s1};
-  spmdb200::stencil3_body(a, b, B_n0, B_n1, c1, T, T, sm);
+  (void)A_base; (void)B_base; (void)T;
+  promoted_stencil_body(A + A_off, A_n0, A_n1, A_s0, A_s1, c1, B + B_off, B_n0, B_n1, B_s0, B_s1);
 }
 
-// out += sum(A[0..N)) with one f32 atomic per block (the reference does one per
-// element; the sum it produces is the same up to f32 rounding order).
+// out += sum(A[0..N)) with one f32 atomic per working block (the reference
+// does one per element; the sum it produces is the same up to f32 rounding
+// order).
 extern "C" __global__ void __launch_bounds__(1024) atomic_sum_kernel(long long tile, long long N,
                                              float *A_base, float *A, long long A_off, long long A_size,
                                              long long A_st,
                                              float *out_base, float *out, long long out_off) {
   (void)tile; (void)A_base; (void)A_size; (void)out_base;
   __shared__ double sh[32];
-  const double b = spmdb200::block_sum_f64(spmdb200::thread_sum_f64(A + A_off, A_st, N), sh);
+  int64_t c0, c1;
+  if (!group_slice<kSumGroup>(N, c0, c1)) return;
+  const double b = block_slice_sum(A + A_off, A_st, c0, c1, sh);
   if (threadIdx.x == 0) atomicAdd(out + out_off, __double2float_rn(b));
 }
 
+// out += sum(A[0..N)): per working block an f64 sum, then one f32 atomic
+// into the rank-0 output -- ReduceToHierarchicalGPU's levels (thread,
+// block, grid atomic; SPMDToGPU.cpp:336-408).
 extern "C" __global__ void __launch_bounds__(1024) hierarchical_sum_kernel(long long tile, long long N, float *A, float *out) {
   (void)tile;
   __shared__ double sh[32];
-  const double b = spmdb200::block_sum_f64(spmdb200::thread_sum_f64(A, 1, N), sh);
+  int64_t c0, c1;
+  if (!group_slice<kSumGroup>(N, c0, c1)) return;
+  const double b = block_slice_sum(A, 1, c0, c1, sh);
   if (threadIdx.x == 0) atomicAdd(out, __double2float_rn(b));
 }

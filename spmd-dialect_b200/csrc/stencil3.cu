@@ -3,7 +3,7 @@
 // (test/SPMD/lower-to-gpu-nvptx-promoted.mlir:32-67).  It is the general
 // promoted-tile stencil with the offsets (0,0), (0,1), (1,0) in that order:
 // footprint cells outside A read as 0 and stores stay inside n x m, exactly
-// as stencil3_body does for the reference-signature kernel.
+// as the reference-signature promoted_stencil_kernel of the kernel module does.
 #include "internal.h"
 
 namespace spmdb200 {

@@ -2,16 +2,22 @@
 for Jacobi-3D.  One process per GPU.
 
 torch.distributed is plumbing only (exchanging CUDA IPC handles, the
-rendezvous before each launch, gathering results for tests).  The data path --
+rendezvous around host-side reads and writes of the slabs, gathering results
+for tests).  The data path --
 the halo exchange and the residual all-gather every `res_every` sweeps -- runs
 inside the persistent kernels over NVLink (spmdb200_jacobi2d_slab,
 spmdb200_jacobi3d_slab): no NCCL call sits between sweeps.
 
 Jacobi-2D: the G x W global grid is cut into contiguous row blocks; rank p owns
-global rows [g_first, g_first + rows) and keeps a (rows + 8) x pitch local
-array whose first and last HALO = 4 rows mirror the neighbours' edge rows
-(four rows deep, because the kernel fuses up to four sweeps per pass; four
-rows move up and four down per pass).
+global rows [g_first, g_first + rows) and keeps a (rows + 16) x pitch local
+array whose first and last HALO = 8 rows mirror the neighbours' edge rows
+(eight rows deep, because the kernel fuses up to eight sweeps per pass; eight
+rows move up and eight down per pass, and each run first sends the edge rows
+of its input).
+
+The kernels wait on halo-delivery counters that only grow; each job keeps
+the count it has received so far and passes it to every run, so runs follow
+one another with no host synchronisation between them.
 
 Jacobi-3D: the D x H x W grid is cut into contiguous plane blocks; rank p owns
 planes [g_first, g_first + planes) plus HALO3 = 1 halo plane on each side (one
@@ -26,8 +32,8 @@ import numpy as np
 
 from ._lib import c_i, c_p, call, lib
 
-HALO = 4  # halo rows on each side of a 2-D slab (kSlabHalo in the C library)
-HALO3 = 1  # halo planes on each side of a 3-D slab (kSlabHalo3)
+HALO = int(lib().spmdb200_jacobi_slab_halo(2))  # halo rows on each side of a 2-D slab (8)
+HALO3 = int(lib().spmdb200_jacobi_slab_halo(3))  # halo planes on each side of a 3-D slab (1)
 
 
 # ---------------------------------------------------------------- decomposition
@@ -97,9 +103,9 @@ def _dist():
 
 
 def rendezvous() -> None:
-    """Every rank reaches this point before any rank launches: a rank that never
-    arrives makes the others fail here (process-group timeout) instead of
-    launching a kernel that would wait on its halo rows."""
+    """Every rank reaches this point before any rank goes on (job set-up, host
+    reads and writes of the slabs, close): a rank that never arrives makes the
+    others fail here with the process-group timeout."""
     d = _dist()
     if d is not None and d.get_world_size() > 1:
         d.barrier()
@@ -132,12 +138,17 @@ class _SlabJob:
         self._ws = DeviceBuffer(int(lib().spmdb200_jacobi_workspace_bytes()))
         self.sweeps_done = 0
         self._nres_last = 0
+        self._deliveries = ctypes.c_int64(0)  # halo deliveries received from each neighbour so far
+        stream = c_p(torch.cuda.current_stream().cuda_stream)
+        call("spmdb200_jacobi_ws_reset", c_p(self._ws.ptr), stream)
         if init is None:
-            stream = c_p(torch.cuda.current_stream().cuda_stream)
             for buf in (self._u, self._v):
                 self._fill(buf.ptr, seed, stream)
         else:
             self.load_global(init)
+        # Every workspace is clear before the handle exchange below, which no
+        # rank passes before all have arrived: no kernel can deliver into an
+        # uncleared workspace.
         torch.cuda.current_stream().synchronize()
         # Map the neighbours' grids and every rank's workspace into this process.
         self._up, self._dn = _Peer(), _Peer()
@@ -231,28 +242,26 @@ class _SlabJob:
     # ---------------------------------------------------------------- running
     def _quiesce(self) -> None:
         """Returns once every rank's previous launch is complete.  A launch's
-        last pass still stores halo rows (the next launch's input) into the
-        neighbours' memory and bumps their delivery counters after a
-        neighbour's own kernel may have ended; nothing may clear those counters
-        or overwrite those rows before then."""
+        last pass still stores halo rows into the neighbours' memory after a
+        neighbour's own kernel may have ended; host code that overwrites a
+        slab (a load or a restore) must not race with those stores."""
         import torch
         torch.cuda.current_stream().synchronize()
         rendezvous()
 
     def run(self, sweeps: int, check: bool = True) -> None:
-        """`sweeps` sweeps on every rank (all ranks must call with the same count)."""
+        """`sweeps` sweeps on every rank (all ranks must call with the same
+        count).  Asynchronous on the current stream: the kernel itself waits
+        for the neighbours' halo rows, so no host synchronisation comes first."""
         import torch
         stream = c_p(torch.cuda.current_stream().cuda_stream)
-        self._quiesce()
-        call("spmdb200_jacobi_ws_reset", c_p(self._ws.ptr), stream)
-        torch.cuda.current_stream().synchronize()
-        rendezvous()  # every workspace is clear before any kernel can deliver a halo
         up, dn = self._up, self._dn
         call(self.entry, *self._desc(self._u.ptr), *self._desc(self._v.ptr), c_i(self.g_first),
              c_i(self.G), c_i(sweeps), c_i(self.res_every), c_p(0), c_p(self._ws.ptr),
              c_p(up.u or None), c_p(up.v or None), c_p(up.ws or None), c_i(self._up_rows),
              c_p(dn.u or None), c_p(dn.v or None), c_p(dn.ws or None),
-             ctypes.c_int(self.rank), ctypes.c_int(self.world), self._all_ws_arr, stream)
+             ctypes.c_int(self.rank), ctypes.c_int(self.world), self._all_ws_arr, ctypes.byref(self._deliveries),
+             stream)
         self._nres_last = sweeps // self.res_every if self.res_every > 0 else 0
         self.sweeps_done += sweeps
         if sweeps % 2 == 1:
@@ -276,6 +285,7 @@ class _SlabJob:
         out = np.zeros(max(self._nres_last, 1), np.float64)
         call("spmdb200_jacobi2d_slab_residuals", c_p(self._ws.ptr), ctypes.c_int(self.world),
              c_i(self._nres_last), out.ctypes.data_as(c_p))
+        rendezvous()  # no rank's next run writes the slots before every rank has read them
         return out[:self._nres_last]
 
     def run_host(self, host_local: np.ndarray, sweeps: int) -> np.ndarray:
@@ -398,13 +408,82 @@ class SlabJacobi3D(_SlabJob):
         return out
 
 
-def e2e_measure(job: _SlabJob, sweeps: int, reps: int = 2) -> dict:
-    """Whole-job end-to-end rate through SlabJacobi2D.run_host with pinned host
-    slabs (H2D + sweeps + D2H timed on every rank, max over ranks)."""
+def run_host_pipelined(jobs: list, hosts: list, sweeps: int, steps: int) -> None:
+    """`steps` runs of `sweeps` sweeps on host slabs, pipelined across two
+    device slots.  jobs: two SlabJacobi2D jobs with the same decomposition
+    (the slots); hosts: two pinned host arrays of this rank's owned rows
+    (rows x pitch, float32), used alternately -- run k reads hosts[k % 2] and
+    writes its result back there.  Uploads, sweeps and downloads run on three
+    streams, so run k's sweeps overlap the download of run k-1 and the upload
+    of run k+1 (which waits for that download: they share a host buffer).
+    Only owned rows cross PCIe: every run first delivers its input's edge rows
+    into the neighbours' halo rows itself.  All ranks call it with the same
+    arguments; it returns once every copy of this rank has finished."""
+    import torch
+    if len(jobs) != 2 or len(hosts) != 2 or not all(isinstance(j, SlabJacobi2D) for j in jobs):
+        raise ValueError("two SlabJacobi2D jobs (slots) and two host arrays are required")
+    own = jobs[0].rows * jobs[0].unit_floats * 4
+    off = jobs[0].halo * jobs[0].unit_floats * 4
+    for h in hosts:
+        if h.nbytes != own or not h.flags["C_CONTIGUOUS"]:
+            raise ValueError(f"host slabs must be contiguous {own}-byte arrays of the owned rows")
+    comp = torch.cuda.current_stream()
+    up, dn = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_up = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_dn = [torch.cuda.Event() for _ in range(2)]
+    for k in range(steps):
+        j, h, e = jobs[k % 2], hosts[k % 2], k % 2
+        if k >= 2:
+            up.wait_event(ev_dn[e])  # the download of run k-2 used this host array and slot
+        call("spmdb200_memcpy_async", c_p(j._u.ptr + off), c_p(h.ctypes.data), ctypes.c_size_t(own),
+             c_p(up.cuda_stream))
+        ev_up[e].record(up)
+        comp.wait_event(ev_up[e])
+        j.run(sweeps, check=False)
+        ev_comp[e].record(comp)
+        dn.wait_event(ev_comp[e])
+        call("spmdb200_memcpy_async", c_p(h.ctypes.data), c_p(j._u.ptr + off), ctypes.c_size_t(own),
+             c_p(dn.cuda_stream))
+        ev_dn[e].record(dn)
+    for s_ in (up, comp, dn):
+        s_.synchronize()
+    for j in jobs:
+        j.check()
+
+
+def e2e_measure(job: _SlabJob, sweeps: int, steps: int = 3, reps: int = 2) -> dict:
+    """Whole-job end-to-end rate with pinned host slabs, every copy inside the
+    timed region, wall clock, max over ranks.  Row slabs: `steps` host slabs
+    per rank through run_host_pipelined (a twin job is the second device
+    slot).  z-slabs: SlabJacobi3D.run_host, whose copies do not overlap."""
     import time
 
     import torch
     d = _dist()
+    cells = job.G * job.cols * (job.H if isinstance(job, SlabJacobi3D) else 1)
+    if isinstance(job, SlabJacobi2D):
+        twin = SlabJacobi2D(cols=job.cols, G=job.G, seed=4, res_every=job.res_every)
+        hosts = [torch.empty((job.rows,) + job.unit_shape, dtype=torch.float32, pin_memory=True).numpy()
+                 for _ in range(2)]
+        own = job.rows * job.unit_floats * 4
+        for h in hosts:  # input: the job's current owned rows
+            call("spmdb200_memcpy", c_p(h.ctypes.data), c_p(job._u.ptr + job.halo * job.unit_floats * 4),
+                 ctypes.c_size_t(own), None)
+        run_host_pipelined([job, twin], hosts, 2, 2)  # warm-up: both slots, copies and launches
+        rendezvous()
+        t0 = time.perf_counter()
+        run_host_pipelined([job, twin], hosts, sweeps, steps)
+        secs = time.perf_counter() - t0
+        twin.close()
+        t = torch.tensor([secs], dtype=torch.float64, device="cuda")
+        if d is not None and job.world > 1:
+            d.all_reduce(t, op=d.ReduceOp.MAX)
+        secs = float(t.item())
+        return {"value": round(steps * cells * sweeps / secs / 1e9, 3), "unit": "Gcell-updates/s",
+                "h2d_bytes_per_step": own, "d2h_bytes_per_step": own,
+                "entry": f"slab.run_host_pipelined: {steps} pinned host slabs per rank (owned rows), two device "
+                         "slots, uploads and downloads overlapping the sweeps, wall clock"}
     host = torch.empty((job.local_rows,) + job.unit_shape, dtype=torch.float32, pin_memory=True)
     arr = host.numpy()
     arr[:] = 0.0
@@ -419,7 +498,6 @@ def e2e_measure(job: _SlabJob, sweeps: int, reps: int = 2) -> dict:
     if d is not None and job.world > 1:
         d.all_reduce(t, op=d.ReduceOp.MAX)
     secs = float(t.item())
-    cells = job.G * job.cols * (job.H if isinstance(job, SlabJacobi3D) else 1)
     return {"value": round(cells * sweeps / secs / 1e9, 3), "unit": "Gcell-updates/s",
             "h2d_bytes_per_step": job.local_rows * job.unit_floats * 4,
             "d2h_bytes_per_step": job.rows * job.unit_floats * 4,

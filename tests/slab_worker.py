@@ -31,7 +31,7 @@ def main() -> None:
     rank = dist.get_rank()
     ok = True
     for (G, W, sweeps, res_every) in [(514, 1000, 13, 3), (67, 130, 8, 1), (4096, 4096, 20, 10),
-                                      (9, 300, 9, 1)]:  # 5 and 4 rows: a rank owns exactly one halo's depth
+                                      (17, 300, 9, 1), (16, 260, 21, 0)]:  # 9+8 / 8+8 rows: a rank owns one halo's depth
         u0 = jacobi_init((G, W), 4)
         job = slab.SlabJacobi2D(cols=W, G=G, res_every=res_every, init=u0)
         job.run(sweeps)
@@ -95,10 +95,11 @@ def main() -> None:
     if rank == 0:
         print(f"sharded axpy bit-exact on every rank={bool(flag_axpy.item())}", flush=True)
         ok = ok and bool(flag_axpy.item())
-    # Back-to-back launches: a launch's last pass still delivers halo rows into
-    # the neighbour after that neighbour's kernel may have ended, so each run
-    # (and each host-buffer run, which overwrites the slab) must wait for every
-    # rank's previous launch before clearing counters or writing the slab.
+    # Back-to-back launches with no host synchronisation between them: each
+    # kernel waits on the neighbours' monotonic delivery counters (this run's
+    # input rows come first), so a rank may start its next run while a
+    # neighbour's previous one is still delivering.  Host-buffer runs, which
+    # overwrite the slab, wait for every rank's previous launch first.
     G, W = 2048, 4096
     u0 = jacobi_init((G, W), 5)
     job = slab.SlabJacobi2D(cols=W, G=G, res_every=0, init=u0)

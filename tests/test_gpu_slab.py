@@ -130,7 +130,8 @@ def test_peer_wait_runs_out_and_reports_timeout(kernels):
         st = lib.spmdb200_jacobi2d_slab(*d(u), *d(v), c_i(rows), c_i(2 * rows), c_i(3), c_i(0), None,
                                         c_p(ws.data_ptr()), c_p(fake_u.data_ptr()), c_p(fake_v.data_ptr()),
                                         c_p(fake_ws.data_ptr()), c_i(rows), None, None, None, ctypes.c_int(1),
-                                        ctypes.c_int(2), (c_p * 2)(c_p(fake_ws.data_ptr()), c_p(ws.data_ptr())), s)
+                                        ctypes.c_int(2), (c_p * 2)(c_p(fake_ws.data_ptr()), c_p(ws.data_ptr())),
+                                        ctypes.byref(ctypes.c_int64(0)), s)
         assert st == 0, lib.spmdb200_last_error_message()
         st = lib.spmdb200_workspace_status(c_p(ws.data_ptr()), s)
         assert st == -3, "the unsatisfiable peer wait must end in SPMDB200_ERR_TIMEOUT"
@@ -170,7 +171,8 @@ def test_zslab_peer_wait_runs_out_and_reports_timeout(kernels):
                                         c_p(ws.data_ptr()), None, None, None, c_i(0),
                                         c_p(fake_u.data_ptr()), c_p(fake_v.data_ptr()), c_p(fake_ws.data_ptr()),
                                         ctypes.c_int(0), ctypes.c_int(2),
-                                        (c_p * 2)(c_p(ws.data_ptr()), c_p(fake_ws.data_ptr())), s)
+                                        (c_p * 2)(c_p(ws.data_ptr()), c_p(fake_ws.data_ptr())),
+                                        ctypes.byref(ctypes.c_int64(0)), s)
         assert st == 0, lib.spmdb200_last_error_message()
         st = lib.spmdb200_workspace_status(c_p(ws.data_ptr()), s)
         assert st == -3, "the unsatisfiable peer wait must end in SPMDB200_ERR_TIMEOUT"

@@ -77,20 +77,33 @@ J2_CASES = [
     (33, 33, 4, 2, None),    # 132-byte rows: per-sweep path
     (1, 1, 1, 1, 4),
     (64, 1024, 11, 1, None),
-    # grids with interior tiles (the straight-line path) for every pass kind:
-    # four-sweep, two-sweep and single-sweep passes, residuals landing in each
+    # grids with interior tiles (the unmasked path) for every pass kind:
+    # passes no longer than the residual interval, so residual intervals of
+    # 1-5 give single-, two- and four-sweep passes, residuals landing in each
     (300, 1000, 7, 3, None),
     (200, 700, 9, 1, 704),
     (260, 1100, 6, 2, None),
     (333, 777, 12, 4, 780),
     (520, 1300, 17, 3, None),
     (130, 245, 16, 5, 248),
-    # tiny grids through four-sweep passes: boxes reach far past every edge
+    # tiny grids through multi-sweep passes: boxes reach far past every edge
     (5, 9, 8, 1, 12),
     (3, 3, 9, 1, 4),
     (1, 5, 8, 2, 8),
     (2, 130, 16, 4, None),
     (41, 121, 13, 13, 124),
+    (2, 130, 24, 8, None),
+    (6, 7, 17, 0, 8),
+    # eight-sweep passes (residual interval >= 8 or none): interior and edge
+    # tiles, the residual on every sweep position of a pass, eight-, four-,
+    # two- and single-sweep passes in one run
+    (300, 1000, 17, 8, None),
+    (520, 1300, 40, 10, None),
+    (260, 1100, 16, 0, 1104),
+    (700, 2100, 31, 0, None),
+    (333, 777, 65, 13, 780),
+    (41, 121, 33, 16, 124),
+    (1024, 4096, 80, 9, None),
 ]
 
 

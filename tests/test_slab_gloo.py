@@ -1,12 +1,12 @@
 """Host logic of the multi-GPU row-slab Jacobi-2D, on CPU ranks (gloo).
 
 * partition / neighbours / local_row_range cover every global row exactly once;
-* the slab protocol (passes of one, two or four sweeps over a (rows+8)-row
-  local array -- sweep f of an F-sweep pass also re-sweeps F-1-f halo rows on
-  each side --, the first/last four owned rows handed to the neighbours' halo
-  rows after each pass, the residual all-gathered and summed in rank order) reproduces
-  the single-domain oracle bit for bit -- the oracle does each rank's sweeps,
-  gloo carries the halos;
+* the slab protocol (passes of one, two, four or eight sweeps over a
+  (rows+16)-row local array -- sweep f of an F-sweep pass also re-sweeps
+  F-1-f halo rows on each side --, the first/last eight owned rows handed to
+  the neighbours' halo rows after each pass, the residual all-gathered and
+  summed in rank order) reproduces the single-domain oracle bit for bit -- the
+  oracle does each rank's sweeps, gloo carries the halos;
 * a rank that never reaches the rendezvous makes the other rank fail there
   (process-group timeout) instead of proceeding to a launch.
 """
@@ -49,13 +49,19 @@ def test_partition_covers_rows_once():
         slab.partition(3, 4, 0)
 
 
-def _pass_plan(sweeps: int) -> list[int]:
-    """Sweeps per pass as the C library schedules them: an even number of
-    four-sweep passes, an even number of two-sweep passes, then the 0-3 sweeps
-    left over one per pass."""
-    four = (sweeps // 8) * 2
-    two = ((sweeps - 4 * four) // 4) * 2
-    return [4] * four + [2] * two + [1] * (sweeps - 4 * four - 2 * two)
+def _pass_plan(sweeps: int, res_every: int) -> list[int]:
+    """Sweeps per pass as the C library schedules them: even numbers of
+    eight-, four- and two-sweep passes (none longer than the residual
+    interval), then the single sweep left over."""
+    fmax = 8
+    while res_every > 0 and fmax > res_every:
+        fmax //= 2
+    plan, left = [], sweeps
+    for f in (8, 4, 2, 1):
+        n = 0 if f > fmax else left if f == 1 else (left // (2 * f)) * 2
+        plan += [f] * n
+        left -= n * f
+    return plan
 
 
 def _slab_worker(rank: int, world: int, port: int, G: int, W: int, sweeps: int, res_every: int, q):
@@ -78,7 +84,7 @@ def _slab_worker(rank: int, world: int, port: int, G: int, W: int, sweeps: int, 
     up, dn = slab.neighbours(G, world, rank)
     res = []
     k = 0
-    for pno, F in enumerate(_pass_plan(sweeps)):
+    for pno, F in enumerate(_pass_plan(sweeps, res_every)):
         # Sweep f of an F-sweep pass also sweeps F-1-f halo rows beyond each
         # edge (the later sweeps of the owned edge rows read them).
         for f in range(F):
@@ -123,20 +129,21 @@ def _slab_worker(rank: int, world: int, port: int, G: int, W: int, sweeps: int, 
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,G,W,sweeps", [(2, 37, 29, 7), (3, 64, 17, 5), (2, 8, 8, 3), (2, 37, 29, 12),
-                                               (4, 41, 13, 9), (2, 50, 21, 22), (3, 40, 9, 17)])
-def test_slab_protocol_matches_single_domain_oracle(oracle_mod, world, G, W, sweeps):
+@pytest.mark.parametrize("world,G,W,sweeps,res_every", [(2, 37, 29, 7, 1), (3, 64, 17, 5, 2), (2, 16, 8, 3, 1),
+                                                         (2, 37, 29, 20, 10), (4, 41, 13, 19, 8),
+                                                         (2, 50, 21, 22, 0), (3, 40, 9, 17, 4)])
+def test_slab_protocol_matches_single_domain_oracle(oracle_mod, world, G, W, sweeps, res_every):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_slab_worker, args=(r, world, port, G, W, sweeps, 1, q)) for r in range(world)]
+    ps = [ctx.Process(target=_slab_worker, args=(r, world, port, G, W, sweeps, res_every, q)) for r in range(world)]
     for p in ps:
         p.start()
     grid, res = q.get(timeout=120)
     for p in ps:
         p.join(timeout=60)
         assert p.exitcode == 0
-    want, wres = oracle_mod.jacobi2d(jacobi_init((G, W), 4), sweeps, 1)
+    want, wres = oracle_mod.jacobi2d(jacobi_init((G, W), 4), sweeps, res_every)
     assert np.array_equal(grid.view(np.uint32), want.view(np.uint32))
     np.testing.assert_allclose(res, wres, rtol=1e-12)
 
