@@ -60,8 +60,21 @@ namespace spmdb200 {
 namespace {
 
 constexpr int kPartialSlots = kJacobiPartialSlots;  // >= 2 x the residuals one pass can produce
-constexpr int WV_WARPS = 8;
-constexpr int WV_THREADS = 32 * WV_WARPS;
+// Warps per CTA and resident CTAs per SM, per pass depth: the register
+// windows of an eight-sweep pass need more registers than 2 x 8 warps leave
+// (65,536 / 512 = 128 per thread).
+#ifndef WV_WARPS_DEEP
+#define WV_WARPS_DEEP 8
+#endif
+#ifndef WV_MINB_DEEP
+#define WV_MINB_DEEP 2
+#endif
+template <int F>
+struct WvLaunch {
+  static constexpr int WARPS = F > 4 ? WV_WARPS_DEEP : 8;
+  static constexpr int MINB = F > 4 ? WV_MINB_DEEP : 2;
+  static constexpr int THREADS = 32 * WARPS;
+};
 constexpr int WV_U = 6;         // unroll of the row loop (the register windows rotate with period 3)
 constexpr int WV_D = 2 * WV_U;  // ring rows per warp
 constexpr int WV_ROW = 512;     // bytes of one ring row (128 floats)
@@ -78,10 +91,11 @@ struct Wv {
   static_assert(F >= 1 && F <= kMaxWaveF, "1..8 sweeps per pass");
 };
 
+template <int NW>
 struct WvSmem {
-  alignas(128) unsigned char ring[WV_WARPS][WV_D][WV_ROW];
-  double racc[WV_WARPS][32];  // per-lane residual sums of the current pass
-  double wsum[WV_WARPS];
+  alignas(128) unsigned char ring[NW][WV_D][WV_ROW];
+  double racc[NW][32];  // per-lane residual sums of the current pass
+  double wsum[NW];
   int abort;
 };
 
@@ -465,24 +479,21 @@ __device__ __forceinline__ void deliver_input_halo(const J2Kernel &k, int gw, in
   }
 }
 
-// Resident CTAs per SM the register budget is sized for (8 warps each):
-// measured at 32768^2, two CTAs (128 registers, no spills in the interior
-// loop) beat three (80 registers, spills) by 11 % with four-sweep passes.
-#ifndef WV_MINB
-#define WV_MINB 2
-#endif
-
+// Two CTAs of 8 warps per SM (128 registers, no spills in the interior loop)
+// beat three (80 registers, spills) by 11 % at 32768^2 with four-sweep passes.
 template <int F>
-__global__ void __launch_bounds__(WV_THREADS, WV_MINB) jacobi2d_wave_kernel(const __grid_constant__ J2Kernel k) {
+__global__ void __launch_bounds__(WvLaunch<F>::THREADS, WvLaunch<F>::MINB)
+    jacobi2d_wave_kernel(const __grid_constant__ J2Kernel k) {
+  constexpr int NW = WvLaunch<F>::WARPS;
   extern __shared__ __align__(128) unsigned char wv_smem_raw[];
-  WvSmem &sm = *reinterpret_cast<WvSmem *>(wv_smem_raw);
+  WvSmem<NW> &sm = *reinterpret_cast<WvSmem<NW> *>(wv_smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) sm.abort = 0;
   __syncthreads();
   volatile int *abort = &sm.abort;
   const int G = gridDim.x;
-  const int GW = G * WV_WARPS;
-  const int gw = blockIdx.x * WV_WARPS + warp;  // a CTA takes neighbouring tiles: adjacent row segments
+  const int GW = G * NW;
+  const int gw = blockIdx.x * NW + warp;  // a CTA takes neighbouring tiles: adjacent row segments
   const int T = k.tiles_x * k.tiles_y;
   const bool slab = k.halo > 0;
   const unsigned per_pass = (unsigned)k.tiles_x * (unsigned)k.halo;
@@ -556,7 +567,7 @@ __global__ void __launch_bounds__(WV_THREADS, WV_MINB) jacobi2d_wave_kernel(cons
     if (threadIdx.x == 0) {
       if (any) {
         double tot = 0.0;
-        for (int i = 0; i < WV_WARPS; ++i) tot = __dadd_rn(tot, sm.wsum[i]);
+        for (int i = 0; i < NW; ++i) tot = __dadd_rn(tot, sm.wsum[i]);
         k.ws->partial[sweep_residual<F>(k, p, rl + 1) % kPartialSlots][blockIdx.x] = tot;
       }
       __threadfence();
@@ -664,30 +675,31 @@ cudaError_t launch_wave(const Jacobi2dProblem &p, const SlabPeers &peers, int64_
   k.init_halo = init_halo;
   k.flag_base = flag_base;
 
+  using L = WvLaunch<F>;
+  constexpr size_t smem = sizeof(WvSmem<L::WARPS>);
   int dev = 0;
   cudaGetDevice(&dev);
   static thread_local int configured_dev = -1;
   cudaError_t e;
   if (configured_dev != dev) {
-    e = cudaFuncSetAttribute(jacobi2d_wave_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(WvSmem));
+    e = cudaFuncSetAttribute(jacobi2d_wave_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, jacobi2d_wave_kernel<F>, WV_THREADS, sizeof(WvSmem));
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, jacobi2d_wave_kernel<F>, L::THREADS, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   long long g = (long long)per_sm * num_sms(dev);
   const long long tiles = (long long)k.tiles_x * k.tiles_y;
-  const long long want = (tiles + WV_WARPS - 1) / WV_WARPS;
+  const long long want = (tiles + L::WARPS - 1) / L::WARPS;
   if (g > want) g = want;
   if (g > kMaxCtas) g = kMaxCtas;
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)g);
-  cfg.blockDim = dim3(WV_THREADS);
-  cfg.dynamicSmemBytes = sizeof(WvSmem);
+  cfg.blockDim = dim3(L::THREADS);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;

@@ -50,7 +50,10 @@ __device__ __forceinline__ bool group_slice(int64_t total, int64_t &c0, int64_t 
   return c0 < c1;
 }
 
-// f64 sum of a[c0..c1) (stride sa) by this block's threads; valid in thread 0.
+// f64 sum of a[c0..c1) (stride sa) by this block's threads; valid in thread
+// 0.  Rounds of kVec 16-byte loads per thread, all issued before any is
+// added, so a working block keeps kVec x 16 B x blockDim bytes in flight.
+constexpr int kVec = 4;
 __device__ __forceinline__ double block_slice_sum(const float *a, int64_t sa, int64_t c0, int64_t c1, double *sh) {
   const int64_t T = blockDim.x;
   double acc0 = 0.0, acc1 = 0.0;
@@ -58,25 +61,20 @@ __device__ __forceinline__ double block_slice_sum(const float *a, int64_t sa, in
   const int64_t n = c1 - c0;
   if (sa == 1 && ((uintptr_t)p & 15u) == 0) {
     const int64_t n4 = n >> 2;
-    int64_t i = threadIdx.x;
-    for (; i + T < n4; i += 2 * T) {
-      const float4 v0 = spmdb200::ld_stream_f4(p + 4 * i);
-      const float4 v1 = spmdb200::ld_stream_f4(p + 4 * (i + T));
-      acc0 = __dadd_rn(acc0, (double)v0.x);
-      acc1 = __dadd_rn(acc1, (double)v1.x);
-      acc0 = __dadd_rn(acc0, (double)v0.y);
-      acc1 = __dadd_rn(acc1, (double)v1.y);
-      acc0 = __dadd_rn(acc0, (double)v0.z);
-      acc1 = __dadd_rn(acc1, (double)v1.z);
-      acc0 = __dadd_rn(acc0, (double)v0.w);
-      acc1 = __dadd_rn(acc1, (double)v1.w);
-    }
-    if (i < n4) {
-      const float4 v0 = spmdb200::ld_stream_f4(p + 4 * i);
-      acc0 = __dadd_rn(acc0, (double)v0.x);
-      acc0 = __dadd_rn(acc0, (double)v0.y);
-      acc0 = __dadd_rn(acc0, (double)v0.z);
-      acc0 = __dadd_rn(acc0, (double)v0.w);
+    for (int64_t base = 0; base < n4; base += kVec * T) {
+      float4 v[kVec];
+#pragma unroll
+      for (int r = 0; r < kVec; ++r) {
+        const int64_t i = base + threadIdx.x + r * T;
+        v[r] = i < n4 ? spmdb200::ld_stream_f4(p + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int r = 0; r < kVec; ++r) {
+        acc0 = __dadd_rn(acc0, (double)v[r].x);
+        acc1 = __dadd_rn(acc1, (double)v[r].y);
+        acc0 = __dadd_rn(acc0, (double)v[r].z);
+        acc1 = __dadd_rn(acc1, (double)v[r].w);
+      }
     }
     const int64_t t = (n4 << 2) + threadIdx.x;
     if (t < n) acc1 = __dadd_rn(acc1, (double)p[t]);
@@ -86,8 +84,14 @@ __device__ __forceinline__ double block_slice_sum(const float *a, int64_t sa, in
   return spmdb200::block_sum_f64(__dadd_rn(acc0, acc1), sh);
 }
 
-constexpr int kSumGroup = 16;     // blocks pooled per working block of the sums
-constexpr int kStencilGroup = 4;  // ... of the promoted stencil
+#ifndef SPMDB200_SUM_GROUP
+#define SPMDB200_SUM_GROUP 16
+#endif
+#ifndef SPMDB200_STENCIL_GROUP
+#define SPMDB200_STENCIL_GROUP 8
+#endif
+constexpr int kSumGroup = SPMDB200_SUM_GROUP;          // blocks pooled per working block of the sums
+constexpr int kStencilGroup = SPMDB200_STENCIL_GROUP;  // ... of the promoted stencil
 
 __device__ __forceinline__ float ld_a(const float *a, long long n0, long long n1, long long s0, long long s1,
                                       long long i, long long j) {
@@ -114,20 +118,34 @@ __device__ __forceinline__ void promoted_stencil_body(const float *A, long long 
     const float *a0 = A + i * A_s0;
     float *b0 = B + i * B_s0;
     const bool fast = c1 >= 0 && i + c1 < A_n0 && j0 + len + c1 <= A_n1;  // every read inside A
-#pragma unroll 4
-    for (long long jj = threadIdx.x; jj < len; jj += blockDim.x) {
-      const long long j = j0 + jj;
-      float x, e, s;
-      if (fast) {
-        x = a0[j * A_s1];
-        e = a0[(j + c1) * A_s1];
-        s = a0[c1 * A_s0 + j * A_s1];
-      } else {
-        x = ld_a(A, A_n0, A_n1, A_s0, A_s1, i, j);
-        e = ld_a(A, A_n0, A_n1, A_s0, A_s1, i, j + c1);
-        s = ld_a(A, A_n0, A_n1, A_s0, A_s1, i + c1, j);
+    // Rounds of kCells cells per thread: every load of a round is issued
+    // before the first add, so a working block keeps ~kCells x 12 B per
+    // thread in flight instead of one round trip per cell.
+    constexpr int kCells = 4;
+    const long long T = blockDim.x;
+    for (long long base = 0; base < len; base += kCells * T) {
+      float x[kCells], e[kCells], s[kCells];
+#pragma unroll
+      for (int r = 0; r < kCells; ++r) {
+        const long long jj = base + threadIdx.x + r * T;
+        const long long j = j0 + jj;
+        if (jj >= len) {
+          x[r] = e[r] = s[r] = 0.0f;
+        } else if (fast) {
+          x[r] = a0[j * A_s1];
+          e[r] = a0[(j + c1) * A_s1];
+          s[r] = a0[c1 * A_s0 + j * A_s1];
+        } else {
+          x[r] = ld_a(A, A_n0, A_n1, A_s0, A_s1, i, j);
+          e[r] = ld_a(A, A_n0, A_n1, A_s0, A_s1, i, j + c1);
+          s[r] = ld_a(A, A_n0, A_n1, A_s0, A_s1, i + c1, j);
+        }
       }
-      b0[j * B_s1] = __fadd_rn(__fadd_rn(x, e), s);
+#pragma unroll
+      for (int r = 0; r < kCells; ++r) {
+        const long long jj = base + threadIdx.x + r * T;
+        if (jj < len) b0[(j0 + jj) * B_s1] = __fadd_rn(__fadd_rn(x[r], e[r]), s[r]);
+      }
     }
     c0 += len;
   }
