@@ -36,7 +36,9 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 // L2 prefetch of the first kBulkStages chunks of [u_lo, u_hi).  A prefetch
 // returns no data, so it may run before griddepcontrol.wait: lines that the
 // previous kernel still writes are updated in L2, the point of coherence, and
-// the stage loads after the wait read them from there.
+// the stage loads after the wait read them from there.  (Prefetching a whole
+// 64 MiB input into L2 at kernel start measured slower: 2^24 f32 single
+// launch 21.5 against 19.5 us.)
 __device__ __forceinline__ void bulk_prefetch_head(const uint4 *base, int64_t u_lo, int64_t u_hi) {
   constexpr int kUnits = kBulkChunk / 16;
   for (int s = 0; s < kBulkStages; ++s) {
@@ -99,7 +101,7 @@ __device__ __forceinline__ bool bulk_stream(const uint4 *base, int64_t u_lo, int
 }
 
 // Block partials of the staged reductions travel as one 64-bit word each.
-// An f64 partial is stored as its bits XOR a signalling-NaN key: the f64 bits XOR a signalling-NaN key.  Every partial is the result of
+// An f64 partial is stored as its bits XOR a signalling-NaN key.  Every partial is the result of
 // __dadd_rn (a number or the canonical quiet NaN), never the key itself, so a
 // stored word is never 0 and 0 means "not written yet".  One word carries the
 // value and its presence, so the writer needs no fence and the combiner no
