@@ -59,6 +59,7 @@ GRID = 32768
 SWEEPS = 1000
 RES_EVERY = 10
 BYTES_PER_CELL_PASS = 8  # algorithmic: each pass reads u[i,j] once and writes v[i,j] once
+J3_FMAX = 2  # longest Jacobi-3D pass (sweeps), = the 3-D z-slab halo depth the library reports
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) per cell update of the dominant Jacobi-2D kernel,
 # measured by ncu on a 16384^2 grid with 8-sweep passes (the benchmark grid is
@@ -72,7 +73,7 @@ def sweep_passes(sweeps: int, res_every: int, fmax: int = 8) -> dict[int, int]:
     """{sweeps per pass: passes} as the Jacobi kernels schedule them: even
     numbers of 8- (2-D only), 4- and 2-sweep passes (none longer than the
     residual interval), then the single sweeps left over.  fmax: 8 for the
-    2-D kernel, 4 for the 3-D one."""
+    2-D kernel, J3_FMAX for the 3-D one."""
     top = fmax
     while res_every > 0 and fmax > res_every:
         fmax //= 2
@@ -487,8 +488,8 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
     kernels.workspace_status(jws)
     gc = 512 ** 3 * 50 / ms / 1e6
     out["jacobi3d_512^3_x50"] = {"ms": round(ms, 3), "Gcell/s": round(gc, 1),
-                                 "passes": sweep_passes(50, 10, 4),
-                                 "frac_of_hbm": round(gc * bytes_per_update(50, 10, 4) / hbm_peak, 3)}
+                                 "passes": sweep_passes(50, 10, J3_FMAX),
+                                 "frac_of_hbm": round(gc * bytes_per_update(50, 10, J3_FMAX) / hbm_peak, 3)}
     del u, v, flush
     torch.cuda.empty_cache()
     out.update(refabi_benchmarks(torch, hbm_peak))
@@ -687,6 +688,9 @@ def run_spmd_arm(args) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     kernels = importlib.import_module("spmd-dialect_b200.kernels")
+    halo3 = int(importlib.import_module("spmd-dialect_b200._lib").lib().spmdb200_jacobi_slab_halo(3))
+    if halo3 != J3_FMAX:
+        raise RuntimeError(f"the library's 3-D passes are up to {halo3} sweeps, bench.py assumes {J3_FMAX}")
     slab = importlib.import_module("spmd-dialect_b200.slab") if world > 1 else None
     shard = importlib.import_module("spmd-dialect_b200.shard") if world > 1 else None
     hbm_peak, peak_kind = measured_peaks()

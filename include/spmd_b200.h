@@ -347,17 +347,17 @@ int spmdb200_jacobi2d_slab(float *U_base, float *U_aligned, int64_t U_offset, in
                            int rank, int nranks, void *const *all_ws, int64_t *deliveries, void *stream);
 /* Jacobi-3D over z-slabs on several GPUs (one process per GPU).  No reference
  * counterpart.  The global grid has D planes of H x W; this rank owns global
- * planes [z_first, z_first + Z), Z >= 1.  U and V are (Z + 2) x H x W local
- * arrays (descriptor sizes (Z+2, H, W), x contiguous, 16-byte aligned rows and
- * planes): local plane 0 is the halo plane above (global z_first - 1), planes
- * 1..Z are owned, plane Z+1 is the halo plane below.  The kernel stores its
- * first / last owned plane straight into the neighbour's halo plane over
- * NVLink every sweep; up_planes is the number of planes the neighbour above
- * owns (our first owned plane lands in its local plane up_planes + 1).  All
- * ranks' arrays share H, W and the row and plane strides.  The halo planes
- * of U must hold the neighbours' planes on the first run (this kernel does
- * not deliver its input; later runs find the planes the previous run
- * delivered).  Neighbour, workspace, delivery-count, residual and ping-pong
+ * planes [z_first, z_first + Z), Z >= 2.  U and V are (Z + 4) x H x W local
+ * arrays (descriptor sizes (Z+4, H, W), x contiguous, 16-byte aligned rows and
+ * planes): local planes 0..1 are the halo planes above (global z_first - 2 ..
+ * z_first - 1), planes 2..Z+1 are owned, planes Z+2..Z+3 are the halo planes
+ * below.  A run advances up to two sweeps per pass; the kernel stores the
+ * first / last owned planes of each pass straight into the neighbour's halo
+ * planes over NVLink, and before its first pass it delivers its input's edge
+ * planes the same way.  up_planes is the number of planes the neighbour
+ * above owns (>= 2; our first owned plane lands in its local plane
+ * up_planes + 2).  All ranks' arrays share H, W and the row and plane
+ * strides.  Neighbour, workspace, delivery-count, residual and ping-pong
  * semantics are those of spmdb200_jacobi2d_slab
  * (spmdb200_jacobi2d_slab_residuals reads the all-gathered residuals);
  * global planes 0 and D-1, rows 0 and H-1 and columns 0 and W-1 are fixed. */
@@ -370,7 +370,7 @@ int spmdb200_jacobi3d_slab(float *U_base, float *U_aligned, int64_t U_offset, in
                            float *dn_u, float *dn_v, void *dn_ws,
                            int rank, int nranks, void *const *all_ws, int64_t *deliveries, void *stream);
 /* Halo depth of the slab layouts: rows on each side of a Jacobi-2D row slab
- * (dims == 2: 8) or planes on each side of a Jacobi-3D z-slab (dims == 3: 1);
+ * (dims == 2: 8) or planes on each side of a Jacobi-3D z-slab (dims == 3: 2);
  * -1 for other dims.  No reference counterpart. */
 int spmdb200_jacobi_slab_halo(int dims);
 /* Clears the 256-byte header of a Jacobi workspace on `stream`. */

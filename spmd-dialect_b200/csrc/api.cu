@@ -565,8 +565,7 @@ int spmdb200_jacobi3d(float *U_base, float *U, int64_t U_off, int64_t U_n0, int6
   p.res_out = res_out;
   p.ws = w;
   if (jacobi3d_tma_ok(p)) {
-    int grid = 0;
-    CUDA_TRY(launch_jacobi3d_persistent(p, SlabPeers{}, s, &grid));
+    CUDA_TRY(run_jacobi3d_tb(p, SlabPeers{}, 0u, s));
   } else {
     CUDA_TRY(launch_jacobi3d_generic(p, s));
   }
@@ -667,9 +666,9 @@ int spmdb200_jacobi3d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   if (U_n0 != V_n0 || U_n1 != V_n1 || U_n2 != V_n2 || U_s0 != V_s0 || U_s1 != V_s1 || U_s2 != V_s2)
     return fail(SPMDB200_ERR_INVALID_ARG, "U and V must have identical sizes and strides");
   const int64_t H = kSlabHalo3;
-  if (U_n0 < 1 + 2 * H || U_n1 < 1 || U_n2 < 1)
-    return fail(SPMDB200_ERR_INVALID_ARG, "a z-slab needs >= 1 owned plane plus %lld halo plane(s) on each side",
-                (long long)H);
+  if (U_n0 < 3 * H || U_n1 < 1 || U_n2 < 1)
+    return fail(SPMDB200_ERR_INVALID_ARG, "a z-slab needs >= %lld owned planes plus %lld halo planes on each side",
+                (long long)H, (long long)H);
   const int64_t Z = U_n0 - 2 * H;
   if (z_first < 0 || D < 1 || z_first + Z > D)
     return fail(SPMDB200_ERR_INVALID_ARG, "owned planes [%lld, %lld) outside the %lld global planes",
@@ -680,9 +679,9 @@ int spmdb200_jacobi3d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
     return fail(SPMDB200_ERR_INVALID_ARG, "neighbour pointers must be given exactly where a neighbour exists");
   if ((up_u && (!up_v || !up_ws)) || (dn_u && (!dn_v || !dn_ws)))
     return fail(SPMDB200_ERR_INVALID_ARG, "incomplete neighbour (U, V, workspace)");
-  if (up_u && (up_planes < 1 || up_planes > z_first))
-    return fail(SPMDB200_ERR_INVALID_ARG, "neighbour above owns %lld planes: must be in [1, %lld]",
-                (long long)up_planes, (long long)z_first);
+  if (up_u && (up_planes < H || up_planes > z_first))
+    return fail(SPMDB200_ERR_INVALID_ARG, "neighbour above owns %lld planes: must be in [%lld, %lld]",
+                (long long)up_planes, (long long)H, (long long)z_first);
   if (nranks > 1 && !all_ws) return fail(SPMDB200_ERR_INVALID_ARG, "all_ws is required for nranks > 1");
   if (sweeps < 0 || res_every < 0) return fail(SPMDB200_ERR_INVALID_ARG, "negative sweeps / res_every");
   if (res_every > 0 && sweeps / res_every > kMaxResSlots)
@@ -715,8 +714,11 @@ int spmdb200_jacobi3d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
   peers.up_v = up_v;
   peers.dn_u = dn_u;
   peers.dn_v = dn_v;
-  peers.up_row = up_planes + H;  // our first owned plane is the bottom halo plane of the rank above
-  peers.dn_row = 0;              // our last owned plane is the top halo plane of the rank below
+  // plane indices: our first owned plane lands in the first bottom halo plane
+  // of the rank above; our last H owned planes land in the top halo planes
+  // [0, H) of the rank below
+  peers.up_row = up_planes + H;
+  peers.dn_row = 0;
   peers.up_flag = up_ws ? &static_cast<JacobiWs *>(up_ws)->from_below : nullptr;
   peers.dn_flag = dn_ws ? &static_cast<JacobiWs *>(dn_ws)->from_above : nullptr;
   peers.rank = rank;
@@ -725,12 +727,10 @@ int spmdb200_jacobi3d_slab(float *U_base, float *U, int64_t U_off, int64_t U_n0,
     peers.peer_ws[q] = static_cast<JacobiWs *>(all_ws ? all_ws[q] : (q == rank ? ws : nullptr));
   if (!peers.peer_ws[rank]) peers.peer_ws[rank] = static_cast<JacobiWs *>(ws);
   if (!deliveries) return fail(SPMDB200_ERR_INVALID_ARG, "deliveries (the halo-delivery count) is required");
-  int grid = 0;
-  // Fresh grid barrier for this launch (stream-ordered); the status word and
-  // the delivery counters carry over.
-  CUDA_TRY(cudaMemsetAsync(&p.ws->barrier, 0, sizeof(unsigned), (cudaStream_t)stream));
-  CUDA_TRY(launch_jacobi3d_persistent(p, peers, (cudaStream_t)stream, &grid, (unsigned)*deliveries));
-  *deliveries += jacobi3d_slab_deliveries(sweeps, U_n1, U_n2);
+  // Each launch of the run starts from a fresh grid barrier (stream-ordered
+  // memsets); the status word and the delivery counters carry over.
+  CUDA_TRY(run_jacobi3d_tb(p, peers, (unsigned)*deliveries, (cudaStream_t)stream));
+  *deliveries += jacobi3d_slab_deliveries(sweeps, res_every, U_n1, U_n2);
   return ok();
 }
 

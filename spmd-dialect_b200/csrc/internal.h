@@ -90,7 +90,7 @@ struct Jacobi2dProblem {
 // so a pass may fuse eight sweeps.
 constexpr int kSlabHalo = 8;
 // Halo depth of the multi-GPU Jacobi-3D z-slab layout (one sweep per pass).
-constexpr int kSlabHalo3 = 1;
+constexpr int kSlabHalo3 = 2;  // the longest 3-D pass (jacobi3d_tb.cu)
 
 // The persistent (register-wavefront) path needs 16-byte aligned rows.
 bool jacobi2d_persistent_ok(const Jacobi2dProblem &p);
@@ -130,13 +130,15 @@ struct Jacobi3dProblem {
   int halo = 0;
 };
 bool jacobi3d_tma_ok(const Jacobi3dProblem &p);
-// SlabPeers.up_row / dn_row are plane indices here.  z-slab mode: flag_base =
-// halo-plane deliveries already received from each neighbour.
-cudaError_t launch_jacobi3d_persistent(const Jacobi3dProblem &p, const SlabPeers &peers, cudaStream_t s,
-                                       int *grid_out, unsigned flag_base = 0);
-// Halo-plane deliveries a z-slab run of `sweeps` sweeps makes to each neighbour.
-int64_t jacobi3d_slab_deliveries(int64_t sweeps, int64_t h, int64_t w);
 cudaError_t launch_jacobi3d_generic(const Jacobi3dProblem &p, cudaStream_t s);
+// Temporal blocking (jacobi3d_tb.cu): passes of 4, 2 and 1 sweeps (plan[0..2]
+// = pass counts; even counts of the multi-sweep passes, at most one residual
+// sweep per pass).  Needs jacobi3d_tma_ok(p).  z-slab mode (a neighbour in
+// `peers`, p.halo = kSlabHalo3): flag_base = halo deliveries already received
+// from each neighbour; a run adds jacobi3d_slab_deliveries(...) to them.
+void jacobi3d_pass_plan(int64_t sweeps, int64_t res_every, int64_t plan[3]);
+cudaError_t run_jacobi3d_tb(const Jacobi3dProblem &p, const SlabPeers &peers, unsigned flag_base, cudaStream_t s);
+int64_t jacobi3d_slab_deliveries(int64_t sweeps, int64_t res_every, int64_t h, int64_t w);
 // Seeded synthetic 3-D Jacobi input (counter hash of (seed, gz * h + y, x)).
 cudaError_t launch_fill_jacobi3d_input(float *p, int64_t sz, int64_t sy, int64_t planes, int64_t h, int64_t w,
                                        int64_t g_z0, int64_t g_d, uint64_t seed, cudaStream_t s);

@@ -62,12 +62,15 @@ namespace {
 constexpr int kPartialSlots = kJacobiPartialSlots;  // >= 2 x the residuals one pass can produce
 // Warps per CTA and resident CTAs per SM, per pass depth: the register
 // windows of an eight-sweep pass need more registers than 2 x 8 warps leave
-// (65,536 / 512 = 128 per thread).
+// (65,536 / 512 = 128 per thread).  Measured at 32768^2 x 200 (residual every
+// 10): 3 CTAs of 4 warps (168 registers) 3019-3027 Gcell/s, 2 of 6 (168)
+// 2979-2992, 2 of 8 (128, spills) 2873-2889, 1 of 8 (216, no spills)
+// 2734-2739.
 #ifndef WV_WARPS_DEEP
-#define WV_WARPS_DEEP 8
+#define WV_WARPS_DEEP 4
 #endif
 #ifndef WV_MINB_DEEP
-#define WV_MINB_DEEP 2
+#define WV_MINB_DEEP 3
 #endif
 template <int F>
 struct WvLaunch {
@@ -78,10 +81,15 @@ struct WvLaunch {
 constexpr int WV_U = 6;         // unroll of the row loop (the register windows rotate with period 3)
 constexpr int WV_D = 2 * WV_U;  // ring rows per warp
 constexpr int WV_ROW = 512;     // bytes of one ring row (128 floats)
-constexpr int WV_BH = 128;      // tile rows
+// Tile rows: chosen per launch (wave_tile_rows) between WV_BH_MIN and the
+// grid height.
+constexpr int WV_BH = 128;
+#ifndef WV_BH_MIN
+#define WV_BH_MIN 32
+#endif
 constexpr int kMaxWaveF = 8;
 static_assert(kSlabHalo >= kMaxWaveF, "slab halos must cover the deepest pass");
-static_assert(WV_BH >= kSlabHalo, "a tile row must hold a whole halo");
+static_assert(WV_BH_MIN >= kSlabHalo, "a tile row must hold a whole halo");
 
 template <int F>
 struct Wv {
@@ -103,6 +111,7 @@ struct J2Kernel {
   float *u, *v;
   long long pitch;
   int w, h_local, row_lo, row_hi, tiles_x, tiles_y, last_start;
+  int bh;  // tile rows
   long long g_row0, g_rows;
   int passes;      // passes in this launch, each advancing F sweeps
   int sweep_base;  // global index of this launch's first sweep (residual numbering)
@@ -156,8 +165,8 @@ __device__ __forceinline__ void tile_rows(const J2Kernel &k, int ty, int &r0, in
     r0 = k.last_start;
     r1 = k.row_hi;
   } else {
-    r0 = k.row_lo + ty * WV_BH;
-    r1 = min(r0 + WV_BH, k.last_start);
+    r0 = k.row_lo + ty * k.bh;
+    r1 = min(r0 + k.bh, k.last_start);
   }
 }
 
@@ -393,7 +402,7 @@ __device__ __forceinline__ unsigned wave_tile(const J2Kernel &k, const float *sr
             acc = __dadd_rn(acc, sq_diff4(o, c, gx0, w));
           } else {
             // Through the lane's shared-memory slot, so the f64 sum holds no
-            // register across rows (the deepest passes are register-bound).
+            // register across rows (two register chains measured the same).
             volatile double *ra = racc;
             *ra = acc_sq4(*ra, o, c);
           }
@@ -643,6 +652,38 @@ __global__ void __launch_bounds__(256) fill_jacobi_input_kernel(float *p, long l
   }
 }
 
+// Tile rows of a pass: warp w takes tiles w, w + warps, ...; every tile
+// streams its rows plus 2F halo rows, so a pass lasts about
+// ceil(tiles / warps) * (bh + 2F) row steps.  The height up to 128 with the
+// least of that wins: small grids get one wave of shorter tiles (4096^2:
+// 86-row tiles on all 1776 warps instead of 128-row tiles on 1120 of them,
+// 803 -> 1039 Gcell/s).  Taller tiles re-sweep fewer halo rows but lose
+// more: one wave of 5461-row tiles at 32768^2 measured 1323 against 3019
+// Gcell/s (a pass waits for its slowest tile, and the edge tiles' masked
+// path is the slow one).
+static int wave_tile_rows(int rows, int tiles_x, long long warps, int F) {
+#ifdef WV_BH_FIXED
+  return WV_BH_FIXED;
+#endif
+  const long long t128 = (long long)tiles_x * ((rows + WV_BH - 1) / WV_BH);
+  const long long n128 = (t128 + warps - 1) / warps;
+  long long best_cost = -1, best = WV_BH;
+  for (long long n = 1; n <= n128 + 1; ++n) {
+    const long long per_col = n * warps / tiles_x;
+    if (per_col < 1) continue;
+    long long bh = (rows + per_col - 1) / per_col;
+    if (bh > WV_BH) continue;
+    if (bh < WV_BH_MIN) bh = WV_BH_MIN;
+    const long long tiles = (long long)tiles_x * ((rows + bh - 1) / bh);
+    const long long cost = (tiles + warps - 1) / warps * (bh + 2 * F);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bh;
+    }
+  }
+  return (int)best;
+}
+
 template <int F>
 cudaError_t launch_wave(const Jacobi2dProblem &p, const SlabPeers &peers, int64_t passes, int64_t sweep_base,
                         unsigned flag_base, int init_halo, cudaStream_t s) {
@@ -655,12 +696,6 @@ cudaError_t launch_wave(const Jacobi2dProblem &p, const SlabPeers &peers, int64_
   k.h_local = (int)p.h_local;
   k.row_lo = (int)p.row_lo;
   k.row_hi = (int)p.row_hi;
-  const int rows = (int)(p.row_hi - p.row_lo);
-  k.tiles_x = (int)((p.w + W::TW - 1) / W::TW);
-  k.tiles_y = (rows + WV_BH - 1) / WV_BH;
-  const int rem = rows - (k.tiles_y - 1) * WV_BH;
-  k.last_start = (p.halo > 0 && k.tiles_y >= 2 && rem < p.halo) ? (int)p.row_hi - p.halo
-                                                                  : (int)p.row_lo + (k.tiles_y - 1) * WV_BH;
   k.g_row0 = p.g_row0;
   k.g_rows = p.g_rows;
   k.passes = (int)passes;
@@ -691,6 +726,13 @@ cudaError_t launch_wave(const Jacobi2dProblem &p, const SlabPeers &peers, int64_
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   long long g = (long long)per_sm * num_sms(dev);
+  const int rows = (int)(p.row_hi - p.row_lo);
+  k.tiles_x = (int)((p.w + W::TW - 1) / W::TW);
+  k.bh = wave_tile_rows(rows, k.tiles_x, g * L::WARPS, F);
+  k.tiles_y = (rows + k.bh - 1) / k.bh;
+  const int rem = rows - (k.tiles_y - 1) * k.bh;
+  k.last_start = (p.halo > 0 && k.tiles_y >= 2 && rem < p.halo) ? (int)p.row_hi - p.halo
+                                                                  : (int)p.row_lo + (k.tiles_y - 1) * k.bh;
   const long long tiles = (long long)k.tiles_x * k.tiles_y;
   const long long want = (tiles + L::WARPS - 1) / L::WARPS;
   if (g > want) g = want;

@@ -20,8 +20,9 @@ the count it has received so far and passes it to every run, so runs follow
 one another with no host synchronisation between them.
 
 Jacobi-3D: the D x H x W grid is cut into contiguous plane blocks; rank p owns
-planes [g_first, g_first + planes) plus HALO3 = 1 halo plane on each side (one
-sweep per pass, one plane up and one down per sweep).
+planes [g_first, g_first + planes) plus HALO3 = 2 halo planes on each side (up
+to two sweeps per pass, two planes up and two down per pass; each run first
+sends the edge planes of its input).
 """
 from __future__ import annotations
 
@@ -33,7 +34,7 @@ import numpy as np
 from ._lib import c_i, c_p, call, lib
 
 HALO = int(lib().spmdb200_jacobi_slab_halo(2))  # halo rows on each side of a 2-D slab (8)
-HALO3 = int(lib().spmdb200_jacobi_slab_halo(3))  # halo planes on each side of a 3-D slab (1)
+HALO3 = int(lib().spmdb200_jacobi_slab_halo(3))  # halo planes on each side of a 3-D slab (2)
 
 
 # ---------------------------------------------------------------- decomposition
@@ -344,6 +345,10 @@ class SlabJacobi2D(_SlabJob):
     def _global_unit_shape(self) -> tuple:
         return (self.cols,)
 
+    def twin(self) -> "SlabJacobi2D":
+        """A job with the same decomposition (a second device slot)."""
+        return SlabJacobi2D(cols=self.cols, G=self.G, seed=4, res_every=self.res_every)
+
     def _fill(self, ptr: int, seed: int, stream) -> None:
         call("spmdb200_fill_jacobi_input", c_p(ptr), c_i(self.pitch), c_i(self.local_rows), c_i(self.cols),
              c_i(self.g_first - self.halo), c_i(self.G), ctypes.c_uint64(seed), stream)
@@ -364,7 +369,7 @@ class SlabJacobi2D(_SlabJob):
 class SlabJacobi3D(_SlabJob):
     """This rank's share of a multi-GPU Jacobi-3D run (z-slabs,
     spmdb200_jacobi3d_slab): D x H x W global grid split into contiguous plane
-    blocks, one halo plane on each side (HALO3).  Same API as SlabJacobi2D."""
+    blocks, two halo planes on each side (HALO3).  Same API as SlabJacobi2D."""
 
     halo = HALO3
     entry = "spmdb200_jacobi3d_slab"
@@ -389,6 +394,10 @@ class SlabJacobi3D(_SlabJob):
     def _global_unit_shape(self) -> tuple:
         return (self.H, self.cols)
 
+    def twin(self) -> "SlabJacobi3D":
+        """A job with the same decomposition (a second device slot)."""
+        return SlabJacobi3D(H=self.H, W=self.cols, D=self.G, seed=3, res_every=self.res_every)
+
     def _fill(self, ptr: int, seed: int, stream) -> None:
         call("spmdb200_fill_jacobi3d_input", c_p(ptr), c_i(self.H * self.pitch), c_i(self.pitch),
              c_i(self.local_rows), c_i(self.H), c_i(self.cols), c_i(self.g_first - self.halo), c_i(self.G),
@@ -410,18 +419,19 @@ class SlabJacobi3D(_SlabJob):
 
 def run_host_pipelined(jobs: list, hosts: list, sweeps: int, steps: int) -> None:
     """`steps` runs of `sweeps` sweeps on host slabs, pipelined across two
-    device slots.  jobs: two SlabJacobi2D jobs with the same decomposition
-    (the slots); hosts: two pinned host arrays of this rank's owned rows
-    (rows x pitch, float32), used alternately -- run k reads hosts[k % 2] and
-    writes its result back there.  Uploads, sweeps and downloads run on three
+    device slots.  jobs: two slab jobs (SlabJacobi2D or SlabJacobi3D) with the
+    same decomposition (the slots); hosts: two pinned host arrays of this
+    rank's owned rows or planes, used alternately -- run k reads
+    hosts[k % 2] and writes its result back there.  Uploads, sweeps and downloads run on three
     streams, so run k's sweeps overlap the download of run k-1 and the upload
     of run k+1 (which waits for that download: they share a host buffer).
-    Only owned rows cross PCIe: every run first delivers its input's edge rows
-    into the neighbours' halo rows itself.  All ranks call it with the same
+    Only owned rows / planes cross PCIe: every run first delivers its input's
+    edge rows / planes into the neighbours' halos itself.  All ranks call it with the same
     arguments; it returns once every copy of this rank has finished."""
     import torch
-    if len(jobs) != 2 or len(hosts) != 2 or not all(isinstance(j, SlabJacobi2D) for j in jobs):
-        raise ValueError("two SlabJacobi2D jobs (slots) and two host arrays are required")
+    if (len(jobs) != 2 or len(hosts) != 2 or type(jobs[0]) is not type(jobs[1])
+            or not isinstance(jobs[0], (SlabJacobi2D, SlabJacobi3D))):
+        raise ValueError("two slab jobs of one kind (slots) and two host arrays are required")
     own = jobs[0].rows * jobs[0].unit_floats * 4
     off = jobs[0].halo * jobs[0].unit_floats * 4
     for h in hosts:
@@ -454,51 +464,32 @@ def run_host_pipelined(jobs: list, hosts: list, sweeps: int, steps: int) -> None
 
 def e2e_measure(job: _SlabJob, sweeps: int, steps: int = 3, reps: int = 2) -> dict:
     """Whole-job end-to-end rate with pinned host slabs, every copy inside the
-    timed region, wall clock, max over ranks.  Row slabs: `steps` host slabs
-    per rank through run_host_pipelined (a twin job is the second device
-    slot).  z-slabs: SlabJacobi3D.run_host, whose copies do not overlap."""
+    timed region, wall clock, max over ranks: `steps` host slabs per rank
+    through run_host_pipelined (a twin job is the second device slot)."""
     import time
 
     import torch
     d = _dist()
     cells = job.G * job.cols * (job.H if isinstance(job, SlabJacobi3D) else 1)
-    if isinstance(job, SlabJacobi2D):
-        twin = SlabJacobi2D(cols=job.cols, G=job.G, seed=4, res_every=job.res_every)
-        hosts = [torch.empty((job.rows,) + job.unit_shape, dtype=torch.float32, pin_memory=True).numpy()
-                 for _ in range(2)]
-        own = job.rows * job.unit_floats * 4
-        for h in hosts:  # input: the job's current owned rows
-            call("spmdb200_memcpy", c_p(h.ctypes.data), c_p(job._u.ptr + job.halo * job.unit_floats * 4),
-                 ctypes.c_size_t(own), None)
-        run_host_pipelined([job, twin], hosts, 2, 2)  # warm-up: both slots, copies and launches
-        rendezvous()
-        t0 = time.perf_counter()
-        run_host_pipelined([job, twin], hosts, sweeps, steps)
-        secs = time.perf_counter() - t0
-        twin.close()
-        t = torch.tensor([secs], dtype=torch.float64, device="cuda")
-        if d is not None and job.world > 1:
-            d.all_reduce(t, op=d.ReduceOp.MAX)
-        secs = float(t.item())
-        return {"value": round(steps * cells * sweeps / secs / 1e9, 3), "unit": "Gcell-updates/s",
-                "h2d_bytes_per_step": own, "d2h_bytes_per_step": own,
-                "entry": f"slab.run_host_pipelined: {steps} pinned host slabs per rank (owned rows), two device "
-                         "slots, uploads and downloads overlapping the sweeps, wall clock"}
-    host = torch.empty((job.local_rows,) + job.unit_shape, dtype=torch.float32, pin_memory=True)
-    arr = host.numpy()
-    arr[:] = 0.0
-    job.run_host(arr, 2)  # warm-up
-    ts = []
-    for _ in range(reps):
-        rendezvous()
-        t0 = time.perf_counter()
-        job.run_host(arr, sweeps)
-        ts.append(time.perf_counter() - t0)
-    t = torch.tensor([sum(ts) / len(ts)], dtype=torch.float64, device="cuda")
+    twin = job.twin()
+    hosts = [torch.empty((job.rows,) + job.unit_shape, dtype=torch.float32, pin_memory=True).numpy()
+             for _ in range(2)]
+    own = job.rows * job.unit_floats * 4
+    for h in hosts:  # input: the job's current owned rows / planes
+        call("spmdb200_memcpy", c_p(h.ctypes.data), c_p(job._u.ptr + job.halo * job.unit_floats * 4),
+             ctypes.c_size_t(own), None)
+    run_host_pipelined([job, twin], hosts, 2, 2)  # warm-up: both slots, copies and launches
+    rendezvous()
+    t0 = time.perf_counter()
+    run_host_pipelined([job, twin], hosts, sweeps, steps)
+    secs = time.perf_counter() - t0
+    twin.close()
+    t = torch.tensor([secs], dtype=torch.float64, device="cuda")
     if d is not None and job.world > 1:
         d.all_reduce(t, op=d.ReduceOp.MAX)
     secs = float(t.item())
-    return {"value": round(cells * sweeps / secs / 1e9, 3), "unit": "Gcell-updates/s",
-            "h2d_bytes_per_step": job.local_rows * job.unit_floats * 4,
-            "d2h_bytes_per_step": job.rows * job.unit_floats * 4,
-            "entry": f"{type(job).__name__}.run_host (pinned host slab per rank)"}
+    unit = "rows" if isinstance(job, SlabJacobi2D) else "planes"
+    return {"value": round(steps * cells * sweeps / secs / 1e9, 3), "unit": "Gcell-updates/s",
+            "h2d_bytes_per_step": own, "d2h_bytes_per_step": own,
+            "entry": f"slab.run_host_pipelined: {steps} pinned host slabs per rank (owned {unit}), two device "
+                     "slots, uploads and downloads overlapping the sweeps, wall clock"}

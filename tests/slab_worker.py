@@ -45,8 +45,9 @@ def main() -> None:
             rel = np.max(np.abs(res - wres) / np.abs(wres)) if wres.size else 0.0
             print(f"G={G} W={W} sweeps={sweeps}: grid bit-exact={same} residual max rel err={rel:.3g}", flush=True)
             ok = ok and same and rel <= 1e-12
-    # Jacobi-3D z-slabs: one halo plane each side, one plane up and down per sweep.
-    for (D, H, W, sweeps, res_every) in [(37, 20, 150, 7, 2), (64, 64, 130, 10, 5), (5, 9, 11, 3, 1)]:
+    # Jacobi-3D z-slabs: HALO3 halo planes each side, passes of up to HALO3 sweeps.
+    for (D, H, W, sweeps, res_every) in [(37, 20, 150, 7, 2), (64, 64, 130, 10, 5), (9, 9, 11, 3, 1),
+                                         (40, 33, 140, 13, 0), (21, 50, 270, 11, 4)]:
         u0 = jacobi_init((D, H, W), 3)
         job = slab.SlabJacobi3D(H=H, W=W, D=D, res_every=res_every, init=u0)
         job.run(sweeps)

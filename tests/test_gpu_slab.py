@@ -151,7 +151,8 @@ def test_zslab_peer_wait_runs_out_and_reports_timeout(kernels):
     lib = L.lib()
     c_i, c_p = ctypes.c_int64, ctypes.c_void_p
     planes, H, W = 6, 16, 128
-    u = torch.zeros((planes + 2, H, W), device="cuda")
+    halo = spmd_mod("slab").HALO3
+    u = torch.zeros((planes + 2 * halo, H, W), device="cuda")
     v = torch.zeros_like(u)
     fake_u, fake_v = torch.zeros_like(u), torch.zeros_like(u)
     nbytes = int(lib.spmdb200_jacobi_workspace_bytes())
@@ -160,7 +161,7 @@ def test_zslab_peer_wait_runs_out_and_reports_timeout(kernels):
 
     def d(t):
         p = c_p(t.data_ptr())
-        return (p, p, c_i(0), c_i(planes + 2), c_i(H), c_i(W), c_i(H * W), c_i(W), c_i(1))
+        return (p, p, c_i(0), c_i(planes + 2 * halo), c_i(H), c_i(W), c_i(H * W), c_i(W), c_i(1))
 
     s = c_p(torch.cuda.current_stream().cuda_stream)
     assert lib.spmdb200_set_wait_budget_ms(c_i(2000), c_i(300)) == 0

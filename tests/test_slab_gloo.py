@@ -49,15 +49,15 @@ def test_partition_covers_rows_once():
         slab.partition(3, 4, 0)
 
 
-def _pass_plan(sweeps: int, res_every: int) -> list[int]:
+def _pass_plan(sweeps: int, res_every: int, fmax: int = 8) -> list[int]:
     """Sweeps per pass as the C library schedules them: even numbers of
-    eight-, four- and two-sweep passes (none longer than the residual
-    interval), then the single sweep left over."""
-    fmax = 8
+    eight- (2-D only), four- and two-sweep passes (none longer than the
+    residual interval), then the single sweeps left over."""
+    top = fmax
     while res_every > 0 and fmax > res_every:
         fmax //= 2
     plan, left = [], sweeps
-    for f in (8, 4, 2, 1):
+    for f in [x for x in (8, 4, 2, 1) if x <= top]:
         n = 0 if f > fmax else left if f == 1 else (left // (2 * f)) * 2
         plan += [f] * n
         left -= n * f
@@ -149,8 +149,10 @@ def test_slab_protocol_matches_single_domain_oracle(oracle_mod, world, G, W, swe
 
 
 def _zslab_worker(rank: int, world: int, port: int, D: int, H: int, W: int, sweeps: int, res_every: int, q):
-    """Jacobi-3D z-slab protocol: one halo plane each side, the first/last owned
-    plane handed to the neighbours after every sweep, residuals summed in rank
+    """Jacobi-3D z-slab protocol: passes of up to HALO3 sweeps over a
+    (planes + 2 HALO3)-plane local array -- sweep f of an F-sweep pass also re-sweeps
+    F-1-f halo planes on each side --, the first/last F owned planes handed to
+    the neighbours' halo planes after each pass, residuals summed in rank
     order."""
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "tests"))
@@ -170,33 +172,42 @@ def _zslab_worker(rank: int, world: int, port: int, D: int, H: int, W: int, swee
     v = np.zeros_like(u)
     up, dn = slab.neighbours(D, world, rank)
     res = []
-    for k in range(1, sweeps + 1):
-        want = res_every > 0 and k % res_every == 0
-        pr = oracle.jacobi3d_planes(u, v, h, h + planes, z0 - h, D, want_res=want)
+    k = 0
+    for pno, F in enumerate(_pass_plan(sweeps, res_every, fmax=h)):
+        for f in range(F):
+            k += 1
+            want = res_every > 0 and k % res_every == 0
+            ext = F - 1 - f
+            src, dst = (u, v) if f % 2 == 0 else (v, u)
+            oracle.jacobi3d_planes(src, dst, h - ext, h + planes + ext, z0 - h, D)
+            pr = oracle.jacobi3d_planes(src, dst, h, h + planes, z0 - h, D, want_res=True) if want else None
+            if want:
+                mine = 0.0
+                for x in pr:
+                    mine = mine + float(x)
+                slots = [None] * world
+                dist.all_gather_object(slots, mine)
+                tot = 0.0
+                for x in slots:
+                    tot = tot + x
+                res.append(tot)
+        out = v if F % 2 == 1 else u
+        # halo hand-off after each pass: the first F owned planes up, the last F down
         reqs = []
         if up is not None:
-            reqs.append(dist.isend(torch.from_numpy(v[h].copy()), up, tag=2 * k))
-            buf = torch.empty((H, W))
-            dist.recv(buf, up, tag=2 * k + 1)
-            v[0] = buf.numpy()
+            reqs.append(dist.isend(torch.from_numpy(out[h:h + F].copy()), up, tag=2 * pno))
+            buf = torch.empty((F, H, W))
+            dist.recv(buf, up, tag=2 * pno + 1)
+            out[h - F:h] = buf.numpy()
         if dn is not None:
-            reqs.append(dist.isend(torch.from_numpy(v[planes].copy()), dn, tag=2 * k + 1))
-            buf = torch.empty((H, W))
-            dist.recv(buf, dn, tag=2 * k)
-            v[planes + h] = buf.numpy()
+            reqs.append(dist.isend(torch.from_numpy(out[h + planes - F:h + planes].copy()), dn, tag=2 * pno + 1))
+            buf = torch.empty((F, H, W))
+            dist.recv(buf, dn, tag=2 * pno)
+            out[h + planes:h + planes + F] = buf.numpy()
         for r in reqs:
             r.wait()
-        if want:
-            mine = 0.0
-            for x in pr:
-                mine = mine + float(x)
-            slots = [None] * world
-            dist.all_gather_object(slots, mine)
-            tot = 0.0
-            for x in slots:
-                tot = tot + x
-            res.append(tot)
-        u, v = v, u
+        if F % 2 == 1:
+            u, v = v, u
     parts = [None] * world
     dist.all_gather_object(parts, u[h:h + planes])
     if rank == 0:
@@ -205,19 +216,22 @@ def _zslab_worker(rank: int, world: int, port: int, D: int, H: int, W: int, swee
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,D,H,W,sweeps", [(2, 9, 6, 7, 5), (3, 13, 5, 9, 4), (4, 4, 3, 5, 3)])
-def test_zslab_protocol_matches_single_domain_oracle(oracle_mod, world, D, H, W, sweeps):
+@pytest.mark.parametrize("world,D,H,W,sweeps,res_every", [(2, 9, 6, 7, 5, 1), (3, 13, 5, 9, 4, 2),
+                                                           (4, 17, 3, 5, 9, 0), (2, 11, 6, 10, 13, 4),
+                                                           (3, 20, 5, 6, 11, 3)])
+def test_zslab_protocol_matches_single_domain_oracle(oracle_mod, world, D, H, W, sweeps, res_every):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_zslab_worker, args=(r, world, port, D, H, W, sweeps, 1, q)) for r in range(world)]
+    ps = [ctx.Process(target=_zslab_worker, args=(r, world, port, D, H, W, sweeps, res_every, q))
+          for r in range(world)]
     for p in ps:
         p.start()
     grid, res = q.get(timeout=120)
     for p in ps:
         p.join(timeout=60)
         assert p.exitcode == 0
-    want, wres = oracle_mod.jacobi3d(jacobi_init((D, H, W), 3), sweeps, 1)
+    want, wres = oracle_mod.jacobi3d(jacobi_init((D, H, W), 3), sweeps, res_every)
     assert np.array_equal(grid.view(np.uint32), want.view(np.uint32))
     np.testing.assert_allclose(res, wres, rtol=1e-12)
 
