@@ -67,7 +67,10 @@ static_assert(kTbGroups * kTbBands <= kTbThreads && kTbThreads % 32 == 0, "whole
 
 template <int F>
 struct Tb {
-  static constexpr int RPW = F >= 4 ? 2 : 3;       // rows per thread (registers: 12 * RPW per level)
+#ifndef SPMDB200_J3TB_RPW2
+#define SPMDB200_J3TB_RPW2 3
+#endif
+  static constexpr int RPW = F >= 4 ? 2 : F == 2 ? SPMDB200_J3TB_RPW2 : 3;  // rows per thread (12 * RPW registers per level)
   // Sweep level 0 (the input) read from the ring instead of registers (four
   // sweeps: 3 x 4 x 24 registers would not fit); the ring then keeps one
   // more plane (the centre's z - 1).
@@ -190,6 +193,16 @@ __device__ __forceinline__ bool tb_wait_barrier(const J3Tb &k, unsigned target) 
   return tb_wait_counter(k, &k.ws->barrier, target, false, k.budget_ns);
 }
 
+// z-slab mode, thread 0, before staging a halo plane: wait until the
+// neighbour delivered it (out of line: it runs a few times per pass).
+__device__ __noinline__ bool tb_halo_wait(const J3Tb &k, bool wait_up, bool wait_dn, unsigned need) {
+  if (wait_up && !tb_wait_counter(k, &k.ws->from_above, need, true, k.peer_budget_ns)) return false;
+  if (wait_dn && !tb_wait_counter(k, &k.ws->from_below, need, true, k.peer_budget_ns)) return false;
+  // the acquire above, then the async-proxy read of the peer-written plane
+  fence_proxy_async_global();
+  return true;
+}
+
 // Thread 0: stage the next plane of this CTA's stream for pass p into the
 // ring.  z-slab mode: a halo plane only once the neighbour delivered it.
 template <int F, bool SLAB>
@@ -200,10 +213,7 @@ __device__ __forceinline__ bool tb_issue(const J3Tb &k, const void *src, float *
   if constexpr (SLAB) {
     const bool wait_up = it_i.first && k.peers.up_u && q < k.z_lo;
     const bool wait_dn = it_i.last && k.peers.dn_u && q >= k.z_hi;
-    if (wait_up && !tb_wait_counter(k, &k.ws->from_above, need, true, k.peer_budget_ns)) return false;
-    if (wait_dn && !tb_wait_counter(k, &k.ws->from_below, need, true, k.peer_budget_ns)) return false;
-    // the acquire above, then the async-proxy read of the peer-written plane
-    if (wait_up || wait_dn) fence_proxy_async_global();
+    if ((wait_up || wait_dn) && !tb_halo_wait(k, wait_up, wait_dn, need)) return false;
   }
   const uint32_t slot = ic % Tb<F>::RING;
   mbar_arrive_expect_tx(&full[slot], (uint32_t)Tb<F>::PLANE * 4u);
@@ -317,13 +327,32 @@ __device__ __forceinline__ void tb_st4_if(bool pred, float *p, float4 v) {
       "l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w));
 }
 
+// z-slab mode: this thread's rows of owned plane gz (one of the first / last
+// F) into the neighbour's halo plane.  Out of line: it runs at 2F steps of an
+// edge item, and inlined it would raise the register count of every step.
+template <int F>
+__device__ __noinline__ void tb_deliver_rows(const J3Tb &k, const float4 *o, const TbLanes<F> &L, int gy0, int gz,
+                                             int p, bool up, bool dn) {
+#pragma unroll 1
+  for (int r = 0; r < Tb<F>::RPW; ++r) {
+    if (!L.rown[r] || !L.ow0) continue;
+    const long long yo = (long long)(gy0 + r) * k.sy + L.gx0;
+    if (up)
+      tb_store4(((p & 1) ? k.peers.up_u : k.peers.up_v) + (k.peers.up_row + gz - k.z_lo) * k.sz + yo, L.gx0, k.w,
+                o[r]);
+    if (dn)
+      tb_store4(((p & 1) ? k.peers.dn_u : k.peers.dn_v) + (k.peers.dn_row + k.halo - (k.z_hi - gz)) * k.sz + yo,
+                L.gx0, k.w, o[r]);
+  }
+}
+
 // One plane step of item `it` (PH = j mod 3): input plane q = z0 - F + j has
 // landed in the ring; sweep l computes plane q - l from the registers of
 // level l - 1 (z neighbours and the rows inside the band), shuffles (x), and
 // the band-edge rows and warp-edge groups of level l - 1's previous plane
 // from shared memory.  EDGE: the tile touches the grid's x or y boundary.
 // Returns false if the wait for the plane timed out (warp-uniform).
-template <int F, bool SLAB, bool EDGE, int PH>
+template <int F, bool DELIV, bool EDGE, int PH>
 __device__ __forceinline__ bool tb_step(const J3Tb &k, TbCtx<F> &C, const TbLanes<F> &L, const TbItem &it, int j,
                                         int p, int rl, float *dst, const float *ring, float *pub, uint64_t *full,
                                         volatile int *abort, int lane, int g, int r0, bool active, bool has_top,
@@ -414,18 +443,12 @@ __device__ __forceinline__ bool tb_step(const J3Tb &k, TbCtx<F> &C, const TbLane
         } else {
           tb_st4_if(L.rown[r] && L.ow0, op, o[r]);
         }
-        if constexpr (SLAB) {
-          // the first / last F owned planes also go to the neighbour's halo
-          if (L.rown[r] && L.ow0) {
-            if (it.first && k.peers.up_u && gz - k.z_lo < F)
-              tb_store4(((p & 1) ? k.peers.up_u : k.peers.up_v) + (k.peers.up_row + gz - k.z_lo) * k.sz + yo,
-                        L.gx0, k.w, o[r]);
-            if (it.last && k.peers.dn_u && k.z_hi - gz <= F)
-              tb_store4(((p & 1) ? k.peers.dn_u : k.peers.dn_v) + (k.peers.dn_row + k.halo - (k.z_hi - gz)) * k.sz +
-                            yo,
-                        L.gx0, k.w, o[r]);
-          }
-        }
+      }
+      if constexpr (DELIV) {
+        // the first / last F owned planes also go to the neighbour's halo
+        const bool up = it.first && k.peers.up_u && gz - k.z_lo < F;
+        const bool dn = it.last && k.peers.dn_u && k.z_hi - gz <= F;
+        if (up || dn) tb_deliver_rows<F>(k, o, L, it.by + r0, gz, p, up, dn);
       }
     }
   }
@@ -435,12 +458,12 @@ __device__ __forceinline__ bool tb_step(const J3Tb &k, TbCtx<F> &C, const TbLane
 // After a plane step: z-slab delivery signals, the CTA barrier, and thread 0
 // refilling the ring slot the step freed.  Returns false if any warp's wait
 // timed out.
-template <int F, bool SLAB>
+template <int F, bool SLAB, bool DELIV>
 __device__ __forceinline__ bool tb_after_step(const J3Tb &k, TbCtx<F> &C, const TbItem &it, int j, bool got,
                                               const void *src, float *ring, uint64_t *full, volatile int *abort,
                                               int items, unsigned need) {
   bool sig_up = false, sig_dn = false;
-  if constexpr (SLAB) {
+  if constexpr (DELIV) {
     const int gz_out = it.z0 - 2 * F + j;  // plane stored at this step (j >= 2F)
     sig_up = j >= 2 * F && it.first && k.peers.up_u && gz_out == k.z_lo + F - 1;
     sig_dn = j >= 2 * F && it.last && k.peers.dn_u && gz_out == k.z_hi - 1;
@@ -453,7 +476,7 @@ __device__ __forceinline__ bool tb_after_step(const J3Tb &k, TbCtx<F> &C, const 
     return false;
   }
   if (threadIdx.x == 0) {
-    if constexpr (SLAB) {
+    if constexpr (DELIV) {
       if (sig_up) red_release_sys_add(k.peers.up_flag, 1u);
       if (sig_dn) red_release_sys_add(k.peers.dn_flag, 1u);
     }
@@ -467,7 +490,9 @@ __device__ __forceinline__ bool tb_after_step(const J3Tb &k, TbCtx<F> &C, const 
 }
 
 // All plane steps of one item, unrolled by three (the register rotation).
-template <int F, bool SLAB, bool EDGE>
+// DELIV: an item of the first / last z-chunk in z-slab mode (its plane steps
+// carry the peer deliveries); the other items run the one-GPU step code.
+template <int F, bool SLAB, bool DELIV, bool EDGE>
 __device__ __forceinline__ bool tb_run_item(const J3Tb &k, TbCtx<F> &C, const TbLanes<F> &L, const TbItem &it,
                                             int p, int rl, const void *src, float *dst, float *ring, float *pub,
                                             uint64_t *full, volatile int *abort, int items, unsigned need, int lane,
@@ -475,9 +500,9 @@ __device__ __forceinline__ bool tb_run_item(const J3Tb &k, TbCtx<F> &C, const Tb
                                             bool e_edge) {
 #define TB_STEP(PH)                                                                                              \
   {                                                                                                              \
-    const bool got = tb_step<F, SLAB, EDGE, PH>(k, C, L, it, j + PH, p, rl, dst, ring, pub, full, abort, lane, g, \
+    const bool got = tb_step<F, DELIV, EDGE, PH>(k, C, L, it, j + PH, p, rl, dst, ring, pub, full, abort, lane, g, \
                                                 r0, active, has_top, has_bot, w_edge, e_edge);                  \
-    if (!tb_after_step<F, SLAB>(k, C, it, j + PH, got, src, ring, full, abort, items, need)) return false;     \
+    if (!tb_after_step<F, SLAB, DELIV>(k, C, it, j + PH, got, src, ring, full, abort, items, need)) return false; \
   }
   int j = 0;
   for (; j + 3 <= it.n; j += 3) {
@@ -593,12 +618,15 @@ __global__ void __launch_bounds__(kTbThreads, 1) jacobi3d_tb_kernel(const __grid
         L.rfix[r] = gy <= 0 || gy >= k.h - 1;
         L.rown[r] = r0 + r >= F && r0 + r < F + T::TH && gy < k.h;
       }
-      const bool ok = it.edge ? tb_run_item<F, SLAB, true>(k, C, L, it, p, rl, src, dst, ring, pub, full, abort, items,
-                                                            need, lane, g, r0, active, has_top, has_bot, w_edge,
-                                                            e_edge)
-                              : tb_run_item<F, SLAB, false>(k, C, L, it, p, rl, src, dst, ring, pub, full, abort,
-                                                             items, need, lane, g, r0, active, has_top, has_bot,
-                                                             w_edge, e_edge);
+#define TB_RUN(DV, ED)                                                                                          \
+  tb_run_item<F, SLAB, DV, ED>(k, C, L, it, p, rl, src, dst, ring, pub, full, abort, items, need, lane, g, r0, active, \
+                               has_top, has_bot, w_edge, e_edge)
+      bool ok;
+      if (SLAB && (it.first || it.last))
+        ok = it.edge ? TB_RUN(SLAB, true) : TB_RUN(SLAB, false);
+      else
+        ok = it.edge ? TB_RUN(false, true) : TB_RUN(false, false);
+#undef TB_RUN
       if (!ok) {
         failed = true;
         break;
