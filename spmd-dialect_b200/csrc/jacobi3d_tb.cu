@@ -29,11 +29,11 @@
 //
 // z-slabs across GPUs (SlabPeers, kSlabHalo3 = 2 halo planes on each side): a
 // rank updates its owned planes [z_lo, z_hi).  The work items of the first
-// (last) z-chunk come first in every pass; when they store their first (last)
-// F owned planes they also store them into the neighbour's halo planes over
-// NVLink, and after the F-th plane thread 0 bumps the neighbour's delivery
-// counter (release, system scope; one delivery per tile per pass, counters
-// only grow across launches).  Before thread 0 stages a halo plane it
+// (last) z-chunk come first in every pass; when one has finished, its threads
+// copy their cells of the first (last) F owned planes into the neighbour's
+// halo planes over NVLink and thread 0 bumps the neighbour's delivery counter
+// (release, system scope; one delivery per tile per pass, counters only grow
+// across launches).  Before thread 0 stages a halo plane it
 // acquires the counter it needs.  A run's first launch first copies the
 // input's edge planes into the neighbours' halos (counted as one pass).  TMA
 // only ever reads this GPU's own memory.  Arithmetic per cell is the
@@ -205,9 +205,20 @@ __device__ __noinline__ bool tb_halo_wait(const J3Tb &k, bool wait_up, bool wait
 
 // Thread 0: stage the next plane of this CTA's stream for pass p into the
 // ring.  z-slab mode: a halo plane only once the neighbour delivered it.
+// Thread 0's issue cursor, kept in shared memory (in registers it would
+// occupy every thread's: the plane loop runs at the 128-register limit).
+struct TbCursor {
+  uint32_t ic;  // input planes issued
+  int t, j;     // item and plane of the item the next load belongs to
+  TbItem it;
+};
+
 template <int F, bool SLAB>
-__device__ __forceinline__ bool tb_issue(const J3Tb &k, const void *src, float *ring, uint64_t *full, uint32_t &ic,
-                                         int &t_i, int &j_i, TbItem &it_i, int items, unsigned need) {
+__device__ __forceinline__ bool tb_issue(const J3Tb &k, const void *src, float *ring, uint64_t *full, TbCursor &cur,
+                                         int items, unsigned need) {
+  uint32_t &ic = cur.ic;
+  int &t_i = cur.t, &j_i = cur.j;
+  TbItem &it_i = cur.it;
   constexpr int PL = Tb<F>::PSTR;
   const int q = it_i.z0 - F + j_i;
   if constexpr (SLAB) {
@@ -310,9 +321,7 @@ struct TbLanes {
 // Mutable state of one thread; registers once everything is inlined.
 template <int F>
 struct TbCtx {
-  uint32_t pc, ic;  // input planes consumed (all threads) / issued (thread 0)
-  int t_i, j_i;     // thread 0's issue cursor: item, plane of the item
-  TbItem it_i;
+  uint32_t pc;      // input planes consumed
   double acc;       // residual partial
   // A[l - L0][s][r]: the thread's cells of box row r0 + r at sweep level l
   // (0: the input) in the plane of the last plane step congruent to s mod 3,
@@ -327,22 +336,38 @@ __device__ __forceinline__ void tb_st4_if(bool pred, float *p, float4 v) {
       "l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w));
 }
 
-// z-slab mode: this thread's rows of owned plane gz (one of the first / last
-// F) into the neighbour's halo plane.  Out of line: it runs at 2F steps of an
-// edge item, and inlined it would raise the register count of every step.
+// z-slab mode, after an item of the first / last z-chunk has stored its
+// planes: the first / last F owned planes (each thread re-reads the cells it
+// stored, L2-resident) go to the neighbour's halo planes over NVLink, then
+// thread 0 counts the delivery.  Outside the plane loop, so that loop is the
+// one-GPU loop (inside it, the slab path spilled and ran ~1.5x slower).
 template <int F>
-__device__ __noinline__ void tb_deliver_rows(const J3Tb &k, const float4 *o, const TbLanes<F> &L, int gy0, int gz,
-                                             int p, bool up, bool dn) {
+__device__ __forceinline__ void tb_deliver_item(const J3Tb &k, const TbLanes<F> &L, const TbItem &it, int p, int r0,
+                                                const float *dst) {
+  const bool up = it.first && k.peers.up_u != nullptr, dn = it.last && k.peers.dn_u != nullptr;
+  if (!up && !dn) return;
 #pragma unroll 1
-  for (int r = 0; r < Tb<F>::RPW; ++r) {
-    if (!L.rown[r] || !L.ow0) continue;
-    const long long yo = (long long)(gy0 + r) * k.sy + L.gx0;
-    if (up)
-      tb_store4(((p & 1) ? k.peers.up_u : k.peers.up_v) + (k.peers.up_row + gz - k.z_lo) * k.sz + yo, L.gx0, k.w,
-                o[r]);
-    if (dn)
-      tb_store4(((p & 1) ? k.peers.dn_u : k.peers.dn_v) + (k.peers.dn_row + k.halo - (k.z_hi - gz)) * k.sz + yo,
-                L.gx0, k.w, o[r]);
+  for (int e = 0; e < 2; ++e) {
+    if (e == 0 ? !up : !dn) continue;
+    float *to = e == 0 ? ((p & 1) ? k.peers.up_u : k.peers.up_v) : ((p & 1) ? k.peers.dn_u : k.peers.dn_v);
+#pragma unroll 1
+    for (int f = 0; f < F; ++f) {
+      const long long gz = e == 0 ? k.z_lo + f : k.z_hi - F + f;
+      const long long tz = e == 0 ? k.peers.up_row + f : k.peers.dn_row + k.halo - F + f;
+#pragma unroll
+      for (int r = 0; r < Tb<F>::RPW; ++r) {
+        if (!L.rown[r] || !L.ow0) continue;
+        const long long yo = (long long)(it.by + r0 + r) * k.sy + L.gx0;
+        // a full float4 stays inside the row pitch (a multiple of 4 floats)
+        tb_store4(to + tz * k.sz + yo, L.gx0, k.w, ld_f4(dst + gz * k.sz + yo));
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (up) red_release_sys_add(k.peers.up_flag, 1u);
+    if (dn) red_release_sys_add(k.peers.dn_flag, 1u);
   }
 }
 
@@ -352,7 +377,7 @@ __device__ __noinline__ void tb_deliver_rows(const J3Tb &k, const float4 *o, con
 // the band-edge rows and warp-edge groups of level l - 1's previous plane
 // from shared memory.  EDGE: the tile touches the grid's x or y boundary.
 // Returns false if the wait for the plane timed out (warp-uniform).
-template <int F, bool DELIV, bool EDGE, int PH>
+template <int F, bool EDGE, int PH>
 __device__ __forceinline__ bool tb_step(const J3Tb &k, TbCtx<F> &C, const TbLanes<F> &L, const TbItem &it, int j,
                                         int p, int rl, float *dst, const float *ring, float *pub, uint64_t *full,
                                         volatile int *abort, int lane, int g, int r0, bool active, bool has_top,
@@ -444,31 +469,17 @@ __device__ __forceinline__ bool tb_step(const J3Tb &k, TbCtx<F> &C, const TbLane
           tb_st4_if(L.rown[r] && L.ow0, op, o[r]);
         }
       }
-      if constexpr (DELIV) {
-        // the first / last F owned planes also go to the neighbour's halo
-        const bool up = it.first && k.peers.up_u && gz - k.z_lo < F;
-        const bool dn = it.last && k.peers.dn_u && k.z_hi - gz <= F;
-        if (up || dn) tb_deliver_rows<F>(k, o, L, it.by + r0, gz, p, up, dn);
-      }
     }
   }
   return true;
 }
 
-// After a plane step: z-slab delivery signals, the CTA barrier, and thread 0
-// refilling the ring slot the step freed.  Returns false if any warp's wait
-// timed out.
-template <int F, bool SLAB, bool DELIV>
-__device__ __forceinline__ bool tb_after_step(const J3Tb &k, TbCtx<F> &C, const TbItem &it, int j, bool got,
-                                              const void *src, float *ring, uint64_t *full, volatile int *abort,
-                                              int items, unsigned need) {
-  bool sig_up = false, sig_dn = false;
-  if constexpr (DELIV) {
-    const int gz_out = it.z0 - 2 * F + j;  // plane stored at this step (j >= 2F)
-    sig_up = j >= 2 * F && it.first && k.peers.up_u && gz_out == k.z_lo + F - 1;
-    sig_dn = j >= 2 * F && it.last && k.peers.dn_u && gz_out == k.z_hi - 1;
-    if (sig_up || sig_dn) __threadfence_system();  // this thread's peer stores before the signal
-  }
+// After a plane step: the CTA barrier, and thread 0 refilling the ring slot
+// the step freed.  Returns false if any warp's wait timed out.
+template <int F, bool SLAB>
+__device__ __forceinline__ bool tb_after_step(const J3Tb &k, TbCtx<F> &C, TbCursor &cur, bool got, const void *src,
+                                              float *ring, uint64_t *full, volatile int *abort, int items,
+                                              unsigned need) {
   ++C.pc;
   if (__syncthreads_or(!got)) {
     if (threadIdx.x == 0 && *abort == 0) tb_record(k.ws, abort, kDevTimeoutFull);
@@ -476,33 +487,28 @@ __device__ __forceinline__ bool tb_after_step(const J3Tb &k, TbCtx<F> &C, const 
     return false;
   }
   if (threadIdx.x == 0) {
-    if constexpr (DELIV) {
-      if (sig_up) red_release_sys_add(k.peers.up_flag, 1u);
-      if (sig_dn) red_release_sys_add(k.peers.dn_flag, 1u);
-    }
     // the slot of the step's centre plane is free: refill it
-    if (C.t_i < items && !tb_issue<F, SLAB>(k, src, ring, full, C.ic, C.t_i, C.j_i, C.it_i, items, need)) {
+    if (cur.t < items && !tb_issue<F, SLAB>(k, src, ring, full, cur, items, need)) {
       tb_record(k.ws, abort, kDevTimeoutPeer);
-      C.t_i = items;
+      cur.t = items;
     }
   }
   return true;
 }
 
 // All plane steps of one item, unrolled by three (the register rotation).
-// DELIV: an item of the first / last z-chunk in z-slab mode (its plane steps
-// carry the peer deliveries); the other items run the one-GPU step code.
-template <int F, bool SLAB, bool DELIV, bool EDGE>
-__device__ __forceinline__ bool tb_run_item(const J3Tb &k, TbCtx<F> &C, const TbLanes<F> &L, const TbItem &it,
+template <int F, bool SLAB, bool EDGE>
+__device__ __forceinline__ bool tb_run_item(const J3Tb &k, TbCtx<F> &C, TbCursor &cur, const TbLanes<F> &L,
+                                            const TbItem &it,
                                             int p, int rl, const void *src, float *dst, float *ring, float *pub,
                                             uint64_t *full, volatile int *abort, int items, unsigned need, int lane,
                                             int g, int r0, bool active, bool has_top, bool has_bot, bool w_edge,
                                             bool e_edge) {
 #define TB_STEP(PH)                                                                                              \
   {                                                                                                              \
-    const bool got = tb_step<F, DELIV, EDGE, PH>(k, C, L, it, j + PH, p, rl, dst, ring, pub, full, abort, lane, g, \
+    const bool got = tb_step<F, EDGE, PH>(k, C, L, it, j + PH, p, rl, dst, ring, pub, full, abort, lane, g,       \
                                                 r0, active, has_top, has_bot, w_edge, e_edge);                  \
-    if (!tb_after_step<F, SLAB, DELIV>(k, C, it, j + PH, got, src, ring, full, abort, items, need)) return false; \
+    if (!tb_after_step<F, SLAB>(k, C, cur, got, src, ring, full, abort, items, need)) return false;           \
   }
   int j = 0;
   for (; j + 3 <= it.n; j += 3) {
@@ -528,6 +534,7 @@ __global__ void __launch_bounds__(kTbThreads, 1) jacobi3d_tb_kernel(const __grid
   __shared__ uint64_t full[T::RING];
   __shared__ double wsum[kTbWarps];
   __shared__ int abort_s;
+  __shared__ TbCursor cur;
   float *ring = reinterpret_cast<float *>(tb_raw + ((128u - (smem_u32(tb_raw) & 127u)) & 127u));
   float *pub = ring + T::RING * T::PSTR;  // [level 1..F-1][2] planes
   volatile int *abort = &abort_s;
@@ -545,6 +552,7 @@ __global__ void __launch_bounds__(kTbThreads, 1) jacobi3d_tb_kernel(const __grid
   if (tid == 0) {
     for (int i = 0; i < T::RING; ++i) mbar_init(&full[i], 1);
     abort_s = 0;
+    cur.ic = 0;
     mbar_fence_init();
     tma_prefetch_desc(&map_u);
     tma_prefetch_desc(&map_v);
@@ -556,7 +564,7 @@ __global__ void __launch_bounds__(kTbThreads, 1) jacobi3d_tb_kernel(const __grid
 
   TbCtx<F> C;
   C.pc = 0;
-  C.ic = 0;
+
   C.acc = 0.0;
 #pragma unroll
   for (int l = 0; l < F - T::L0; ++l)
@@ -589,14 +597,14 @@ __global__ void __launch_bounds__(kTbThreads, 1) jacobi3d_tb_kernel(const __grid
     }
 
     const unsigned need = k.flag_base + (unsigned)(k.init_halo + p) * per_pass;  // halo deliveries for pass p
-    C.t_i = blockIdx.x;
-    C.j_i = 0;
     if (tid == 0) {
-      if (C.t_i < items) C.it_i = tb_item<F>(k, C.t_i);
-      for (int s = 0; s < T::RING - 1 - T::L0 && C.t_i < items; ++s)
-        if (!tb_issue<F, SLAB>(k, src, ring, full, C.ic, C.t_i, C.j_i, C.it_i, items, need)) {
+      cur.t = blockIdx.x;
+      cur.j = 0;
+      if (cur.t < items) cur.it = tb_item<F>(k, cur.t);
+      for (int s = 0; s < T::RING - 1 - T::L0 && cur.t < items; ++s)
+        if (!tb_issue<F, SLAB>(k, src, ring, full, cur, items, need)) {
           tb_record(k.ws, abort, kDevTimeoutPeer);
-          C.t_i = items;  // issue nothing more; the consumers see the abort flag
+          cur.t = items;  // issue nothing more; the consumers see the abort flag
         }
     }
 
@@ -618,15 +626,15 @@ __global__ void __launch_bounds__(kTbThreads, 1) jacobi3d_tb_kernel(const __grid
         L.rfix[r] = gy <= 0 || gy >= k.h - 1;
         L.rown[r] = r0 + r >= F && r0 + r < F + T::TH && gy < k.h;
       }
-#define TB_RUN(DV, ED)                                                                                          \
-  tb_run_item<F, SLAB, DV, ED>(k, C, L, it, p, rl, src, dst, ring, pub, full, abort, items, need, lane, g, r0, active, \
-                               has_top, has_bot, w_edge, e_edge)
-      bool ok;
-      if (SLAB && (it.first || it.last))
-        ok = it.edge ? TB_RUN(SLAB, true) : TB_RUN(SLAB, false);
-      else
-        ok = it.edge ? TB_RUN(false, true) : TB_RUN(false, false);
-#undef TB_RUN
+      const bool ok = it.edge ? tb_run_item<F, SLAB, true>(k, C, cur, L, it, p, rl, src, dst, ring, pub, full, abort, items,
+                                                            need, lane, g, r0, active, has_top, has_bot, w_edge,
+                                                            e_edge)
+                              : tb_run_item<F, SLAB, false>(k, C, cur, L, it, p, rl, src, dst, ring, pub, full, abort,
+                                                             items, need, lane, g, r0, active, has_top, has_bot,
+                                                             w_edge, e_edge);
+      if constexpr (SLAB) {
+        if (ok) tb_deliver_item<F>(k, L, it, p, r0, dst);
+      }
       if (!ok) {
         failed = true;
         break;
@@ -661,7 +669,7 @@ __global__ void __launch_bounds__(kTbThreads, 1) jacobi3d_tb_kernel(const __grid
   }
   if (failed && tid == 0) {
     // planes issued but not consumed must land before shared memory is released
-    for (uint32_t i = C.pc; (int)(C.ic - i) > 0; ++i) {
+    for (uint32_t i = C.pc; (int)(cur.ic - i) > 0; ++i) {
       int no_abort = 0;
       mbar_wait_bounded(&full[i % T::RING], (i / T::RING) & 1u, &no_abort);
     }
