@@ -434,6 +434,12 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
                     "frac_of_hbm_single_launch": round(n * 4 / ms1 / 1e6 / hbm_peak, 3),
                     "l2": "4 rotating 64 MiB inputs", "timing": "mean of 40 back-to-back launches; single launch: "
                     "median of 20, CUDA events around one launch"}
+    # The single-launch method's own floor: an empty kernel between the same
+    # two events (the reductions' single-launch times include it).
+    out["single_launch_floor"] = {"ms_empty_kernel": round(timed(lambda: torch.cuda._sleep(0), reps=20,
+                                                                 flush_l2=False), 5),
+                                  "ms_sum_f32_4096_elements": round(timed(lambda: kernels.sum_f32(bufs[0][:4096], o, ws),
+                                                                          reps=20, flush_l2=False), 5)}
     # Other spmd.reduce kinds on the same inputs (f32 max: integer max over
     # order-preserving keys; i32 xor), same timing.
     ok_ = torch.zeros(1, device=dev)
