@@ -380,8 +380,8 @@ __device__ __forceinline__ void tb_deliver_item(const J3Tb &k, const TbLanes<F> 
 template <int F, bool EDGE, int PH>
 __device__ __forceinline__ bool tb_step(const J3Tb &k, TbCtx<F> &C, const TbLanes<F> &L, const TbItem &it, int j,
                                         int p, int rl, float *dst, const float *ring, float *pub, uint64_t *full,
-                                        volatile int *abort, int lane, int g, int r0, bool active, bool has_top,
-                                        bool has_bot, bool w_edge, bool e_edge) {
+                                        volatile int *abort, int lane, int g, int r0, bool active, int top_off,
+                                        int bot_off, bool w_edge, bool e_edge) {
   constexpr int RPW = Tb<F>::RPW, PL = Tb<F>::PSTR, RING = Tb<F>::RING, L0 = Tb<F>::L0;
   constexpr int P1 = (PH + 2) % 3, P2 = (PH + 1) % 3;  // the previous step, two steps back
   const uint32_t slot = C.pc % RING;
@@ -417,8 +417,10 @@ __device__ __forceinline__ bool tb_step(const J3Tb &k, TbCtx<F> &C, const TbLane
       c = C.A[l - 1 - L0][P1];
       zp = C.A[l - 1 - L0][PH];
     }
-    const float4 top = has_top ? lds4(nb + off - kTbBoxW) : c[0];
-    const float4 bot = has_bot ? lds4(nb + off + RPW * kTbBoxW) : c[RPW - 1];
+    // the rows above / below the band (band 0 and the last band read their own
+    // edge row instead: their outer rows are halo rows, never kept)
+    const float4 top = lds4(nb + off + top_off);
+    const float4 bot = lds4(nb + off + bot_off);
     float4 o[RPW];
 #pragma unroll
     for (int r = 0; r < RPW; ++r) {
@@ -502,12 +504,12 @@ __device__ __forceinline__ bool tb_run_item(const J3Tb &k, TbCtx<F> &C, TbCursor
                                             const TbItem &it,
                                             int p, int rl, const void *src, float *dst, float *ring, float *pub,
                                             uint64_t *full, volatile int *abort, int items, unsigned need, int lane,
-                                            int g, int r0, bool active, bool has_top, bool has_bot, bool w_edge,
+                                            int g, int r0, bool active, int top_off, int bot_off, bool w_edge,
                                             bool e_edge) {
 #define TB_STEP(PH)                                                                                              \
   {                                                                                                              \
     const bool got = tb_step<F, EDGE, PH>(k, C, L, it, j + PH, p, rl, dst, ring, pub, full, abort, lane, g,       \
-                                                r0, active, has_top, has_bot, w_edge, e_edge);                  \
+                                                r0, active, top_off, bot_off, w_edge, e_edge);                  \
     if (!tb_after_step<F, SLAB>(k, C, cur, got, src, ring, full, abort, items, need)) return false;           \
   }
   int j = 0;
@@ -545,7 +547,8 @@ __global__ void __launch_bounds__(kTbThreads, 1) jacobi3d_tb_kernel(const __grid
   const int G = gridDim.x;
   const int items = k.tiles_x * k.tiles_y * k.zchunks;
   const bool own_g = active && g >= 1 && g <= kTbGroups - 2;
-  const bool has_top = band > 0, has_bot = band < kTbBands - 1;
+  const int top_off = band > 0 ? -kTbBoxW : 0;                               // row above the band
+  const int bot_off = (band < kTbBands - 1 ? RPW : RPW - 1) * kTbBoxW;        // row below the band
   const bool w_edge = lane == 0 && g > 0, e_edge = lane == 31 && g < kTbGroups - 1;
   const unsigned per_pass = (unsigned)(k.tiles_x * k.tiles_y);  // deliveries to each neighbour per pass
 
@@ -627,10 +630,10 @@ __global__ void __launch_bounds__(kTbThreads, 1) jacobi3d_tb_kernel(const __grid
         L.rown[r] = r0 + r >= F && r0 + r < F + T::TH && gy < k.h;
       }
       const bool ok = it.edge ? tb_run_item<F, SLAB, true>(k, C, cur, L, it, p, rl, src, dst, ring, pub, full, abort, items,
-                                                            need, lane, g, r0, active, has_top, has_bot, w_edge,
+                                                            need, lane, g, r0, active, top_off, bot_off, w_edge,
                                                             e_edge)
                               : tb_run_item<F, SLAB, false>(k, C, cur, L, it, p, rl, src, dst, ring, pub, full, abort,
-                                                             items, need, lane, g, r0, active, has_top, has_bot,
+                                                             items, need, lane, g, r0, active, top_off, bot_off,
                                                              w_edge, e_edge);
       if constexpr (SLAB) {
         if (ok) tb_deliver_item<F>(k, L, it, p, r0, dst);
