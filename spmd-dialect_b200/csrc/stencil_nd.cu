@@ -258,15 +258,19 @@ struct ParamTaps {  // tap offsets of the tiled kernels (kernel parameters)
   const NdStencil &k;
   __device__ __forceinline__ int operator()(int j) const { return k.tap_lin[j]; }
 };
-template <int CPL, int ST2, bool GUARD, typename Taps = ParamTaps>
+// NT > 0: the tap count as a compile-time constant (the tap loop unrolls and
+// the offsets stay in registers); 0: k.ntaps at run time.
+template <int CPL, int ST2, bool GUARD, typename Taps = ParamTaps, int NT = 0>
 __device__ __forceinline__ void fold_staged(const NdStencil &k, const float *sp, int st2, int nlive, float *acc,
                                             Taps taps) {
   const int cs = 32 * (ST2 > 0 ? ST2 : st2);
+  const int nt = NT > 0 ? NT : k.ntaps;
   const float *q = sp + taps(0);
   if (!k.has_w) {
 #pragma unroll
     for (int u = 0; u < CPL; ++u) acc[u] = (!GUARD || u < nlive) ? q[u * cs] : 0.0f;
-    for (int j = 1; j < k.ntaps; ++j) {
+#pragma unroll (NT > 0 ? NT : 1)
+    for (int j = 1; j < nt; ++j) {
       q = sp + taps(j);
 #pragma unroll
       for (int u = 0; u < CPL; ++u) acc[u] = __fadd_rn(acc[u], (!GUARD || u < nlive) ? q[u * cs] : 0.0f);
@@ -275,7 +279,8 @@ __device__ __forceinline__ void fold_staged(const NdStencil &k, const float *sp,
     float w = k.w[0];
 #pragma unroll
     for (int u = 0; u < CPL; ++u) acc[u] = __fmul_rn(w, (!GUARD || u < nlive) ? q[u * cs] : 0.0f);
-    for (int j = 1; j < k.ntaps; ++j) {
+#pragma unroll (NT > 0 ? NT : 1)
+    for (int j = 1; j < nt; ++j) {
       q = sp + taps(j);
       w = k.w[j];
 #pragma unroll
@@ -363,7 +368,9 @@ __global__ void __launch_bounds__(kNdThreads, 3) stencil_nd_promoted_kernel(cons
 // halo rows and columns are staged once per plane rather than once per
 // z-extent of a tile, so the staged cells per point drop from ~1.9 (tiles of
 // 4 x 8 x 128) to ~1.16.
-template <int CPL, int PF>
+// NT > 0: the tap count at compile time (offsets of a plane's taps held in
+// registers, the tap loop unrolled); 0: any tap count.
+template <int CPL, int PF, int NT>
 __global__ void __launch_bounds__(kNdThreads, 4) stencil_nd_stream3_kernel(const float *__restrict__ A,
                                                                            float *__restrict__ B,
                                                                            const __grid_constant__ NdStencil k) {
@@ -426,7 +433,12 @@ __global__ void __launch_bounds__(kNdThreads, 4) stencil_nd_stream3_kernel(const
       asm volatile("cp.async.wait_group %0;" ::"n"(PF) : "memory");  // planes up to zo + span0 have landed
       __syncthreads();
       const int *toff = s_toff[zo & R1];
-      auto taps = [toff](int j) { return toff[j]; };
+      int toffr[NT > 0 ? NT : 1];
+      if constexpr (NT > 0) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j) toffr[j] = toff[j];
+      }
+      auto taps = [&](int j) { return NT > 0 ? toffr[j] : toff[j]; };
       int i1 = row0, seg = seg0;
       for (int n = 0; n < nu; ++n) {
         if (i1 < rows1) {
@@ -435,14 +447,14 @@ __global__ void __launch_bounds__(kNdThreads, 4) stencil_nd_stream3_kernel(const
           float *bp = bplane + (i1 * k.bs1 + cb);
           float acc[CPL];
           if (ncols - seg * SEG >= SEG) {
-            fold_staged<CPL, 1, false>(k, sp, 1, CPL, acc, taps);
+            fold_staged<CPL, 1, false, decltype(taps), NT>(k, sp, 1, CPL, acc, taps);
 #pragma unroll
             for (int u = 0; u < CPL; ++u) bp[u * 32] = acc[u];
           } else {
             const int rem = ncols - seg * SEG - lane;
             const int nlive = rem <= 0 ? 0 : ((rem + 31) >> 5);
             if (nlive > 0) {
-              fold_staged<CPL, 1, true>(k, sp, 1, nlive, acc, taps);
+              fold_staged<CPL, 1, true, decltype(taps), NT>(k, sp, 1, nlive, acc, taps);
 #pragma unroll
               for (int u = 0; u < CPL; ++u)
                 if (u < nlive) bp[u * 32] = acc[u];
@@ -612,8 +624,11 @@ cudaError_t launch_stream3(NdStencil k, const int *span, const float *a, float *
   if (k.ntiles == 0) return cudaSuccess;
   if (k.ntiles > 0x7fffffffLL) return cudaErrorNotSupported;
   const size_t smem = (size_t)k.slot_cells * k.ring * sizeof(float);
-  return kCpl == 8 ? launch_grid(stencil_nd_stream3_kernel<8, kPf>, k, smem, a, b, s)
-                   : launch_grid(stencil_nd_stream3_kernel<4, kPf>, k, smem, a, b, s);
+  if (k.ntaps == 7)  // the 3-D star
+    return kCpl == 8 ? launch_grid(stencil_nd_stream3_kernel<8, kPf, 7>, k, smem, a, b, s)
+                     : launch_grid(stencil_nd_stream3_kernel<4, kPf, 7>, k, smem, a, b, s);
+  return kCpl == 8 ? launch_grid(stencil_nd_stream3_kernel<8, kPf, 0>, k, smem, a, b, s)
+                   : launch_grid(stencil_nd_stream3_kernel<4, kPf, 0>, k, smem, a, b, s);
 }
 
 }  // namespace
