@@ -30,7 +30,7 @@
 // warps stream adjacent 512-byte segments of the same rows.  Tiles without a
 // fixed boundary cell, halo row or grid edge in reach run an unmasked loop
 // with the pass's residual sweep fixed at compile time; the others (a few
-// percent) run out of line, zero-fill loads outside the array, keep fixed
+// percent) zero-fill loads outside the array, keep fixed
 // boundary cells, mask stores past the last column and deliver slab halo
 // rows to the neighbours.
 //
@@ -436,13 +436,24 @@ __device__ __forceinline__ unsigned wave_tile(const J2Kernel &k, const float *sr
   return (unsigned)n_up | ((unsigned)n_dn << 16);
 }
 
-// Edge tiles run out of line, so their masks and bounds do not raise the
-// register count of the interior loop.
-template <int F, bool RES>
-__device__ __noinline__ unsigned wave_tile_edge(const J2Kernel &k, const float *src, float *dst, float *up_dst,
-                                                float *dn_dst, int r0, int r1, int x0, uint32_t ring, int lane,
-                                                int rl, double *racc) {
-  return wave_tile<F, true, RES>(k, src, dst, up_dst, dn_dst, r0, r1, x0, ring, lane, rl, racc);
+// Edge tile with the residual sweep RL fixed at compile time, inlined like
+// the interior tiles.  A pass waits for its slowest warp, and edge tiles set
+// the pace wherever a warp holds few tiles: out of line with the residual
+// sweep a run-time value they ran 2.55x slower than interior tiles (every
+// tile forced onto the edge path at 32768^2: 1172 Gcell/s), inlined 1.76x
+// (1693); with normal dispatch 4096^2 x 100 went 1038 -> 1321 Gcell/s and
+// 32768^2 x 200 2991 -> 3250.
+template <int F, int RL>
+__device__ __forceinline__ unsigned wave_tile_edge(const J2Kernel &k, const float *src, float *dst, float *up_dst,
+                                                   float *dn_dst, int r0, int r1, int x0, uint32_t ring, int lane,
+                                                   int rl, double *racc) {
+  if constexpr (RL >= F) {
+    return 0u;
+  } else {
+    if (rl == RL)
+      return wave_tile<F, true, true, RL>(k, src, dst, up_dst, dn_dst, r0, r1, x0, ring, lane, rl, racc);
+    return wave_tile_edge<F, RL + 1>(k, src, dst, up_dst, dn_dst, r0, r1, x0, ring, lane, rl, racc);
+  }
 }
 
 // Interior tile with the residual sweep RL (0-based within the pass) fixed at
@@ -556,9 +567,9 @@ __global__ void __launch_bounds__(WvLaunch<F>::THREADS, WvLaunch<F>::MINB)
           nd = wave_tile<F, false, false>(k, src, dst, up_dst, dn_dst, r0, r1, x0, ring, lane, rl, racc);
       } else {
         if (any)
-          nd = wave_tile_edge<F, true>(k, src, dst, up_dst, dn_dst, r0, r1, x0, ring, lane, rl, racc);
+          nd = wave_tile_edge<F, 0>(k, src, dst, up_dst, dn_dst, r0, r1, x0, ring, lane, rl, racc);
         else
-          nd = wave_tile_edge<F, false>(k, src, dst, up_dst, dn_dst, r0, r1, x0, ring, lane, rl, racc);
+          nd = wave_tile<F, true, false>(k, src, dst, up_dst, dn_dst, r0, r1, x0, ring, lane, rl, racc);
       }
       if (slab && nd) {
         __syncwarp();
