@@ -438,7 +438,12 @@ __global__ void __launch_bounds__(kNdThreads, 4) stencil_nd_stream3_kernel(const
 #pragma unroll
         for (int j = 0; j < NT; ++j) toffr[j] = toff[j];
       }
-      auto taps = [&](int j) { return NT > 0 ? toffr[j] : toff[j]; };
+      auto taps = [&](int j) {
+        if constexpr (NT > 0)
+          return toffr[j];
+        else
+          return toff[j];
+      };
       int i1 = row0, seg = seg0;
       for (int n = 0; n < nu; ++n) {
         if (i1 < rows1) {
