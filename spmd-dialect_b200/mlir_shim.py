@@ -38,6 +38,7 @@ from __future__ import annotations
 import json
 import re
 import shutil
+import struct
 import sys
 from dataclasses import dataclass, field
 from pathlib import Path
@@ -60,6 +61,7 @@ class Op:
     region: list = field(default_factory=list)
     block_args: list = field(default_factory=list)
     type: str = ""
+    more_regions: list = field(default_factory=list)  # regions after the first (spmd.if's else)
 
 
 @dataclass
@@ -101,7 +103,39 @@ def _match_brace(s: str, i: int) -> int:
 
 
 def _vals(s: str) -> list:
-    return [v.strip() for v in s.split(",") if v.strip()]
+    """Comma-separated items of s, splitting only outside <>, (), [] and {}
+    (a memref type such as memref<?xf32, #spmd.addr_space<global>> is one item)."""
+    out, depth, cur = [], 0, []
+    for ch in s:
+        if ch in "<([{":
+            depth += 1
+        elif ch in ">)]}":
+            depth -= 1
+        if ch == "," and depth == 0:
+            out.append("".join(cur))
+            cur = []
+        else:
+            cur.append(ch)
+    out.append("".join(cur))
+    return [v.strip() for v in out if v.strip()]
+
+
+def _const_value(text: str, typ: str):
+    """An arith.constant literal: decimal, or a hexadecimal bit pattern (MLIR
+    prints f32 infinities and NaNs as 0x7F800000-style literals)."""
+    text = text.strip()
+    if typ in ("f32", "f64"):
+        if text.lower().startswith("0x"):
+            bits = int(text, 16)
+            fmt, width = ("<f", 4) if typ == "f32" else ("<d", 8)
+            return struct.unpack(fmt, bits.to_bytes(width, "little"))[0]
+        return float(text)
+    if text in ("true", "false"):
+        return int(text == "true")
+    v = int(text, 16) if text.lower().startswith("0x") else int(text)
+    if typ == "i32" and v >= 2 ** 31:
+        v -= 2 ** 32  # a hexadecimal i32 literal is a bit pattern
+    return v
 
 
 def _parse_simple(line: str) -> Op:
@@ -129,7 +163,7 @@ def _parse_simple(line: str) -> Op:
         mm = re.match(r'\(([^)]*)\)', rest)
         return Op(name, None, _vals(mm.group(1)) if mm else [])
     if name in ("func.return", "return"):
-        return Op("func.return", None, [])
+        return Op("func.return", None, _vals(rest.split(":", 1)[0]))
     if name.startswith("arith."):
         ops, t = rest.rsplit(":", 1)
         return Op(name, res, _vals(ops), type=t.strip())
@@ -152,8 +186,20 @@ def _parse_ops(s: str) -> list:
             block_args = [a.split(":")[0].strip() for a in _vals(bb.group(1))] if bb else []
             region = _parse_ops(inner[bb.end():] if bb else inner)
             pos = close + 1
-            while s[pos].isspace():
+            more = []  # further regions: spmd.if carries a then and an else region
+            while True:
+                while s[pos].isspace():
+                    pos += 1
+                if s[pos] != ",":
+                    break
                 pos += 1
+                while s[pos].isspace():
+                    pos += 1
+                if s[pos] != "{":
+                    raise ShimError(f"{m.group(2)}: expected a region after ','")
+                close = _match_brace(s, pos)
+                more.append(_parse_ops(s[pos + 1:close]))
+                pos = close + 1
             if s[pos] != ")":
                 raise ShimError(f"{m.group(2)}: expected ')' after its region")
             pos += 1
@@ -168,7 +214,7 @@ def _parse_ops(s: str) -> list:
             if sig:
                 pos = sig.end()
             ops.append(Op(m.group(2), m.group(1), _vals(m.group(3)), attrs=attrs, region=region,
-                          block_args=block_args))
+                          block_args=block_args, more_regions=more))
             continue
         eol = s.find("\n", pos)
         eol = len(s) if eol < 0 else eol
@@ -274,7 +320,7 @@ class _Env:
         if op.result:
             self.defs[op.result] = op
         if op.name == "arith.constant":
-            val = float(op.extra) if op.type in ("f32", "f64") else int(op.extra)
+            val = _const_value(op.extra, op.type)
             self.consts[op.result] = val
             if op.type == "index":
                 self.idx[op.result] = _Aff({}, val)
@@ -302,6 +348,8 @@ def _walk(ops, env: _Env, path=()):
             for a in op.block_args:
                 env.idx[a] = _Aff({a: 1})
             yield from _walk(op.region, env, path + (op,))
+        for r in op.more_regions:
+            yield from _walk(r, env, path + (op,))
 
 
 def _fold(env: _Env, v: str, loads: list) -> tuple:
@@ -347,8 +395,11 @@ def analyse(func: Func) -> Mapping:
     reduces = [(op, p) for op, p in nodes if op.name == "spmd.reduce"]
     atomics = [(op, p) for op, p in nodes if op.name == "memref.atomic_rmw"]
     stores = [(op, p) for op, p in nodes if op.name == "memref.store"]
+    ifs = [op for op, _ in nodes if op.name == "spmd.if"]
+    if ifs:
+        raise ShimError(f"{func.name}: spmd.if (a guarded store or a select) is not mapped")
     if not foralls:
-        raise ShimError(f"{func.name}: no spmd.forall")
+        return _analyse_returned_reduce(func, env, args, reduces)
     group = foralls[0]
     lbs, ubs, steps = _segments(group)
     tile = _attr_ints(group.attrs, "spmd.tile_sizes")
@@ -362,13 +413,16 @@ def analyse(func: Func) -> Mapping:
         if reduces:
             red, _ = reduces[0]
             kind = _attr_enum(red.attrs, "spmd.kind") or "add"
-            yields = [o for o in red.region if o.name == "spmd.yield"]
-            y = env.defs.get(yields[-1].operands[0]) if yields and yields[-1].operands else None
-            while y is not None and y.name == "arith.select":
-                y = env.defs.get(y.operands[1])
-            if y is None or y.name != "memref.load":
-                raise ShimError(f"{func.name}: spmd.reduce body must yield one (masked) load")
-            src = y.operands[0]
+            src = _reduce_source(func, env, red)
+            if at.extra not in _COMBINES[kind]:
+                # Each tile's `kind` result is folded into out by a different
+                # operation: out = out (+) r_0 (+) r_1 ..., not one reduction.
+                raise ShimError(f"{func.name}: per-tile {kind} results combined by atomic_rmw {at.extra}: "
+                                f"not a single {kind} reduction")
+            init = env.consts.get(red.operands[3]) if len(red.operands) > 3 else None
+            if init is None or not _is_identity(kind, init):
+                raise ShimError(f"{func.name}: the spmd.reduce init must be the identity of {kind} "
+                                f"(each tile folds it in once)")
         else:
             kind = {"addf": "add", "addi": "add"}.get(at.extra)
             v = env.defs.get(val)
@@ -442,6 +496,63 @@ def analyse(func: Func) -> Mapping:
         "memory_policy": policy or "none"})
 
 
+# memref.atomic_rmw kinds that combine per-tile results of each reduction kind
+# into the output with the same operation (signed i32 max/min; f32 max/min
+# with arith.maximumf/minimumf's NaN and signed-zero rules).
+_COMBINES = {"add": ("addf", "addi"), "mul": ("mulf", "muli"), "max": ("maximumf", "maxs"),
+             "min": ("minimumf", "mins"), "and": ("andi",), "or": ("ori",), "xor": ("xori",)}
+
+
+def _is_identity(kind: str, v) -> bool:
+    if kind in ("add", "or", "xor"):
+        return v == 0
+    if kind == "mul":
+        return v == 1
+    if kind == "and":
+        return v == -1
+    if kind == "max":
+        return v == float("-inf") or v == -2 ** 31
+    return v == float("inf") or v == 2 ** 31 - 1  # min
+
+
+def _reduce_source(func: Func, env: _Env, red: Op) -> str:
+    """The memref an spmd.reduce body loads and yields (through masking selects)."""
+    yields = [o for o in red.region if o.name == "spmd.yield"]
+    y = env.defs.get(yields[-1].operands[0]) if yields and yields[-1].operands else None
+    while y is not None and y.name == "arith.select":
+        y = env.defs.get(y.operands[1])
+    if y is None or y.name != "memref.load":
+        raise ShimError(f"{func.name}: spmd.reduce body must yield one (masked) load")
+    return y.operands[0]
+
+
+def _analyse_returned_reduce(func: Func, env: _Env, args: dict, reduces: list) -> Mapping:
+    """A top-level spmd.reduce over [0, N) whose value the function returns
+    (the host-level reduction the SCF and OpenMP lowerings take, e.g.
+    test/SPMD/sum.mlir @sum): the value is init (+) A[0] (+) ... (+) A[N-1]."""
+    rets = [op for op in func.ops if op.name == "func.return"]
+    top = [op for op in func.ops if op.name == "spmd.reduce"]
+    if len(reduces) != 1 or len(top) != 1 or not rets or rets[-1].operands != [top[0].result]:
+        raise ShimError(f"{func.name}: no spmd.forall")
+    red = top[0]
+    lb, ub, step = (env.index(v) for v in red.operands[:3])
+    if lb.terms or lb.const != 0 or step.terms or step.const != 1:
+        raise ShimError(f"{func.name}: the returned spmd.reduce must run over [0, N) with step 1")
+    src = _reduce_source(func, env, red)
+    ld = next(op for op in _iter_ops(red.region) if op.name == "memref.load" and op.operands[0] == src)
+    idx = [env.index(v) for v in _vals(ld.extra)]
+    if len(idx) != 1 or idx[0].const != 0 or idx[0].terms != {red.block_args[0]: 1}:
+        raise ShimError(f"{func.name}: the reduce must load {src}[iv]")
+    kind = _attr_enum(red.attrs, "spmd.kind") or "add"
+    init = env.consts.get(red.operands[3]) if len(red.operands) > 3 else None
+    if init is None:
+        raise ShimError(f"{func.name}: the spmd.reduce init must be a constant")
+    n_arg = red.operands[1] if red.operands[1] in args else ub.const
+    elem = args[src].elem
+    return Mapping(func.name, "reduce", f"spmdb200_reduce_{elem}", {
+        "kind": kind, "input": src, "output": None, "n": n_arg, "combine": "return", "elem": elem, "init": init})
+
+
 # ----------------------------------------------------------------------------- binding
 class BoundKernel:
     """Calls the mapped entry with the MLIR function's own argument list."""
@@ -480,6 +591,12 @@ class BoundKernel:
             return k.stencil_nd(env[d["input"]], out, offs, weights=d["weights"],
                                 scale=1.0 if d["scale"] is None else d["scale"], tile_sizes=d["tile_sizes"],
                                 steps=d["steps"], policy=policy, stream=stream)
+        if m.pattern == "reduce" and d["output"] is None:  # the function returns the value
+            n = num(d["n"]) if isinstance(d["n"], str) else int(d["n"])
+            a = env[d["input"]][:n]
+            out = a.new_empty(1)
+            k.reduce(d["kind"], a, d["init"], out=out, stream=stream)
+            return out.item()
         if m.pattern == "reduce":
             n = num(d["n"]) if d["n"] else env[d["input"]].shape[0]
             a, out = env[d["input"]][:n], env[d["output"]].reshape(1)
@@ -502,6 +619,8 @@ def _iter_ops(ops):
     for op in ops:
         yield op
         yield from _iter_ops(op.region)
+        for r in op.more_regions:
+            yield from _iter_ops(r)
 
 
 def load(text: str, skip_unmapped: bool = False) -> dict:

@@ -94,3 +94,92 @@ def test_reference_kernel_files_map():
     steps = {d["function"]: (d["offsets"], d["steps"]) for d in shim.describe((REFERENCE / "promotion.mlir").read_text())}
     assert steps["stencil1d_stepped"] == ([[0], [1]], [2])
     assert steps["stencil_pos_halo"][0] == [[1], [2]] and steps["stencil_neg_halo"][0] == [[-1], [-2]]
+
+
+_FORMS = r'''
+func.func @sum_returned(%A: memref<?xf32, #spmd.addr_space<global>>, %N: index) -> f32 attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  %z = arith.constant 0.0 : f32
+  %r = "spmd.reduce"(%c0, %N, %c1, %z) ({
+  ^bb0(%k: index):
+    %v = memref.load %A[%k] : memref<?xf32, #spmd.addr_space<global>>
+    "spmd.yield"(%v) : (f32) -> ()
+  }) {"spmd.kind" = #spmd.reduction_kind<add>} : (index, index, index, f32) -> f32
+  func.return %r : f32
+}
+
+func.func @max_then_add(%A: memref<?xf32>, %out: memref<f32>, %N: index) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  %c64 = arith.constant 64 : index
+  "spmd.forall"(%c0, %N, %c64) ({
+  ^bb0(%t: index):
+    %lo = arith.constant 0xFF800000 : f32
+    %m = "spmd.reduce"(%c0, %c64, %c1, %lo) ({
+    ^bb1(%l: index):
+      %g = arith.addi %t, %l : index
+      %v = memref.load %A[%g] : memref<?xf32>
+      "spmd.yield"(%v) : (f32) -> ()
+    }) {"spmd.kind" = #spmd.reduction_kind<max>} : (index, index, index, f32) -> f32
+    memref.atomic_rmw addf %m, %out[] : (f32, memref<f32>) -> f32
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>, "spmd.mapping" = #spmd.level<group>} : (index, index, index) -> ()
+  func.return
+}
+
+func.func @max_f32(%A: memref<?xf32>, %out: memref<f32>, %N: index) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  %c64 = arith.constant 64 : index
+  "spmd.forall"(%c0, %N, %c64) ({
+  ^bb0(%t: index):
+    %lo = arith.constant 0xFF800000 : f32
+    %m = "spmd.reduce"(%c0, %c64, %c1, %lo) ({
+    ^bb1(%l: index):
+      %g = arith.addi %t, %l : index
+      %v = memref.load %A[%g] : memref<?xf32>
+      "spmd.yield"(%v) : (f32) -> ()
+    }) {"spmd.kind" = #spmd.reduction_kind<max>} : (index, index, index, f32) -> f32
+    memref.atomic_rmw maximumf %m, %out[] : (f32, memref<f32>) -> f32
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>, "spmd.mapping" = #spmd.level<group>} : (index, index, index) -> ()
+  func.return
+}
+
+func.func @guarded(%A: memref<?xf32>, %N: index, %t: f32) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  "spmd.forall"(%c0, %N, %c1) ({
+  ^bb0(%i: index):
+    %v = memref.load %A[%i] : memref<?xf32>
+    %c = arith.cmpf ogt, %v, %t : f32
+    "spmd.if"(%c) ({
+      memref.store %t, %A[%i] : memref<?xf32>
+      "spmd.yield"() : () -> ()
+    }, {
+      "spmd.yield"() : () -> ()
+    }) : (i1) -> ()
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
+  func.return
+}
+'''
+
+
+def test_forms_beyond_the_kernel_file():
+    """Hexadecimal f32 literals, memref types with attributes, multi-region
+    spmd.if, a returned top-level reduce, and per-tile results combined by an
+    operation other than the reduction's own kind (reported, not mapped)."""
+    shim = spmd_mod("mlir_shim")
+    d = {x["function"]: x for x in shim.describe(_FORMS)}
+    r = d["sum_returned"]
+    assert r["pattern"] == "reduce" and r["output"] is None and r["combine"] == "return" and r["init"] == 0.0
+    assert "not a single max reduction" in d["max_then_add"]["error"]
+    assert d["max_f32"]["entry"] == "spmdb200_reduce_f32" and d["max_f32"]["kind"] == "max"
+    assert "spmd.if" in d["guarded"]["error"]
+    assert shim._const_value("0xFF800000", "f32") == float("-inf")
+    assert shim._const_value("0x7FC00000", "f32") != shim._const_value("0x7FC00000", "f32")  # NaN
+    assert shim._const_value("0xFFFFFFFF", "i32") == -1
+    assert shim._vals("%A: memref<?xf32, #spmd.addr_space<global>>, %N: index") == [
+        "%A: memref<?xf32, #spmd.addr_space<global>>", "%N: index"]
