@@ -457,7 +457,25 @@ def secondary_benchmarks(kernels, torch, hbm_peak: float) -> dict:
     ms = timed(lambda: kernels.axpy(2.5, x, y), flush_l2=False)
     gbs = n * 12 / ms / 1e6
     out["axpy_2^28"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3)}
-    del x, y
+    # The general elementwise forall (body program in shared-memory registers)
+    # on the same axpy body, and on a three-input body sqrt(|a*b - c|).
+    fp = importlib.import_module("spmd-dialect_b200.forall_program")
+    ax = fp.compile_dag("s", {"x": ("load", 0), "y": ("load", 1), "a": ("const", 0), "m": ("mul", "a", "x"),
+                              "s": ("add", "m", "y")})
+    ms = timed(lambda: kernels.forall_map([x, y], y, ax[0], [2.5], n_regs=ax[1]), flush_l2=False)
+    gbs = n * 12 / ms / 1e6
+    out["forall_map_axpy_body_2^28"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
+                                        "frac_of_hbm": round(gbs / hbm_peak, 3), "insns": len(ax[0])}
+    z = torch.empty_like(x)
+    b3 = fp.compile_dag("r", {"a": ("load", 0), "b": ("load", 1), "c": ("load", 2), "p": ("mul", "a", "b"),
+                              "d": ("sub", "p", "c"), "q": ("abs", "d"), "r": ("sqrt", "q")})
+    n3 = n // 2
+    xs, ys, zs = x[:n3], y[:n3], y[n3:]
+    ms = timed(lambda: kernels.forall_map([xs, ys, zs], z[:n3], b3[0], n_regs=b3[1]), flush_l2=False)
+    gbs = n3 * 16 / ms / 1e6
+    out["forall_map_3in_2^27"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 3),
+                                  "insns": len(b3[0])}
+    del x, y, z
     # Promoted 3-point stencil B = (A + A east) + A south on the harness layout
     # (A is (N+1) x (N+1)): 4096^2 is the reference's own configuration, 8192^2
     # the same above the L2 size.  Bytes: A read once, B written once.

@@ -125,6 +125,46 @@ int spmdb200_axpy(float a,
                   float *Y_base, float *Y_aligned, int64_t Y_offset, int64_t Y_size, int64_t Y_stride,
                   int64_t N, void *stream);
 
+/* Elementwise spmd.forall with a general f32 body, y[p] = f(x0[p], x1[p], ...)
+ * over a rank 1-3 domain (the lane lowering of SPMDToGPU.cpp:491-580 applied
+ * to any body of arith ops, not only C = A + B).  The body is a straight-line
+ * program of `n_insns` instructions, two int32 words each:
+ *   w0 = op | dst << 8 | a << 16 | b << 24,  w1 = aux
+ * over `n_regs` f32 registers (<= SPMDB200_MAP_MAX_REGS):
+ *   LOAD     r[dst] = inputs[aux][p]        (all LOADs come first)
+ *   CONST    r[dst] = consts[aux]
+ *   ADD SUB MUL DIV   r[dst] = r[a] op r[b], IEEE round-to-nearest, each
+ *                     rounded on its own (never contracted to an FMA)
+ *   MAXIMUM MINIMUM   arith.maximumf / minimumf (NaN in, NaN out; -0 < +0)
+ *   NEG ABS SQRT      r[dst] = f(r[a]) (sign flip, sign clear, IEEE sqrt)
+ *   CMP      r[dst] = cmpf(aux, r[a], r[b]) ? 1 : 0, aux = arith.cmpf's
+ *            predicate number (0 false, 1 oeq, 2 ogt, 3 oge, 4 olt, 5 ole,
+ *            6 one, 7 ord, 8 ueq, 9 ugt, 10 uge, 11 ult, 12 ule, 13 une,
+ *            14 uno, 15 true)
+ *   SELECT   r[dst] = r[aux] != 0 ? r[a] : r[b]
+ *   AND OR XOR        booleans (nonzero = true) -> 1 / 0
+ *   STORE    out[p] = r[a]                  (exactly one, the last)
+ * Every register is written before it is read.  sizes[d] is the domain;
+ * input_strides holds rank strides (in elements) per input, row after row;
+ * out_strides likewise.  The output may be one of the inputs (same view: each
+ * point is read before it is written); other overlaps are undefined.  NaN
+ * results are NaN (the payload is not specified).  No reference entry. */
+enum {
+  SPMDB200_MAP_LOAD = 0, SPMDB200_MAP_CONST = 1, SPMDB200_MAP_ADD = 2, SPMDB200_MAP_SUB = 3,
+  SPMDB200_MAP_MUL = 4, SPMDB200_MAP_DIV = 5, SPMDB200_MAP_MAXIMUM = 6, SPMDB200_MAP_MINIMUM = 7,
+  SPMDB200_MAP_NEG = 8, SPMDB200_MAP_ABS = 9, SPMDB200_MAP_SQRT = 10, SPMDB200_MAP_CMP = 11,
+  SPMDB200_MAP_SELECT = 12, SPMDB200_MAP_AND = 13, SPMDB200_MAP_OR = 14, SPMDB200_MAP_XOR = 15,
+  SPMDB200_MAP_STORE = 16
+};
+#define SPMDB200_MAP_MAX_INPUTS 8
+#define SPMDB200_MAP_MAX_REGS 16
+#define SPMDB200_MAP_MAX_INSNS 64
+#define SPMDB200_MAP_MAX_CONSTS 32
+int spmdb200_forall_map(int rank, const int64_t *sizes, int n_inputs, const float *const *inputs,
+                        const int64_t *input_strides, float *out, const int64_t *out_strides,
+                        const int32_t *code, int n_insns, const float *consts, int n_consts, int n_regs,
+                        void *stream);
+
 /* 3-point promoted stencil B[i,j] = (A[i,j] + A[i,j+1]) + A[i+1,j] over
  * i < N, j < M with a shared-memory tile plus 1-cell halo; reads outside A's
  * sizes contribute 0.  Device-pointer form of promoted_stencil_kernel

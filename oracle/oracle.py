@@ -39,6 +39,7 @@ _SIGS = {
     "oracle_jacobi3d": (None, D3 + D3 + [c_i, c_i, c_p]),
     "oracle_num_threads": (ctypes.c_int, []),
     "oracle_set_num_threads": (ctypes.c_int, [ctypes.c_int]),
+    "oracle_forall_map": (None, [ctypes.c_int, c_p, ctypes.c_int, c_p, c_p, c_p, c_p, c_p, ctypes.c_int, c_p]),
     "oracle_stencil_nd": (None, [ctypes.c_int, c_p, c_p, c_p, c_p, c_p, c_p, ctypes.c_int, c_p, c_p, c_f, c_p]),
 }
 
@@ -204,4 +205,24 @@ def stencil_nd(A: np.ndarray, out_shape: tuple, offsets, weights=None, scale: fl
     st = None if steps is None else i64(steps)
     lib().oracle_stencil_nd(rank, _p(A), _p(a_size), _p(a_str), _p(B), _p(b_size), _p(b_str), off.shape[0],
                             _p(off), _p(w) if w is not None else None, c_f(scale), _p(st) if st is not None else None)
+    return B
+
+
+def forall_map(inputs, out_shape, code, consts=(), out: np.ndarray | None = None) -> np.ndarray:
+    """The general elementwise forall on host arrays (see oracle_forall_map):
+    every point of out_shape gets the body program's STORE; inputs are arrays
+    (any strides) of out_shape."""
+    rank = len(out_shape)
+    ins = [np.asarray(a, dtype=np.float32) for a in inputs]
+    for a in ins:
+        if a.shape != tuple(out_shape):
+            raise ValueError("every input has the domain's shape")
+    B = np.zeros(out_shape, np.float32) if out is None else out
+    i64 = lambda v: np.ascontiguousarray(np.asarray(v, dtype=np.int64))
+    ptrs = (c_p * max(len(ins), 1))(*[a.ctypes.data for a in ins])
+    st = i64([s // 4 for a in ins for s in a.strides] or [0])
+    words = np.ascontiguousarray(np.asarray([w for ins_ in code for w in ins_], dtype=np.int32))
+    cs = np.ascontiguousarray(np.asarray(list(consts) or [0.0], dtype=np.float32))
+    lib().oracle_forall_map(rank, _p(i64(out_shape)), len(ins), ctypes.cast(ptrs, c_p), _p(st), _p(B),
+                            _p(i64([s // 4 for s in B.strides])), _p(words), len(code), _p(cs))
     return B

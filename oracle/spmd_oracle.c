@@ -274,6 +274,82 @@ EXPORT int32_t oracle_reduce_i32(int kind, const int32_t *A, int64_t N, int32_t 
 }
 
 /* ---------------------------------------------------------------------------
+ * Elementwise forall with a general f32 body.  SPMDToSCF.cpp:38-78 turns the
+ * forall into nested scf.for loops (row-major order) and the body's arith ops
+ * run once per point in SSA order, each rounded on its own.  The body arrives
+ * as the straight-line program spmdb200_forall_map takes: two int32 words per
+ * instruction, w0 = op | dst << 8 | a << 16 | b << 24, w1 = aux; opcodes
+ * 0 LOAD, 1 CONST, 2 ADD, 3 SUB, 4 MUL, 5 DIV, 6 MAXIMUM (arith.maximumf),
+ * 7 MINIMUM, 8 NEG, 9 ABS (math.absf), 10 SQRT (math.sqrt), 11 CMP
+ * (arith.cmpf, aux = predicate number), 12 SELECT (aux = condition register),
+ * 13 AND, 14 OR, 15 XOR (i1 values as 0 / 1), 16 STORE.  Strides in elements,
+ * `rank` per input, row after row.
+ * ------------------------------------------------------------------------- */
+static int cmpf_pred(int pred, float x, float y) {
+  const int u = isnan(x) || isnan(y);
+  switch (pred) {
+    case 1: return x == y;
+    case 2: return x > y;
+    case 3: return x >= y;
+    case 4: return x < y;
+    case 5: return x <= y;
+    case 6: return !u && x != y;
+    case 7: return !u;
+    case 8: return u || x == y;
+    case 9: return u || x > y;
+    case 10: return u || x >= y;
+    case 11: return u || x < y;
+    case 12: return u || x <= y;
+    case 13: return x != y;
+    case 14: return u;
+    case 15: return 1;
+    default: return 0;
+  }
+}
+EXPORT void oracle_forall_map(int rank, const int64_t *sizes, int n_in, const float *const *in,
+                              const int64_t *in_st, float *out, const int64_t *out_st, const int32_t *code,
+                              int n_insns, const float *consts) {
+  int64_t sz[3] = {1, 1, 1}, ost[3] = {0, 0, 0}, ist[8][3];
+  memset(ist, 0, sizeof(ist));
+  for (int d = 0; d < rank; ++d) {
+    sz[3 - rank + d] = sizes[d];
+    ost[3 - rank + d] = out_st[d];
+    for (int k = 0; k < n_in && k < 8; ++k) ist[k][3 - rank + d] = in_st[k * rank + d];
+  }
+  for (int64_t i0 = 0; i0 < sz[0]; ++i0)
+    for (int64_t i1 = 0; i1 < sz[1]; ++i1)
+      for (int64_t i2 = 0; i2 < sz[2]; ++i2) {
+        float r[16] = {0};
+        for (int pc = 0; pc < n_insns; ++pc) {
+          const int32_t w0 = code[2 * pc], aux = code[2 * pc + 1];
+          const int op = w0 & 255, d = (w0 >> 8) & 255, a = (w0 >> 16) & 255, b = (int)((uint32_t)w0 >> 24);
+          const float x = r[a & 15], y = r[b & 15];
+          float v = 0.0f;
+          switch (op) {
+            case 0: v = in[aux][i0 * ist[aux][0] + i1 * ist[aux][1] + i2 * ist[aux][2]]; break;
+            case 1: v = consts[aux]; break;
+            case 2: v = x + y; break;
+            case 3: v = x - y; break;
+            case 4: v = x * y; break;
+            case 5: v = x / y; break;
+            case 6: v = f_maximum(x, y); break;
+            case 7: v = f_minimum(x, y); break;
+            case 8: v = -x; break;
+            case 9: v = fabsf(x); break;
+            case 10: v = sqrtf(x); break;
+            case 11: v = cmpf_pred(aux, x, y) ? 1.0f : 0.0f; break;
+            case 12: v = r[aux & 15] != 0.0f ? x : y; break;
+            case 13: v = (x != 0.0f && y != 0.0f) ? 1.0f : 0.0f; break;
+            case 14: v = (x != 0.0f || y != 0.0f) ? 1.0f : 0.0f; break;
+            case 15: v = ((x != 0.0f) != (y != 0.0f)) ? 1.0f : 0.0f; break;
+            default: out[i0 * ost[0] + i1 * ost[1] + i2 * ost[2]] = x; continue;
+          }
+          r[d & 15] = v;
+        }
+      }
+}
+
+/* ---------------------------------------------------------------------------
  * Jacobi-2D 5-point sweep over local rows [row_lo, row_hi) of a row-major grid
  * with `pitch` elements per row and W columns.  Global row index of local row r
  * is g_row0 + r; global rows 0 and G-1 and columns 0 and W-1 are the fixed

@@ -49,6 +49,8 @@ _SIGS = {
     "spmdb200_ewise": (ctypes.c_int, D1 + D1 + D1 + [c_i, c_p]),
     "spmdb200_axpy": (ctypes.c_int, [c_f] + D1 + D1 + [c_i, c_p]),
     "spmdb200_stencil3pt": (ctypes.c_int, D2 + D2 + [c_i, c_i, c_p]),
+    "spmdb200_forall_map": (ctypes.c_int, [ctypes.c_int, c_p, ctypes.c_int, c_p, c_p, c_p, c_p, c_p, ctypes.c_int,
+                                           c_p, ctypes.c_int, ctypes.c_int, c_p]),
     "spmdb200_sum_workspace_bytes": (c_sz, [c_i]),
     "spmdb200_sum_f32": (ctypes.c_int, D1 + D0 + [c_i, c_p, c_sz, c_p]),
     "spmdb200_sum_f32_noalloc": (ctypes.c_int, D1 + D0 + [c_i, c_p]),

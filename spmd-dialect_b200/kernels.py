@@ -12,6 +12,7 @@ import ctypes
 import torch
 
 from ._lib import c_i, c_p, call, lib
+from .forall_program import insn as map_insn  # noqa: F401  (re-exported)
 
 _DTYPES = {torch.float32: "f32", torch.int32: "i32", torch.uint8: "u8", torch.float64: "f64"}
 
@@ -97,6 +98,30 @@ def stencil_nd(a: torch.Tensor, out: torch.Tensor, offsets, weights=None, scale:
          _i64(steps) if steps is not None else None, c_i(max_group_bytes), policy, ctypes.byref(promoted),
          _stream(stream))
     return bool(promoted.value)
+
+
+def forall_map(inputs, out: torch.Tensor, code, consts=(), n_regs: int | None = None, stream=None) -> torch.Tensor:
+    """out[p] = f(inputs[0][p], ...) over out's domain (rank 1-3), f the
+    straight-line program `code` (a list of forall_program.insn pairs; LOADs
+    first, one STORE last).  Each input is a view with out's shape."""
+    rank = out.dim()
+    if not 1 <= rank <= 3:
+        raise ValueError("forall_map: rank 1-3")
+    for t in inputs:
+        if tuple(t.shape) != tuple(out.shape) or t.dtype != torch.float32 or not t.is_cuda:
+            raise ValueError("forall_map: every input is a CUDA f32 view with out's shape")
+    if out.dtype != torch.float32 or not out.is_cuda:
+        raise ValueError("forall_map: out must be a CUDA f32 tensor")
+    words = [int(w) for ins in code for w in ins]
+    if n_regs is None:
+        n_regs = 1 + max(max((w0 >> 8) & 255, (w0 >> 16) & 255, (w0 >> 24) & 255) for w0 in words[0::2])
+    ptrs = (c_p * max(len(inputs), 1))(*[t.data_ptr() for t in inputs])
+    strides = _i64([s for t in inputs for s in t.stride()] or [0])
+    cs = (ctypes.c_float * max(len(consts), 1))(*[float(c) for c in consts])
+    call("spmdb200_forall_map", rank, _i64(out.shape), len(inputs), ptrs, strides, c_p(out.data_ptr()),
+         _i64(out.stride()), (ctypes.c_int32 * len(words))(*words), len(code), cs, len(consts), n_regs,
+         _stream(stream))
+    return out
 
 
 def sum_workspace(n: int, device=None) -> torch.Tensor:

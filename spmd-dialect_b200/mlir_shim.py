@@ -45,6 +45,11 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 
+if __package__:
+    from . import forall_program as _fp
+else:  # run as a script from its own directory
+    import forall_program as _fp
+
 
 class ShimError(ValueError):
     """The MLIR text uses a form or pattern the shim does not map."""
@@ -164,7 +169,7 @@ def _parse_simple(line: str) -> Op:
         return Op(name, None, _vals(mm.group(1)) if mm else [])
     if name in ("func.return", "return"):
         return Op("func.return", None, _vals(rest.split(":", 1)[0]))
-    if name.startswith("arith."):
+    if name.startswith("arith.") or name.startswith("math."):
         ops, t = rest.rsplit(":", 1)
         return Op(name, res, _vals(ops), type=t.strip())
     return Op("unknown", res, [], extra=line)
@@ -440,9 +445,24 @@ def analyse(func: Func) -> Mapping:
         return Mapping(func.name, "reduce", entry, {"kind": kind, "input": src, "output": out, "n": n_arg,
                                                     "combine": at.extra, "elem": elem})
 
+    if not stores and not reduces and all(op.name in ("spmd.forall", "spmd.yield", "arith.constant", "func.return")
+                                          for op, _ in nodes):
+        # A forall whose body does nothing (test/SPMD/normalize.mlir): no effect to run.
+        return Mapping(func.name, "empty", None, {})
     if len(stores) != 1:
         raise ShimError(f"{func.name}: expected exactly one memref.store, found {len(stores)}")
     st, _ = stores[0]
+    try:
+        return _analyse_linear(func, env, args, st, foralls, lbs, ubs, tile, policy)
+    except ShimError as linear_err:
+        try:
+            return _analyse_map(func, env, args, st, foralls, lbs, ubs, steps)
+        except ShimError as map_err:
+            raise ShimError(f"{linear_err}; as an elementwise map: {str(map_err).split(': ', 1)[-1]}") from None
+
+
+def _analyse_linear(func: Func, env: _Env, args: dict, st: Op, foralls: list, lbs, ubs, tile, policy) -> Mapping:
+    """ewise add / axpy / a linear stencil (a left fold of weighted loads)."""
     val, dst = st.operands
     dst_idx = [env.index(v) for v in _vals(st.extra)]
     rank = len(dst_idx)
@@ -496,6 +516,121 @@ def analyse(func: Func) -> Mapping:
         "memory_policy": policy or "none"})
 
 
+# arith / math ops of an elementwise body and their forall_map opcodes.
+_MAP_ARITH = {"arith.addf": "add", "arith.subf": "sub", "arith.mulf": "mul", "arith.divf": "div",
+              "arith.maximumf": "maximum", "arith.minimumf": "minimum", "arith.negf": "neg", "math.absf": "abs",
+              "math.sqrt": "sqrt", "arith.cmpf": "cmp", "arith.select": "select", "arith.andi": "and",
+              "arith.ori": "or", "arith.xori": "xor"}
+
+
+def _analyse_map(func: Func, env: _Env, args: dict, st: Op, foralls: list, lbs, ubs, steps) -> Mapping:
+    """An elementwise forall with a general f32 body: out[p] = f(in_k[p], ...)
+    where every load reads its memref at the store's own index and f is any
+    DAG of the ops in _MAP_ARITH, f32 constants and f32 scalar arguments --
+    the per-point body SPMDToGPU.cpp:491-580 lowers, run by
+    spmdb200_forall_map."""
+    val, dst = st.operands
+    if args.get(dst) is None or args[dst].kind != "memref" or args[dst].elem != "f32":
+        raise ShimError(f"{func.name}: the stored memref must be an f32 memref argument")
+    dst_idx = [env.index(v) for v in _vals(st.extra)]
+    rank = len(dst_idx)
+    if not 1 <= rank <= 3 or args[dst].rank != rank:
+        raise ShimError(f"{func.name}: rank 1-3 stores of the memref's full rank only")
+    if len(foralls) > 2:
+        raise ShimError(f"{func.name}: at most a group and a lane forall")
+    group, inner = foralls[0], (foralls[1] if len(foralls) > 1 else None)
+    if len(group.block_args) < rank or (inner is not None and len(inner.block_args) < rank):
+        raise ShimError(f"{func.name}: the forall's rank is below the store's")
+    lower, upper, dom_step = [], [], []
+    for d in range(rank):
+        want = {group.block_args[d]: 1}
+        g_step = env.index(steps[d])
+        if inner is not None:
+            want[inner.block_args[d]] = 1
+            i_lb, i_ub, i_st = (env.index(x[d]) for x in _segments(inner))
+            if (i_lb.terms or i_lb.const != 0 or i_st.terms or i_st.const != 1 or i_ub.terms or g_step.terms
+                    or i_ub.const != g_step.const):
+                raise ShimError(f"{func.name}: the lane forall must cover [0, group step) with step 1")
+        elif g_step.terms or g_step.const < 1:
+            raise ShimError(f"{func.name}: the forall step must be a positive constant")
+        if dst_idx[d].terms != want or dst_idx[d].const != 0:
+            raise ShimError(f"{func.name}: the store index is not the loop index in dimension {d}")
+        a = env.index(lbs[d])
+        if len(a.terms) > 1 or any(c != 1 for c in a.terms.values()) or (a.terms and a.const):
+            raise ShimError(f"{func.name}: lower bound {lbs[d]} must be a constant or an index argument")
+        lower.append(next(iter(a.terms)) if a.terms else a.const)
+        u = env.index(ubs[d])
+        if len(u.terms) > 1 or any(c != 1 for c in u.terms.values()) or (u.terms and u.const):
+            raise ShimError(f"{func.name}: upper bound {ubs[d]} must be a constant or an index argument")
+        upper.append(next(iter(u.terms)) if u.terms else u.const)
+        dom_step.append(1 if inner is not None else g_step.const)
+
+    inputs: list = []
+    consts: list = []
+    nodes: dict = {}
+
+    def visit(v):
+        if v in nodes:
+            return
+        op = env.defs.get(v)
+        if op is None:
+            a = args.get(v)
+            if a is None or a.kind != "f32":
+                raise ShimError(f"{func.name}: value {v} is neither an op result nor an f32 argument")
+            consts.append(v)
+            nodes[v] = ("const", len(consts) - 1)
+            return
+        if op.name == "memref.load":
+            src = op.operands[0]
+            if args.get(src) is None or args[src].kind != "memref" or args[src].elem != "f32" \
+                    or args[src].rank != rank:
+                raise ShimError(f"{func.name}: {src} is not an f32 memref argument of rank {rank}")
+            idx = [env.index(x) for x in _vals(op.extra)]
+            if any(i.terms != j.terms or i.const != j.const for i, j in zip(idx, dst_idx)):
+                raise ShimError(f"{func.name}: {src} is read off the store's index (not elementwise)")
+            if src not in inputs:
+                inputs.append(src)
+            nodes[v] = ("load", inputs.index(src))
+            return
+        if op.name == "arith.constant":
+            if op.type not in ("f32", "i1"):
+                raise ShimError(f"{func.name}: constant of type {op.type} in an elementwise body")
+            consts.append(float(env.consts[v]))
+            nodes[v] = ("const", len(consts) - 1)
+            return
+        kind = _MAP_ARITH.get(op.name)
+        if kind is None:
+            raise ShimError(f"{func.name}: {op.name} in an elementwise body is not mapped")
+        want_t = "i1" if kind in ("and", "or", "xor") else "f32"
+        if kind == "select":
+            if op.type != "f32":
+                raise ShimError(f"{func.name}: select of type {op.type}")
+        elif op.type != want_t:
+            raise ShimError(f"{func.name}: {op.name} of type {op.type} (f32 bodies only)")
+        for o in op.operands:
+            visit(o)
+        if kind == "cmp":
+            pred = op.extra.strip()
+            if pred not in _fp.CMPF:
+                raise ShimError(f"{func.name}: arith.cmpf predicate {pred}")
+            nodes[v] = ("cmp", op.operands[0], op.operands[1], _fp.CMPF[pred])
+        else:
+            nodes[v] = (kind, *op.operands)
+
+    visit(val)
+    if not inputs:
+        raise ShimError(f"{func.name}: a body that loads nothing (a fill) is not mapped")
+    if len(consts) > _fp.MAX_CONSTS:
+        raise ShimError(f"{func.name}: more than {_fp.MAX_CONSTS} constants")
+    try:
+        code, n_regs, _, _ = _fp.compile_dag(val, nodes)
+    except ValueError as e:
+        raise ShimError(f"{func.name}: {e}") from None
+    return Mapping(func.name, "map", "spmdb200_forall_map", {
+        "rank": rank, "inputs": inputs, "output": dst, "lower": lower, "domain": upper, "steps": dom_step,
+        "code": [list(c) for c in code], "consts": consts, "n_regs": n_regs})
+
+
 # memref.atomic_rmw kinds that combine per-tile results of each reduction kind
 # into the output with the same operation (signed i32 max/min; f32 max/min
 # with arith.maximumf/minimumf's NaN and signed-zero rules).
@@ -532,9 +667,20 @@ def _analyse_returned_reduce(func: Func, env: _Env, args: dict, reduces: list) -
     test/SPMD/sum.mlir @sum): the value is init (+) A[0] (+) ... (+) A[N-1]."""
     rets = [op for op in func.ops if op.name == "func.return"]
     top = [op for op in func.ops if op.name == "spmd.reduce"]
-    if len(reduces) != 1 or len(top) != 1 or not rets or rets[-1].operands != [top[0].result]:
+    if len(reduces) != 1 or len(top) != 1:
         raise ShimError(f"{func.name}: no spmd.forall")
     red = top[0]
+    stored = [op for op in func.ops if op.name == "memref.store" and op.operands[0] == red.result]
+    target = None
+    if stored and len([op for op in func.ops if op.name == "memref.store"]) == 1:
+        # memref.store %r, %out[c] (test/SPMD/ops.mlir @sum): out[c] = the value
+        st = stored[0]
+        at = [env.index(v) for v in _vals(st.extra)]
+        if args.get(st.operands[1]) is None or any(a.terms for a in at):
+            raise ShimError(f"{func.name}: the reduce's value is stored to a non-argument or a varying index")
+        target = (st.operands[1], [a.const for a in at])
+    elif not rets or rets[-1].operands != [red.result]:
+        raise ShimError(f"{func.name}: no spmd.forall")
     lb, ub, step = (env.index(v) for v in red.operands[:3])
     if lb.terms or lb.const != 0 or step.terms or step.const != 1:
         raise ShimError(f"{func.name}: the returned spmd.reduce must run over [0, N) with step 1")
@@ -550,7 +696,8 @@ def _analyse_returned_reduce(func: Func, env: _Env, args: dict, reduces: list) -
     n_arg = red.operands[1] if red.operands[1] in args else ub.const
     elem = args[src].elem
     return Mapping(func.name, "reduce", f"spmdb200_reduce_{elem}", {
-        "kind": kind, "input": src, "output": None, "n": n_arg, "combine": "return", "elem": elem, "init": init})
+        "kind": kind, "input": src, "output": target[0] if target else None, "at": target[1] if target else None,
+        "n": n_arg, "combine": "store" if target else "return", "elem": elem, "init": init})
 
 
 # ----------------------------------------------------------------------------- binding
@@ -591,9 +738,26 @@ class BoundKernel:
             return k.stencil_nd(env[d["input"]], out, offs, weights=d["weights"],
                                 scale=1.0 if d["scale"] is None else d["scale"], tile_sizes=d["tile_sizes"],
                                 steps=d["steps"], policy=policy, stream=stream)
-        if m.pattern == "reduce" and d["output"] is None:  # the function returns the value
+        if m.pattern == "empty":
+            return None
+        if m.pattern == "map":
+            lo = [int(env[v]) if isinstance(v, str) else int(v) for v in d["lower"]]
+            hi = [num(u) if u in env else self._const(u) if isinstance(u, str) else int(u) for u in d["domain"]]
+            box = tuple(slice(a, max(a, b), s) for a, b, s in zip(lo, hi, d["steps"]))
+            views = [env[x][box] for x in d["inputs"]]
+            out = env[d["output"]][box]
+            if out.numel() == 0:
+                return out
+            consts = [float(env[c]) if isinstance(c, str) else c for c in d["consts"]]
+            return k.forall_map(views, out, [tuple(c) for c in d["code"]], consts, n_regs=d["n_regs"],
+                                stream=stream)
+        if m.pattern == "reduce" and d["combine"] in ("return", "store"):
             n = num(d["n"]) if isinstance(d["n"], str) else int(d["n"])
             a = env[d["input"]][:n]
+            if d["combine"] == "store":  # out[c] = init (+) a[0] (+) ...
+                target = env[d["output"]][tuple(d["at"])].reshape(1)
+                k.reduce(d["kind"], a, d["init"], out=target, stream=stream)
+                return None
             out = a.new_empty(1)
             k.reduce(d["kind"], a, d["init"], out=out, stream=stream)
             return out.item()

@@ -206,3 +206,95 @@ func.func @smooth_interior(%A: memref<?xf32>, %B: memref<?xf32>, %Nm1: index) at
      : (index, index, index) -> ()
   func.return
 }
+
+// Elementwise bodies beyond add / axpy (the general forall map).
+func.func @mul2d(%A: memref<?x?xf32>, %B: memref<?x?xf32>, %C: memref<?x?xf32>, %N: index, %M: index)
+    attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  "spmd.forall"(%c0, %c0, %N, %M, %c1, %c1) ({
+  ^bb0(%i: index, %j: index):
+    %a = memref.load %A[%i, %j] : memref<?x?xf32>
+    %b = memref.load %B[%i, %j] : memref<?x?xf32>
+    %p = arith.mulf %a, %b : f32
+    memref.store %p, %C[%i, %j] : memref<?x?xf32>
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 2, 2, 2>} : (index, index, index, index, index, index) -> ()
+  func.return
+}
+
+func.func @plus_one_from4(%A: memref<?xf32>, %B: memref<?xf32>, %N: index) attributes {spmd.kernel} {
+  %c4 = arith.constant 4 : index
+  %c1 = arith.constant 1 : index
+  %one = arith.constant 1.0 : f32
+  "spmd.forall"(%c4, %N, %c1) ({
+  ^bb0(%i: index):
+    %a = memref.load %A[%i] : memref<?xf32>
+    %b = arith.addf %a, %one : f32
+    memref.store %b, %B[%i] : memref<?xf32>
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
+  func.return
+}
+
+func.func @clamp_tiled(%A: memref<?xf32>, %B: memref<?xf32>, %N: index, %lim: f32) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  %c128 = arith.constant 128 : index
+  "spmd.forall"(%c0, %N, %c128) ({
+  ^bb0(%t: index):
+    "spmd.forall"(%c0, %c128, %c1) ({
+    ^bb1(%l: index):
+      %i = arith.addi %t, %l : index
+      %a = memref.load %A[%i] : memref<?xf32>
+      %big = arith.cmpf ogt, %a, %lim : f32
+      %neg = arith.negf %lim : f32
+      %small = arith.cmpf olt, %a, %neg : f32
+      %hi = arith.select %big, %lim, %a : f32
+      %v = arith.select %small, %neg, %hi : f32
+      memref.store %v, %B[%i] : memref<?xf32>
+      "spmd.yield"() : () -> ()
+    }) {operandSegmentSizes = array<i32: 1, 1, 1>, "spmd.mapping" = #spmd.level<lane>} : (index, index, index) -> ()
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>, "spmd.mapping" = #spmd.level<group>,
+      "spmd.tile_sizes" = array<i64: 128>} : (index, index, index) -> ()
+  func.return
+}
+
+func.func @hypot3d(%X: memref<?x?x?xf32>, %Y: memref<?x?x?xf32>, %R: memref<?x?x?xf32>, %D: index, %H: index,
+                   %W: index) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  %c2 = arith.constant 2 : index
+  "spmd.forall"(%c0, %c0, %c0, %D, %H, %W, %c1, %c1, %c2) ({
+  ^bb0(%i: index, %j: index, %k: index):
+    %x = memref.load %X[%i, %j, %k] : memref<?x?x?xf32>
+    %y = memref.load %Y[%i, %j, %k] : memref<?x?x?xf32>
+    %xx = arith.mulf %x, %x : f32
+    %yy = arith.mulf %y, %y : f32
+    %s = arith.addf %xx, %yy : f32
+    %r = math.sqrt %s : f32
+    %ax = math.absf %x : f32
+    %m = arith.maximumf %r, %ax : f32
+    %d = arith.divf %m, %r : f32
+    memref.store %d, %R[%i, %j, %k] : memref<?x?x?xf32>
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 3, 3, 3>} : (index, index, index, index, index, index, index, index, index) -> ()
+  func.return
+}
+
+func.func @scale_in_place(%B: memref<?xf32>, %N: index) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  %two = arith.constant 2.0 : f32
+  %one = arith.constant 1.0 : f32
+  "spmd.forall"(%c0, %N, %c1) ({
+  ^bb0(%i: index):
+    %b = memref.load %B[%i] : memref<?xf32>
+    %t = arith.mulf %b, %two : f32
+    %u = arith.addf %t, %one : f32
+    memref.store %u, %B[%i] : memref<?xf32>
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
+  func.return
+}

@@ -91,6 +91,16 @@ def test_reference_kernel_files_map():
         got = {d["function"]: d.get("entry") for d in shim.describe((REFERENCE / f).read_text())}
         for n, e in names.items():
             assert got.get(n) == e, (f, n, got)
+    maps = {"ewise.mlir": ["ewise2d"], "ops.mlir": ["ewise_square"],
+            "cross-pipeline-regression.mlir": ["ewise_regression", "ewise_nonzero_lb"],
+            "subset_positive.mlir": ["legal_kernel"]}
+    for f, names in maps.items():
+        got = {d["function"]: d for d in shim.describe((REFERENCE / f).read_text())}
+        for n in names:
+            assert got[n]["entry"] == "spmdb200_forall_map", (f, n, got[n])
+    kinds = {d["function"]: d for d in shim.describe((REFERENCE / "reduction-hierarchical-f32-kinds.mlir").read_text())}
+    assert kinds["reduce_add"]["entry"] == "spmdb200_hierarchical_sum"
+    assert all(kinds[k]["pattern"] is None for k in ("reduce_mul", "reduce_max", "reduce_min"))
     steps = {d["function"]: (d["offsets"], d["steps"]) for d in shim.describe((REFERENCE / "promotion.mlir").read_text())}
     assert steps["stencil1d_stepped"] == ([[0], [1]], [2])
     assert steps["stencil_pos_halo"][0] == [[1], [2]] and steps["stencil_neg_halo"][0] == [[-1], [-2]]
@@ -183,3 +193,46 @@ def test_forms_beyond_the_kernel_file():
     assert shim._const_value("0xFFFFFFFF", "i32") == -1
     assert shim._vals("%A: memref<?xf32, #spmd.addr_space<global>>, %N: index") == [
         "%A: memref<?xf32, #spmd.addr_space<global>>", "%N: index"]
+
+
+def test_general_elementwise_bodies(oracle_mod):
+    """Bodies beyond add / axpy map to the forall-map program; running the
+    program through the oracle equals numpy evaluating the MLIR ops one by one."""
+    import numpy as np
+    d = _by_name()
+    m = d["mul2d"]
+    assert m["pattern"] == "map" and m["inputs"] == ["%A", "%B"] and m["n_regs"] == 2
+    assert d["plus_one_from4"]["lower"] == [4] and d["plus_one_from4"]["consts"] == [1.0]
+    assert d["clamp_tiled"]["consts"] == ["%lim"] and d["clamp_tiled"]["steps"] == [1]
+    assert d["hypot3d"]["steps"] == [1, 1, 2] and d["hypot3d"]["rank"] == 3
+    assert d["scale_in_place"]["inputs"] == ["%B"] and d["scale_in_place"]["output"] == "%B"
+    rs = np.random.RandomState(3)
+    x, y = rs.randn(4, 6, 10).astype(np.float32), rs.randn(4, 6, 10).astype(np.float32)
+    h = d["hypot3d"]
+    got = oracle_mod.forall_map([x[:, :, ::2], y[:, :, ::2]], (4, 6, 5), h["code"], h["consts"])
+    xs, ys = x[:, :, ::2], y[:, :, ::2]
+    r = np.sqrt(xs * xs + ys * ys)
+    want = (np.maximum(r, np.abs(xs)) / r).astype(np.float32)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    c = d["clamp_tiled"]
+    a = rs.uniform(-3, 3, 300).astype(np.float32)
+    got = oracle_mod.forall_map([a], a.shape, c["code"], [1.5])
+    assert np.array_equal(got, np.clip(a, np.float32(-1.5), np.float32(1.5)))
+
+
+def test_empty_forall_maps_to_nothing():
+    shim = spmd_mod("mlir_shim")
+    text = """
+func.func @nothing(%N: index) attributes {spmd.kernel} {
+  %c2 = arith.constant 2 : index
+  %c3 = arith.constant 3 : index
+  "spmd.forall"(%c2, %N, %c3) ({
+  ^bb0(%i: index):
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
+  func.return
+}
+"""
+    (d,) = shim.describe(text)
+    assert d["pattern"] == "empty" and d["entry"] is None
+    assert shim.load(text)["nothing"](10) is None
