@@ -313,7 +313,8 @@ extern "C" int spmdb200_forall_map(int rank, const int64_t *sizes, int n_inputs,
   for (int j = 0; j < n_consts; ++j) p.consts[j] = consts[j];
   if (p.n == 0) return record_api_status(SPMDB200_OK, "");
   if (!out) return bad("null out");
-  bool vec = contiguous(p.size, p.out_st) && ((uintptr_t)out & 15u) == 0;
+  p.out = out;
+  bool vec =contiguous(p.size, p.out_st) && ((uintptr_t)out & 15u) == 0;
   for (int i = 0; i < nl; ++i) {
     const int in = code[2 * i + 1];
     const float *src = inputs[in];
