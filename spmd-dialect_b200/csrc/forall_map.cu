@@ -38,9 +38,11 @@ namespace spmdb200 {
 namespace {
 
 constexpr int kMapThreads = 256;
-constexpr int kMapSlots = 2;
-constexpr int64_t kMapChunk = (int64_t)kMapThreads * kMapSlots * 4;
 constexpr int kMaxLoads = SPMDB200_MAP_MAX_INPUTS;
+
+// float4 groups a thread owns per chunk, for a body with nl inputs.
+constexpr int map_slots(int /*nl*/) { return 2; }
+constexpr int64_t map_chunk(int nl) { return (int64_t)kMapThreads * map_slots(nl) * 4; }
 
 struct MapParams {
   const float *ld_src[kMaxLoads];  // source of the i-th leading LOAD
@@ -92,13 +94,13 @@ __device__ __forceinline__ bool cmpf(int pred, float x, float y) {
 
 __device__ __forceinline__ float bool_f(bool b) { return b ? 1.0f : 0.0f; }
 
-// rd = f(ra, rb) for each of the thread's slots (rows of kMapSlots float4s,
-// kMapThreads apart).  Operands are read before the result is written, so rd
-// may be ra or rb.
-template <class F>
+// rd = f(ra, rb) for each of the thread's S slots (float4s kMapThreads
+// apart).  Operands are read before the result is written, so rd may be ra or
+// rb.
+template <int S, class F>
 __device__ __forceinline__ void apply(float4 *rd, const float4 *ra, const float4 *rb, F f) {
 #pragma unroll
-  for (int s = 0; s < kMapSlots; ++s) {
+  for (int s = 0; s < S; ++s) {
     const int o = s * kMapThreads;
     const float4 x = ra[o], y = rb[o];
     rd[o] = make_float4(f(x.x, y.x), f(x.y, y.y), f(x.z, y.z), f(x.w, y.w));
@@ -143,28 +145,30 @@ __device__ __forceinline__ void store4(const MapParams &p, int64_t e, float4 v) 
 // contiguous in the domain's row-major order and 16-byte aligned.
 template <int NL, bool VEC>
 __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_constant__ MapParams p) {
-  extern __shared__ float4 regs[];  // n_regs x kMapSlots x kMapThreads
+  constexpr int S = map_slots(NL);
+  constexpr int64_t kChunk = map_chunk(NL);
+  extern __shared__ float4 regs[];  // n_regs x S x kMapThreads
   __shared__ int32_t s_code[2 * SPMDB200_MAP_MAX_INSNS];
   __shared__ float s_consts[SPMDB200_MAP_MAX_CONSTS];
   const int t = threadIdx.x;
   for (int i = t; i < 2 * p.n_insns; i += kMapThreads) s_code[i] = p.code[i];
   for (int i = t; i < SPMDB200_MAP_MAX_CONSTS; i += kMapThreads) s_consts[i] = p.consts[i];
   __syncthreads();
-  constexpr int kRow = kMapSlots * kMapThreads;  // float4s per register
+  constexpr int kRow = S * kMapThreads;  // float4s per register
   float4 *mine = regs + t;
-  const int64_t nchunks = (p.n + kMapChunk - 1) / kMapChunk;
+  const int64_t nchunks = (p.n + kChunk - 1) / kChunk;
   for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
-    const int64_t base = c * kMapChunk + 4 * (int64_t)t;
-    float4 v[NL][kMapSlots];
+    const int64_t base = c * kChunk + 4 * (int64_t)t;
+    float4 v[NL][S];
 #pragma unroll
     for (int i = 0; i < NL; ++i)
 #pragma unroll
-      for (int s = 0; s < kMapSlots; ++s)
+      for (int s = 0; s < S; ++s)
         v[i][s] = load4<VEC>(p.ld_src[i], p.ld_st[i], p, base + (int64_t)s * 4 * kMapThreads);
 #pragma unroll
     for (int i = 0; i < NL; ++i)
 #pragma unroll
-      for (int s = 0; s < kMapSlots; ++s) mine[p.ld_dst[i] * kRow + s * kMapThreads] = v[i][s];
+      for (int s = 0; s < S; ++s) mine[p.ld_dst[i] * kRow + s * kMapThreads] = v[i][s];
     for (int pc = NL; pc < p.n_insns - 1; ++pc) {
       const int w0 = s_code[2 * pc], aux = s_code[2 * pc + 1];
       float4 *rd = mine + ((w0 >> 8) & 255) * kRow;
@@ -174,27 +178,27 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
         case SPMDB200_MAP_CONST: {
           const float cv = s_consts[aux];
 #pragma unroll
-          for (int s = 0; s < kMapSlots; ++s) rd[s * kMapThreads] = make_float4(cv, cv, cv, cv);
+          for (int s = 0; s < S; ++s) rd[s * kMapThreads] = make_float4(cv, cv, cv, cv);
           break;
         }
-        case SPMDB200_MAP_ADD: apply(rd, ra, rb, [](float a, float b) { return __fadd_rn(a, b); }); break;
-        case SPMDB200_MAP_SUB: apply(rd, ra, rb, [](float a, float b) { return __fsub_rn(a, b); }); break;
-        case SPMDB200_MAP_MUL: apply(rd, ra, rb, [](float a, float b) { return __fmul_rn(a, b); }); break;
-        case SPMDB200_MAP_DIV: apply(rd, ra, rb, [](float a, float b) { return __fdiv_rn(a, b); }); break;
-        case SPMDB200_MAP_MAXIMUM: apply(rd, ra, rb, [](float a, float b) { return f_maximum(a, b); }); break;
-        case SPMDB200_MAP_MINIMUM: apply(rd, ra, rb, [](float a, float b) { return f_minimum(a, b); }); break;
+        case SPMDB200_MAP_ADD: apply<S>(rd, ra, rb, [](float a, float b) { return __fadd_rn(a, b); }); break;
+        case SPMDB200_MAP_SUB: apply<S>(rd, ra, rb, [](float a, float b) { return __fsub_rn(a, b); }); break;
+        case SPMDB200_MAP_MUL: apply<S>(rd, ra, rb, [](float a, float b) { return __fmul_rn(a, b); }); break;
+        case SPMDB200_MAP_DIV: apply<S>(rd, ra, rb, [](float a, float b) { return __fdiv_rn(a, b); }); break;
+        case SPMDB200_MAP_MAXIMUM: apply<S>(rd, ra, rb, [](float a, float b) { return f_maximum(a, b); }); break;
+        case SPMDB200_MAP_MINIMUM: apply<S>(rd, ra, rb, [](float a, float b) { return f_minimum(a, b); }); break;
         case SPMDB200_MAP_NEG:
-          apply(rd, ra, ra, [](float a, float) { return __int_as_float(__float_as_int(a) ^ (int)0x80000000u); });
+          apply<S>(rd, ra, ra, [](float a, float) { return __int_as_float(__float_as_int(a) ^ (int)0x80000000u); });
           break;
         case SPMDB200_MAP_ABS:
-          apply(rd, ra, ra, [](float a, float) { return __int_as_float(__float_as_int(a) & 0x7fffffff); });
+          apply<S>(rd, ra, ra, [](float a, float) { return __int_as_float(__float_as_int(a) & 0x7fffffff); });
           break;
-        case SPMDB200_MAP_SQRT: apply(rd, ra, ra, [](float a, float) { return __fsqrt_rn(a); }); break;
-        case SPMDB200_MAP_CMP: apply(rd, ra, rb, [aux](float a, float b) { return bool_f(cmpf(aux, a, b)); }); break;
+        case SPMDB200_MAP_SQRT: apply<S>(rd, ra, ra, [](float a, float) { return __fsqrt_rn(a); }); break;
+        case SPMDB200_MAP_CMP: apply<S>(rd, ra, rb, [aux](float a, float b) { return bool_f(cmpf(aux, a, b)); }); break;
         case SPMDB200_MAP_SELECT: {
           const float4 *rk = mine + aux * kRow;
 #pragma unroll
-          for (int s = 0; s < kMapSlots; ++s) {
+          for (int s = 0; s < S; ++s) {
             const int o = s * kMapThreads;
             const float4 k = rk[o], x = ra[o], y = rb[o];
             rd[o] = make_float4(k.x != 0.0f ? x.x : y.x, k.y != 0.0f ? x.y : y.y, k.z != 0.0f ? x.z : y.z,
@@ -203,25 +207,25 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
           break;
         }
         case SPMDB200_MAP_AND:
-          apply(rd, ra, rb, [](float a, float b) { return bool_f(a != 0.0f && b != 0.0f); });
+          apply<S>(rd, ra, rb, [](float a, float b) { return bool_f(a != 0.0f && b != 0.0f); });
           break;
         case SPMDB200_MAP_OR:
-          apply(rd, ra, rb, [](float a, float b) { return bool_f(a != 0.0f || b != 0.0f); });
+          apply<S>(rd, ra, rb, [](float a, float b) { return bool_f(a != 0.0f || b != 0.0f); });
           break;
         default:  // XOR: the host accepts no other opcode before the STORE
-          apply(rd, ra, rb, [](float a, float b) { return bool_f((a != 0.0f) != (b != 0.0f)); });
+          apply<S>(rd, ra, rb, [](float a, float b) { return bool_f((a != 0.0f) != (b != 0.0f)); });
           break;
       }
     }
 #pragma unroll
-    for (int s = 0; s < kMapSlots; ++s)
+    for (int s = 0; s < S; ++s)
       store4<VEC>(p, base + (int64_t)s * 4 * kMapThreads, mine[p.out_reg * kRow + s * kMapThreads]);
   }
 }
 
 template <int NL>
 cudaError_t launch_nl(const MapParams &p, bool vec, int n_regs, cudaStream_t stream) {
-  const size_t smem = (size_t)n_regs * kMapSlots * kMapThreads * sizeof(float4);
+  const size_t smem = (size_t)n_regs * map_slots(NL) * kMapThreads * sizeof(float4);
   auto kern = vec ? forall_map_kernel<NL, true> : forall_map_kernel<NL, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -229,7 +233,7 @@ cudaError_t launch_nl(const MapParams &p, bool vec, int n_regs, cudaStream_t str
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
   if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kMapThreads, smem)) != cudaSuccess) return e;
   if (per_sm < 1) per_sm = 1;
-  const int64_t nchunks = (p.n + kMapChunk - 1) / kMapChunk;
+  const int64_t nchunks = (p.n + map_chunk(NL) - 1) / map_chunk(NL);
   const int64_t cap = (int64_t)num_sms(dev) * per_sm;
   const int grid = (int)(nchunks < cap ? nchunks : cap);
   kern<<<grid, kMapThreads, smem, stream>>>(p);

@@ -9,7 +9,8 @@ JSON line with the CUDA-event time per rep and the bandwidth it implies.
     python spmd-dialect_b200/run.py jacobi3d --shape 512x512x512 --sweeps 4
 
 Kernels: ewise, axpy, sum_f32, sum_i32, hierarchical_sum, stencil3, jacobi2d,
-jacobi3d, reduce_f32 / reduce_i32 (--kind add|mul|max|min|and|or|xor).  No checking
+jacobi3d, reduce_f32 / reduce_i32 (--kind add|mul|max|min|and|or|xor), forall_map
+(--body axpy: y = 2.5*x + y in place; --body 3in: r = sqrt(|a*b - c|)).  No checking
 happens here (the parity tests compare against the
 oracle); this is for timing and for profiler captures.
 """
@@ -28,8 +29,9 @@ sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["ewise", "axpy", "sum_f32", "sum_i32", "hierarchical_sum", "stencil3",
-                                       "stencil_nd", "jacobi2d", "jacobi3d", "reduce_f32", "reduce_i32"])
+                                       "stencil_nd", "jacobi2d", "jacobi3d", "reduce_f32", "reduce_i32", "forall_map"])
     ap.add_argument("--kind", default="max", help="reduction kind for reduce_f32 / reduce_i32")
+    ap.add_argument("--body", default="3in", choices=["axpy", "3in"], help="forall_map body")
     ap.add_argument("--size", type=int, default=1 << 24)
     ap.add_argument("--shape", default="4096x4096")
     ap.add_argument("--sweeps", type=int, default=100)
@@ -54,6 +56,21 @@ def main() -> None:
         out = torch.empty_like(x)
         fn = (lambda: k.ewise(x, y, out)) if a.kernel == "ewise" else (lambda: k.axpy(2.5, x, y))
         work_bytes = 12 * a.size
+    elif a.kernel == "forall_map":
+        fp = importlib.import_module("spmd-dialect_b200.forall_program")
+        xs = [torch.rand(a.size, device=dev, generator=g) for _ in range(2 if a.body == "axpy" else 3)]
+        if a.body == "axpy":
+            code, n_regs, _, _ = fp.compile_dag("s", {"x": ("load", 0), "y": ("load", 1), "a": ("const", 0),
+                                                      "m": ("mul", "a", "x"), "s": ("add", "m", "y")})
+            fn = lambda: k.forall_map(xs, xs[1], code, [2.5], n_regs=n_regs)  # noqa: E731
+            work_bytes = 12 * a.size
+        else:
+            code, n_regs, _, _ = fp.compile_dag("r", {"a": ("load", 0), "b": ("load", 1), "c": ("load", 2),
+                                                      "p": ("mul", "a", "b"), "d": ("sub", "p", "c"),
+                                                      "q": ("abs", "d"), "r": ("sqrt", "q")})
+            out = torch.empty_like(xs[0])
+            fn = lambda: k.forall_map(xs, out, code, n_regs=n_regs)  # noqa: E731
+            work_bytes = 16 * a.size
     elif a.kernel in ("sum_f32", "hierarchical_sum"):
         x = torch.rand(a.size, device=dev, generator=g)
         o = torch.zeros(1, device=dev)
