@@ -59,6 +59,7 @@ extern "C" {
 #define SPMDB200_ERR_UNSUPPORTED (-4) /* layout outside what the entry accepts */
 #define SPMDB200_ERR_WORKSPACE   (-5) /* workspace null, too small or misaligned */
 #define SPMDB200_ERR_NO_DEVICE   (-6) /* no CUDA device visible */
+#define SPMDB200_ERR_BOUNDS      (-7) /* a checked build recorded an out-of-range access */
 
 const char *spmdb200_status_string(int status);
 /* Last status recorded by any entry on this host thread (0 after success). */
@@ -164,6 +165,20 @@ int spmdb200_forall_map(int rank, const int64_t *sizes, int n_inputs, const floa
                         const int64_t *input_strides, float *out, const int64_t *out_strides,
                         const int32_t *code, int n_insns, const float *consts, int n_consts, int n_regs,
                         void *stream);
+
+/* Checked builds (libspmdb200_checked.so, from `build.py --checked`): the
+ * general kernels (spmdb200_forall_map, spmdb200_stencil_nd and the stencils
+ * on it) test every global index against its view's extent and every shared
+ * register index against the program's, skip a failing access and record the
+ * first one; the promoted stencil also fills each shared tile with NaN before
+ * staging it, so a read of a cell the staging did not write comes out NaN.
+ * Synchronises the device and returns SPMDB200_OK, or SPMDB200_ERR_BOUNDS
+ * with *first_out = the first record (bit 63 set, site in bits 48-62: 1 input
+ * load, 2 output store, 3 shared register; low 48 bits: the index) and
+ * clears it; SPMDB200_ERR_UNSUPPORTED in a release build.  No counterpart in
+ * the reference (its checks are static, lib/Conversion/SPMDToGPU/
+ * SPMDToGPU.cpp:771-780). */
+int spmdb200_check_status(unsigned long long *first_out);
 
 /* 3-point promoted stencil B[i,j] = (A[i,j] + A[i,j+1]) + A[i+1,j] over
  * i < N, j < M with a shared-memory tile plus 1-cell halo; reads outside A's

@@ -7,10 +7,14 @@ binding, and every entry returning a non-zero status raises SpmdError.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
-LIB_PATH = PKG_DIR / "libspmdb200.so"
+# SPMDB200_VARIANT=checked loads the checked build (run-time index checks that
+# record instead of trapping; spmdb200_check_status reads the record).
+VARIANT = os.environ.get("SPMDB200_VARIANT", "")
+LIB_PATH = PKG_DIR / ("libspmdb200_checked.so" if VARIANT == "checked" else "libspmdb200.so")
 CUBIN_PATH = PKG_DIR / "spmdb200_kernels.cubin"
 
 c_p = ctypes.c_void_p
@@ -26,7 +30,7 @@ D3 = [c_p, c_p, c_i, c_i, c_i, c_i, c_i, c_i, c_i]
 
 STATUS = {
     0: "ok", -1: "invalid argument", -2: "CUDA error", -3: "device wait timed out",
-    -4: "unsupported layout", -5: "bad workspace", -6: "no CUDA device",
+    -4: "unsupported layout", -5: "bad workspace", -6: "no CUDA device", -7: "out-of-range access (checked build)",
 }
 
 
@@ -49,6 +53,7 @@ _SIGS = {
     "spmdb200_ewise": (ctypes.c_int, D1 + D1 + D1 + [c_i, c_p]),
     "spmdb200_axpy": (ctypes.c_int, [c_f] + D1 + D1 + [c_i, c_p]),
     "spmdb200_stencil3pt": (ctypes.c_int, D2 + D2 + [c_i, c_i, c_p]),
+    "spmdb200_check_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64)]),
     "spmdb200_forall_map": (ctypes.c_int, [ctypes.c_int, c_p, ctypes.c_int, c_p, c_p, c_p, c_p, c_p, ctypes.c_int,
                                            c_p, ctypes.c_int, ctypes.c_int, c_p]),
     "spmdb200_sum_workspace_bytes": (c_sz, [c_i]),

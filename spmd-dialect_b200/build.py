@@ -1,12 +1,14 @@
 """Builds libspmdb200.so and spmdb200_kernels.cubin in place (sm_100a only).
 
-    python spmd-dialect_b200/build.py [--force] [-j N]
+    python spmd-dialect_b200/build.py [--force] [-j N] [--no-checked]
 
 Each csrc/*.cu except refabi.cu is compiled to an object under _build/ and
 linked with the static CUDA runtime into libspmdb200.so (no link-time
 dependency on libcuda, so the library also loads on machines without a GPU
 driver).  refabi.cu -- the kernels with the reference's PTX entry names -- is
-compiled to spmdb200_kernels.cubin for cuModuleLoadData callers.  ptxas
+compiled to spmdb200_kernels.cubin for cuModuleLoadData callers.
+libspmdb200_checked.so is the same library with the general kernels
+(forall_map.cu, stencil_nd.cu) compiled with -DSPMDB200_CHECKED.  ptxas
 register / spill reports go to _build/ptxas.log.
 """
 from __future__ import annotations
@@ -23,6 +25,11 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libspmdb200.so"
+# The checked variant: the general kernels rebuilt with run-time index checks
+# that record instead of trapping (and NaN-poisoned shared tiles), linked with
+# the release objects of every other file.  Loaded when SPMDB200_VARIANT=checked.
+CHECKED_LIB = PKG / "libspmdb200_checked.so"
+CHECKED_UNITS = ("forall_map.cu", "stencil_nd.cu")
 CUBIN = PKG / "spmdb200_kernels.cubin"
 INCLUDE = PKG.parent / "include"
 
@@ -58,7 +65,7 @@ def _run(cmd: list[str]) -> str:
     return r.stdout + r.stderr
 
 
-def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -> Path:
+def build(force: bool = False, jobs: int | None = None, verbose: bool = False, checked: bool = True) -> Path:
     BUILD.mkdir(exist_ok=True)
     cc = nvcc()
     deps = _deps()
@@ -76,6 +83,23 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
     if force or todo or _stale(LIB, objs):
         _run([cc, "-shared", *ARCH, "-cudart", "static", "-Xcompiler", "-fPIC", "-o", str(LIB),
               *map(str, objs), "-lpthread", "-ldl", "-lrt"])
+    if checked:
+        cdir = BUILD / "checked"
+        cdir.mkdir(exist_ok=True)
+        cobjs = []
+        with cf.ThreadPoolExecutor(max_workers=len(CHECKED_UNITS)) as ex:
+            futs = {}
+            for name in CHECKED_UNITS:
+                u, o = CSRC / name, cdir / (Path(name).stem + ".o")
+                cobjs.append(o)
+                if force or _stale(o, [u] + deps):
+                    futs[ex.submit(_run, [cc, *NVCC_FLAGS, "-DSPMDB200_CHECKED", "-c", str(u), "-o", str(o)])] = u
+            for f in cf.as_completed(futs):
+                logs["checked/" + futs[f].name] = f.result()
+        rest = [o for u, o in zip(units, objs) if u.name not in CHECKED_UNITS]
+        if force or _stale(CHECKED_LIB, cobjs + rest):
+            _run([cc, "-shared", *ARCH, "-cudart", "static", "-Xcompiler", "-fPIC", "-o", str(CHECKED_LIB),
+                  *map(str, rest + cobjs), "-lpthread", "-ldl", "-lrt"])
     if logs:
         with open(BUILD / "ptxas.log", "a") as fh:
             for name, text in sorted(logs.items()):
@@ -91,8 +115,9 @@ def main() -> None:
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-j", type=int, default=None)
     ap.add_argument("-v", action="store_true")
+    ap.add_argument("--no-checked", action="store_true", help="skip libspmdb200_checked.so")
     a = ap.parse_args()
-    print(build(force=a.force, jobs=a.j, verbose=a.v))
+    print(build(force=a.force, jobs=a.j, verbose=a.v, checked=not a.no_checked))
 
 
 if __name__ == "__main__":

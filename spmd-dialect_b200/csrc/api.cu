@@ -250,6 +250,7 @@ const char *spmdb200_status_string(int status) {
     case SPMDB200_ERR_UNSUPPORTED: return "unsupported layout";
     case SPMDB200_ERR_WORKSPACE: return "bad workspace";
     case SPMDB200_ERR_NO_DEVICE: return "no CUDA device";
+    case SPMDB200_ERR_BOUNDS: return "out-of-range access recorded (checked build)";
     default: return "unknown status";
   }
 }

@@ -196,6 +196,21 @@ __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned *p, unsigned v
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// ---- checked builds -----------------------------------------------------------
+// Compiled with -DSPMDB200_CHECKED, the general kernels (forall_map.cu,
+// stencil_nd.cu) test their global and shared indices against the extent of
+// what they address.  An access that fails is skipped, and the first failure
+// of each file is kept in a device word of that file (bit 63 set, the site in
+// bits 48-62, the low 48 bits of the index), which spmdb200_check_status()
+// reads and clears.  Nothing traps.  Release builds compile the checks to
+// nothing.
+__device__ __forceinline__ bool record_check(unsigned long long *word, bool ok, unsigned site, long long idx) {
+  if (!ok)
+    atomicCAS(word, 0ull,
+              (1ull << 63) | ((unsigned long long)(site & 0x7fffu) << 48) | ((unsigned long long)idx & 0xffffffffffffull));
+  return ok;
+}
+
 template <class... KArgs, class... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
                               cudaStream_t s, Args... args) {

@@ -56,7 +56,17 @@ struct MapParams {
   float consts[SPMDB200_MAP_MAX_CONSTS];
   int n_insns;  // all instructions, the LOAD prefix and the final STORE included
   int out_reg;
+  int n_regs;
+  int64_t ld_span[kMaxLoads];  // elements each view covers (1 + max offset), for checked builds
+  int64_t out_span;
 };
+
+#ifdef SPMDB200_CHECKED
+__device__ unsigned long long g_check_first;  // first out-of-range access (see common.cuh)
+#define IN_RANGE(cond, site, idx) record_check(&g_check_first, (cond), (site), (long long)(idx))
+#else
+#define IN_RANGE(cond, site, idx) true
+#endif
 
 __device__ __forceinline__ float f_maximum(float a, float b) {
   if (isnan(a) || isnan(b)) return __int_as_float(0x7fc00000);
@@ -116,13 +126,21 @@ __device__ __forceinline__ int64_t point_offset(int64_t e, const int64_t *sz, co
 
 // Four consecutive points from e; points at or past n read as 0.
 template <bool VEC>
-__device__ __forceinline__ float4 load4(const float *src, const int64_t *st, const MapParams &p, int64_t e) {
-  if (VEC && e + 3 < p.n) return ld_f4(src + e);
+__device__ __forceinline__ float4 load4(const float *src, const int64_t *st, int64_t span, const MapParams &p,
+                                        int64_t e) {
+  if (VEC && e + 3 < p.n) {
+    if (!IN_RANGE(e + 3 < span, 1, e)) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    return ld_f4(src + e);
+  }
   float v[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int64_t q = e + k;
-    v[k] = q < p.n ? src[VEC ? q : point_offset(q, p.size, st)] : 0.0f;
+    v[k] = 0.0f;
+    if (q < p.n) {
+      const int64_t o = VEC ? q : point_offset(q, p.size, st);
+      if (IN_RANGE(o >= 0 && o < span, 1, o)) v[k] = src[o];
+    }
   }
   return make_float4(v[0], v[1], v[2], v[3]);
 }
@@ -130,14 +148,17 @@ __device__ __forceinline__ float4 load4(const float *src, const int64_t *st, con
 template <bool VEC>
 __device__ __forceinline__ void store4(const MapParams &p, int64_t e, float4 v) {
   if (VEC && e + 3 < p.n) {
-    st_f4(p.out + e, v);
+    if (IN_RANGE(e + 3 < p.out_span, 2, e)) st_f4(p.out + e, v);
     return;
   }
   const float w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int64_t q = e + k;
-    if (q < p.n) p.out[VEC ? q : point_offset(q, p.size, p.out_st)] = w[k];
+    if (q < p.n) {
+      const int64_t o = VEC ? q : point_offset(q, p.size, p.out_st);
+      if (IN_RANGE(o >= 0 && o < p.out_span, 2, o)) p.out[o] = w[k];
+    }
   }
 }
 
@@ -164,13 +185,19 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
     for (int i = 0; i < NL; ++i)
 #pragma unroll
       for (int s = 0; s < S; ++s)
-        v[i][s] = load4<VEC>(p.ld_src[i], p.ld_st[i], p, base + (int64_t)s * 4 * kMapThreads);
+        v[i][s] = load4<VEC>(p.ld_src[i], p.ld_st[i], p.ld_span[i], p, base + (int64_t)s * 4 * kMapThreads);
 #pragma unroll
-    for (int i = 0; i < NL; ++i)
+    for (int i = 0; i < NL; ++i) {
+      if (!IN_RANGE(p.ld_dst[i] < p.n_regs, 3, p.ld_dst[i])) continue;
 #pragma unroll
       for (int s = 0; s < S; ++s) mine[p.ld_dst[i] * kRow + s * kMapThreads] = v[i][s];
+    }
     for (int pc = NL; pc < p.n_insns - 1; ++pc) {
       const int w0 = s_code[2 * pc], aux = s_code[2 * pc + 1];
+      if (!IN_RANGE(((w0 >> 8) & 255) < p.n_regs && ((w0 >> 16) & 255) < p.n_regs &&
+                        (int)((unsigned)w0 >> 24) < p.n_regs,
+                    3, pc))
+        continue;
       float4 *rd = mine + ((w0 >> 8) & 255) * kRow;
       const float4 *ra = mine + ((w0 >> 16) & 255) * kRow;
       const float4 *rb = mine + ((unsigned)w0 >> 24) * kRow;
@@ -196,6 +223,7 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
         case SPMDB200_MAP_SQRT: apply<S>(rd, ra, ra, [](float a, float) { return __fsqrt_rn(a); }); break;
         case SPMDB200_MAP_CMP: apply<S>(rd, ra, rb, [aux](float a, float b) { return bool_f(cmpf(aux, a, b)); }); break;
         case SPMDB200_MAP_SELECT: {
+          if (!IN_RANGE(aux < p.n_regs, 3, aux)) break;
           const float4 *rk = mine + aux * kRow;
 #pragma unroll
           for (int s = 0; s < S; ++s) {
@@ -217,9 +245,11 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
           break;
       }
     }
+    if (IN_RANGE(p.out_reg < p.n_regs, 3, p.out_reg)) {
 #pragma unroll
-    for (int s = 0; s < S; ++s)
-      store4<VEC>(p, base + (int64_t)s * 4 * kMapThreads, mine[p.out_reg * kRow + s * kMapThreads]);
+      for (int s = 0; s < S; ++s)
+        store4<VEC>(p, base + (int64_t)s * 4 * kMapThreads, mine[p.out_reg * kRow + s * kMapThreads]);
+    }
   }
 }
 
@@ -249,7 +279,29 @@ bool contiguous(const int64_t *sz, const int64_t *st) {
   return true;
 }
 
+// Elements a view covers: 1 + its largest offset over the domain.
+int64_t view_span(const int64_t *sz, const int64_t *st) {
+  int64_t sp = 1;
+  for (int d = 0; d < 3; ++d) sp += (sz[d] - 1) * st[d];
+  return sp;
+}
+
 }  // namespace
+
+int check_read_forall_map(unsigned long long *first) {
+#ifdef SPMDB200_CHECKED
+  if (!first) return 1;  // only asks whether this is a checked build
+  unsigned long long v = 0, z = 0;
+  cudaMemcpyFromSymbol(&v, g_check_first, sizeof(v));
+  cudaMemcpyToSymbol(g_check_first, &z, sizeof(z));
+  *first = v;
+  return 1;
+#else
+  if (first) *first = 0;
+  return 0;
+#endif
+}
+
 }  // namespace spmdb200
 
 using namespace spmdb200;
@@ -314,6 +366,7 @@ extern "C" int spmdb200_forall_map(int rank, const int64_t *sizes, int n_inputs,
   }
   if (nl == 0) return record_api_status(SPMDB200_ERR_UNSUPPORTED, "a body with no LOAD (a fill) is not mapped");
   p.n_insns = n_insns;
+  p.n_regs = n_regs;
   for (int j = 0; j < n_consts; ++j) p.consts[j] = consts[j];
   if (p.n == 0) return record_api_status(SPMDB200_OK, "");
   if (!out) return bad("null out");
@@ -328,7 +381,9 @@ extern "C" int spmdb200_forall_map(int rank, const int64_t *sizes, int n_inputs,
     for (int d = 0; d < 3; ++d) p.ld_st[i][d] = 0;
     for (int d = 0; d < rank; ++d) p.ld_st[i][3 - rank + d] = input_strides[in * rank + d];
     vec = vec && contiguous(p.size, p.ld_st[i]) && ((uintptr_t)src & 15u) == 0;
+    p.ld_span[i] = view_span(p.size, p.ld_st[i]);
   }
+  p.out_span = view_span(p.size, p.out_st);
   for (int d = 0; d < 3; ++d)
     for (int i = 0; i < nl; ++i)
       if (p.ld_st[i][d] < 0 || p.out_st[d] < 0) return bad("negative stride");

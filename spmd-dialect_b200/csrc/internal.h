@@ -176,6 +176,13 @@ int encode_tensor_map_f32(void *tmap /*CUtensorMap*/, void *gaddr, int rank, con
 
 int num_sms(int device);
 
+// The first out-of-range access a checked build recorded in each file's device
+// word (0: none), read and cleared.  Return 1 in a checked build of that file,
+// 0 in a release build (nothing read); with first == nullptr they only answer
+// that, without a CUDA call.
+int check_read_forall_map(unsigned long long *first);
+int check_read_stencil_nd(unsigned long long *first);
+
 // Bounded-wait limits of the persistent kernels (process-wide, nanoseconds).
 unsigned long long wait_budget_ns(bool peer);
 

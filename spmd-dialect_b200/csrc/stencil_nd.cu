@@ -62,6 +62,8 @@ struct NdStencil {
   // congruent to A's plane stride mod 4 and ring a multiple of 4, so the
   // 16-byte phase of every staged cell again matches A's.
   int kz, ring, slot_cells;
+  float *b_base;       // B, and the elements it covers (1 + its largest offset): checked builds
+  long long b_span;
   int tap_dz[kNdMaxTaps];  // off_j[0] - min_off[0]
   int tap_in[kNdMaxTaps];  // (off_j[1] - min_off[1]) * pitch1 + off_j[2] - min_off[2]
   int off[kNdMaxTaps][3];
@@ -205,12 +207,25 @@ __device__ __forceinline__ void fold_taps(const NdStencil &k, Load ld, int nlive
   }
 }
 
+#ifdef SPMDB200_CHECKED
+__device__ unsigned long long g_check_first;  // first out-of-range access (see common.cuh)
+#endif
+
+// One output store; a checked build skips (and records) a store outside B.
+__device__ __forceinline__ void st_out(const NdStencil &k, float *p, float v) {
+#ifdef SPMDB200_CHECKED
+  const long long o = p - k.b_base;
+  if (!record_check(&g_check_first, o >= 0 && o < k.b_span, 2, o)) return;
+#endif
+  *p = v;
+}
+
 template <int CPL, bool GUARD>
 __device__ __forceinline__ void store_points(const NdStencil &k, float *bp, long long bstep, int nlive,
                                              const float *acc) {
 #pragma unroll
   for (int u = 0; u < CPL; ++u)
-    if (!GUARD || u < nlive) bp[u * bstep] = k.has_scale ? __fmul_rn(acc[u], k.scale) : acc[u];
+    if (!GUARD || u < nlive) st_out(k, bp + u * bstep, k.has_scale ? __fmul_rn(acc[u], k.scale) : acc[u]);
 }
 
 __device__ __forceinline__ void tile_base(const NdStencil &k, const TileIter &it, long long *base) {
@@ -226,6 +241,13 @@ template <bool UNIT>
 __device__ __forceinline__ int stage_tile(const NdStencil &k, const float *__restrict__ A, const TileIter &it,
                                           float *buf, int r0, int r1) {
   const int f0 = k.fdim[0], f1 = k.fdim[1], f2 = k.fdim[2];
+#ifdef SPMDB200_CHECKED
+  // Checked builds: every cell of the buffer starts as a NaN, so a read of a
+  // cell that the staging below does not write shows up in the output.  The
+  // caller's barrier released the buffer; all threads get here together.
+  for (int i = threadIdx.x; i < k.buf_cells; i += kNdThreads) buf[i] = __int_as_float(0x7fc0dead);
+  __syncthreads();
+#endif
   const long long s2a = UNIT ? 1 : k.a_stride[2];
   long long base[3];  // A index of footprint cell (0, 0, 0)
   tile_base(k, it, base);
@@ -341,7 +363,7 @@ __global__ void __launch_bounds__(kNdThreads, 3) stencil_nd_promoted_kernel(cons
       if (ncols - seg * SEG >= SEG) {
         fold_staged<CPL, UNIT ? 1 : 0, false>(k, sp, st2, CPL, acc, ParamTaps{k});
 #pragma unroll
-        for (int u = 0; u < CPL; ++u) bp[u * 32 * bcol] = acc[u];
+        for (int u = 0; u < CPL; ++u) st_out(k, bp + u * 32 * bcol, acc[u]);
       } else {
         // points of this lane before the tile's last column: lane + 32u < ncols - seg*SEG
         const int rem = ncols - seg * SEG - lane;
@@ -350,7 +372,7 @@ __global__ void __launch_bounds__(kNdThreads, 3) stencil_nd_promoted_kernel(cons
         fold_staged<CPL, UNIT ? 1 : 0, true>(k, sp, st2, nlive, acc, ParamTaps{k});
 #pragma unroll
         for (int u = 0; u < CPL; ++u)
-          if (u < nlive) bp[u * 32 * bcol] = acc[u];
+          if (u < nlive) st_out(k, bp + u * 32 * bcol, acc[u]);
       }
     }
     __syncthreads();  // every warp is done with this buffer before it is refilled
@@ -454,7 +476,7 @@ __global__ void __launch_bounds__(kNdThreads, 4) stencil_nd_stream3_kernel(const
           if (ncols - seg * SEG >= SEG) {
             fold_staged<CPL, 1, false, decltype(taps), NT>(k, sp, 1, CPL, acc, taps);
 #pragma unroll
-            for (int u = 0; u < CPL; ++u) bp[u * 32] = acc[u];
+            for (int u = 0; u < CPL; ++u) st_out(k, bp + u * 32, acc[u]);
           } else {
             const int rem = ncols - seg * SEG - lane;
             const int nlive = rem <= 0 ? 0 : ((rem + 31) >> 5);
@@ -462,7 +484,7 @@ __global__ void __launch_bounds__(kNdThreads, 4) stencil_nd_stream3_kernel(const
               fold_staged<CPL, 1, true, decltype(taps), NT>(k, sp, 1, nlive, acc, taps);
 #pragma unroll
               for (int u = 0; u < CPL; ++u)
-                if (u < nlive) bp[u * 32] = acc[u];
+                if (u < nlive) st_out(k, bp + u * 32, acc[u]);
             }
           }
         }
@@ -662,11 +684,28 @@ int promotion_plan(int rank, const int64_t *tile_sizes, const int64_t *steps, co
   return kPlanSkipNoReuse;
 }
 
+int check_read_stencil_nd(unsigned long long *first) {
+#ifdef SPMDB200_CHECKED
+  if (!first) return 1;  // only asks whether this is a checked build
+  unsigned long long v = 0, z = 0;
+  cudaMemcpyFromSymbol(&v, g_check_first, sizeof(v));
+  cudaMemcpyToSymbol(g_check_first, &z, sizeof(z));
+  *first = v;
+  return 1;
+#else
+  if (first) *first = 0;
+  return 0;
+#endif
+}
+
 cudaError_t launch_stencil_nd(const StencilNdProblem &p, int promote, cudaStream_t s) {
   // The plan decides whether to stage (on the caller's tile); the kernel then
   // stages its own, larger tiles -- staging changes where values are read
   // from, never the values.  Dimensions are right-aligned into 3 slots.
   NdStencil k{};
+  k.b_base = p.b;
+  k.b_span = 1;
+  for (int q = 0; q < p.rank; ++q) k.b_span += (p.b_size[q] > 0 ? p.b_size[q] - 1 : 0) * p.b_stride[q];
   k.ntaps = p.ntaps;
   k.has_w = p.weights != nullptr;
   k.has_scale = p.scale != 1.0f;

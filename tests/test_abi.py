@@ -164,3 +164,17 @@ def test_jacobi2d_host_batch_wrapper_checks_layout():
                 [a.astype(np.float64)]):                       # not float32
         with pytest.raises(ValueError):
             host.jacobi2d_host_batch(bad, 3)
+
+
+def test_check_status_release_and_checked_exports():
+    """The release library answers 'not a checked build' without a CUDA call;
+    the checked library exports every declared function too."""
+    lib = spmd_mod("_lib").lib()
+    v = ctypes.c_uint64(1)
+    if spmd_mod("_lib").VARIANT != "checked":
+        assert lib.spmdb200_check_status(ctypes.byref(v)) == -4 and v.value == 0
+    checked = ROOT / "spmd-dialect_b200" / "libspmdb200_checked.so"
+    assert checked.exists(), "libspmdb200_checked.so not built"
+    ch = ctypes.CDLL(str(checked))
+    missing = [n for n in declared_functions() if not hasattr(ch, n)]
+    assert not missing, f"not exported by the checked build: {missing}"

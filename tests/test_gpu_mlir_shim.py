@@ -12,7 +12,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture(scope="module")
-def fns():
+def fns(kernels):
     shim = spmd_mod("mlir_shim")
     return shim.load((ROOT / "tests" / "mlir" / "kernels.mlir").read_text(), skip_unmapped=True)
 
@@ -71,3 +71,39 @@ def test_reductions(fns, oracle_mod):
     o = torch.tensor([-5], dtype=torch.int32, device="cuda")
     fns["max_i32"](torch.from_numpy(v).cuda(), o.reshape(()), 123457)
     assert int(o.item()) == max(int(v.max()), -5)
+
+
+def test_top_level_reduces_and_float_identities(kernels, oracle_mod):
+    """A returned top-level spmd.reduce, one stored to out[c], and a max
+    reduction whose init is a hexadecimal -inf, through their bindings."""
+    from test_mlir_shim import _FORMS
+    shim = spmd_mod("mlir_shim")
+    fns = shim.load(_FORMS, skip_unmapped=True)
+    x = _r(300001, 21)
+    tx = torch.from_numpy(x).cuda()
+    got = fns["sum_returned"](tx, 300001)
+    exact = oracle_mod.sum_f64(x)
+    assert isinstance(got, float) and abs(got - exact) <= 1e-6 * abs(exact)
+    o = torch.tensor(-7.0, device="cuda")
+    fns["max_f32"](tx, o, 300001)
+    assert float(o.item()) == float(x.max())
+    stored = shim.load("""
+func.func @sum_stored(%A: memref<?xf32>, %out: memref<3xf32>, %N: index) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  %c2 = arith.constant 2 : index
+  %z = arith.constant 0.0 : f32
+  %s = "spmd.reduce"(%c0, %N, %c1, %z) ({
+  ^bb0(%k: index):
+    %v = memref.load %A[%k] : memref<?xf32>
+    "spmd.yield"(%v) : (f32) -> ()
+  }) {"spmd.kind" = #spmd.reduction_kind<add>} : (index, index, index, f32) -> f32
+  memref.store %s, %out[%c2] : memref<3xf32>
+  func.return
+}
+""")
+    out = torch.full((3,), 5.0, device="cuda")
+    stored["sum_stored"](tx, out, 1000)
+    got = out.cpu().numpy()
+    assert got[0] == 5.0 and got[1] == 5.0
+    assert abs(float(got[2]) - oracle_mod.sum_f64(x[:1000])) <= 1e-6 * oracle_mod.sum_f64(x[:1000])
