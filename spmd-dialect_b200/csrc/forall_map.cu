@@ -20,8 +20,9 @@
 // per 8 points, uniformly across the warp.  The loads of all inputs are
 // issued before the first operation (the LOADs are a prefix of the program),
 // so a chunk's input traffic is in flight at once.  Contiguous, 16-byte
-// aligned views take 128-bit loads and stores; any other strides take
-// per-point addressing.
+// aligned views take 128-bit loads and stores; contiguous unaligned ones
+// 4-byte accesses at the flat index; other strides address each group of four
+// points from one index decomposition shared by every view.
 //
 // Arithmetic is spelled with the _rn intrinsics (round to nearest even, never
 // contracted to an FMA), so the result equals a CPU evaluation of the same
@@ -117,6 +118,12 @@ __device__ __forceinline__ void apply(float4 *rd, const float4 *ra, const float4
   }
 }
 
+// How a launch addresses its views.  VEC: every view contiguous in the
+// domain's row-major order and 16-byte aligned (128-bit accesses, offset =
+// flat index).  CONTIG: every view contiguous, some not 16-byte aligned
+// (4-byte accesses, offset = flat index).  GENERAL: any strides.
+enum MapMode { kVec = 0, kContig = 1, kGeneral = 2 };
+
 // Offset of flat point e in a view with strides st over the rank-3 domain sz.
 __device__ __forceinline__ int64_t point_offset(int64_t e, const int64_t *sz, const int64_t *st) {
   const int64_t i2 = e % sz[2], q = e / sz[2];
@@ -124,47 +131,73 @@ __device__ __forceinline__ int64_t point_offset(int64_t e, const int64_t *sz, co
   return i0 * st[0] + i1 * st[1] + i2 * st[2];
 }
 
+// GENERAL: the index of the first of four consecutive points, found once per
+// group and shared by every view; `run` when the four lie in one row below n.
+struct Idx3 {
+  int64_t i0, i1, i2;
+  bool run;
+};
+template <int MODE>
+__device__ __forceinline__ Idx3 group_index(const MapParams &p, int64_t e) {
+  Idx3 x{0, 0, 0, false};
+  if constexpr (MODE == kGeneral) {
+    x.i2 = e % p.size[2];
+    const int64_t q = e / p.size[2];
+    x.i1 = q % p.size[1];
+    x.i0 = q / p.size[1];
+    x.run = e + 3 < p.n && x.i2 + 3 < p.size[2];
+  }
+  return x;
+}
+
+// Offset of point e + k in a view: the flat index when every view is
+// contiguous; else from the group's index (within a row) or by division.
+template <int MODE>
+__device__ __forceinline__ int64_t view_offset(const MapParams &p, const int64_t *st, int64_t e, int k,
+                                               const Idx3 &x) {
+  if constexpr (MODE != kGeneral) return e + k;
+  if (x.run) return x.i0 * st[0] + x.i1 * st[1] + (x.i2 + k) * st[2];
+  return point_offset(e + k, p.size, st);
+}
+
 // Four consecutive points from e; points at or past n read as 0.
-template <bool VEC>
+template <int MODE>
 __device__ __forceinline__ float4 load4(const float *src, const int64_t *st, int64_t span, const MapParams &p,
-                                        int64_t e) {
-  if (VEC && e + 3 < p.n) {
+                                        int64_t e, const Idx3 &x) {
+  if (MODE == kVec && e + 3 < p.n) {
     if (!IN_RANGE(e + 3 < span, 1, e)) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     return ld_f4(src + e);
   }
   float v[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int64_t q = e + k;
     v[k] = 0.0f;
-    if (q < p.n) {
-      const int64_t o = VEC ? q : point_offset(q, p.size, st);
+    if (e + k < p.n) {
+      const int64_t o = view_offset<MODE>(p, st, e, k, x);
       if (IN_RANGE(o >= 0 && o < span, 1, o)) v[k] = src[o];
     }
   }
   return make_float4(v[0], v[1], v[2], v[3]);
 }
 
-template <bool VEC>
-__device__ __forceinline__ void store4(const MapParams &p, int64_t e, float4 v) {
-  if (VEC && e + 3 < p.n) {
+template <int MODE>
+__device__ __forceinline__ void store4(const MapParams &p, int64_t e, const Idx3 &x, float4 v) {
+  if (MODE == kVec && e + 3 < p.n) {
     if (IN_RANGE(e + 3 < p.out_span, 2, e)) st_f4(p.out + e, v);
     return;
   }
   const float w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int64_t q = e + k;
-    if (q < p.n) {
-      const int64_t o = VEC ? q : point_offset(q, p.size, p.out_st);
+    if (e + k < p.n) {
+      const int64_t o = view_offset<MODE>(p, p.out_st, e, k, x);
       if (IN_RANGE(o >= 0 && o < p.out_span, 2, o)) p.out[o] = w[k];
     }
   }
 }
 
-// NL: the number of leading LOAD instructions (1..8).  VEC: every view is
-// contiguous in the domain's row-major order and 16-byte aligned.
-template <int NL, bool VEC>
+// NL: the number of leading LOAD instructions (1..8); MODE: a MapMode.
+template <int NL, int MODE>
 __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_constant__ MapParams p) {
   constexpr int S = map_slots(NL);
   constexpr int64_t kChunk = map_chunk(NL);
@@ -180,12 +213,15 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
   const int64_t nchunks = (p.n + kChunk - 1) / kChunk;
   for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
     const int64_t base = c * kChunk + 4 * (int64_t)t;
+    Idx3 gx[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) gx[s] = group_index<MODE>(p, base + (int64_t)s * 4 * kMapThreads);
     float4 v[NL][S];
 #pragma unroll
     for (int i = 0; i < NL; ++i)
 #pragma unroll
       for (int s = 0; s < S; ++s)
-        v[i][s] = load4<VEC>(p.ld_src[i], p.ld_st[i], p.ld_span[i], p, base + (int64_t)s * 4 * kMapThreads);
+        v[i][s] = load4<MODE>(p.ld_src[i], p.ld_st[i], p.ld_span[i], p, base + (int64_t)s * 4 * kMapThreads, gx[s]);
 #pragma unroll
     for (int i = 0; i < NL; ++i) {
       if (!IN_RANGE(p.ld_dst[i] < p.n_regs, 3, p.ld_dst[i])) continue;
@@ -248,15 +284,16 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
     if (IN_RANGE(p.out_reg < p.n_regs, 3, p.out_reg)) {
 #pragma unroll
       for (int s = 0; s < S; ++s)
-        store4<VEC>(p, base + (int64_t)s * 4 * kMapThreads, mine[p.out_reg * kRow + s * kMapThreads]);
+        store4<MODE>(p, base + (int64_t)s * 4 * kMapThreads, gx[s], mine[p.out_reg * kRow + s * kMapThreads]);
     }
   }
 }
 
 template <int NL>
-cudaError_t launch_nl(const MapParams &p, bool vec, int n_regs, cudaStream_t stream) {
+cudaError_t launch_nl(const MapParams &p, int mode, int n_regs, cudaStream_t stream) {
   const size_t smem = (size_t)n_regs * map_slots(NL) * kMapThreads * sizeof(float4);
-  auto kern = vec ? forall_map_kernel<NL, true> : forall_map_kernel<NL, false>;
+  auto kern = mode == kVec ? forall_map_kernel<NL, kVec>
+              : mode == kContig ? forall_map_kernel<NL, kContig> : forall_map_kernel<NL, kGeneral>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int dev = 0, per_sm = 0;
@@ -371,7 +408,7 @@ extern "C" int spmdb200_forall_map(int rank, const int64_t *sizes, int n_inputs,
   if (p.n == 0) return record_api_status(SPMDB200_OK, "");
   if (!out) return bad("null out");
   p.out = out;
-  bool vec =contiguous(p.size, p.out_st) && ((uintptr_t)out & 15u) == 0;
+  bool contig = contiguous(p.size, p.out_st), aligned = ((uintptr_t)out & 15u) == 0;
   for (int i = 0; i < nl; ++i) {
     const int in = code[2 * i + 1];
     const float *src = inputs[in];
@@ -380,24 +417,26 @@ extern "C" int spmdb200_forall_map(int rank, const int64_t *sizes, int n_inputs,
     p.ld_dst[i] = (code[2 * i] >> 8) & 255;
     for (int d = 0; d < 3; ++d) p.ld_st[i][d] = 0;
     for (int d = 0; d < rank; ++d) p.ld_st[i][3 - rank + d] = input_strides[in * rank + d];
-    vec = vec && contiguous(p.size, p.ld_st[i]) && ((uintptr_t)src & 15u) == 0;
+    contig = contig && contiguous(p.size, p.ld_st[i]);
+    aligned = aligned && ((uintptr_t)src & 15u) == 0;
     p.ld_span[i] = view_span(p.size, p.ld_st[i]);
   }
   p.out_span = view_span(p.size, p.out_st);
   for (int d = 0; d < 3; ++d)
     for (int i = 0; i < nl; ++i)
       if (p.ld_st[i][d] < 0 || p.out_st[d] < 0) return bad("negative stride");
+  const int mode = !contig ? kGeneral : aligned ? kVec : kContig;
   cudaError_t e;
   cudaStream_t s = (cudaStream_t)stream;
   switch (nl) {
-    case 1: e = launch_nl<1>(p, vec, n_regs, s); break;
-    case 2: e = launch_nl<2>(p, vec, n_regs, s); break;
-    case 3: e = launch_nl<3>(p, vec, n_regs, s); break;
-    case 4: e = launch_nl<4>(p, vec, n_regs, s); break;
-    case 5: e = launch_nl<5>(p, vec, n_regs, s); break;
-    case 6: e = launch_nl<6>(p, vec, n_regs, s); break;
-    case 7: e = launch_nl<7>(p, vec, n_regs, s); break;
-    default: e = launch_nl<8>(p, vec, n_regs, s); break;
+    case 1: e = launch_nl<1>(p, mode, n_regs, s); break;
+    case 2: e = launch_nl<2>(p, mode, n_regs, s); break;
+    case 3: e = launch_nl<3>(p, mode, n_regs, s); break;
+    case 4: e = launch_nl<4>(p, mode, n_regs, s); break;
+    case 5: e = launch_nl<5>(p, mode, n_regs, s); break;
+    case 6: e = launch_nl<6>(p, mode, n_regs, s); break;
+    case 7: e = launch_nl<7>(p, mode, n_regs, s); break;
+    default: e = launch_nl<8>(p, mode, n_regs, s); break;
   }
   if (e != cudaSuccess) {
     cudaGetLastError();

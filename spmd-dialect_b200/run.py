@@ -32,6 +32,9 @@ def main() -> None:
                                        "stencil_nd", "jacobi2d", "jacobi3d", "reduce_f32", "reduce_i32", "forall_map"])
     ap.add_argument("--kind", default="max", help="reduction kind for reduce_f32 / reduce_i32")
     ap.add_argument("--body", default="3in", choices=["axpy", "3in"], help="forall_map body")
+    ap.add_argument("--layout", default="vec", choices=["vec", "contig", "strided"],
+                    help="forall_map views: 16-byte aligned, contiguous from element 1, or rows of 4096 in a "
+                         "4097-element pitch")
     ap.add_argument("--size", type=int, default=1 << 24)
     ap.add_argument("--shape", default="4096x4096")
     ap.add_argument("--sweeps", type=int, default=100)
@@ -58,7 +61,16 @@ def main() -> None:
         work_bytes = 12 * a.size
     elif a.kernel == "forall_map":
         fp = importlib.import_module("spmd-dialect_b200.forall_program")
-        xs = [torch.rand(a.size, device=dev, generator=g) for _ in range(2 if a.body == "axpy" else 3)]
+        nv = 2 if a.body == "axpy" else 3
+
+        def view(t):
+            if a.layout == "contig":
+                return t[1:a.size + 1]
+            if a.layout == "strided":
+                return t[: a.size // 4096 * 4097].view(-1, 4097)[:, :4096]
+            return t[: a.size]
+
+        xs = [view(torch.rand(a.size + 4097, device=dev, generator=g)) for _ in range(nv)]
         if a.body == "axpy":
             code, n_regs, _, _ = fp.compile_dag("s", {"x": ("load", 0), "y": ("load", 1), "a": ("const", 0),
                                                       "m": ("mul", "a", "x"), "s": ("add", "m", "y")})
@@ -68,7 +80,7 @@ def main() -> None:
             code, n_regs, _, _ = fp.compile_dag("r", {"a": ("load", 0), "b": ("load", 1), "c": ("load", 2),
                                                       "p": ("mul", "a", "b"), "d": ("sub", "p", "c"),
                                                       "q": ("abs", "d"), "r": ("sqrt", "q")})
-            out = torch.empty_like(xs[0])
+            out = view(torch.empty(a.size + 4097, device=dev))
             fn = lambda: k.forall_map(xs, out, code, n_regs=n_regs)  # noqa: E731
             work_bytes = 16 * a.size
     elif a.kernel in ("sum_f32", "hierarchical_sum"):

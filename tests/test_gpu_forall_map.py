@@ -66,10 +66,15 @@ def test_strided_misaligned_and_in_place_views(kernels, oracle_mod):
     base = rs.uniform(0.5, 2, size=(70, 90)).astype(np.float32)
     other = rs.uniform(0.5, 2, size=(90, 70)).astype(np.float32)
     tb, to = torch.from_numpy(base).cuda(), torch.from_numpy(other).cuda()
+    flat, flat2 = tb.reshape(-1), to.reshape(-1)
     views = [
         ("transposed", tb[:64, :64], to.t()[:64, :64]),
         ("offset by one", tb[:, 1:65], tb[:, 2:66]),  # 4-byte aligned only
         ("row step 2", tb[::2, :], to.t()[:35, :90]),
+        ("short strided rows", tb[:50, :3], to.t()[:50, :3]),  # every group crosses a row end
+        ("contiguous, misaligned 1-D", flat[1:4001], flat2[3:4003]),
+        ("contiguous, misaligned 2-D", flat[1:1 + 63 * 97].view(63, 97), flat2[2:2 + 63 * 97].view(63, 97)),
+        ("contiguous 3-D, one misaligned", flat[:5 * 7 * 11].view(5, 7, 11), flat2[1:1 + 385].view(5, 7, 11)),
     ]
     for what, va, vb in views:
         out = torch.zeros(va.shape, device="cuda")
