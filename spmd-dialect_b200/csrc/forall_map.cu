@@ -120,8 +120,12 @@ __device__ __forceinline__ void apply(float4 *rd, const float4 *ra, const float4
 
 // How a launch addresses its views.  VEC: every view contiguous in the
 // domain's row-major order and 16-byte aligned (128-bit accesses, offset =
-// flat index).  CONTIG: every view contiguous, some not 16-byte aligned
-// (4-byte accesses, offset = flat index).  GENERAL: any strides.
+// flat index; a thread's float4 holds four consecutive points).  CONTIG:
+// every view contiguous, some not 16-byte aligned (4-byte accesses at the
+// flat index; component k of slot s is point (4s + k) * threads + thread of
+// the chunk, so each warp access covers 32 consecutive floats).  GENERAL:
+// any strides (four consecutive points per float4, addressed from one index
+// decomposition).
 enum MapMode { kVec = 0, kContig = 1, kGeneral = 2 };
 
 // Offset of flat point e in a view with strides st over the rank-3 domain sz.
@@ -160,7 +164,14 @@ __device__ __forceinline__ int64_t view_offset(const MapParams &p, const int64_t
   return point_offset(e + k, p.size, st);
 }
 
-// Four consecutive points from e; points at or past n read as 0.
+// The chunk point behind component k of a slot whose first point is e: e + k,
+// or e + k * threads for CONTIG (e = chunk start + 4 * slot * threads + thread).
+template <int MODE>
+__device__ __forceinline__ int64_t comp_point(int64_t e, int k) {
+  return MODE == kContig ? e + (int64_t)k * kMapThreads : e + k;
+}
+
+// The four points of a slot; points at or past n read as 0.
 template <int MODE>
 __device__ __forceinline__ float4 load4(const float *src, const int64_t *st, int64_t span, const MapParams &p,
                                         int64_t e, const Idx3 &x) {
@@ -172,8 +183,9 @@ __device__ __forceinline__ float4 load4(const float *src, const int64_t *st, int
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     v[k] = 0.0f;
-    if (e + k < p.n) {
-      const int64_t o = view_offset<MODE>(p, st, e, k, x);
+    const int64_t q = comp_point<MODE>(e, k);
+    if (q < p.n) {
+      const int64_t o = MODE == kContig ? q : view_offset<MODE>(p, st, e, k, x);
       if (IN_RANGE(o >= 0 && o < span, 1, o)) v[k] = src[o];
     }
   }
@@ -189,8 +201,9 @@ __device__ __forceinline__ void store4(const MapParams &p, int64_t e, const Idx3
   const float w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    if (e + k < p.n) {
-      const int64_t o = view_offset<MODE>(p, p.out_st, e, k, x);
+    const int64_t q = comp_point<MODE>(e, k);
+    if (q < p.n) {
+      const int64_t o = MODE == kContig ? q : view_offset<MODE>(p, p.out_st, e, k, x);
       if (IN_RANGE(o >= 0 && o < p.out_span, 2, o)) p.out[o] = w[k];
     }
   }
@@ -212,7 +225,9 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
   float4 *mine = regs + t;
   const int64_t nchunks = (p.n + kChunk - 1) / kChunk;
   for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
-    const int64_t base = c * kChunk + 4 * (int64_t)t;
+    // slot s starts at base + s * 4 * threads (CONTIG: its components are
+    // threads apart; otherwise consecutive)
+    const int64_t base = c * kChunk + (MODE == kContig ? (int64_t)t : 4 * (int64_t)t);
     Idx3 gx[S];
 #pragma unroll
     for (int s = 0; s < S; ++s) gx[s] = group_index<MODE>(p, base + (int64_t)s * 4 * kMapThreads);

@@ -70,7 +70,8 @@ def main() -> None:
                 return t[: a.size // 4096 * 4097].view(-1, 4097)[:, :4096]
             return t[: a.size]
 
-        xs = [view(torch.rand(a.size + 4097, device=dev, generator=g)) for _ in range(nv)]
+        alloc = a.size // 4096 * 4097 + 4097  # room for every layout
+        xs = [view(torch.rand(alloc, device=dev, generator=g)) for _ in range(nv)]
         if a.body == "axpy":
             code, n_regs, _, _ = fp.compile_dag("s", {"x": ("load", 0), "y": ("load", 1), "a": ("const", 0),
                                                       "m": ("mul", "a", "x"), "s": ("add", "m", "y")})
@@ -80,7 +81,7 @@ def main() -> None:
             code, n_regs, _, _ = fp.compile_dag("r", {"a": ("load", 0), "b": ("load", 1), "c": ("load", 2),
                                                       "p": ("mul", "a", "b"), "d": ("sub", "p", "c"),
                                                       "q": ("abs", "d"), "r": ("sqrt", "q")})
-            out = view(torch.empty(a.size + 4097, device=dev))
+            out = view(torch.empty(alloc, device=dev))
             fn = lambda: k.forall_map(xs, out, code, n_regs=n_regs)  # noqa: E731
             work_bytes = 16 * a.size
     elif a.kernel in ("sum_f32", "hierarchical_sum"):
