@@ -20,9 +20,8 @@
 // per 8 points, uniformly across the warp.  The loads of all inputs are
 // issued before the first operation (the LOADs are a prefix of the program),
 // so a chunk's input traffic is in flight at once.  Contiguous, 16-byte
-// aligned views take 128-bit loads and stores; contiguous unaligned ones
-// 4-byte accesses at the flat index; other strides address each group of four
-// points from one index decomposition shared by every view.
+// aligned views take 128-bit loads and stores; other views 4-byte accesses,
+// 32 consecutive points per warp access (MapMode below).
 //
 // Arithmetic is spelled with the _rn intrinsics (round to nearest even, never
 // contracted to an FMA), so the result equals a CPU evaluation of the same
@@ -119,13 +118,13 @@ __device__ __forceinline__ void apply(float4 *rd, const float4 *ra, const float4
 }
 
 // How a launch addresses its views.  VEC: every view contiguous in the
-// domain's row-major order and 16-byte aligned (128-bit accesses, offset =
-// flat index; a thread's float4 holds four consecutive points).  CONTIG:
-// every view contiguous, some not 16-byte aligned (4-byte accesses at the
-// flat index; component k of slot s is point (4s + k) * threads + thread of
-// the chunk, so each warp access covers 32 consecutive floats).  GENERAL:
-// any strides (four consecutive points per float4, addressed from one index
-// decomposition).
+// domain's row-major order and 16-byte aligned: a thread's float4 holds four
+// consecutive points, moved with 128-bit accesses at the flat index.
+// CONTIG (every view contiguous, some not 16-byte aligned) and GENERAL (any
+// strides): component k of slot s is point (4s + k) * threads + thread of the
+// chunk, so a warp access covers 32 consecutive points; CONTIG addresses them
+// at the flat index, GENERAL from their (i0, i1, i2) index, decomposed once
+// per slot and stepped by `threads` points per component.
 enum MapMode { kVec = 0, kContig = 1, kGeneral = 2 };
 
 // Offset of flat point e in a view with strides st over the rank-3 domain sz.
@@ -135,77 +134,85 @@ __device__ __forceinline__ int64_t point_offset(int64_t e, const int64_t *sz, co
   return i0 * st[0] + i1 * st[1] + i2 * st[2];
 }
 
-// GENERAL: the index of the first of four consecutive points, found once per
-// group and shared by every view; `run` when the four lie in one row below n.
+// GENERAL: the (i0, i1, i2) index of a slot's first point, shared by every view.
 struct Idx3 {
   int64_t i0, i1, i2;
-  bool run;
 };
 template <int MODE>
-__device__ __forceinline__ Idx3 group_index(const MapParams &p, int64_t e) {
-  Idx3 x{0, 0, 0, false};
+__device__ __forceinline__ Idx3 slot_index(const MapParams &p, int64_t e) {
+  Idx3 x{0, 0, 0};
   if constexpr (MODE == kGeneral) {
     x.i2 = e % p.size[2];
     const int64_t q = e / p.size[2];
     x.i1 = q % p.size[1];
     x.i0 = q / p.size[1];
-    x.run = e + 3 < p.n && x.i2 + 3 < p.size[2];
   }
   return x;
 }
 
-// Offset of point e + k in a view: the flat index when every view is
-// contiguous; else from the group's index (within a row) or by division.
-template <int MODE>
-__device__ __forceinline__ int64_t view_offset(const MapParams &p, const int64_t *st, int64_t e, int k,
-                                               const Idx3 &x) {
-  if constexpr (MODE != kGeneral) return e + k;
-  if (x.run) return x.i0 * st[0] + x.i1 * st[1] + (x.i2 + k) * st[2];
-  return point_offset(e + k, p.size, st);
+// x += kMapThreads points: rows at least that long wrap at most once; shorter
+// ones are decomposed again.
+__device__ __forceinline__ void step_index(const MapParams &p, Idx3 &x, int64_t next_point) {
+  if (p.size[2] >= kMapThreads) {
+    x.i2 += kMapThreads;
+    if (x.i2 >= p.size[2]) {
+      x.i2 -= p.size[2];
+      if (++x.i1 >= p.size[1]) {
+        x.i1 = 0;
+        ++x.i0;
+      }
+    }
+  } else {
+    x.i2 = next_point % p.size[2];
+    const int64_t q = next_point / p.size[2];
+    x.i1 = q % p.size[1];
+    x.i0 = q / p.size[1];
+  }
 }
 
-// The chunk point behind component k of a slot whose first point is e: e + k,
-// or e + k * threads for CONTIG (e = chunk start + 4 * slot * threads + thread).
-template <int MODE>
-__device__ __forceinline__ int64_t comp_point(int64_t e, int k) {
-  return MODE == kContig ? e + (int64_t)k * kMapThreads : e + k;
-}
-
-// The four points of a slot; points at or past n read as 0.
+// The four points of a slot whose first point is e; points at or past n read as 0.
 template <int MODE>
 __device__ __forceinline__ float4 load4(const float *src, const int64_t *st, int64_t span, const MapParams &p,
                                         int64_t e, const Idx3 &x) {
-  if (MODE == kVec && e + 3 < p.n) {
-    if (!IN_RANGE(e + 3 < span, 1, e)) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    return ld_f4(src + e);
+  if (MODE == kVec) {
+    if (e + 3 < p.n) {
+      if (!IN_RANGE(e + 3 < span, 1, e)) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      return ld_f4(src + e);
+    }
   }
   float v[4];
+  Idx3 y = x;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     v[k] = 0.0f;
-    const int64_t q = comp_point<MODE>(e, k);
+    const int64_t q = MODE == kVec ? e + k : e + (int64_t)k * kMapThreads;
     if (q < p.n) {
-      const int64_t o = MODE == kContig ? q : view_offset<MODE>(p, st, e, k, x);
+      const int64_t o = MODE == kGeneral ? y.i0 * st[0] + y.i1 * st[1] + y.i2 * st[2] : q;
       if (IN_RANGE(o >= 0 && o < span, 1, o)) v[k] = src[o];
     }
+    if (MODE == kGeneral && k < 3) step_index(p, y, q + kMapThreads);
   }
   return make_float4(v[0], v[1], v[2], v[3]);
 }
 
 template <int MODE>
 __device__ __forceinline__ void store4(const MapParams &p, int64_t e, const Idx3 &x, float4 v) {
-  if (MODE == kVec && e + 3 < p.n) {
-    if (IN_RANGE(e + 3 < p.out_span, 2, e)) st_f4(p.out + e, v);
-    return;
+  if (MODE == kVec) {
+    if (e + 3 < p.n) {
+      if (IN_RANGE(e + 3 < p.out_span, 2, e)) st_f4(p.out + e, v);
+      return;
+    }
   }
   const float w[4] = {v.x, v.y, v.z, v.w};
+  Idx3 y = x;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int64_t q = comp_point<MODE>(e, k);
+    const int64_t q = MODE == kVec ? e + k : e + (int64_t)k * kMapThreads;
     if (q < p.n) {
-      const int64_t o = MODE == kContig ? q : view_offset<MODE>(p, p.out_st, e, k, x);
+      const int64_t o = MODE == kGeneral ? y.i0 * p.out_st[0] + y.i1 * p.out_st[1] + y.i2 * p.out_st[2] : q;
       if (IN_RANGE(o >= 0 && o < p.out_span, 2, o)) p.out[o] = w[k];
     }
+    if (MODE == kGeneral && k < 3) step_index(p, y, q + kMapThreads);
   }
 }
 
@@ -225,12 +232,12 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
   float4 *mine = regs + t;
   const int64_t nchunks = (p.n + kChunk - 1) / kChunk;
   for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
-    // slot s starts at base + s * 4 * threads (CONTIG: its components are
-    // threads apart; otherwise consecutive)
-    const int64_t base = c * kChunk + (MODE == kContig ? (int64_t)t : 4 * (int64_t)t);
+    // slot s starts at base + s * 4 * threads (VEC: its components are
+    // consecutive; otherwise threads apart)
+    const int64_t base = c * kChunk + (MODE == kVec ? 4 * (int64_t)t : (int64_t)t);
     Idx3 gx[S];
 #pragma unroll
-    for (int s = 0; s < S; ++s) gx[s] = group_index<MODE>(p, base + (int64_t)s * 4 * kMapThreads);
+    for (int s = 0; s < S; ++s) gx[s] = slot_index<MODE>(p, base + (int64_t)s * 4 * kMapThreads);
     float4 v[NL][S];
 #pragma unroll
     for (int i = 0; i < NL; ++i)
