@@ -170,6 +170,95 @@ __device__ __forceinline__ void step_index(const MapParams &p, Idx3 &x, int64_t 
   }
 }
 
+// GENERAL, per chunk: the index of the thread's first point and, for each of
+// the 4 * S - 1 steps of `threads` points that follow, whether it wraps a row
+// (bit 2j) and a plane (bit 2j + 1).  Rows shorter than `threads` can wrap
+// more than once per step: those are decomposed point by point (`multi`).
+struct ChunkIdx {
+  Idx3 x;
+  uint32_t wraps;
+  bool multi;
+};
+template <int S>
+__device__ __forceinline__ ChunkIdx chunk_index(const MapParams &p, int64_t first) {
+  ChunkIdx g;
+  g.x = slot_index<kGeneral>(p, first);
+  g.wraps = 0;
+  g.multi = p.size[2] < kMapThreads;
+  if (!g.multi) {
+    Idx3 y = g.x;
+#pragma unroll
+    for (int j = 0; j < 4 * S - 1; ++j) {
+      y.i2 += kMapThreads;
+      if (y.i2 >= p.size[2]) {
+        y.i2 -= p.size[2];
+        g.wraps |= 1u << (2 * j);
+        if (++y.i1 >= p.size[1]) {
+          y.i1 = 0;
+          ++y.i0;
+          g.wraps |= 2u << (2 * j);
+        }
+      }
+    }
+  }
+  return g;
+}
+
+// GENERAL: the 4 * S points of a chunk for one view (component k of slot s =
+// point first + (4s + k) * threads), the offset advanced by adds along the
+// chunk's recorded wraps.
+template <int S>
+__device__ __forceinline__ void load_general(const float *src, const int64_t *st, int64_t span, const MapParams &p,
+                                             int64_t first, const ChunkIdx &g, float4 *out) {
+  int64_t o = g.x.i0 * st[0] + g.x.i1 * st[1] + g.x.i2 * st[2];
+  const int64_t d_step = (int64_t)kMapThreads * st[2];
+  const int64_t d_row = st[1] - p.size[2] * st[2], d_plane = st[0] - p.size[1] * st[1];
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 4 * s + k;
+      const int64_t q = first + (int64_t)j * kMapThreads;
+      const int64_t oq = g.multi ? point_offset(q, p.size, st) : o;
+      v[k] = 0.0f;
+      if (q < p.n && IN_RANGE(oq >= 0 && oq < span, 1, oq)) v[k] = src[oq];
+      if (j < 4 * S - 1) {
+        o += d_step;
+        if (g.wraps & (1u << (2 * j))) o += d_row;
+        if (g.wraps & (2u << (2 * j))) o += d_plane;
+      }
+    }
+    out[s] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+template <int S>
+__device__ __forceinline__ void store_general(const MapParams &p, int64_t first, const ChunkIdx &g,
+                                              const float4 *vals, int row) {
+  const int64_t *st = p.out_st;
+  int64_t o = g.x.i0 * st[0] + g.x.i1 * st[1] + g.x.i2 * st[2];
+  const int64_t d_step = (int64_t)kMapThreads * st[2];
+  const int64_t d_row = st[1] - p.size[2] * st[2], d_plane = st[0] - p.size[1] * st[1];
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    const float4 v4 = vals[s * row];
+    const float w[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 4 * s + k;
+      const int64_t q = first + (int64_t)j * kMapThreads;
+      const int64_t oq = g.multi ? point_offset(q, p.size, st) : o;
+      if (q < p.n && IN_RANGE(oq >= 0 && oq < p.out_span, 2, oq)) p.out[oq] = w[k];
+      if (j < 4 * S - 1) {
+        o += d_step;
+        if (g.wraps & (1u << (2 * j))) o += d_row;
+        if (g.wraps & (2u << (2 * j))) o += d_plane;
+      }
+    }
+  }
+}
+
 // The four points of a slot whose first point is e; points at or past n read as 0.
 template <int MODE>
 __device__ __forceinline__ float4 load4(const float *src, const int64_t *st, int64_t span, const MapParams &p,
@@ -235,15 +324,20 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
     // slot s starts at base + s * 4 * threads (VEC: its components are
     // consecutive; otherwise threads apart)
     const int64_t base = c * kChunk + (MODE == kVec ? 4 * (int64_t)t : (int64_t)t);
-    Idx3 gx[S];
-#pragma unroll
-    for (int s = 0; s < S; ++s) gx[s] = slot_index<MODE>(p, base + (int64_t)s * 4 * kMapThreads);
+    const Idx3 none{0, 0, 0};
+    ChunkIdx g{};
+    if constexpr (MODE == kGeneral) g = chunk_index<S>(p, base);
     float4 v[NL][S];
 #pragma unroll
-    for (int i = 0; i < NL; ++i)
+    for (int i = 0; i < NL; ++i) {
+      if constexpr (MODE == kGeneral) {
+        load_general<S>(p.ld_src[i], p.ld_st[i], p.ld_span[i], p, base, g, v[i]);
+      } else {
 #pragma unroll
-      for (int s = 0; s < S; ++s)
-        v[i][s] = load4<MODE>(p.ld_src[i], p.ld_st[i], p.ld_span[i], p, base + (int64_t)s * 4 * kMapThreads, gx[s]);
+        for (int s = 0; s < S; ++s)
+          v[i][s] = load4<MODE>(p.ld_src[i], p.ld_st[i], p.ld_span[i], p, base + (int64_t)s * 4 * kMapThreads, none);
+      }
+    }
 #pragma unroll
     for (int i = 0; i < NL; ++i) {
       if (!IN_RANGE(p.ld_dst[i] < p.n_regs, 3, p.ld_dst[i])) continue;
@@ -304,9 +398,13 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
       }
     }
     if (IN_RANGE(p.out_reg < p.n_regs, 3, p.out_reg)) {
+      if constexpr (MODE == kGeneral) {
+        store_general<S>(p, base, g, mine + p.out_reg * kRow, kMapThreads);
+      } else {
 #pragma unroll
-      for (int s = 0; s < S; ++s)
-        store4<MODE>(p, base + (int64_t)s * 4 * kMapThreads, gx[s], mine[p.out_reg * kRow + s * kMapThreads]);
+        for (int s = 0; s < S; ++s)
+          store4<MODE>(p, base + (int64_t)s * 4 * kMapThreads, none, mine[p.out_reg * kRow + s * kMapThreads]);
+      }
     }
   }
 }
