@@ -134,40 +134,17 @@ __device__ __forceinline__ int64_t point_offset(int64_t e, const int64_t *sz, co
   return i0 * st[0] + i1 * st[1] + i2 * st[2];
 }
 
-// GENERAL: the (i0, i1, i2) index of a slot's first point, shared by every view.
+// GENERAL: the (i0, i1, i2) index of flat point e.
 struct Idx3 {
   int64_t i0, i1, i2;
 };
-template <int MODE>
-__device__ __forceinline__ Idx3 slot_index(const MapParams &p, int64_t e) {
-  Idx3 x{0, 0, 0};
-  if constexpr (MODE == kGeneral) {
-    x.i2 = e % p.size[2];
-    const int64_t q = e / p.size[2];
-    x.i1 = q % p.size[1];
-    x.i0 = q / p.size[1];
-  }
+__device__ __forceinline__ Idx3 point_index(const MapParams &p, int64_t e) {
+  Idx3 x;
+  x.i2 = e % p.size[2];
+  const int64_t q = e / p.size[2];
+  x.i1 = q % p.size[1];
+  x.i0 = q / p.size[1];
   return x;
-}
-
-// x += kMapThreads points: rows at least that long wrap at most once; shorter
-// ones are decomposed again.
-__device__ __forceinline__ void step_index(const MapParams &p, Idx3 &x, int64_t next_point) {
-  if (p.size[2] >= kMapThreads) {
-    x.i2 += kMapThreads;
-    if (x.i2 >= p.size[2]) {
-      x.i2 -= p.size[2];
-      if (++x.i1 >= p.size[1]) {
-        x.i1 = 0;
-        ++x.i0;
-      }
-    }
-  } else {
-    x.i2 = next_point % p.size[2];
-    const int64_t q = next_point / p.size[2];
-    x.i1 = q % p.size[1];
-    x.i0 = q / p.size[1];
-  }
 }
 
 // GENERAL, per chunk: the index of the thread's first point and, for each of
@@ -182,7 +159,7 @@ struct ChunkIdx {
 template <int S>
 __device__ __forceinline__ ChunkIdx chunk_index(const MapParams &p, int64_t first) {
   ChunkIdx g;
-  g.x = slot_index<kGeneral>(p, first);
+  g.x = point_index(p, first);
   g.wraps = 0;
   g.multi = p.size[2] < kMapThreads;
   if (!g.multi) {
@@ -259,49 +236,35 @@ __device__ __forceinline__ void store_general(const MapParams &p, int64_t first,
   }
 }
 
-// The four points of a slot whose first point is e; points at or past n read as 0.
+// VEC / CONTIG: the four points of a slot whose first point is e (VEC:
+// e..e+3; CONTIG: threads apart); points at or past n read as 0.
 template <int MODE>
-__device__ __forceinline__ float4 load4(const float *src, const int64_t *st, int64_t span, const MapParams &p,
-                                        int64_t e, const Idx3 &x) {
-  if (MODE == kVec) {
-    if (e + 3 < p.n) {
-      if (!IN_RANGE(e + 3 < span, 1, e)) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      return ld_f4(src + e);
-    }
+__device__ __forceinline__ float4 load4(const float *src, int64_t span, const MapParams &p, int64_t e) {
+  if (MODE == kVec && e + 3 < p.n) {
+    if (!IN_RANGE(e + 3 < span, 1, e)) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    return ld_f4(src + e);
   }
   float v[4];
-  Idx3 y = x;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     v[k] = 0.0f;
     const int64_t q = MODE == kVec ? e + k : e + (int64_t)k * kMapThreads;
-    if (q < p.n) {
-      const int64_t o = MODE == kGeneral ? y.i0 * st[0] + y.i1 * st[1] + y.i2 * st[2] : q;
-      if (IN_RANGE(o >= 0 && o < span, 1, o)) v[k] = src[o];
-    }
-    if (MODE == kGeneral && k < 3) step_index(p, y, q + kMapThreads);
+    if (q < p.n && IN_RANGE(q < span, 1, q)) v[k] = src[q];
   }
   return make_float4(v[0], v[1], v[2], v[3]);
 }
 
 template <int MODE>
-__device__ __forceinline__ void store4(const MapParams &p, int64_t e, const Idx3 &x, float4 v) {
-  if (MODE == kVec) {
-    if (e + 3 < p.n) {
-      if (IN_RANGE(e + 3 < p.out_span, 2, e)) st_f4(p.out + e, v);
-      return;
-    }
+__device__ __forceinline__ void store4(const MapParams &p, int64_t e, float4 v) {
+  if (MODE == kVec && e + 3 < p.n) {
+    if (IN_RANGE(e + 3 < p.out_span, 2, e)) st_f4(p.out + e, v);
+    return;
   }
   const float w[4] = {v.x, v.y, v.z, v.w};
-  Idx3 y = x;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int64_t q = MODE == kVec ? e + k : e + (int64_t)k * kMapThreads;
-    if (q < p.n) {
-      const int64_t o = MODE == kGeneral ? y.i0 * p.out_st[0] + y.i1 * p.out_st[1] + y.i2 * p.out_st[2] : q;
-      if (IN_RANGE(o >= 0 && o < p.out_span, 2, o)) p.out[o] = w[k];
-    }
-    if (MODE == kGeneral && k < 3) step_index(p, y, q + kMapThreads);
+    if (q < p.n && IN_RANGE(q < p.out_span, 2, q)) p.out[q] = w[k];
   }
 }
 
@@ -324,7 +287,6 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
     // slot s starts at base + s * 4 * threads (VEC: its components are
     // consecutive; otherwise threads apart)
     const int64_t base = c * kChunk + (MODE == kVec ? 4 * (int64_t)t : (int64_t)t);
-    const Idx3 none{0, 0, 0};
     ChunkIdx g{};
     if constexpr (MODE == kGeneral) g = chunk_index<S>(p, base);
     float4 v[NL][S];
@@ -335,7 +297,7 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
       } else {
 #pragma unroll
         for (int s = 0; s < S; ++s)
-          v[i][s] = load4<MODE>(p.ld_src[i], p.ld_st[i], p.ld_span[i], p, base + (int64_t)s * 4 * kMapThreads, none);
+          v[i][s] = load4<MODE>(p.ld_src[i], p.ld_span[i], p, base + (int64_t)s * 4 * kMapThreads);
       }
     }
 #pragma unroll
@@ -403,7 +365,7 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
       } else {
 #pragma unroll
         for (int s = 0; s < S; ++s)
-          store4<MODE>(p, base + (int64_t)s * 4 * kMapThreads, none, mine[p.out_reg * kRow + s * kMapThreads]);
+          store4<MODE>(p, base + (int64_t)s * 4 * kMapThreads, mine[p.out_reg * kRow + s * kMapThreads]);
       }
     }
   }
