@@ -401,14 +401,17 @@ def analyse(func: Func) -> Mapping:
     atomics = [(op, p) for op, p in nodes if op.name == "memref.atomic_rmw"]
     stores = [(op, p) for op, p in nodes if op.name == "memref.store"]
     ifs = [op for op, _ in nodes if op.name == "spmd.if"]
-    if ifs:
-        raise ShimError(f"{func.name}: spmd.if (a guarded store or a select) is not mapped")
+    if ifs and (reduces or atomics or not foralls):
+        raise ShimError(f"{func.name}: spmd.if (a guarded store or a select) is not mapped here "
+                        f"(only as the guarded store of an elementwise forall)")
     if not foralls:
         return _analyse_returned_reduce(func, env, args, reduces)
     group = foralls[0]
     lbs, ubs, steps = _segments(group)
     tile = _attr_ints(group.attrs, "spmd.tile_sizes")
     policy = _attr_enum(group.attrs, "spmd.memory_policy")
+    if ifs:
+        return _analyse_guarded(func, env, args, ifs, stores, foralls, lbs, ubs, steps)
 
     if atomics:  # ---------------------------------------------------------- reductions
         at, _ = atomics[0]
@@ -629,6 +632,37 @@ def _analyse_map(func: Func, env: _Env, args: dict, st: Op, foralls: list, lbs, 
     return Mapping(func.name, "map", "spmdb200_forall_map", {
         "rank": rank, "inputs": inputs, "output": dst, "lower": lower, "domain": upper, "steps": dom_step,
         "code": [list(c) for c in code], "consts": consts, "n_regs": n_regs})
+
+
+def _analyse_guarded(func: Func, env: _Env, args: dict, ifs: list, stores: list, foralls: list, lbs, ubs,
+                     steps) -> Mapping:
+    """A forall whose only store sits in an spmd.if: `if (c) A[p] = v`, with
+    an empty else region or `else A[p] = w`, is the elementwise map
+    A[p] = select(c, v, w) -- with A[p] itself for the missing else (an
+    in-place map: each point is read before it is written).  The guarded-store
+    form of test/SPMD/lower-to-gpu.mlir:200-213, run by spmdb200_forall_map."""
+    if len(ifs) != 1 or ifs[0].result:
+        raise ShimError(f"{func.name}: one spmd.if without results (a guarded store) is mapped, not {len(ifs)}")
+    op_if = ifs[0]
+    then_st = [o for o in _iter_ops(op_if.region) if o.name == "memref.store"]
+    else_st = [o for r in op_if.more_regions for o in _iter_ops(r) if o.name == "memref.store"]
+    if len(then_st) != 1 or len(else_st) > 1 or len(stores) != len(then_st) + len(else_st):
+        raise ShimError(f"{func.name}: the spmd.if must hold the forall's only store (one per region)")
+    st = then_st[0]
+    if else_st:
+        a = [env.index(v) for v in _vals(st.extra)]
+        b = [env.index(v) for v in _vals(else_st[0].extra)]
+        if else_st[0].operands[1] != st.operands[1] or any(x.terms != y.terms or x.const != y.const
+                                                           for x, y in zip(a, b)):
+            raise ShimError(f"{func.name}: the two regions store to different places")
+        other = else_st[0].operands[0]
+    else:
+        other = "%__guarded_old"
+        env.defs[other] = Op("memref.load", other, [st.operands[1]], extra=st.extra, type=st.type)
+    sel = "%__guarded_select"
+    env.defs[sel] = Op("arith.select", sel, [op_if.operands[0], st.operands[0], other], type="f32")
+    synth = Op("memref.store", None, [sel, st.operands[1]], extra=st.extra, type=st.type)
+    return _analyse_map(func, env, args, synth, foralls, lbs, ubs, steps)
 
 
 # memref.atomic_rmw kinds that combine per-tile results of each reduction kind

@@ -298,3 +298,43 @@ func.func @scale_in_place(%B: memref<?xf32>, %N: index) attributes {spmd.kernel}
   }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
   func.return
 }
+
+// Guarded stores (spmd.if inside an elementwise forall).
+func.func @clamp_guarded(%A: memref<?xf32>, %N: index, %t: f32) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  "spmd.forall"(%c0, %N, %c1) ({
+  ^bb0(%i: index):
+    %v = memref.load %A[%i] : memref<?xf32>
+    %big = arith.cmpf ogt, %v, %t : f32
+    "spmd.if"(%big) ({
+      memref.store %t, %A[%i] : memref<?xf32>
+      "spmd.yield"() : () -> ()
+    }, {
+      "spmd.yield"() : () -> ()
+    }) : (i1) -> ()
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>, "spmd.mapping" = #spmd.level<group>} : (index, index, index) -> ()
+  func.return
+}
+
+func.func @abs_if_else(%A: memref<?x?xf32>, %B: memref<?x?xf32>, %N: index, %M: index) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  %zero = arith.constant 0.0 : f32
+  "spmd.forall"(%c0, %c0, %N, %M, %c1, %c1) ({
+  ^bb0(%i: index, %j: index):
+    %a = memref.load %A[%i, %j] : memref<?x?xf32>
+    %pos = arith.cmpf oge, %a, %zero : f32
+    "spmd.if"(%pos) ({
+      memref.store %a, %B[%i, %j] : memref<?x?xf32>
+      "spmd.yield"() : () -> ()
+    }, {
+      %n = arith.negf %a : f32
+      memref.store %n, %B[%i, %j] : memref<?x?xf32>
+      "spmd.yield"() : () -> ()
+    }) : (i1) -> ()
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 2, 2, 2>} : (index, index, index, index, index, index) -> ()
+  func.return
+}

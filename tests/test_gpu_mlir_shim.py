@@ -107,3 +107,17 @@ func.func @sum_stored(%A: memref<?xf32>, %out: memref<3xf32>, %N: index) attribu
     got = out.cpu().numpy()
     assert got[0] == 5.0 and got[1] == 5.0
     assert abs(float(got[2]) - oracle_mod.sum_f64(x[:1000])) <= 1e-6 * oracle_mod.sum_f64(x[:1000])
+
+
+def test_guarded_stores(fns):
+    rs = np.random.RandomState(33)
+    a = rs.uniform(-2, 2, 5001).astype(np.float32)
+    ta = torch.from_numpy(a).cuda()
+    fns["clamp_guarded"](ta, 5000, 0.5)
+    want = a.copy()
+    want[:5000] = np.where(a[:5000] > np.float32(0.5), np.float32(0.5), a[:5000])
+    assert np.array_equal(ta.cpu().numpy(), want)
+    m = rs.uniform(-2, 2, (33, 70)).astype(np.float32)
+    tb = torch.zeros((33, 70), device="cuda")
+    fns["abs_if_else"](torch.from_numpy(m).cuda(), tb, 33, 70)
+    assert np.array_equal(tb.cpu().numpy(), np.where(m >= 0, m, -m).astype(np.float32))

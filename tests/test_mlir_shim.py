@@ -179,15 +179,16 @@ func.func @guarded(%A: memref<?xf32>, %N: index, %t: f32) attributes {spmd.kerne
 
 def test_forms_beyond_the_kernel_file():
     """Hexadecimal f32 literals, memref types with attributes, multi-region
-    spmd.if, a returned top-level reduce, and per-tile results combined by an
-    operation other than the reduction's own kind (reported, not mapped)."""
+    spmd.if (a guarded store), a returned top-level reduce, and per-tile
+    results combined by an operation other than the reduction's own kind
+    (reported, not mapped)."""
     shim = spmd_mod("mlir_shim")
     d = {x["function"]: x for x in shim.describe(_FORMS)}
     r = d["sum_returned"]
     assert r["pattern"] == "reduce" and r["output"] is None and r["combine"] == "return" and r["init"] == 0.0
     assert "not a single max reduction" in d["max_then_add"]["error"]
     assert d["max_f32"]["entry"] == "spmdb200_reduce_f32" and d["max_f32"]["kind"] == "max"
-    assert "spmd.if" in d["guarded"]["error"]
+    assert d["guarded"]["pattern"] == "map" and d["guarded"]["output"] == "%A"  # a guarded store: a select
     assert shim._const_value("0xFF800000", "f32") == float("-inf")
     assert shim._const_value("0x7FC00000", "f32") != shim._const_value("0x7FC00000", "f32")  # NaN
     assert shim._const_value("0xFFFFFFFF", "i32") == -1
@@ -236,3 +237,20 @@ func.func @nothing(%N: index) attributes {spmd.kernel} {
     (d,) = shim.describe(text)
     assert d["pattern"] == "empty" and d["entry"] is None
     assert shim.load(text)["nothing"](10) is None
+
+
+def test_guarded_stores_map_to_selects(oracle_mod):
+    """`if (c) A[i] = t` is the in-place map A[i] = select(c, t, A[i]); an
+    if / else pair storing to one place is select(c, then, else)."""
+    import numpy as np
+    d = _by_name()
+    g = d["clamp_guarded"]
+    assert g["pattern"] == "map" and g["inputs"] == ["%A"] and g["output"] == "%A" and g["consts"] == ["%t"]
+    a = np.random.RandomState(31).uniform(-2, 2, 777).astype(np.float32)
+    got = oracle_mod.forall_map([a], a.shape, g["code"], [0.5])
+    assert np.array_equal(got, np.where(a > np.float32(0.5), np.float32(0.5), a))
+    e = d["abs_if_else"]
+    assert e["pattern"] == "map" and e["inputs"] == ["%A"] and e["output"] == "%B"
+    m = np.random.RandomState(32).uniform(-2, 2, (9, 13)).astype(np.float32)
+    got = oracle_mod.forall_map([m], m.shape, e["code"], e["consts"])
+    assert np.array_equal(got.view(np.uint32), np.where(m >= 0, m, -m).astype(np.float32).view(np.uint32))
