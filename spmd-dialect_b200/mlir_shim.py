@@ -400,8 +400,8 @@ def analyse(func: Func) -> Mapping:
     reduces = [(op, p) for op, p in nodes if op.name == "spmd.reduce"]
     atomics = [(op, p) for op, p in nodes if op.name == "memref.atomic_rmw"]
     stores = [(op, p) for op, p in nodes if op.name == "memref.store"]
-    ifs = [op for op, _ in nodes if op.name == "spmd.if"]
-    if ifs and (reduces or atomics or not foralls):
+    ifs = [op for op, _ in nodes if op.name == "spmd.if" and not op.result]  # guarded stores
+    if [op for op, _ in nodes if op.name == "spmd.if"] and (reduces or atomics or not foralls):
         raise ShimError(f"{func.name}: spmd.if (a guarded store or a select) is not mapped here "
                         f"(only as the guarded store of an elementwise forall)")
     if not foralls:
@@ -600,6 +600,17 @@ def _analyse_map(func: Func, env: _Env, args: dict, st: Op, foralls: list, lbs, 
                 raise ShimError(f"{func.name}: constant of type {op.type} in an elementwise body")
             consts.append(float(env.consts[v]))
             nodes[v] = ("const", len(consts) - 1)
+            return
+        if op.name == "spmd.if":
+            # %r = spmd.if(%c) {yield %x} else {yield %y}: select(c, x, y); both
+            # regions are side-effect free here (the forall's only store is outside)
+            ys = [[o for o in r if o.name == "spmd.yield"] for r in [op.region, *op.more_regions]]
+            if len(ys) != 2 or any(len(y) != 1 or len(y[0].operands) != 1 for y in ys):
+                raise ShimError(f"{func.name}: an spmd.if value needs one yielded value per region")
+            x, y = ys[0][0].operands[0], ys[1][0].operands[0]
+            for o in (op.operands[0], x, y):
+                visit(o)
+            nodes[v] = ("select", op.operands[0], x, y)
             return
         kind = _MAP_ARITH.get(op.name)
         if kind is None:

@@ -338,3 +338,24 @@ func.func @abs_if_else(%A: memref<?x?xf32>, %B: memref<?x?xf32>, %N: index, %M: 
   }) {operandSegmentSizes = array<i32: 2, 2, 2>} : (index, index, index, index, index, index) -> ()
   func.return
 }
+
+func.func @select_by_if(%A: memref<?xf32>, %B: memref<?xf32>, %C: memref<?xf32>, %N: index) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  "spmd.forall"(%c0, %N, %c1) ({
+  ^bb0(%i: index):
+    %a = memref.load %A[%i] : memref<?xf32>
+    %b = memref.load %B[%i] : memref<?xf32>
+    %lt = arith.cmpf olt, %a, %b : f32
+    %m = "spmd.if"(%lt) ({
+      %d = arith.subf %b, %a : f32
+      "spmd.yield"(%d) : (f32) -> ()
+    }, {
+      %e = arith.subf %a, %b : f32
+      "spmd.yield"(%e) : (f32) -> ()
+    }) : (i1) -> f32
+    memref.store %m, %C[%i] : memref<?xf32>
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
+  func.return
+}

@@ -121,3 +121,11 @@ def test_guarded_stores(fns):
     tb = torch.zeros((33, 70), device="cuda")
     fns["abs_if_else"](torch.from_numpy(m).cuda(), tb, 33, 70)
     assert np.array_equal(tb.cpu().numpy(), np.where(m >= 0, m, -m).astype(np.float32))
+
+
+def test_spmd_if_value(fns):
+    rs = np.random.RandomState(35)
+    a, b = rs.randn(3001).astype(np.float32), rs.randn(3001).astype(np.float32)
+    tc = torch.zeros(3001, device="cuda")
+    fns["select_by_if"](torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda(), tc, 3001)
+    assert np.array_equal(tc.cpu().numpy(), np.where(a < b, b - a, a - b).astype(np.float32))

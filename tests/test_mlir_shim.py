@@ -254,3 +254,13 @@ def test_guarded_stores_map_to_selects(oracle_mod):
     m = np.random.RandomState(32).uniform(-2, 2, (9, 13)).astype(np.float32)
     got = oracle_mod.forall_map([m], m.shape, e["code"], e["consts"])
     assert np.array_equal(got.view(np.uint32), np.where(m >= 0, m, -m).astype(np.float32).view(np.uint32))
+
+
+def test_spmd_if_value_is_a_select(oracle_mod):
+    import numpy as np
+    d = _by_name()["select_by_if"]
+    assert d["pattern"] == "map" and d["inputs"] == ["%A", "%B"] and d["output"] == "%C"
+    rs = np.random.RandomState(34)
+    a, b = rs.randn(501).astype(np.float32), rs.randn(501).astype(np.float32)
+    got = oracle_mod.forall_map([a, b], a.shape, d["code"], d["consts"])
+    assert np.array_equal(got, np.where(a < b, b - a, a - b).astype(np.float32))
