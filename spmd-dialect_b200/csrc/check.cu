@@ -19,8 +19,10 @@ extern "C" int spmdb200_check_status(unsigned long long *first_out) {
     return record_api_status(SPMDB200_ERR_CUDA, "check_status: %s", cudaGetErrorString(e));
   }
   unsigned long long a = 0, b = 0;
-  check_read_forall_map(&a);
-  check_read_stencil_nd(&b);
+  if (check_read_forall_map(&a) < 0 || check_read_stencil_nd(&b) < 0) {
+    e = cudaGetLastError();
+    return record_api_status(SPMDB200_ERR_CUDA, "check_status: reading the record: %s", cudaGetErrorString(e));
+  }
   const unsigned long long first = a ? a : b;
   if (!first) return record_api_status(SPMDB200_OK, "");
   if (first_out) *first_out = first;

@@ -411,8 +411,9 @@ int check_read_forall_map(unsigned long long *first) {
 #ifdef SPMDB200_CHECKED
   if (!first) return 1;  // only asks whether this is a checked build
   unsigned long long v = 0, z = 0;
-  cudaMemcpyFromSymbol(&v, g_check_first, sizeof(v));
-  cudaMemcpyToSymbol(g_check_first, &z, sizeof(z));
+  if (cudaMemcpyFromSymbol(&v, g_check_first, sizeof(v)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_check_first, &z, sizeof(z)) != cudaSuccess)
+    return -1;
   *first = v;
   return 1;
 #else

@@ -178,8 +178,9 @@ int num_sms(int device);
 
 // The first out-of-range access a checked build recorded in each file's device
 // word (0: none), read and cleared.  Return 1 in a checked build of that file,
-// 0 in a release build (nothing read); with first == nullptr they only answer
-// that, without a CUDA call.
+// 0 in a release build (nothing read), -1 when the device word could not be
+// read; with first == nullptr they only answer whether the build is checked,
+// without a CUDA call.
 int check_read_forall_map(unsigned long long *first);
 int check_read_stencil_nd(unsigned long long *first);
 
