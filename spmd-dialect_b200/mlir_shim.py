@@ -527,11 +527,14 @@ _MAP_ARITH = {"arith.addf": "add", "arith.subf": "sub", "arith.mulf": "mul", "ar
 
 
 def _analyse_map(func: Func, env: _Env, args: dict, st: Op, foralls: list, lbs, ubs, steps) -> Mapping:
-    """An elementwise forall with a general f32 body: out[p] = f(in_k[p], ...)
-    where every load reads its memref at the store's own index and f is any
-    DAG of the ops in _MAP_ARITH, f32 constants and f32 scalar arguments --
+    """A forall with a general f32 body: out[p] = f(in_0[p + o_0], ...) where
+    every load reads its memref at the store's index plus a constant offset
+    (each (memref, offset) pair becomes a view shifted by the offset, so a
+    non-linear stencil -- a max filter, an upwind select -- maps too) and f is
+    any DAG of the ops in _MAP_ARITH, f32 constants and f32 scalar arguments:
     the per-point body SPMDToGPU.cpp:491-580 lowers, run by
-    spmdb200_forall_map."""
+    spmdb200_forall_map.  The stored memref may be read only at the store's
+    own index."""
     val, dst = st.operands
     if args.get(dst) is None or args[dst].kind != "memref" or args[dst].elem != "f32":
         raise ShimError(f"{func.name}: the stored memref must be an f32 memref argument")
@@ -589,11 +592,19 @@ def _analyse_map(func: Func, env: _Env, args: dict, st: Op, foralls: list, lbs, 
                     or args[src].rank != rank:
                 raise ShimError(f"{func.name}: {src} is not an f32 memref argument of rank {rank}")
             idx = [env.index(x) for x in _vals(op.extra)]
-            if any(i.terms != j.terms or i.const != j.const for i, j in zip(idx, dst_idx)):
-                raise ShimError(f"{func.name}: {src} is read off the store's index (not elementwise)")
-            if src not in inputs:
-                inputs.append(src)
-            nodes[v] = ("load", inputs.index(src))
+            off = []
+            for i, j in zip(idx, dst_idx):
+                d = i - j
+                if d.terms:
+                    raise ShimError(f"{func.name}: {src} is read off the store's index plus a constant")
+                off.append(d.const)
+            if src == dst and any(off):
+                # every point would read values other points overwrite
+                raise ShimError(f"{func.name}: the stored memref is also read at another point")
+            key = (src, tuple(off))  # a constant offset is a shifted view of the memref
+            if key not in inputs:
+                inputs.append(key)
+            nodes[v] = ("load", inputs.index(key))
             return
         if op.name == "arith.constant":
             if op.type not in ("f32", "i1"):
@@ -641,7 +652,8 @@ def _analyse_map(func: Func, env: _Env, args: dict, st: Op, foralls: list, lbs, 
     except ValueError as e:
         raise ShimError(f"{func.name}: {e}") from None
     return Mapping(func.name, "map", "spmdb200_forall_map", {
-        "rank": rank, "inputs": inputs, "output": dst, "lower": lower, "domain": upper, "steps": dom_step,
+        "rank": rank, "inputs": [m for m, _ in inputs], "input_offsets": [list(o) for _, o in inputs],
+        "output": dst, "lower": lower, "domain": upper, "steps": dom_step,
         "code": [list(c) for c in code], "consts": consts, "n_regs": n_regs})
 
 
@@ -789,8 +801,18 @@ class BoundKernel:
             lo = [int(env[v]) if isinstance(v, str) else int(v) for v in d["lower"]]
             hi = [num(u) if u in env else self._const(u) if isinstance(u, str) else int(u) for u in d["domain"]]
             box = tuple(slice(a, max(a, b), s) for a, b, s in zip(lo, hi, d["steps"]))
-            views = [env[x][box] for x in d["inputs"]]
-            out = env[d["output"]][box]
+            ot = env[d["output"]]
+            if any(b > a and (a < 0 or b > ot.shape[k]) for k, (a, b) in enumerate(zip(lo, hi))):
+                raise ShimError(f"{self.func.name}: the domain {lo}..{hi} is outside {d['output']}'s sizes "
+                                f"{tuple(ot.shape)}")
+            out = ot[box]
+            views = []
+            for x, off in zip(d["inputs"], d["input_offsets"]):
+                t = env[x]
+                if out.numel() and any(a + o < 0 or max(a, b) + o > t.shape[k]
+                                       for k, (a, b, o) in enumerate(zip(lo, hi, off))):
+                    raise ShimError(f"{self.func.name}: {x} read at offset {off} outside its sizes {tuple(t.shape)}")
+                views.append(t[tuple(slice(a + o, max(a, b) + o, s) for a, b, o, s in zip(lo, hi, off, d["steps"]))])
             if out.numel() == 0:
                 return out
             consts = [float(env[c]) if isinstance(c, str) else c for c in d["consts"]]

@@ -359,3 +359,56 @@ func.func @select_by_if(%A: memref<?xf32>, %B: memref<?xf32>, %C: memref<?xf32>,
   }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
   func.return
 }
+
+// Non-linear stencils: loads at constant offsets are shifted views.
+func.func @max_filter_interior(%A: memref<?xf32>, %B: memref<?xf32>, %Nm1: index) attributes {spmd.kernel} {
+  %c1 = arith.constant 1 : index
+  "spmd.forall"(%c1, %Nm1, %c1) ({
+  ^bb0(%i: index):
+    %im = arith.subi %i, %c1 : index
+    %ip = arith.addi %i, %c1 : index
+    %l = memref.load %A[%im] : memref<?xf32>
+    %r = memref.load %A[%ip] : memref<?xf32>
+    %c = memref.load %A[%i] : memref<?xf32>
+    %m = arith.maximumf %l, %r : f32
+    %d = arith.subf %m, %c : f32
+    memref.store %d, %B[%i] : memref<?xf32>
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
+  func.return
+}
+
+func.func @upwind2d(%A: memref<?x?xf32>, %B: memref<?x?xf32>, %Nm1: index, %M: index) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  %zero = arith.constant 0.0 : f32
+  "spmd.forall"(%c1, %c0, %Nm1, %M, %c1, %c1) ({
+  ^bb0(%i: index, %j: index):
+    %im = arith.subi %i, %c1 : index
+    %ip = arith.addi %i, %c1 : index
+    %c = memref.load %A[%i, %j] : memref<?x?xf32>
+    %n = memref.load %A[%im, %j] : memref<?x?xf32>
+    %s = memref.load %A[%ip, %j] : memref<?x?xf32>
+    %pos = arith.cmpf ogt, %c, %zero : f32
+    %back = arith.subf %c, %n : f32
+    %fwd = arith.subf %s, %c : f32
+    %v = arith.select %pos, %back, %fwd : f32
+    memref.store %v, %B[%i, %j] : memref<?x?xf32>
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 2, 2, 2>} : (index, index, index, index, index, index) -> ()
+  func.return
+}
+
+func.func @in_place_neighbour_unsupported(%A: memref<?xf32>, %N: index) attributes {spmd.kernel} {
+  %c1 = arith.constant 1 : index
+  "spmd.forall"(%c1, %N, %c1) ({
+  ^bb0(%i: index):
+    %im = arith.subi %i, %c1 : index
+    %l = memref.load %A[%im] : memref<?xf32>
+    %c = memref.load %A[%i] : memref<?xf32>
+    %m = arith.maximumf %l, %c : f32
+    memref.store %m, %A[%i] : memref<?xf32>
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
+  func.return
+}

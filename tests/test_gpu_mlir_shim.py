@@ -129,3 +129,23 @@ def test_spmd_if_value(fns):
     tc = torch.zeros(3001, device="cuda")
     fns["select_by_if"](torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda(), tc, 3001)
     assert np.array_equal(tc.cpu().numpy(), np.where(a < b, b - a, a - b).astype(np.float32))
+
+
+def test_nonlinear_stencils(fns):
+    rs = np.random.RandomState(38)
+    a = rs.randn(4000).astype(np.float32)
+    tb = torch.full((4000,), 9.0, device="cuda")
+    fns["max_filter_interior"](torch.from_numpy(a).cuda(), tb, 3999)
+    want = np.full(4000, 9.0, np.float32)
+    want[1:3999] = np.maximum(a[:3998], a[2:]) - a[1:3999]
+    assert np.array_equal(tb.cpu().numpy(), want)
+    m = rs.randn(70, 130).astype(np.float32)
+    tu = torch.zeros((70, 130), device="cuda")
+    fns["upwind2d"](torch.from_numpy(m).cuda(), tu, 69, 130)
+    c = m[1:69]
+    got = tu.cpu().numpy()
+    assert np.array_equal(got[1:69], np.where(c > 0, c - m[:68], m[2:] - c).astype(np.float32))
+    assert not got[0].any() and not got[69].any()
+    shim = spmd_mod("mlir_shim")
+    with pytest.raises(shim.ShimError):  # a shifted view would start before the memref
+        fns["max_filter_interior"](torch.from_numpy(a).cuda(), tb, 4001)

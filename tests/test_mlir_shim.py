@@ -264,3 +264,24 @@ def test_spmd_if_value_is_a_select(oracle_mod):
     a, b = rs.randn(501).astype(np.float32), rs.randn(501).astype(np.float32)
     got = oracle_mod.forall_map([a, b], a.shape, d["code"], d["consts"])
     assert np.array_equal(got, np.where(a < b, b - a, a - b).astype(np.float32))
+
+
+def test_nonlinear_stencils_map_as_shifted_views(oracle_mod):
+    import numpy as np
+    d = _by_name()
+    mf = d["max_filter_interior"]
+    assert mf["pattern"] == "map" and mf["inputs"] == ["%A"] * 3
+    assert sorted(mf["input_offsets"]) == [[-1], [0], [1]] and mf["lower"] == [1]
+    a = np.random.RandomState(36).randn(600).astype(np.float32)
+    views = [a[1 + o[0]:599 + o[0]] for o in mf["input_offsets"]]
+    got = oracle_mod.forall_map(views, (598,), mf["code"], mf["consts"])
+    assert np.array_equal(got, np.maximum(a[:598], a[2:]) - a[1:599])
+    up = d["upwind2d"]
+    assert up["pattern"] == "map" and sorted(up["input_offsets"]) == [[-1, 0], [0, 0], [1, 0]]
+    m = np.random.RandomState(37).randn(20, 30).astype(np.float32)
+    views = [m[1 + o[0]:19 + o[0], o[1]:30 + o[1]] for o in up["input_offsets"]]
+    got = oracle_mod.forall_map(views, (18, 30), up["code"], up["consts"])
+    c = m[1:19]
+    assert np.array_equal(got, np.where(c > 0, c - m[:18], m[2:] - c).astype(np.float32))
+    bad = d["in_place_neighbour_unsupported"]
+    assert bad["pattern"] is None and "also read at another point" in bad["error"]
