@@ -125,7 +125,12 @@ __device__ __forceinline__ void apply(float4 *rd, const float4 *ra, const float4
 // chunk, so a warp access covers 32 consecutive points; CONTIG addresses them
 // at the flat index, GENERAL from their (i0, i1, i2) index, decomposed once
 // per slot and stepped by `threads` points per component.
-enum MapMode { kVec = 0, kContig = 1, kGeneral = 2 };
+// ROWS (strided views whose rows hold at least kRowsMin points): a chunk is
+// a segment of one row, component k of slot s its column (4s + k) *
+// threads + thread, each view's offset the row's plus the column times the
+// column stride, advanced by one add per point.
+enum MapMode { kVec = 0, kContig = 1, kGeneral = 2, kRows = 3 };
+constexpr int64_t kRowsMin = 1024;
 
 // Offset of flat point e in a view with strides st over the rank-3 domain sz.
 __device__ __forceinline__ int64_t point_offset(int64_t e, const int64_t *sz, const int64_t *st) {
@@ -236,6 +241,48 @@ __device__ __forceinline__ void store_general(const MapParams &p, int64_t first,
   }
 }
 
+// ROWS: the chunk's row (i0, i1) and the thread's first column.
+struct RowChunk {
+  int64_t i0, i1, col0;
+};
+
+template <int S>
+__device__ __forceinline__ void load_rows(const float *src, const int64_t *st, int64_t span, const MapParams &p,
+                                          const RowChunk &rc, float4 *out) {
+  int64_t o = rc.i0 * st[0] + rc.i1 * st[1] + rc.col0 * st[2];
+  const int64_t d_step = (int64_t)kMapThreads * st[2];
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t col = rc.col0 + (int64_t)(4 * s + k) * kMapThreads;
+      v[k] = 0.0f;
+      if (col < p.size[2] && IN_RANGE(o >= 0 && o < span, 1, o)) v[k] = src[o];
+      o += d_step;
+    }
+    out[s] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+template <int S>
+__device__ __forceinline__ void store_rows(const MapParams &p, const RowChunk &rc, const float4 *vals, int row) {
+  const int64_t *st = p.out_st;
+  int64_t o = rc.i0 * st[0] + rc.i1 * st[1] + rc.col0 * st[2];
+  const int64_t d_step = (int64_t)kMapThreads * st[2];
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    const float4 v4 = vals[s * row];
+    const float w[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t col = rc.col0 + (int64_t)(4 * s + k) * kMapThreads;
+      if (col < p.size[2] && IN_RANGE(o >= 0 && o < p.out_span, 2, o)) p.out[o] = w[k];
+      o += d_step;
+    }
+  }
+}
+
 // VEC / CONTIG: the four points of a slot whose first point is e (VEC:
 // e..e+3; CONTIG: threads apart); points at or past n read as 0.
 template <int MODE>
@@ -282,18 +329,28 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
   __syncthreads();
   constexpr int kRow = S * kMapThreads;  // float4s per register
   float4 *mine = regs + t;
-  const int64_t nchunks = (p.n + kChunk - 1) / kChunk;
+  const int64_t row_chunks = MODE == kRows ? (p.size[2] + kChunk - 1) / kChunk : 1;  // chunks per row
+  const int64_t nchunks = MODE == kRows ? p.size[0] * p.size[1] * row_chunks : (p.n + kChunk - 1) / kChunk;
   for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
     // slot s starts at base + s * 4 * threads (VEC: its components are
     // consecutive; otherwise threads apart)
     const int64_t base = c * kChunk + (MODE == kVec ? 4 * (int64_t)t : (int64_t)t);
     ChunkIdx g{};
     if constexpr (MODE == kGeneral) g = chunk_index<S>(p, base);
+    RowChunk rc{};
+    if constexpr (MODE == kRows) {
+      const int64_t r = c / row_chunks;
+      rc.i0 = r / p.size[1];
+      rc.i1 = r - rc.i0 * p.size[1];
+      rc.col0 = (c - r * row_chunks) * kChunk + t;
+    }
     float4 v[NL][S];
 #pragma unroll
     for (int i = 0; i < NL; ++i) {
       if constexpr (MODE == kGeneral) {
         load_general<S>(p.ld_src[i], p.ld_st[i], p.ld_span[i], p, base, g, v[i]);
+      } else if constexpr (MODE == kRows) {
+        load_rows<S>(p.ld_src[i], p.ld_st[i], p.ld_span[i], p, rc, v[i]);
       } else {
 #pragma unroll
         for (int s = 0; s < S; ++s)
@@ -362,6 +419,8 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
     if (IN_RANGE(p.out_reg < p.n_regs, 3, p.out_reg)) {
       if constexpr (MODE == kGeneral) {
         store_general<S>(p, base, g, mine + p.out_reg * kRow, kMapThreads);
+      } else if constexpr (MODE == kRows) {
+        store_rows<S>(p, rc, mine + p.out_reg * kRow, kMapThreads);
       } else {
 #pragma unroll
         for (int s = 0; s < S; ++s)
@@ -374,15 +433,18 @@ __global__ void __launch_bounds__(kMapThreads) forall_map_kernel(const __grid_co
 template <int NL>
 cudaError_t launch_nl(const MapParams &p, int mode, int n_regs, cudaStream_t stream) {
   const size_t smem = (size_t)n_regs * map_slots(NL) * kMapThreads * sizeof(float4);
-  auto kern = mode == kVec ? forall_map_kernel<NL, kVec>
-              : mode == kContig ? forall_map_kernel<NL, kContig> : forall_map_kernel<NL, kGeneral>;
+  auto kern = mode == kVec      ? forall_map_kernel<NL, kVec>
+              : mode == kContig ? forall_map_kernel<NL, kContig>
+              : mode == kRows   ? forall_map_kernel<NL, kRows>
+                                : forall_map_kernel<NL, kGeneral>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int dev = 0, per_sm = 0;
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
   if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kMapThreads, smem)) != cudaSuccess) return e;
   if (per_sm < 1) per_sm = 1;
-  const int64_t nchunks = (p.n + map_chunk(NL) - 1) / map_chunk(NL);
+  const int64_t nchunks = mode == kRows ? p.size[0] * p.size[1] * ((p.size[2] + map_chunk(NL) - 1) / map_chunk(NL))
+                                        : (p.n + map_chunk(NL) - 1) / map_chunk(NL);
   const int64_t cap = (int64_t)num_sms(dev) * per_sm;
   const int grid = (int)(nchunks < cap ? nchunks : cap);
   kern<<<grid, kMapThreads, smem, stream>>>(p);
@@ -508,7 +570,7 @@ extern "C" int spmdb200_forall_map(int rank, const int64_t *sizes, int n_inputs,
   for (int d = 0; d < 3; ++d)
     for (int i = 0; i < nl; ++i)
       if (p.ld_st[i][d] < 0 || p.out_st[d] < 0) return bad("negative stride");
-  const int mode = !contig ? kGeneral : aligned ? kVec : kContig;
+  const int mode = contig ? (aligned ? kVec : kContig) : p.size[2] >= kRowsMin ? kRows : kGeneral;
   cudaError_t e;
   cudaStream_t s = (cudaStream_t)stream;
   switch (nl) {

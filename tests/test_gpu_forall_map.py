@@ -76,6 +76,13 @@ def test_strided_misaligned_and_in_place_views(kernels, oracle_mod):
         ("contiguous, misaligned 2-D", flat[1:1 + 63 * 97].view(63, 97), flat2[2:2 + 63 * 97].view(63, 97)),
         ("contiguous 3-D, one misaligned", flat[:5 * 7 * 11].view(5, 7, 11), flat2[1:1 + 385].view(5, 7, 11)),
     ]
+    long_a = torch.from_numpy(rs.uniform(0.5, 2, size=(8, 3000)).astype(np.float32)).cuda()
+    long_b = torch.from_numpy(rs.uniform(0.5, 2, size=(3, 4, 1600)).astype(np.float32)).cuda()
+    views += [
+        ("long pitched rows", long_a[:, :2500], long_a[:, 7:2507]),  # rows of >= 1024 points: row chunks
+        ("long pitched rows 3-D", long_b[:, :, :1500], long_b[:, :, 100:1600]),
+        ("long rows, column step 2", long_a[:, :2400:2], long_a[:, 1:2401:2]),
+    ]
     for what, va, vb in views:
         out = torch.zeros(va.shape, device="cuda")
         kernels.forall_map([va, vb], out, code, [0.25], n_regs=n_regs)
