@@ -13,8 +13,10 @@
 //
 // Execution: one pass over the domain, grid-stride over chunks of
 // 256 threads x 2 slots x 4 points.  A thread owns two float4 groups of
-// consecutive points per chunk and keeps the program's registers for them in
-// its own rows of shared memory (row r, slot s at [(r*2 + s)*256 + thread]:
+// points per chunk (four consecutive points each for aligned contiguous
+// views; otherwise points 256 apart, see MapMode) and keeps the program's
+// registers for them in its own rows of shared memory (row r, slot s at
+// [(r*2 + s)*256 + thread]:
 // 16-byte accesses by consecutive threads, no bank conflicts, no barriers,
 // since no thread reads another's rows).  Every instruction is decoded once
 // per 8 points, uniformly across the warp.  The loads of all inputs are
@@ -123,8 +125,9 @@ __device__ __forceinline__ void apply(float4 *rd, const float4 *ra, const float4
 // CONTIG (every view contiguous, some not 16-byte aligned) and GENERAL (any
 // strides): component k of slot s is point (4s + k) * threads + thread of the
 // chunk, so a warp access covers 32 consecutive points; CONTIG addresses them
-// at the flat index, GENERAL from their (i0, i1, i2) index, decomposed once
-// per slot and stepped by `threads` points per component.
+// at the flat index, GENERAL from the (i0, i1, i2) index of the thread's
+// first point, decomposed once per chunk, with each view's offset advanced
+// along the row and plane wraps of the following steps.
 // ROWS (strided views whose rows hold at least kRowsMin points): a chunk is
 // a segment of one row, component k of slot s its column (4s + k) *
 // threads + thread, each view's offset the row's plus the column times the
