@@ -164,7 +164,8 @@ def _map_call(lib, rank=1, sizes=(8,), n_in=1, code=None, n_regs=2, consts=(1.0,
 
 
 @pytest.mark.parametrize("case", ["rank", "opcode", "reg_field", "read_before_write", "store_not_last",
-                                  "load_after_op", "bad_input", "no_load", "bad_const"])
+                                  "load_after_op", "bad_input", "no_load", "bad_const", "too_many_regs",
+                                  "too_many_insns", "select_cond_unwritten", "bad_predicate", "negative_size"])
 def test_forall_map_rejects_bad_programs_before_launch(case):
     lib = spmd_mod("_lib").lib()
     I = fp.insn
@@ -187,6 +188,16 @@ def test_forall_map_rejects_bad_programs_before_launch(case):
         kw = dict(code=[I("const", 0, aux=0), I("store", 0, 0)])
     elif case == "bad_const":
         kw = dict(code=[I("load", 0, aux=0), I("const", 1, aux=4), I("store", 0, 1)])
+    elif case == "too_many_regs":
+        kw = dict(n_regs=fp.MAX_REGS + 1)
+    elif case == "too_many_insns":
+        kw = dict(code=[I("load", 0, aux=0)] + [I("neg", 0, 0)] * (fp.MAX_INSNS - 1) + [I("store", 0, 0)])
+    elif case == "select_cond_unwritten":
+        kw = dict(code=[I("load", 0, aux=0), I("select", 0, 0, 0, aux=1), I("store", 0, 0)])
+    elif case == "bad_predicate":
+        kw = dict(code=[I("load", 0, aux=0), I("cmp", 1, 0, 0, aux=16), I("store", 0, 1)])
+    elif case == "negative_size":
+        kw = dict(sizes=(-1,))
     st = _map_call(lib, **kw)
     assert st in (-1, -4), st  # invalid argument / unsupported, before any CUDA call
     assert lib.spmdb200_last_error_message().decode()
