@@ -285,3 +285,54 @@ def test_nonlinear_stencils_map_as_shifted_views(oracle_mod):
     assert np.array_equal(got, np.where(c > 0, c - m[:18], m[2:] - c).astype(np.float32))
     bad = d["in_place_neighbour_unsupported"]
     assert bad["pattern"] is None and "also read at another point" in bad["error"]
+
+
+def _one(body: str, args: str = "%A: memref<?xf32>, %B: memref<?xf32>, %N: index") -> dict:
+    shim = spmd_mod("mlir_shim")
+    text = f"""
+func.func @k({args}) attributes {{spmd.kernel}} {{
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  "spmd.forall"(%c0, %N, %c1) ({{
+  ^bb0(%i: index):
+{body}
+    "spmd.yield"() : () -> ()
+  }}) {{operandSegmentSizes = array<i32: 1, 1, 1>}} : (index, index, index) -> ()
+  func.return
+}}
+"""
+    (d,) = shim.describe(text)
+    return d
+
+
+def test_map_bodies_the_shim_reports():
+    fill = _one("""    %z = arith.constant 2.0 : f32
+    memref.store %z, %B[%i] : memref<?xf32>""")
+    assert fill["pattern"] is None and "fill" in fill["error"]
+    f64 = _one("""    %a = memref.load %A[%i] : memref<?xf64>
+    %b = arith.mulf %a, %a : f64
+    memref.store %b, %B[%i] : memref<?xf64>""", "%A: memref<?xf64>, %B: memref<?xf64>, %N: index")
+    assert f64["pattern"] is None
+    i32 = _one("""    %a = memref.load %A[%i] : memref<?xi32>
+    %b = arith.muli %a, %a : i32
+    memref.store %b, %B[%i] : memref<?xi32>""", "%A: memref<?xi32>, %B: memref<?xi32>, %N: index")
+    assert i32["pattern"] is None
+    # 17 values live at once exceed the 16 registers of a body program
+    loads = "\n".join(f"    %x{k} = memref.load %A{k}[%i] : memref<?xf32>" for k in range(8))
+    muls = "\n".join(f"    %y{k} = arith.mulf %x{k}, %x{k} : f32" for k in range(8))
+    tree = ["%y0"]
+    chain = []
+    for k in range(1, 8):
+        chain.append(f"    %s{k} = arith.addf {tree[-1]}, %y{k} : f32")
+        tree.append(f"%s{k}")
+    big = _one(loads + "\n" + muls + "\n" + "\n".join(chain) + f"\n    memref.store {tree[-1]}, %B[%i] : memref<?xf32>",
+               ", ".join(f"%A{k}: memref<?xf32>" for k in range(8)) + ", %B: memref<?xf32>, %N: index")
+    assert big["pattern"] == "map" and big["n_regs"] <= 16  # the allocator reuses registers
+    nine = "\n".join(f"    %x{k} = memref.load %A{k}[%i] : memref<?xf32>" for k in range(9))
+    sums = ["%x0"]
+    for k in range(1, 9):
+        nine += f"\n    %t{k} = arith.addf {sums[-1]}, %x{k} : f32"
+        sums.append(f"%t{k}")
+    too_many = _one(nine + f"\n    memref.store {sums[-1]}, %B[%i] : memref<?xf32>",
+                    ", ".join(f"%A{k}: memref<?xf32>" for k in range(9)) + ", %B: memref<?xf32>, %N: index")
+    assert too_many["pattern"] is None and "inputs" in too_many["error"]
