@@ -2,7 +2,8 @@
  * spmd_b200.h -- C ABI of libspmdb200.so, the B200 (sm_100a) implementation of
  * the kernels that spmd-dialect's SPMDToGPU lowering emits:
  *
- *   (1) elementwise spmd.forall maps            (ewise, axpy)
+ *   (1) elementwise spmd.forall maps            (ewise, axpy, any f32 body:
+ *                                                forall_map)
  *   (2) PromoteGroupMemory-tiled stencil sweeps (3-point promoted stencil,
  *       Jacobi-2D 5-point, Jacobi-3D 7-point)
  *   (3) ReduceToHierarchicalGPU spmd.reduce     (f32 sum, i32 sum)
