@@ -452,6 +452,8 @@ def analyse(func: Func) -> Mapping:
                                           for op, _ in nodes):
         # A forall whose body does nothing (test/SPMD/normalize.mlir): no effect to run.
         return Mapping(func.name, "empty", None, {})
+    if len(stores) > 1 and not reduces and not atomics:
+        return _analyse_multi_store(func, env, args, nodes, stores, foralls, lbs, ubs, steps)
     if len(stores) != 1:
         raise ShimError(f"{func.name}: expected exactly one memref.store, found {len(stores)}")
     st, _ = stores[0]
@@ -657,6 +659,56 @@ def _analyse_map(func: Func, env: _Env, args: dict, st: Op, foralls: list, lbs, 
         "code": [list(c) for c in code], "consts": consts, "n_regs": n_regs})
 
 
+def _analyse_multi_store(func: Func, env: _Env, args: dict, nodes: list, stores: list, foralls: list, lbs, ubs,
+                         steps) -> Mapping:
+    """A forall body with several stores (several outputs per point) runs as
+    one general map per store, in store order.  That order reproduces the
+    body's own program order when (1) a memref that is stored anywhere in the
+    body is read only at the store's own index, and (2) no store to a memref
+    lies between a load of it and the store that load feeds (so each load
+    sees the same value -- the old one, or the one an earlier store left --
+    in both orders).  Anything else is reported."""
+    pos = {id(op): i for i, (op, _) in enumerate(nodes)}
+    if len({tuple(id(o) for o in p) for _, p in stores}) != 1:
+        raise ShimError(f"{func.name}: the stores sit in different regions")
+    stored: dict = {}
+    for st, _ in stores:
+        stored.setdefault(st.operands[1], []).append(pos[id(st)])
+    maps = []
+    for st, _ in stores:
+        m = _analyse_map(func, env, args, st, foralls, lbs, ubs, steps)
+        for name, off in zip(m.detail["inputs"], m.detail["input_offsets"]):
+            if name in stored and any(off):
+                raise ShimError(f"{func.name}: {name} is stored in the body and read at offset {off}")
+        for ld in _dag_loads(env, st.operands[0]):
+            src = ld.operands[0]
+            if any(pos[id(ld)] < q < pos[id(st)] for q in stored.get(src, [])):
+                raise ShimError(f"{func.name}: {src} is stored between a load of it and the store that uses it")
+        maps.append(m.detail)
+    return Mapping(func.name, "maps", "spmdb200_forall_map", {"maps": maps, "outputs": [d["output"] for d in maps]})
+
+
+def _dag_loads(env: _Env, root: str) -> list:
+    """The memref.load ops an SSA value depends on."""
+    out, seen, todo = [], set(), [root]
+    while todo:
+        v = todo.pop()
+        if v in seen:
+            continue
+        seen.add(v)
+        op = env.defs.get(v)
+        if op is None:
+            continue
+        if op.name == "memref.load":
+            out.append(op)
+            continue
+        todo.extend(op.operands)
+        if op.name == "spmd.if":  # a value spmd.if depends on what its regions yield
+            for r in [op.region, *op.more_regions]:
+                todo.extend(o for y in r if y.name == "spmd.yield" for o in y.operands)
+    return out
+
+
 def _analyse_guarded(func: Func, env: _Env, args: dict, ifs: list, stores: list, foralls: list, lbs, ubs,
                      steps) -> Mapping:
     """A forall whose only store sits in an spmd.if: `if (c) A[p] = v`, with
@@ -797,27 +849,12 @@ class BoundKernel:
                                 steps=d["steps"], policy=policy, stream=stream)
         if m.pattern == "empty":
             return None
+        if m.pattern == "maps":  # several outputs per point: one map per store, in store order
+            for sub in d["maps"]:
+                self._run_map(k, sub, env, num, stream)
+            return None
         if m.pattern == "map":
-            lo = [int(env[v]) if isinstance(v, str) else int(v) for v in d["lower"]]
-            hi = [num(u) if u in env else self._const(u) if isinstance(u, str) else int(u) for u in d["domain"]]
-            box = tuple(slice(a, max(a, b), s) for a, b, s in zip(lo, hi, d["steps"]))
-            ot = env[d["output"]]
-            if any(b > a and (a < 0 or b > ot.shape[k]) for k, (a, b) in enumerate(zip(lo, hi))):
-                raise ShimError(f"{self.func.name}: the domain {lo}..{hi} is outside {d['output']}'s sizes "
-                                f"{tuple(ot.shape)}")
-            out = ot[box]
-            views = []
-            for x, off in zip(d["inputs"], d["input_offsets"]):
-                t = env[x]
-                if out.numel() and any(a + o < 0 or max(a, b) + o > t.shape[k]
-                                       for k, (a, b, o) in enumerate(zip(lo, hi, off))):
-                    raise ShimError(f"{self.func.name}: {x} read at offset {off} outside its sizes {tuple(t.shape)}")
-                views.append(t[tuple(slice(a + o, max(a, b) + o, s) for a, b, o, s in zip(lo, hi, off, d["steps"]))])
-            if out.numel() == 0:
-                return out
-            consts = [float(env[c]) if isinstance(c, str) else c for c in d["consts"]]
-            return k.forall_map(views, out, [tuple(c) for c in d["code"]], consts, n_regs=d["n_regs"],
-                                stream=stream)
+            return self._run_map(k, d, env, num, stream)
         if m.pattern == "reduce" and d["combine"] in ("return", "store"):
             n = num(d["n"]) if isinstance(d["n"], str) else int(d["n"])
             a = env[d["input"]][:n]
@@ -838,6 +875,30 @@ class BoundKernel:
             init = out.item()  # the combine folds the old value in, as atomic_rmw does
             return k.reduce(d["kind"], a, init, out=out, stream=stream)
         raise ShimError(f"unbound pattern {m.pattern}")
+
+    def _run_map(self, k, d: dict, env: dict, num, stream):
+        """One general forall map: views of the domain box (shifted by each
+        load's offset), checked against the tensors' sizes on the host."""
+        lo = [int(env[v]) if isinstance(v, str) else int(v) for v in d["lower"]]
+        hi = [num(u) if u in env else self._const(u) if isinstance(u, str) else int(u) for u in d["domain"]]
+        box = tuple(slice(a, max(a, b), s) for a, b, s in zip(lo, hi, d["steps"]))
+        ot = env[d["output"]]
+        if any(b > a and (a < 0 or b > ot.shape[k]) for k, (a, b) in enumerate(zip(lo, hi))):
+            raise ShimError(f"{self.func.name}: the domain {lo}..{hi} is outside {d['output']}'s sizes "
+                            f"{tuple(ot.shape)}")
+        out = ot[box]
+        views = []
+        for x, off in zip(d["inputs"], d["input_offsets"]):
+            t = env[x]
+            if out.numel() and any(a + o < 0 or max(a, b) + o > t.shape[k]
+                                   for k, (a, b, o) in enumerate(zip(lo, hi, off))):
+                raise ShimError(f"{self.func.name}: {x} read at offset {off} outside its sizes {tuple(t.shape)}")
+            views.append(t[tuple(slice(a + o, max(a, b) + o, s) for a, b, o, s in zip(lo, hi, off, d["steps"]))])
+        if out.numel() == 0:
+            return out
+        consts = [float(env[c]) if isinstance(c, str) else c for c in d["consts"]]
+        return k.forall_map(views, out, [tuple(c) for c in d["code"]], consts, n_regs=d["n_regs"],
+                            stream=stream)
 
     def _const(self, v):
         for op in _iter_ops(self.func.ops):

@@ -336,3 +336,74 @@ def test_map_bodies_the_shim_reports():
     too_many = _one(nine + f"\n    memref.store {sums[-1]}, %B[%i] : memref<?xf32>",
                     ", ".join(f"%A{k}: memref<?xf32>" for k in range(9)) + ", %B: memref<?xf32>, %N: index")
     assert too_many["pattern"] is None and "inputs" in too_many["error"]
+
+
+_TWO_OUTPUTS = r"""
+func.func @two_outputs(%A: memref<?xf32>, %B: memref<?xf32>, %C: memref<?xf32>, %N: index) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  %two = arith.constant 2.0 : f32
+  "spmd.forall"(%c0, %N, %c1) ({
+  ^bb0(%i: index):
+    %a = memref.load %A[%i] : memref<?xf32>
+    %b = arith.mulf %a, %two : f32
+    memref.store %b, %B[%i] : memref<?xf32>
+    %bb = memref.load %B[%i] : memref<?xf32>
+    %c = arith.addf %bb, %a : f32
+    memref.store %c, %C[%i] : memref<?xf32>
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
+  func.return
+}
+
+func.func @stale_read(%A: memref<?xf32>, %B: memref<?xf32>, %C: memref<?xf32>, %N: index) attributes {spmd.kernel} {
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  "spmd.forall"(%c0, %N, %c1) ({
+  ^bb0(%i: index):
+    %old = memref.load %B[%i] : memref<?xf32>
+    %a = memref.load %A[%i] : memref<?xf32>
+    memref.store %a, %B[%i] : memref<?xf32>
+    %c = arith.addf %old, %a : f32
+    memref.store %c, %C[%i] : memref<?xf32>
+    "spmd.yield"() : () -> ()
+  }) {operandSegmentSizes = array<i32: 1, 1, 1>} : (index, index, index) -> ()
+  func.return
+}
+"""
+
+
+def test_several_outputs_run_as_maps_in_store_order(oracle_mod):
+    """B = 2a; C = B + a (reading B after its store) runs as two maps in order;
+    a load of B before B's store, used after it, is reported."""
+    import numpy as np
+    shim = spmd_mod("mlir_shim")
+    d = {x["function"]: x for x in shim.describe(_TWO_OUTPUTS)}
+    two = d["two_outputs"]
+    assert two["pattern"] == "maps" and two["outputs"] == ["%B", "%C"]
+    a = np.random.RandomState(39).randn(300).astype(np.float32)
+    b = oracle_mod.forall_map([a], a.shape, two["maps"][0]["code"], two["maps"][0]["consts"])
+    env = {"%A": a, "%B": b}
+    m1 = two["maps"][1]
+    c = oracle_mod.forall_map([env[x] for x in m1["inputs"]], a.shape, m1["code"], m1["consts"])
+    assert np.array_equal(b, a * np.float32(2)) and np.array_equal(c, b + a)
+    assert d["stale_read"]["pattern"] is None and "between a load" in d["stale_read"]["error"]
+
+
+def test_map_binding_builds_views_before_the_device_call():
+    """On the host the bound maps slice their views (offsets, lower bounds,
+    several outputs) and check ranges; the device wrapper then refuses CPU
+    tensors, so nothing runs without a GPU."""
+    import torch
+    shim = spmd_mod("mlir_shim")
+    fns = shim.load((ROOT / "tests" / "mlir" / "kernels.mlir").read_text(), skip_unmapped=True)
+    a, b = torch.zeros(600), torch.zeros(600)
+    with pytest.raises(ValueError, match="CUDA"):
+        fns["max_filter_interior"](a, b, 599)
+    with pytest.raises(shim.ShimError, match="outside"):
+        fns["max_filter_interior"](a, b, 601)
+    with pytest.raises(ValueError, match="CUDA"):
+        fns["mul2d"](torch.zeros(4, 5), torch.zeros(4, 5), torch.zeros(4, 5), 4, 5)
+    two = shim.load(_TWO_OUTPUTS, skip_unmapped=True)["two_outputs"]
+    with pytest.raises(ValueError, match="CUDA"):
+        two(torch.zeros(8), torch.zeros(8), torch.zeros(8), 8)
