@@ -14,10 +14,15 @@ path:
   `spmd.tile_sizes`, the lane step and `spmd.memory_policy` handed to the
   promotion plan (lib/Analysis/PromotionPlanAnalysis.cpp:53-164) -- e.g. the
   promoted 3-point stencil (test/SPMD/lower-to-gpu-nvptx-promoted.mlir:32-67);
+* any other per-point body -- a DAG of arith / math f32 ops over loads at the
+  store's index plus constant offsets, f32 constants and scalar arguments,
+  `spmd.if` values and guarded stores, several stores per point -- as the
+  straight-line programs of the general forall entry (spmdb200_forall_map);
 * reductions: an `spmd.reduce` (any kind, include/spmd/IR/SPMDAttrs.td:74-80)
-  of one memref, combined into a rank-0 memref with memref.atomic_rmw (the
-  hierarchical sum, SPMDToGPU.cpp:249-415) or one atomic per element (the
-  atomic baseline).
+  of one memref, combined into a rank-0 memref with memref.atomic_rmw of the
+  same kind (the hierarchical sum, SPMDToGPU.cpp:249-415) or one atomic per
+  element (the atomic baseline), and a top-level `spmd.reduce` whose value
+  the function returns or stores.
 
 `load(text)` returns callables taking the function's own arguments (CUDA
 tensors for memrefs, ints for index, floats for f32).  The command line adds
