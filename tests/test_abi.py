@@ -178,3 +178,44 @@ def test_check_status_release_and_checked_exports():
     ch = ctypes.CDLL(str(checked))
     missing = [n for n in declared_functions() if not hasattr(ch, n)]
     assert not missing, f"not exported by the checked build: {missing}"
+
+
+C_CALLER = r"""
+#include <stdio.h>
+#include "spmd_b200.h"
+int main(void) {
+  int64_t n = 8, st = 1;
+  const float *in[1] = {(const float *)0x1000};
+  int32_t bad[] = {SPMDB200_MAP_LOAD, 0, SPMDB200_MAP_NEG | 1 << 8 | 1 << 16, 0, SPMDB200_MAP_STORE, 0};
+  int a = spmdb200_forall_map(4, &n, 1, in, &st, (float *)0x2000, &st, bad, 3, NULL, 0, 2, NULL);
+  int b = spmdb200_forall_map(1, &n, 1, in, &st, (float *)0x2000, &st, bad, 3, NULL, 0, 2, NULL);
+  unsigned long long first = 1;
+  int c = spmdb200_check_status(&first);
+  printf("%d %d %d %llu %s\n", a, b, c, first, spmdb200_status_string(SPMDB200_ERR_BOUNDS));
+  return 0;
+}
+"""
+
+
+def test_c_program_links_and_calls_the_abi(tmp_path):
+    """A C caller compiles against include/spmd_b200.h, links libspmdb200.so
+    and gets the argument checks' statuses (no CUDA call is reached)."""
+    import shutil
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lib = spmd_mod("_lib")
+    src = tmp_path / "caller.c"
+    src.write_text(C_CALLER)
+    exe = tmp_path / "caller"
+    pkg = lib.PKG_DIR
+    r = subprocess.run([cc, "-std=c11", "-Wall", "-Werror", f"-I{ROOT / 'include'}", str(src), "-o", str(exe),
+                        f"-L{pkg}", "-lspmdb200", f"-Wl,-rpath,{pkg}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, out.stderr
+    a, b, c, first, *msg = out.stdout.split()
+    assert int(a) == -1        # rank 4: invalid argument
+    assert int(b) == -1        # register 1 read before it is written
+    assert int(c) == -4 and int(first) == 0  # a release build has no out-of-range record
+    assert "checked build" in " ".join(msg)
