@@ -1,0 +1,149 @@
+"""End to end on the host: random elementwise forall bodies written as MLIR
+text go through the shim's parser and program compiler, the oracle runs the
+programs, and numpy evaluates the generator's own op list (independently of
+the shim) op by op in float32.  Bit-exact, NaN matching NaN."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import spmd_mod
+from test_forall_program import bits_equal_nan
+
+BIN = {"addf": np.add, "subf": np.subtract, "mulf": np.multiply, "divf": np.divide}
+PREDS = ["oeq", "ogt", "oge", "olt", "ole", "one", "ord", "ueq", "ugt", "uge", "ult", "ule", "une", "uno"]
+
+
+def _maximum(x, y, take_max):
+    nan = np.isnan(x) | np.isnan(y)
+    if take_max:
+        m = np.where(x == y, np.where(np.signbit(x), y, x), np.where(x > y, x, y))
+    else:
+        m = np.where(x == y, np.where(np.signbit(x), x, y), np.where(x < y, x, y))
+    return np.where(nan, np.float32(np.nan), m).astype(np.float32)
+
+
+def _cmp(pred, x, y):
+    u = np.isnan(x) | np.isnan(y)
+    return {"oeq": x == y, "ogt": x > y, "oge": x >= y, "olt": x < y, "ole": x <= y, "one": ~u & (x != y),
+            "ord": ~u, "ueq": u | (x == y), "ugt": u | (x > y), "uge": u | (x >= y), "ult": u | (x < y),
+            "ule": u | (x <= y), "une": x != y, "uno": u}[pred]
+
+
+def random_body(rs, n_in: int, n_ops: int):
+    """(MLIR body lines, numpy evaluator) of a random f32 DAG ending in a store to %Out."""
+    lines, evals = [], []
+    vals = []
+    for k in range(n_in):
+        lines.append(f"    %x{k} = memref.load %In{k}[%i] : memref<?xf32>")
+        vals.append((f"%x{k}", ("in", k)))
+    c = float(np.float32(rs.uniform(-2, 2)))
+    lines.append(f"    %k0 = arith.constant {c!r} : f32")
+    vals.append(("%k0", ("const", np.float32(c))))
+    bools = []
+    for j in range(n_ops):
+        r = rs.random_sample()
+        name = f"%t{j}"
+        pick = lambda: vals[rs.randint(len(vals))]  # noqa: E731
+        if r < 0.45:
+            op = list(BIN)[rs.randint(4)]
+            a, b = pick(), pick()
+            lines.append(f"    {name} = arith.{op} {a[0]}, {b[0]} : f32")
+            vals.append((name, (op, a[0], b[0])))
+        elif r < 0.6:
+            op = ["maximumf", "minimumf"][rs.randint(2)]
+            a, b = pick(), pick()
+            lines.append(f"    {name} = arith.{op} {a[0]}, {b[0]} : f32")
+            vals.append((name, (op, a[0], b[0])))
+        elif r < 0.75:
+            op = ["arith.negf", "math.absf", "math.sqrt"][rs.randint(3)]
+            a = pick()
+            lines.append(f"    {name} = {op} {a[0]} : f32")
+            vals.append((name, (op, a[0])))
+        elif r < 0.88:
+            pred = PREDS[rs.randint(len(PREDS))]
+            a, b = pick(), pick()
+            lines.append(f"    {name} = arith.cmpf {pred}, {a[0]}, {b[0]} : f32")
+            bools.append((name, ("cmp", pred, a[0], b[0])))
+        elif bools:
+            cnd = bools[rs.randint(len(bools))]
+            a, b = pick(), pick()
+            lines.append(f"    {name} = arith.select {cnd[0]}, {a[0]}, {b[0]} : f32")
+            vals.append((name, ("select", cnd[0], a[0], b[0])))
+    root = vals[-1][0]
+    table0 = dict(vals + bools)
+
+    def loads_something(v, seen=None):
+        seen = set() if seen is None else seen
+        if v in seen:
+            return False
+        seen.add(v)
+        d = table0[v]
+        if d[0] == "in":
+            return True
+        return any(loads_something(o, seen) for o in d[1:] if isinstance(o, str) and o.startswith("%"))
+
+    if root.startswith("%x") or not loads_something(root):  # compute something, from a load
+        lines.append(f"    %tz = arith.addf {root}, %x0 : f32")
+        vals.append(("%tz", ("addf", root, "%x0")))
+        root = "%tz"
+    lines.append(f"    memref.store {root}, %Out[%i] : memref<?xf32>")
+    table = dict(vals + bools)
+
+    def evaluate(inputs):
+        memo = {}
+
+        def ev(v):
+            if v in memo:
+                return memo[v]
+            d = table[v]
+            with np.errstate(all="ignore"):
+                if d[0] == "in":
+                    r = inputs[d[1]]
+                elif d[0] == "const":
+                    r = np.full(inputs[0].shape, d[1], np.float32)
+                elif d[0] in BIN:
+                    r = BIN[d[0]](ev(d[1]), ev(d[2])).astype(np.float32)
+                elif d[0] in ("maximumf", "minimumf"):
+                    r = _maximum(ev(d[1]), ev(d[2]), d[0] == "maximumf")
+                elif d[0] == "arith.negf":
+                    r = np.negative(ev(d[1]))
+                elif d[0] == "math.absf":
+                    r = np.abs(ev(d[1]))
+                elif d[0] == "math.sqrt":
+                    r = np.sqrt(ev(d[1])).astype(np.float32)
+                elif d[0] == "cmp":
+                    r = _cmp(d[1], ev(d[2]), ev(d[3]))
+                else:  # select
+                    r = np.where(ev(d[1]), ev(d[2]), ev(d[3])).astype(np.float32)
+            memo[v] = r
+            return r
+
+        return ev(root)
+
+    return lines, evaluate
+
+
+@pytest.mark.parametrize("seed", range(64))
+def test_random_mlir_bodies(seed, oracle_mod):
+    rs = np.random.RandomState(900 + seed)
+    n_in = 1 + seed % 4
+    lines, evaluate = random_body(rs, n_in, 3 + seed % 9)
+    args = ", ".join([f"%In{k}: memref<?xf32>" for k in range(n_in)] + ["%Out: memref<?xf32>", "%N: index"])
+    text = (f"func.func @k({args}) attributes {{spmd.kernel}} {{\n"
+            "  %c0 = arith.constant 0 : index\n  %c1 = arith.constant 1 : index\n"
+            "  \"spmd.forall\"(%c0, %N, %c1) ({\n  ^bb0(%i: index):\n" + "\n".join(lines) +
+            "\n    \"spmd.yield\"() : () -> ()\n  }) {operandSegmentSizes = array<i32: 1, 1, 1>} : "
+            "(index, index, index) -> ()\n  func.return\n}\n")
+    shim = spmd_mod("mlir_shim")
+    (d,) = shim.describe(text)
+    assert d["pattern"] in ("map", "ewise", "axpy", "stencil"), d
+    ins = [rs.uniform(-3, 3, 257).astype(np.float32) for _ in range(n_in)]
+    ins[0][:4] = [0.0, -0.0, np.inf, -np.inf]
+    want = evaluate(ins)
+    if d["pattern"] != "map":
+        pytest.skip(f"mapped to the fixed {d['pattern']} entry (covered by its own tests)")
+    views = [ins[int(name[3:])] for name in d["inputs"]]
+    consts = [float(c) for c in d["consts"]]
+    got = oracle_mod.forall_map(views, (257,), d["code"], consts)
+    assert bits_equal_nan(got, want)
