@@ -147,3 +147,68 @@ def test_random_mlir_bodies(seed, oracle_mod):
     consts = [float(c) for c in d["consts"]]
     got = oracle_mod.forall_map(views, (257,), d["code"], consts)
     assert bits_equal_nan(got, want)
+
+
+@pytest.mark.parametrize("seed", range(24))
+def test_random_2d_stencil_bodies(seed, oracle_mod):
+    """2-D interior domains whose loads read neighbours at offsets in
+    {-1, 0, 1}: each (memref, offset) pair becomes a shifted view."""
+    rs = np.random.RandomState(1900 + seed)
+    n_in = 1 + seed % 2
+    N, M = 23, 37
+    offs = [(int(rs.randint(-1, 2)), int(rs.randint(-1, 2))) for _ in range(2 + seed % 3)]
+    lines = ["    %im = arith.subi %i, %c1 : index", "    %ip = arith.addi %i, %c1 : index",
+             "    %jm = arith.subi %j, %c1 : index", "    %jp = arith.addi %j, %c1 : index"]
+    idx = {-1: ("%im", "%jm"), 0: ("%i", "%j"), 1: ("%ip", "%jp")}
+    loads = []
+    for q, (di, dj) in enumerate(offs):
+        k = q % n_in
+        lines.append(f"    %l{q} = memref.load %In{k}[{idx[di][0]}, {idx[dj][1]}] : memref<?x?xf32>")
+        loads.append((k, di, dj))
+    # a non-linear fold: t = max(l0, l1) - l2 ..., alternating ops
+    ops = ["arith.maximumf", "arith.subf", "arith.mulf", "arith.minimumf", "arith.addf"]
+    acc = "%l0"
+    chosen = []
+    for q in range(1, len(offs)):
+        op = ops[int(rs.randint(len(ops)))]
+        lines.append(f"    %a{q} = {op} {acc}, %l{q} : f32")
+        chosen.append(op)
+        acc = f"%a{q}"
+    if len(offs) == 1 or all(o == "arith.addf" for o in chosen):
+        lines.append(f"    %sq = arith.mulf {acc}, {acc} : f32")
+        chosen.append("square")
+        acc = "%sq"
+    lines.append(f"    memref.store {acc}, %Out[%i, %j] : memref<?x?xf32>")
+    args = ", ".join([f"%In{k}: memref<?x?xf32>" for k in range(n_in)] +
+                     ["%Out: memref<?x?xf32>", "%Nm1: index", "%Mm1: index"])
+    text = (f"func.func @k({args}) attributes {{spmd.kernel}} {{\n"
+            "  %c1 = arith.constant 1 : index\n"
+            "  \"spmd.forall\"(%c1, %c1, %Nm1, %Mm1, %c1, %c1) ({\n  ^bb0(%i: index, %j: index):\n" +
+            "\n".join(lines) + "\n    \"spmd.yield\"() : () -> ()\n  }) {operandSegmentSizes = array<i32: 2, 2, 2>} : "
+            "(index, index, index, index, index, index) -> ()\n  func.return\n}\n")
+    shim = spmd_mod("mlir_shim")
+    (d,) = shim.describe(text)
+    ins = [rs.uniform(-2, 2, (N, M)).astype(np.float32) for _ in range(n_in)]
+    sl = lambda k, di, dj: ins[k][1 + di:N - 1 + di, 1 + dj:M - 1 + dj]  # noqa: E731
+    vals = [sl(*ld) for ld in loads]
+    with np.errstate(all="ignore"):
+        acc_v = vals[0]
+        for q, op in enumerate(chosen, start=1):
+            if op == "square":
+                acc_v = (acc_v * acc_v).astype(np.float32)
+                continue
+            x, y = acc_v, vals[q]
+            if op == "arith.maximumf":
+                acc_v = _maximum(x, y, True)
+            elif op == "arith.minimumf":
+                acc_v = _maximum(x, y, False)
+            else:
+                acc_v = {"arith.subf": np.subtract, "arith.mulf": np.multiply, "arith.addf": np.add}[op](x, y)
+                acc_v = acc_v.astype(np.float32)
+    if d["pattern"] == "stencil":
+        pytest.skip("a linear fold: the promoted-stencil entry (covered by its own tests)")
+    assert d["pattern"] == "map", d
+    views = [ins[int(name[3:])][1 + o[0]:N - 1 + o[0], 1 + o[1]:M - 1 + o[1]]
+             for name, o in zip(d["inputs"], d["input_offsets"])]
+    got = oracle_mod.forall_map(views, (N - 2, M - 2), d["code"], [float(c) for c in d["consts"]])
+    assert bits_equal_nan(got, acc_v)
