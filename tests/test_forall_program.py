@@ -201,3 +201,26 @@ def test_forall_map_rejects_bad_programs_before_launch(case):
     st = _map_call(lib, **kw)
     assert st in (-1, -4), st  # invalid argument / unsupported, before any CUDA call
     assert lib.spmdb200_last_error_message().decode()
+
+
+def test_compiled_programs_pass_the_library_validator():
+    """Every program compile_dag emits satisfies spmdb200_forall_map's checks
+    (LOAD prefix, one final STORE, fields in range, registers written before
+    they are read).  An empty domain makes the entry validate the program
+    and return without any CUDA call."""
+    lib = spmd_mod("_lib").lib()
+    rs = np.random.RandomState(77)
+    for trial in range(200):
+        n_in = 1 + trial % 6
+        root, nodes, consts = random_dag(rs, n_in, 2 + trial % 15)
+        try:
+            code, n_regs, _, _ = fp.compile_dag(root, nodes)
+        except ValueError:
+            continue  # over the register / instruction limits: the shim reports these
+        words = (ctypes.c_int32 * (2 * len(code)))(*[w for c in code for w in c])
+        i64 = lambda v: (ctypes.c_int64 * max(len(v), 1))(*v)  # noqa: E731
+        ptrs = (ctypes.c_void_p * n_in)(*([0x1000] * n_in))
+        cs = (ctypes.c_float * len(consts))(*consts)
+        st = lib.spmdb200_forall_map(1, i64([0]), n_in, ptrs, i64([1] * n_in), ctypes.c_void_p(0x2000), i64([1]),
+                                     words, len(code), cs, len(consts), n_regs, None)
+        assert st == 0, (trial, lib.spmdb200_last_error_message().decode())
