@@ -212,3 +212,73 @@ def test_random_2d_stencil_bodies(seed, oracle_mod):
              for name, o in zip(d["inputs"], d["input_offsets"])]
     got = oracle_mod.forall_map(views, (N - 2, M - 2), d["code"], [float(c) for c in d["consts"]])
     assert bits_equal_nan(got, acc_v)
+
+
+@pytest.mark.parametrize("seed", range(16))
+def test_random_guarded_and_multi_output_bodies(seed, oracle_mod):
+    """`if (a <pred> b) Out[i] = v` (in place, or with an else store) and
+    bodies with two outputs, the second reading the first after its store."""
+    rs = np.random.RandomState(2900 + seed)
+    pred = PREDS[seed % len(PREDS)]
+    n = 301
+    a = rs.uniform(-2, 2, n).astype(np.float32)
+    b = rs.uniform(-2, 2, n).astype(np.float32)
+    out0 = rs.uniform(-2, 2, n).astype(np.float32)
+    shim = spmd_mod("mlir_shim")
+    with_else = bool(seed % 2)
+    else_region = ("      %w = arith.subf %a, %b : f32\n      memref.store %w, %Out[%i] : memref<?xf32>\n"
+                   if with_else else "")
+    text = f"""
+func.func @g(%A: memref<?xf32>, %B: memref<?xf32>, %Out: memref<?xf32>, %N: index) attributes {{spmd.kernel}} {{
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  "spmd.forall"(%c0, %N, %c1) ({{
+  ^bb0(%i: index):
+    %a = memref.load %A[%i] : memref<?xf32>
+    %b = memref.load %B[%i] : memref<?xf32>
+    %c = arith.cmpf {pred}, %a, %b : f32
+    %v = arith.mulf %a, %b : f32
+    "spmd.if"(%c) ({{
+      memref.store %v, %Out[%i] : memref<?xf32>
+      "spmd.yield"() : () -> ()
+    }}, {{
+{else_region}      "spmd.yield"() : () -> ()
+    }}) : (i1) -> ()
+    "spmd.yield"() : () -> ()
+  }}) {{operandSegmentSizes = array<i32: 1, 1, 1>}} : (index, index, index) -> ()
+  func.return
+}}
+
+func.func @two(%A: memref<?xf32>, %B: memref<?xf32>, %Out: memref<?xf32>, %N: index) attributes {{spmd.kernel}} {{
+  %c0 = arith.constant 0 : index
+  %c1 = arith.constant 1 : index
+  "spmd.forall"(%c0, %N, %c1) ({{
+  ^bb0(%i: index):
+    %a = memref.load %A[%i] : memref<?xf32>
+    %s = arith.maximumf %a, %a : f32
+    memref.store %s, %B[%i] : memref<?xf32>
+    %bb = memref.load %B[%i] : memref<?xf32>
+    %q = arith.divf %bb, %a : f32
+    memref.store %q, %Out[%i] : memref<?xf32>
+    "spmd.yield"() : () -> ()
+  }}) {{operandSegmentSizes = array<i32: 1, 1, 1>}} : (index, index, index) -> ()
+  func.return
+}}
+"""
+    d = {x["function"]: x for x in shim.describe(text)}
+    g = d["g"]
+    assert g["pattern"] == "map", g
+    env = {"%A": a, "%B": b, "%Out": out0}
+    got = oracle_mod.forall_map([env[x] for x in g["inputs"]], (n,), g["code"], [float(c) for c in g["consts"]])
+    with np.errstate(all="ignore"):
+        cond = _cmp(pred, a, b)
+        want = np.where(cond, a * b, (a - b) if with_else else out0).astype(np.float32)
+    assert bits_equal_nan(got, want)
+    two = d["two"]
+    assert two["pattern"] == "maps"
+    env = {"%A": a, "%B": b.copy(), "%Out": out0.copy()}
+    for m in two["maps"]:
+        env[m["output"]] = oracle_mod.forall_map([env[x] for x in m["inputs"]], (n,), m["code"],
+                                                 [float(c) for c in m["consts"]])
+    with np.errstate(all="ignore"):
+        assert bits_equal_nan(env["%B"], a) and bits_equal_nan(env["%Out"], (a / a).astype(np.float32))
